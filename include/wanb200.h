@@ -1,0 +1,160 @@
+/*
+ * wanb200.h -- C ABI of libwanb200.so, the B200 (sm_100a) kernels behind the Wan2.2-TI2V-5B
+ * DiT block forward.
+ *
+ * The reference (yahavb/wan2-ti2v-5b) has no C boundary: its block is the Python unit
+ * `_FastBlock.forward(x, e, cos, sin, ck, cv)` (models/fast_dit.py:270-311), built from
+ * PyTorch ops (`_lin` fast_dit.py:108, `_modulate` 172-176, `_tp_rms_qk` 134-147, `_tp_rms`
+ * 156-160, `_rope` 163-169, `_gate` 179-181) and an attention backend seam
+ * `fn(q[B,Lq,n,d], k[B,Lk,n,d], v) -> [B,Lq,n,d]` (`_sdpa` 186-189, `_cte` 228-241,
+ * `_nki_cross` 244-255).  Each entry point below replaces one of those ops; the Python package
+ * `wanb200` sequences them behind the same call signature.
+ *
+ * Conventions.  All tensors are device pointers to row-major bf16 ("bf16" below) unless typed
+ * float.  Strides are in elements.  `stream` is a cudaStream_t passed as void*.  Every entry
+ * point validates its arguments on the host, launches asynchronously on `stream`, and returns
+ * 0 or a negative WANB200_E* code; wanb200_last_error() gives a message for the calling
+ * thread's last failure.  Nothing here allocates per call except a one-time per-device error
+ * word (see wanb200_device_error).
+ */
+#ifndef WANB200_H_
+#define WANB200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define WANB200_OK 0
+#define WANB200_EINVAL (-1)   /* bad argument: shape, stride, alignment, null pointer */
+#define WANB200_ECUDA (-2)    /* a CUDA runtime/driver call failed */
+#define WANB200_EDEVICE (-3)  /* a kernel reported a device-side error (see wanb200_device_error) */
+
+/* ---------------------------------------------------------------- GEMM
+ * d[M, N] = epilogue(a[M, K] . w[N, K]^T)  -- nn.Linear with the weight as stored.
+ * Replaces `_lin` / `_mm` (fast_dit.py:103-109) and the elementwise ops that follow them:
+ *   WANB200_EPI_BIAS          d = acc + bias                                  (_lin)
+ *   WANB200_EPI_BIAS_GELU     d = gelu_tanh(acc + bias)                       (ffn[0], ffn[1])
+ *   WANB200_EPI_BIAS_GATE_RES d = residual + (acc + bias) * gate[frame(row)]  (_gate + residual, 294/311)
+ *   WANB200_EPI_BIAS_RES      d = residual + acc + bias                       (cross-attn residual, 305)
+ *   WANB200_EPI_BIAS_SUMSQ    d = acc + bias; rowss[s*M + row] += sum over section s of d^2
+ *                             (the sum of squares of `_tp_rms_qk` 138-140 / `_tp_rms` 158)
+ *   WANB200_EPI_NONE          d = acc (row-parallel partial sum before the TP all-reduce, 127)
+ * gate[f, n] = gate_mod[n] + gate_e0[f * gate_frame_stride + n] (modulation + e0 chunk,
+ * fast_dit.py:276-277), frame(row) = (row % seq_len) / tokens_per_frame.
+ * Limits: K % 64 == 0, N % 32 == 0, lda/ldw/ldd/ldr % 8 == 0, 16-byte aligned pointers.
+ * d may alias residual (in place). */
+#define WANB200_EPI_NONE 0
+#define WANB200_EPI_BIAS 1
+#define WANB200_EPI_BIAS_GELU 2
+#define WANB200_EPI_BIAS_GATE_RES 3
+#define WANB200_EPI_BIAS_RES 4
+#define WANB200_EPI_BIAS_SUMSQ 5
+
+typedef struct wanb200_gemm_params {
+  const void* a; int64_t lda;      /* [M, K] bf16 */
+  const void* w; int64_t ldw;      /* [N, K] bf16 */
+  void* d; int64_t ldd;            /* [M, N] bf16 */
+  int64_t M, N, K;
+  int epilogue;                    /* WANB200_EPI_* */
+  const void* bias;                /* [N] bf16 (required unless EPI_NONE) */
+  const void* residual; int64_t ldr;               /* [M, N] bf16 for *_RES */
+  const void* gate_mod;                            /* [N] bf16 for GATE_RES */
+  const float* gate_e0; int64_t gate_frame_stride; /* e0 row of frame 0, stride between frames */
+  int64_t seq_len, tokens_per_frame;               /* frame(row) for GATE_RES */
+  float* rowss; int64_t ss_section; int ss_nsections; /* SUMSQ: [ss_nsections, M] fp32, pre-zeroed */
+} wanb200_gemm_params;
+
+int wanb200_gemm_bf16(const wanb200_gemm_params* p, void* stream);
+
+/* ---------------------------------------------------------------- attention
+ * o[b, i, h, :] = softmax_j(q[b,i,h,:] . k[b,j,h,:] * softmax_scale) v[b, j, h, :]
+ * Exact (online-softmax) non-causal attention, head_dim 128, any q_len / kv_len >= 1.
+ * Replaces the attention seam `_sdpa` (fast_dit.py:186-189) / `_cte` (228-241) / the NKI NST
+ * kernel `wan_flash_self_attn` (kernels/self_attention_nst.py:49-117) for self-attention and
+ * `_nki_cross` / `wan_cross_attn` (kernels/cross_attention.py:17-123) for cross-attention.
+ * Layout [B, L, H, 128] with the head stride fixed at 128 and token / batch strides given, so
+ * q, k and v may be column slices of one fused QKV buffer.
+ * Limits: head_dim == 128, strides % 8 == 0, 16-byte aligned pointers. */
+typedef struct wanb200_attn_params {
+  const void* q; int64_t q_tok_stride, q_batch_stride;
+  const void* k; int64_t k_tok_stride, k_batch_stride;
+  const void* v; int64_t v_tok_stride, v_batch_stride;
+  void* o; int64_t o_tok_stride, o_batch_stride;
+  int64_t batch, heads, q_len, kv_len, head_dim;
+  float softmax_scale;
+} wanb200_attn_params;
+
+int wanb200_attn_fwd(const wanb200_attn_params* p, void* stream);
+
+/* ---------------------------------------------------------------- LayerNorm (+ modulation)
+ * mode WANB200_LN_MODULATE: out = LN(x) * (1 + scale[frame]) + shift[frame]
+ *   (`blk.norm1/norm2` = WanLayerNorm, wan/modules/model.py:89-99, then `_modulate`,
+ *   fast_dit.py:172-176), shift/scale[f, c] = modulation[idx, c] + e0[f, idx, c].
+ * mode WANB200_LN_AFFINE: out = LN(x) * weight + bias   (`blk.norm3`, model.py:207-209)
+ * LN has no affine in MODULATE mode, eps as given (1e-6).  Optionally zeroes zero_buf[0..n)
+ * (the GEMM sum-of-squares accumulators of the next projection).
+ * Limits: dim % 256 == 0, dim <= 4096. */
+#define WANB200_LN_MODULATE 0
+#define WANB200_LN_AFFINE 1
+
+typedef struct wanb200_ln_params {
+  const void* x; void* out; int64_t rows, dim; float eps;
+  int mode;
+  const void* modulation;                 /* [6, dim] bf16 */
+  const float* e0; int64_t e0_frame_stride; /* [F, 6, dim] fp32 -> frame stride 6*dim */
+  int shift_idx, scale_idx;
+  int64_t seq_len, tokens_per_frame;
+  const void* weight; const void* bias;   /* [dim] bf16 for AFFINE */
+  float* zero_buf; int64_t zero_count;
+} wanb200_ln_params;
+
+int wanb200_layernorm(const wanb200_ln_params* p, void* stream);
+
+/* ---------------------------------------------------------------- QK RMSNorm + 3-D RoPE
+ * In place on column sections of x: y = x * rsqrt(ss[row] * inv_dim + eps) * gamma[c], then
+ * (if rope) the interleaved-pair rotation with cos/sin[pos, pair], pos = row % seq_len,
+ * pair = (c % 128) / 2.  `_tp_rms_qk` + `_rope` (fast_dit.py:134-147, 163-169) for self-attn
+ * q and k (nsections 2); `_tp_rms` (fast_dit.py:156-160) for cross-attn q (nsections 1,
+ * rope 0).  ss are the (TP all-reduced) sums of squares over the global 3072 channels.
+ * Limits: width % 128 == 0, ld % 8 == 0. */
+typedef struct wanb200_qknorm_params {
+  void* x; int64_t ld, rows;
+  int nsections; int64_t col0[2]; int64_t width;
+  const float* ss[2]; const void* gamma[2];
+  float inv_dim, eps;
+  int rope; const float* cos; const float* sin; int64_t seq_len; /* tables [seq_len, 64] fp32 */
+} wanb200_qknorm_params;
+
+int wanb200_qk_norm_rope(const wanb200_qknorm_params* p, void* stream);
+
+/* ---------------------------------------------------------------- bias + gate + residual
+ * out = residual + (y + bias) * gate[frame(row)]   (gate_mod != NULL)
+ * out = residual + y + bias                        (gate_mod == NULL)
+ * The tail of `_row_linear` + `_gate` + residual (fast_dit.py:126-131, 179-181, 294, 305, 311)
+ * when the projection is row-parallel: y is the all-reduced partial sum (the GEMM ran with
+ * WANB200_EPI_NONE).  All tensors [rows, dim] contiguous; out may alias residual.
+ * Limits: dim % 8 == 0. */
+typedef struct wanb200_residual_params {
+  void* out; const void* residual; const void* y; int64_t rows, dim;
+  const void* bias;
+  const void* gate_mod; const float* gate_e0; int64_t gate_frame_stride;
+  int64_t seq_len, tokens_per_frame;
+} wanb200_residual_params;
+
+int wanb200_bias_gate_residual(const wanb200_residual_params* p, void* stream);
+
+/* ---------------------------------------------------------------- status */
+const char* wanb200_last_error(void);
+/* Device-side error word of the current device: 0 or a code (a bounded wait expired inside a
+ * kernel).  Synchronizes the device.  reset != 0 clears it. */
+int wanb200_device_error(int reset);
+/* Library version, e.g. 100 for 0.1.0. */
+int wanb200_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WANB200_H_ */

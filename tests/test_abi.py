@@ -1,0 +1,144 @@
+"""CPU checks of the C ABI: the library loads, exports every entry point include/wanb200.h
+declares, the ctypes parameter structs have the C layout, and argument validation rejects bad
+calls on the host (before any CUDA call, so these run without a GPU)."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from conftest import ROOT
+from wanb200 import _lib as L
+
+HEADER = os.path.join(ROOT, "include", "wanb200.h")
+
+
+def header_functions():
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(wanb200_\w+)\s*\(", src, re.M)))
+
+
+def test_library_exports_every_declared_function():
+    lib = L.load()
+    names = header_functions()
+    assert len(names) >= 8
+    for n in names:
+        assert hasattr(lib, n), n
+    assert set(names) == set(L.EXPORTS)
+    assert lib.wanb200_version() == 100
+
+
+STRUCTS = {
+    "wanb200_gemm_params": L.GemmParams,
+    "wanb200_attn_params": L.AttnParams,
+    "wanb200_ln_params": L.LnParams,
+    "wanb200_qknorm_params": L.QkNormParams,
+    "wanb200_residual_params": L.ResidualParams,
+}
+
+
+def test_ctypes_structs_match_c_layout(tmp_path):
+    lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"', "int main(void) {"]
+    for cname, cls in STRUCTS.items():
+        lines.append(f'  printf("{cname} size %zu\\n", sizeof({cname}));')
+        for fname, _ in cls._fields_:
+            lines.append(f'  printf("{cname} {fname} %zu\\n", offsetof({cname}, {fname}));')
+    lines.append("  return 0;\n}")
+    c = tmp_path / "layout.c"
+    c.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.check_call(["gcc", "-o", str(exe), str(c)])
+    out = subprocess.check_output([str(exe)]).decode().split("\n")
+    got = {}
+    for ln in out:
+        if ln:
+            s, f, v = ln.split()
+            got[(s, f)] = int(v)
+    for cname, cls in STRUCTS.items():
+        assert got[(cname, "size")] == ctypes.sizeof(cls), cname
+        for fname, _ in cls._fields_:
+            assert got[(cname, fname)] == getattr(cls, fname).offset, (cname, fname)
+
+
+def _rc_msg(fn, p):
+    rc = fn(ctypes.byref(p), None)
+    return rc, L.load().wanb200_last_error().decode()
+
+
+def test_gemm_rejects_bad_shapes_on_host():
+    lib = L.load()
+    p = L.GemmParams()
+    p.a = p.w = p.d = 16
+    p.lda = p.ldw = p.ldd = 96
+    p.M, p.N, p.K, p.epilogue = 8, 64, 96, L.EPI_NONE
+    rc, msg = _rc_msg(lib.wanb200_gemm_bf16, p)
+    assert rc == -1 and "multiple of 64" in msg
+    p.K, p.lda, p.ldw = 128, 128, 128
+    p.N = 40
+    rc, msg = _rc_msg(lib.wanb200_gemm_bf16, p)
+    assert rc == -1 and "multiple of 32" in msg
+    p.N, p.ldd = 64, 64
+    p.a = 24  # not 16-byte aligned
+    rc, msg = _rc_msg(lib.wanb200_gemm_bf16, p)
+    assert rc == -1 and "aligned" in msg
+    p.a = 32
+    p.epilogue = L.EPI_BIAS  # bias missing
+    rc, msg = _rc_msg(lib.wanb200_gemm_bf16, p)
+    assert rc == -1 and "bias" in msg
+    p.epilogue = 9
+    rc, msg = _rc_msg(lib.wanb200_gemm_bf16, p)
+    assert rc == -1 and "epilogue" in msg
+
+
+def test_attn_rejects_bad_args_on_host():
+    lib = L.load()
+    p = L.AttnParams()
+    p.q = p.k = p.v = p.o = 256
+    for f in ("q_tok_stride", "k_tok_stride", "v_tok_stride", "o_tok_stride"):
+        setattr(p, f, 384)
+    for f in ("q_batch_stride", "k_batch_stride", "v_batch_stride", "o_batch_stride"):
+        setattr(p, f, 384 * 100)
+    p.batch, p.heads, p.q_len, p.kv_len, p.head_dim, p.softmax_scale = 2, 3, 100, 100, 64, 0.1
+    rc, msg = _rc_msg(lib.wanb200_attn_fwd, p)
+    assert rc == -1 and "head_dim" in msg
+    p.head_dim = 128
+    p.kv_len = 0
+    rc, msg = _rc_msg(lib.wanb200_attn_fwd, p)
+    assert rc == -1 and "positive" in msg
+    p.kv_len = 100
+    p.k_tok_stride = 100  # not a multiple of 8
+    rc, msg = _rc_msg(lib.wanb200_attn_fwd, p)
+    assert rc == -1 and "strides" in msg
+    p.k_tok_stride = 256  # smaller than heads * 128
+    rc, msg = _rc_msg(lib.wanb200_attn_fwd, p)
+    assert rc == -1 and "token stride" in msg
+
+
+def test_layernorm_and_qknorm_reject_bad_args_on_host():
+    lib = L.load()
+    p = L.LnParams()
+    p.x = p.out = 64
+    p.rows, p.dim, p.mode = 4, 300, L.LN_MODULATE
+    rc, msg = _rc_msg(lib.wanb200_layernorm, p)
+    assert rc == -1 and "multiple of 256" in msg
+    p.dim = 512
+    rc, msg = _rc_msg(lib.wanb200_layernorm, p)
+    assert rc == -1 and "modulate" in msg
+    q = L.QkNormParams()
+    q.x, q.ld, q.rows, q.width, q.nsections = 64, 384, 4, 100, 1
+    rc, msg = _rc_msg(lib.wanb200_qk_norm_rope, q)
+    assert rc == -1 and "width" in msg
+    r = L.ResidualParams()
+    r.out = r.residual = r.y = r.bias = 64
+    r.rows, r.dim = 4, 12
+    rc, msg = _rc_msg(lib.wanb200_bias_gate_residual, r)
+    assert rc == -1 and "dim % 8" in msg
+
+
+def test_ops_refuse_cpu_tensors():
+    import torch
+    from wanb200 import ops
+    a = torch.zeros(128, 128, dtype=torch.bfloat16)
+    with pytest.raises(L.WanB200Error):
+        ops.linear(a, a, None, epilogue=L.EPI_NONE)

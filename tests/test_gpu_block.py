@@ -1,0 +1,111 @@
+"""Block- and step-level parity on a B200 against the CPU fp32 oracle (itself pinned to the
+reference by tests/golden).  rel-RMS <= 2e-2 per block and <= 5e-2 at
+the step-0 noise prediction."""
+import os
+
+import pytest
+import torch
+
+from oracle import dit_ref as R
+from wanb200 import _lib as L
+from wanb200 import BlockWeights, FastBlock, FastCrossKV, FastWanDiT, WanSpec, random_block_state
+from wanb200.dit import rope_tables
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+BLOCK_TOL = 2e-2
+STEP_TOL = 5e-2
+
+
+@pytest.fixture(autouse=True)
+def _no_device_error():
+    L.device_error(reset=True)
+    yield
+    assert L.device_error(reset=True) == 0
+
+
+def fp32(sd):
+    return {k: v.float() for k, v in sd.items()}
+
+
+def test_block_matches_reference_golden():
+    """The small golden block (dim 256, 2 heads) from the reference's own ref_fp32.block_fwd."""
+    mg = torch.load(os.path.join(GOLD, "model_small.pt"), weights_only=False)
+    g = torch.load(os.path.join(GOLD, "block_small.pt"), weights_only=False)
+    bsd = R.block_params(mg["state_dict"], 0)
+    w = BlockWeights(bsd, g["num_heads"], DEV)
+    blk = FastBlock(w, g["grid"][0])
+    ck, cv = FastCrossKV(w)(g["context"].to(DEV, torch.bfloat16))
+    x = g["x"].to(DEV, torch.bfloat16)
+    y = blk(x, g["e0"].to(DEV), g["cos"].to(DEV), g["sin"].to(DEV), ck, cv)
+    err = R.rel_rms(y.float().cpu(), g["y"])
+    assert err < BLOCK_TOL, err
+    # the cross K/V on the device against the reference's
+    assert R.rel_rms(ck.float().cpu(), g["ck"]) < 1e-2 and R.rel_rms(cv.float().cpu(), g["cv"]) < 1e-2
+
+
+def test_step_matches_reference_golden():
+    """Two-layer model step-0 noise prediction vs the reference's ref_fp32.main() output."""
+    mg = torch.load(os.path.join(GOLD, "model_small.pt"), weights_only=False)
+    cfg = mg["cfg"]
+    spec = WanSpec(dim=cfg["dim"], ffn_dim=cfg["ffn_dim"], num_heads=cfg["num_heads"], num_layers=cfg["num_layers"],
+                   freq_dim=cfg["freq_dim"], text_dim=cfg["text_dim"], in_dim=cfg["in_dim"], out_dim=cfg["out_dim"],
+                   text_len=cfg["text_len"])
+    lat = mg["latent"]
+    grid = (lat.shape[1], lat.shape[2] // 2, lat.shape[3] // 2)
+    fast = FastWanDiT((spec, mg["state_dict"]), grid, mg["guide"], DEV)
+    fast.set_context(mg["ctx"].to(DEV), mg["ctx_null"].to(DEV))
+    pred = fast(lat.to(DEV), mg["t"])
+    err = R.rel_rms(pred.float().cpu(), mg["noise_pred"])
+    assert err < STEP_TOL, err
+
+
+def _config0_inputs(seed=0, L_grid=(6, 12, 15), B=2, Lc=512):
+    spec = WanSpec()
+    sd = random_block_state(spec, seed)
+    g = torch.Generator().manual_seed(seed + 1)
+    Lx = L_grid[0] * L_grid[1] * L_grid[2]
+    x = torch.randn(B, Lx, spec.dim, generator=g).to(torch.bfloat16).float()
+    e0 = torch.randn(1, L_grid[0], 6, spec.dim, generator=g) * 0.1
+    context = torch.randn(B, Lc, spec.dim, generator=g).to(torch.bfloat16).float()
+    return spec, sd, x, e0, context
+
+
+def test_block_config0_vs_oracle():
+    """one block, dim 3072, 24 heads, B=2, L=1080 (6x12x15), 512 context
+    tokens, seeded N(0, 0.02) weights -- device vs the fp32 CPU oracle."""
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    grid = (6, 12, 15)
+    spec, sd, x, e0, context = _config0_inputs(L_grid=grid)
+    cos, sin = R.rope_tables(R.model_freqs(128), grid, 128)
+    p32 = fp32(sd)
+    ck, cv = R.cross_kv(p32, context, spec.num_heads)
+    y_ref = R.block_fwd(p32, x, e0, cos, sin, ck, cv, grid[0], spec.num_heads)
+
+    w = BlockWeights(sd, spec.num_heads, DEV)
+    ckd, cvd = FastCrossKV(w)(context.to(DEV, torch.bfloat16))
+    cosd, sind = rope_tables(grid, 128, DEV)
+    y = FastBlock(w, grid[0])(x.to(DEV, torch.bfloat16), e0.to(DEV), cosd, sind, ckd, cvd)
+    err = R.rel_rms(y.float().cpu(), y_ref)
+    upd = R.rel_rms((y.float().cpu() - x), (y_ref - x))
+    print(f"config0 block rel-RMS output {err:.2e}, update {upd:.2e}")
+    assert err < BLOCK_TOL
+    assert upd < 5e-2
+
+
+def test_block_is_deterministic_and_functional():
+    grid = (2, 8, 8)
+    spec, sd, x, e0, context = _config0_inputs(seed=3, L_grid=grid, Lc=64)
+    w = BlockWeights(sd, spec.num_heads, DEV)
+    ck, cv = FastCrossKV(w)(context.to(DEV, torch.bfloat16))
+    cos, sin = rope_tables(grid, 128, DEV)
+    blk = FastBlock(w, grid[0])
+    xd = x.to(DEV, torch.bfloat16)
+    x0 = xd.clone()
+    y1 = blk(xd, e0.to(DEV), cos, sin, ck, cv).clone()
+    y2 = blk(xd, e0.to(DEV), cos, sin, ck, cv)
+    assert torch.equal(xd, x0), "the block must not modify its input"
+    # Σx² uses fp32 atomics, so runs may differ in the last bits of the norm scale
+    assert R.rel_rms(y1.float(), y2.float()) < 1e-3

@@ -1,0 +1,191 @@
+"""Kernel parity on a B200: each libwanb200 entry point against a plain PyTorch fp32 reference
+of the same op, at ragged sizes.  Tolerances are relative RMS errors (bf16 output rounding is
+~2^-9 relative, i.e. about 2e-3 RMS)."""
+import math
+
+import pytest
+import torch
+
+from wanb200 import _lib as L
+from wanb200 import ops
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def rel(a, b):
+    a, b = a.double(), b.double()
+    return float((a - b).norm() / b.norm().clamp_min(1e-30))
+
+
+@pytest.fixture(autouse=True)
+def _no_device_error():
+    L.device_error(reset=True)
+    yield
+    assert L.device_error(reset=True) == 0, "a kernel reported a device-side timeout"
+
+
+def randn(*shape, scale=1.0, seed=0):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    return (torch.randn(*shape, generator=g, device=DEV) * scale).to(torch.bfloat16)
+
+
+# ---------------------------------------------------------------------------- GEMM
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 512, 192), (1000, 384, 3072), (77, 1152, 384),
+                                   (2160, 3072, 3072)])
+def test_gemm_bias(M, N, K):
+    a, w, b = randn(M, K, seed=1), randn(N, K, scale=0.05, seed=2), randn(N, scale=0.1, seed=3)
+    out = ops.linear(a, w, b, epilogue=L.EPI_BIAS)
+    ref = a.float() @ w.float().t() + b.float()
+    assert rel(out, ref) < 4e-3
+
+
+def test_gemm_none_and_strided_views():
+    M, N, K = 513, 768, 256
+    big = randn(M, 2 * K, seed=4)
+    a = big[:, K:]  # row stride 2K
+    w = randn(N, K, scale=0.05, seed=5)
+    out = torch.zeros(M, N + 64, dtype=torch.bfloat16, device=DEV)
+    ops.linear(a, w, None, epilogue=L.EPI_NONE, out=out[:, :N])
+    ref = a.float() @ w.float().t()
+    assert rel(out[:, :N], ref) < 4e-3
+    assert torch.count_nonzero(out[:, N:]) == 0
+
+
+def test_gemm_gelu():
+    M, N, K = 700, 1792, 3072
+    a, w, b = randn(M, K, seed=6), randn(N, K, scale=0.02, seed=7), randn(N, scale=0.1, seed=8)
+    out = ops.linear(a, w, b, epilogue=L.EPI_BIAS_GELU)
+    ref = torch.nn.functional.gelu(a.float() @ w.float().t() + b.float(), approximate="tanh")
+    assert rel(out, ref) < 4e-3
+
+
+@pytest.mark.parametrize("inplace", [False, True])
+def test_gemm_gate_residual(inplace):
+    Lx, nf, B = 360, 6, 2
+    M, N, K = B * Lx, 512, 384
+    a, w, b = randn(M, K, seed=9), randn(N, K, scale=0.05, seed=10), randn(N, scale=0.1, seed=11)
+    res = randn(M, N, seed=12)
+    mod = randn(6, N, scale=0.1, seed=13)
+    e0 = torch.randn(nf, 6, N, device=DEV) * 0.1
+    gate = (mod[2], e0[:, 2, :])
+    res0 = res.clone()
+    out = res if inplace else None
+    out = ops.linear(a, w, b, epilogue=L.EPI_BIAS_GATE_RES, residual=res, gate=gate, frames=(Lx, Lx // nf), out=out)
+    g = (mod[2].float() + e0[:, 2, :]).repeat_interleave(Lx // nf, 0).repeat(B, 1)
+    ref = res0.float() + (a.float() @ w.float().t() + b.float()) * g
+    assert rel(out, ref) < 4e-3
+
+
+def test_gemm_residual():
+    M, N, K = 333, 256, 128
+    a, w, b, res = randn(M, K, seed=14), randn(N, K, scale=0.05, seed=15), randn(N, seed=16), randn(M, N, seed=17)
+    out = ops.linear(a, w, b, epilogue=L.EPI_BIAS_RES, residual=res)
+    assert rel(out, res.float() + a.float() @ w.float().t() + b.float()) < 4e-3
+
+
+@pytest.mark.parametrize("Cl", [384, 3072])
+def test_gemm_sumsq_sections(Cl):
+    M, K = 517, 256
+    N = 3 * Cl
+    a, w, b = randn(M, K, seed=18), randn(N, K, scale=0.05, seed=19), randn(N, scale=0.1, seed=20)
+    ss = torch.zeros(2, M, device=DEV)
+    out = ops.linear(a, w, b, epilogue=L.EPI_BIAS_SUMSQ, rowss=ss, ss_section=Cl, ss_nsections=2)
+    ref = a.float() @ w.float().t() + b.float()
+    assert rel(out, ref) < 4e-3
+    ref_ss = torch.stack([ref[:, :Cl].pow(2).sum(1), ref[:, Cl:2 * Cl].pow(2).sum(1)])
+    assert rel(ss, ref_ss) < 1e-3
+
+
+# ---------------------------------------------------------------------------- attention
+def sdpa_ref(q, k, v, scale=None):
+    return torch.nn.functional.scaled_dot_product_attention(
+        q.float().transpose(1, 2), k.float().transpose(1, 2), v.float().transpose(1, 2), scale=scale).transpose(1, 2)
+
+
+@pytest.mark.parametrize("B,H,Lq,Lk", [(1, 1, 128, 128), (2, 3, 200, 77), (2, 3, 1, 1), (1, 2, 127, 129),
+                                       (2, 2, 1080, 1080), (2, 3, 1000, 512), (1, 1, 300, 4100)])
+def test_attention_vs_sdpa(B, H, Lq, Lk):
+    q, k, v = randn(B, Lq, H, 128, seed=21), randn(B, Lk, H, 128, seed=22), randn(B, Lk, H, 128, seed=23)
+    o = ops.attention(q, k, v)
+    assert rel(o, sdpa_ref(q, k, v)) < 1e-2
+
+
+def test_attention_fused_qkv_layout_and_scaled_scores():
+    """q, k, v as column slices of one [B*L, 3*H*128] buffer (the QKV GEMM output); RMS-normed
+    inputs with a gain of 3 so the scores are large (softmax far from uniform)."""
+    B, Lx, H = 2, 1080, 3
+    qkv = randn(B * Lx, 3 * H * 128, seed=24).float()
+    qkv[:, :2 * H * 128] *= 3.0
+    qkv = qkv.to(torch.bfloat16)
+    q = qkv[:, :H * 128].view(B, Lx, H, 128)
+    k = qkv[:, H * 128:2 * H * 128].view(B, Lx, H, 128)
+    v = qkv[:, 2 * H * 128:].view(B, Lx, H, 128)
+    o = ops.attention(q, k, v)
+    assert rel(o, sdpa_ref(q, k, v)) < 1e-2
+
+
+def test_attention_op_registered():
+    q = randn(1, 256, 2, 128, seed=25)
+    o = torch.ops.wanb200.attn(q, q, q, 1.0 / math.sqrt(128))
+    assert rel(o, sdpa_ref(q, q, q)) < 1e-2
+
+
+# ---------------------------------------------------------------------------- norms
+def test_layernorm_modulate_and_affine():
+    B, Lx, nf, C = 2, 1080, 6, 3072
+    x = randn(B * Lx, C, seed=26)
+    mod = randn(6, C, scale=0.1, seed=27)
+    e0 = torch.randn(nf, 6, C, device=DEV) * 0.1
+    zero = torch.full((3, B * Lx), 7.0, device=DEV)
+    h = ops.layernorm_modulate(x, mod, e0, 0, 1, (Lx, Lx // nf), zero=zero)
+    ln = torch.nn.functional.layer_norm(x.float(), (C,), eps=1e-6)
+    sh = (mod[0].float() + e0[:, 0]).repeat_interleave(Lx // nf, 0).repeat(B, 1)
+    sc = (mod[1].float() + e0[:, 1]).repeat_interleave(Lx // nf, 0).repeat(B, 1)
+    assert rel(h, ln * (1 + sc) + sh) < 4e-3
+    assert torch.count_nonzero(zero) == 0
+    wgt, bia = randn(C, seed=28), randn(C, seed=29)
+    h2 = ops.layernorm_affine(x, wgt, bia)
+    ref2 = torch.nn.functional.layer_norm(x.float(), (C,), wgt.float(), bia.float(), eps=1e-6)
+    assert rel(h2, ref2) < 4e-3
+
+
+def test_layernorm_small_dim():
+    x = randn(37, 256, seed=30)
+    wgt, bia = randn(256, seed=31), randn(256, seed=32)
+    h = ops.layernorm_affine(x, wgt, bia)
+    assert rel(h, torch.nn.functional.layer_norm(x.float(), (256,), wgt.float(), bia.float(), eps=1e-6)) < 4e-3
+
+
+def test_qk_norm_rope_vs_oracle():
+    from oracle import dit_ref as R
+    grid = (3, 5, 7)
+    Lx = 105
+    B, H = 2, 3
+    Cl = H * 128
+    qkv = randn(B * Lx, 3 * Cl, seed=33)
+    ref_in = qkv.float().clone()
+    ss = torch.stack([ref_in[:, :Cl].pow(2).sum(1), ref_in[:, Cl:2 * Cl].pow(2).sum(1)]) * 8.0  # "global" dim 8x
+    gq, gk = randn(Cl, scale=0.1, seed=34).float().add(1).to(torch.bfloat16), randn(Cl, seed=35)
+    cos, sin = R.rope_tables(R.model_freqs(128), grid, 128)
+    ops.qk_norm_rope(qkv, [(0, ss[0], gq), (Cl, ss[1], gk)], Cl, 8 * Cl, cos=cos.reshape(Lx, 64).to(DEV),
+                     sin=sin.reshape(Lx, 64).to(DEV), seq_len=Lx)
+    for sec, g in ((0, gq), (1, gk)):
+        x = ref_in[:, sec * Cl:(sec + 1) * Cl]
+        y = x * torch.rsqrt(ss[sec][:, None] / (8 * Cl) + 1e-6) * g.float()
+        y = R.rope(y.view(B, Lx, H, 128).cpu(), cos, sin).reshape(B * Lx, Cl)
+        assert rel(qkv[:, sec * Cl:(sec + 1) * Cl].cpu(), y) < 4e-3
+    assert torch.equal(qkv[:, 2 * Cl:], ref_in[:, 2 * Cl:].to(torch.bfloat16))
+
+
+def test_bias_gate_residual():
+    B, Lx, nf, C = 2, 120, 4, 768
+    res, y, b = randn(B * Lx, C, seed=36), randn(B * Lx, C, seed=37), randn(C, seed=38)
+    mod = randn(6, C, scale=0.1, seed=39)
+    e0 = torch.randn(nf, 6, C, device=DEV) * 0.1
+    out = ops.bias_gate_residual(res, y, b, gate=(mod[5], e0[:, 5, :]), frames=(Lx, Lx // nf))
+    g = (mod[5].float() + e0[:, 5]).repeat_interleave(Lx // nf, 0).repeat(B, 1)
+    assert rel(out, res.float() + (y.float() + b.float()) * g) < 4e-3
+    out2 = ops.bias_gate_residual(res, y, b)
+    assert rel(out2, res.float() + y.float() + b.float()) < 4e-3

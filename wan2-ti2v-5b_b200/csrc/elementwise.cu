@@ -1,0 +1,347 @@
+// HBM-bound kernels of the block: LayerNorm (+ per-frame AdaLN modulation) and the
+// QK-RMSNorm + 3-D RoPE pass.  Both are vectorised 16-byte loads/stores, fp32 math, one
+// rounding to bf16 on the way out.
+#include "common.cuh"
+#include "internal.h"
+
+namespace wanb200 {
+
+constexpr int LN_MAX_VEC = 16;  // dim <= 16 * 256 = 4096
+
+struct LnArgs {
+  const __nv_bfloat16* x;
+  __nv_bfloat16* out;
+  int64_t rows;
+  int dim;
+  float eps;
+  const __nv_bfloat16* modulation;
+  const float* e0;
+  int64_t e0_frame_stride;
+  int shift_idx, scale_idx;
+  int64_t seq_len, tokens_per_frame;
+  const __nv_bfloat16* weight;
+  const __nv_bfloat16* bias;
+  float* zero_buf;
+  int64_t zero_count;
+};
+
+// One warp per row: lane l holds the 16-byte vectors at columns (i*32 + l)*8, i < dim/256.
+//   MODE 0 (modulate): WanLayerNorm without affine (wan/modules/model.py:89-99), then
+//     `_modulate` (models/fast_dit.py:172-176): y * (1 + scale[f]) + shift[f] with
+//     shift/scale[f, c] = modulation[idx, c] + e0[f, idx, c] (fast_dit.py:276-277).
+//   MODE 1 (affine): norm3 = WanLayerNorm(elementwise_affine=True) (model.py:207-209).
+template <int MODE, int NVEC>
+__global__ void __launch_bounds__(256) layernorm_kernel(const LnArgs a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < a.zero_count;
+       i += (int64_t)gridDim.x * blockDim.x)
+    a.zero_buf[i] = 0.f;
+  const int64_t row = (int64_t)blockIdx.x * 8 + warp;
+  if (row >= a.rows) return;
+  const uint4* xr = reinterpret_cast<const uint4*>(a.x + row * a.dim);
+  float x[NVEC][8];
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < NVEC; ++i) {
+    {
+      unpack_bf16x8(__ldg(xr + i * 32 + lane), x[i]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) sum += x[i][k];
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float mean = sum / a.dim;
+  float var = 0.f;
+#pragma unroll
+  for (int i = 0; i < NVEC; ++i) {
+    {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float d = x[i][k] - mean;
+        var = fmaf(d, d, var);
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
+  const float rstd = rsqrtf(var / a.dim + a.eps);
+
+  const float* shp = nullptr;
+  const float* scp = nullptr;
+  if constexpr (MODE == 0) {
+    const int64_t f = (row % a.seq_len) / a.tokens_per_frame;
+    shp = a.e0 + f * a.e0_frame_stride + (int64_t)a.shift_idx * a.dim;
+    scp = a.e0 + f * a.e0_frame_stride + (int64_t)a.scale_idx * a.dim;
+  }
+  uint4* outr = reinterpret_cast<uint4*>(a.out + row * a.dim);
+#pragma unroll
+  for (int i = 0; i < NVEC; ++i) {
+    {
+      const int col = (i * 32 + lane) * 8;
+      float y[8];
+      if constexpr (MODE == 0) {
+        float ms[8], mc[8];
+        unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.modulation + (int64_t)a.shift_idx * a.dim + col)), ms);
+        unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.modulation + (int64_t)a.scale_idx * a.dim + col)), mc);
+        const float4 s0 = __ldg(reinterpret_cast<const float4*>(shp + col));
+        const float4 s1 = __ldg(reinterpret_cast<const float4*>(shp + col + 4));
+        const float4 c0 = __ldg(reinterpret_cast<const float4*>(scp + col));
+        const float4 c1 = __ldg(reinterpret_cast<const float4*>(scp + col + 4));
+        const float sh[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+        const float sc[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) y[k] = fmaf((x[i][k] - mean) * rstd, 1.f + (mc[k] + sc[k]), ms[k] + sh[k]);
+      } else {
+        float w[8], bb[8];
+        unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.weight + col)), w);
+        unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.bias + col)), bb);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) y[k] = fmaf((x[i][k] - mean) * rstd, w[k], bb[k]);
+      }
+      uint4 u;
+      u.x = pack_bf16x2(y[0], y[1]);
+      u.y = pack_bf16x2(y[2], y[3]);
+      u.z = pack_bf16x2(y[4], y[5]);
+      u.w = pack_bf16x2(y[6], y[7]);
+      outr[i * 32 + lane] = u;
+    }
+  }
+}
+
+template <int MODE>
+static void launch_ln(int nvec, const LnArgs& a, unsigned blocks, cudaStream_t st) {
+  switch (nvec) {
+#define WANB200_LN_CASE(n) \
+  case n: layernorm_kernel<MODE, n><<<blocks, 256, 0, st>>>(a); break;
+    WANB200_LN_CASE(1) WANB200_LN_CASE(2) WANB200_LN_CASE(3) WANB200_LN_CASE(4) WANB200_LN_CASE(5)
+    WANB200_LN_CASE(6) WANB200_LN_CASE(7) WANB200_LN_CASE(8) WANB200_LN_CASE(9) WANB200_LN_CASE(10)
+    WANB200_LN_CASE(11) WANB200_LN_CASE(12) WANB200_LN_CASE(13) WANB200_LN_CASE(14) WANB200_LN_CASE(15)
+    default: layernorm_kernel<MODE, 16><<<blocks, 256, 0, st>>>(a); break;
+#undef WANB200_LN_CASE
+  }
+}
+
+int layernorm(const wanb200_ln_params* p, cudaStream_t st) {
+  if (!p) return set_error(WANB200_EINVAL, "layernorm: null params");
+  if (!p->x || !p->out) return set_error(WANB200_EINVAL, "layernorm: null x/out");
+  if (p->rows <= 0 || p->dim <= 0 || p->dim % 256 || p->dim > 256 * LN_MAX_VEC)
+    return set_error(WANB200_EINVAL, "layernorm: dim must be a positive multiple of 256, at most 4096");
+  if (!aligned16(p->x) || !aligned16(p->out)) return set_error(WANB200_EINVAL, "layernorm: x/out must be 16-byte aligned");
+  if (p->mode == WANB200_LN_MODULATE) {
+    if (!p->modulation || !p->e0 || !aligned16(p->modulation) || !aligned16(p->e0) || p->e0_frame_stride % 4 ||
+        p->shift_idx < 0 || p->shift_idx > 5 || p->scale_idx < 0 || p->scale_idx > 5 || p->seq_len <= 0 ||
+        p->tokens_per_frame <= 0)
+      return set_error(WANB200_EINVAL, "layernorm: modulate mode needs modulation, e0, indices, seq_len, tokens_per_frame");
+  } else if (p->mode == WANB200_LN_AFFINE) {
+    if (!p->weight || !p->bias || !aligned16(p->weight) || !aligned16(p->bias))
+      return set_error(WANB200_EINVAL, "layernorm: affine mode needs 16-byte aligned weight and bias");
+  } else {
+    return set_error(WANB200_EINVAL, "layernorm: bad mode");
+  }
+  if (p->zero_count < 0 || (p->zero_count > 0 && !p->zero_buf))
+    return set_error(WANB200_EINVAL, "layernorm: zero_count > 0 needs zero_buf");
+  LnArgs a;
+  a.x = reinterpret_cast<const __nv_bfloat16*>(p->x);
+  a.out = reinterpret_cast<__nv_bfloat16*>(p->out);
+  a.rows = p->rows;
+  a.dim = (int)p->dim;
+  a.eps = p->eps;
+  a.modulation = reinterpret_cast<const __nv_bfloat16*>(p->modulation);
+  a.e0 = p->e0;
+  a.e0_frame_stride = p->e0_frame_stride;
+  a.shift_idx = p->shift_idx;
+  a.scale_idx = p->scale_idx;
+  a.seq_len = p->seq_len > 0 ? p->seq_len : 1;
+  a.tokens_per_frame = p->tokens_per_frame > 0 ? p->tokens_per_frame : 1;
+  a.weight = reinterpret_cast<const __nv_bfloat16*>(p->weight);
+  a.bias = reinterpret_cast<const __nv_bfloat16*>(p->bias);
+  a.zero_buf = p->zero_buf;
+  a.zero_count = p->zero_count;
+  const int64_t blocks = (p->rows + 7) / 8;
+  if (blocks > INT32_MAX) return set_error(WANB200_EINVAL, "layernorm: too many rows");
+  const int nvec = a.dim / 256;
+  if (p->mode == WANB200_LN_MODULATE)
+    launch_ln<0>(nvec, a, (unsigned)blocks, st);
+  else
+    launch_ln<1>(nvec, a, (unsigned)blocks, st);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error("layernorm_kernel launch", e);
+  return WANB200_OK;
+}
+
+// ------------------------------------------------------------------ QK RMSNorm + RoPE
+struct QkArgs {
+  __nv_bfloat16* x;
+  int64_t ld, rows;
+  int64_t col0[2];
+  int width;
+  const float* ss[2];
+  const __nv_bfloat16* gamma[2];
+  float inv_dim, eps;
+  int rope;
+  const float* cos;
+  const float* sin;
+  int64_t seq_len;
+};
+
+// Thread = 8 consecutive channels (4 rotation pairs) of one row of one section.
+// `_tp_rms_qk` (models/fast_dit.py:134-147): x * rsqrt(ss/3072 + eps) * gamma, then `_rope`
+// (fast_dit.py:163-169): (x0, x1) -> (x0 c - x1 s, x0 s + x1 c) with the pair's angle.
+__global__ void __launch_bounds__(256) qknorm_rope_kernel(const QkArgs a) {
+  const int sec = blockIdx.y;
+  const int64_t vpr = a.width >> 3;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= a.rows * vpr) return;
+  const int64_t row = idx / vpr;
+  const int cv = (int)(idx - row * vpr) * 8;
+  const int64_t col0 = sec ? a.col0[1] : a.col0[0];
+  const float* ss = sec ? a.ss[1] : a.ss[0];
+  const __nv_bfloat16* gamma = sec ? a.gamma[1] : a.gamma[0];
+  uint4* p = reinterpret_cast<uint4*>(a.x + row * a.ld + col0 + cv);
+  float v[8], g[8];
+  unpack_bf16x8(*p, v);
+  unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(gamma + cv)), g);
+  const float rs = rsqrtf(__ldg(ss + row) * a.inv_dim + a.eps);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) v[k] *= rs * g[k];
+  if (a.rope) {
+    const int64_t pos = row % a.seq_len;
+    const int pair0 = (cv & 127) >> 1;
+    const float4 c4 = __ldg(reinterpret_cast<const float4*>(a.cos + pos * 64 + pair0));
+    const float4 s4 = __ldg(reinterpret_cast<const float4*>(a.sin + pos * 64 + pair0));
+    float x0, x1;
+    x0 = v[0]; x1 = v[1]; v[0] = x0 * c4.x - x1 * s4.x; v[1] = x0 * s4.x + x1 * c4.x;
+    x0 = v[2]; x1 = v[3]; v[2] = x0 * c4.y - x1 * s4.y; v[3] = x0 * s4.y + x1 * c4.y;
+    x0 = v[4]; x1 = v[5]; v[4] = x0 * c4.z - x1 * s4.z; v[5] = x0 * s4.z + x1 * c4.z;
+    x0 = v[6]; x1 = v[7]; v[6] = x0 * c4.w - x1 * s4.w; v[7] = x0 * s4.w + x1 * c4.w;
+  }
+  uint4 u;
+  u.x = pack_bf16x2(v[0], v[1]);
+  u.y = pack_bf16x2(v[2], v[3]);
+  u.z = pack_bf16x2(v[4], v[5]);
+  u.w = pack_bf16x2(v[6], v[7]);
+  *p = u;
+}
+
+int qk_norm_rope(const wanb200_qknorm_params* p, cudaStream_t st) {
+  if (!p) return set_error(WANB200_EINVAL, "qk_norm_rope: null params");
+  if (!p->x || p->rows <= 0 || p->width <= 0 || p->width % 128 || p->ld % 8 || p->ld <= 0)
+    return set_error(WANB200_EINVAL, "qk_norm_rope: need x, rows > 0, width % 128 == 0, ld % 8 == 0");
+  if (p->nsections < 1 || p->nsections > 2) return set_error(WANB200_EINVAL, "qk_norm_rope: nsections must be 1 or 2");
+  if (!aligned16(p->x)) return set_error(WANB200_EINVAL, "qk_norm_rope: x must be 16-byte aligned");
+  for (int s = 0; s < p->nsections; ++s) {
+    if (!p->ss[s] || !p->gamma[s] || !aligned16(p->gamma[s]) || p->col0[s] < 0 || p->col0[s] % 8 ||
+        p->col0[s] + p->width > p->ld)
+      return set_error(WANB200_EINVAL, "qk_norm_rope: bad section (ss, gamma, col0)");
+  }
+  if (p->rope && (!p->cos || !p->sin || !aligned16(p->cos) || !aligned16(p->sin) || p->seq_len <= 0))
+    return set_error(WANB200_EINVAL, "qk_norm_rope: rope needs 16-byte aligned cos/sin tables and seq_len");
+  QkArgs a;
+  a.x = reinterpret_cast<__nv_bfloat16*>(p->x);
+  a.ld = p->ld;
+  a.rows = p->rows;
+  a.col0[0] = p->col0[0];
+  a.col0[1] = p->col0[1];
+  a.width = (int)p->width;
+  a.ss[0] = p->ss[0];
+  a.ss[1] = p->ss[1];
+  a.gamma[0] = reinterpret_cast<const __nv_bfloat16*>(p->gamma[0]);
+  a.gamma[1] = reinterpret_cast<const __nv_bfloat16*>(p->gamma[1]);
+  a.inv_dim = p->inv_dim;
+  a.eps = p->eps;
+  a.rope = p->rope;
+  a.cos = p->cos;
+  a.sin = p->sin;
+  a.seq_len = p->seq_len > 0 ? p->seq_len : 1;
+  const int64_t total = p->rows * (p->width / 8);
+  const int64_t blocks = (total + 255) / 256;
+  if (blocks > INT32_MAX) return set_error(WANB200_EINVAL, "qk_norm_rope: too large");
+  qknorm_rope_kernel<<<dim3((unsigned)blocks, (unsigned)p->nsections), 256, 0, st>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error("qknorm_rope_kernel launch", e);
+  return WANB200_OK;
+}
+
+// ------------------------------------------------------------------ bias + gate + residual
+struct ResArgs {
+  __nv_bfloat16* out;
+  const __nv_bfloat16* residual;
+  const __nv_bfloat16* y;
+  int64_t rows;
+  int dim;
+  const __nv_bfloat16* bias;
+  const __nv_bfloat16* gate_mod;
+  const float* gate_e0;
+  int64_t gate_frame_stride, seq_len, tokens_per_frame;
+};
+
+// Thread = 8 channels of one row.  `x + _gate(y + b, e[k])` / `x + (y + b)` after the TP
+// all-reduce of a row-parallel projection (models/fast_dit.py:126-131, 179-181).
+template <bool GATE>
+__global__ void __launch_bounds__(256) bias_gate_residual_kernel(const ResArgs a) {
+  const int64_t vpr = a.dim >> 3;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= a.rows * vpr) return;
+  const int64_t row = idx / vpr;
+  const int col = (int)(idx - row * vpr) * 8;
+  float r[8], y[8], b[8];
+  unpack_bf16x8(*reinterpret_cast<const uint4*>(a.residual + row * a.dim + col), r);
+  unpack_bf16x8(*reinterpret_cast<const uint4*>(a.y + row * a.dim + col), y);
+  unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.bias + col)), b);
+  if constexpr (GATE) {
+    float g[8];
+    unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.gate_mod + col)), g);
+    const float* e = a.gate_e0 + ((row % a.seq_len) / a.tokens_per_frame) * a.gate_frame_stride + col;
+    const float4 e0 = __ldg(reinterpret_cast<const float4*>(e)), e1 = __ldg(reinterpret_cast<const float4*>(e + 4));
+    g[0] += e0.x; g[1] += e0.y; g[2] += e0.z; g[3] += e0.w;
+    g[4] += e1.x; g[5] += e1.y; g[6] += e1.z; g[7] += e1.w;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) r[k] = fmaf(y[k] + b[k], g[k], r[k]);
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) r[k] += y[k] + b[k];
+  }
+  uint4 u;
+  u.x = pack_bf16x2(r[0], r[1]);
+  u.y = pack_bf16x2(r[2], r[3]);
+  u.z = pack_bf16x2(r[4], r[5]);
+  u.w = pack_bf16x2(r[6], r[7]);
+  *reinterpret_cast<uint4*>(a.out + row * a.dim + col) = u;
+}
+
+int bias_gate_residual(const wanb200_residual_params* p, cudaStream_t st) {
+  if (!p) return set_error(WANB200_EINVAL, "bias_gate_residual: null params");
+  if (!p->out || !p->residual || !p->y || !p->bias || p->rows <= 0 || p->dim <= 0 || p->dim % 8 ||
+      p->dim > INT32_MAX)
+    return set_error(WANB200_EINVAL, "bias_gate_residual: need out, residual, y, bias, rows > 0, dim % 8 == 0");
+  if (!aligned16(p->out) || !aligned16(p->residual) || !aligned16(p->y) || !aligned16(p->bias))
+    return set_error(WANB200_EINVAL, "bias_gate_residual: pointers must be 16-byte aligned");
+  const bool gate = p->gate_mod != nullptr;
+  if (gate && (!p->gate_e0 || !aligned16(p->gate_mod) || !aligned16(p->gate_e0) || p->gate_frame_stride % 4 ||
+               p->seq_len <= 0 || p->tokens_per_frame <= 0))
+    return set_error(WANB200_EINVAL, "bias_gate_residual: gate needs gate_e0, seq_len, tokens_per_frame");
+  ResArgs a;
+  a.out = reinterpret_cast<__nv_bfloat16*>(p->out);
+  a.residual = reinterpret_cast<const __nv_bfloat16*>(p->residual);
+  a.y = reinterpret_cast<const __nv_bfloat16*>(p->y);
+  a.rows = p->rows;
+  a.dim = (int)p->dim;
+  a.bias = reinterpret_cast<const __nv_bfloat16*>(p->bias);
+  a.gate_mod = reinterpret_cast<const __nv_bfloat16*>(p->gate_mod);
+  a.gate_e0 = p->gate_e0;
+  a.gate_frame_stride = p->gate_frame_stride;
+  a.seq_len = p->seq_len > 0 ? p->seq_len : 1;
+  a.tokens_per_frame = p->tokens_per_frame > 0 ? p->tokens_per_frame : 1;
+  const int64_t blocks = (p->rows * (p->dim / 8) + 255) / 256;
+  if (blocks > INT32_MAX) return set_error(WANB200_EINVAL, "bias_gate_residual: too large");
+  if (gate)
+    bias_gate_residual_kernel<true><<<(unsigned)blocks, 256, 0, st>>>(a);
+  else
+    bias_gate_residual_kernel<false><<<(unsigned)blocks, 256, 0, st>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error("bias_gate_residual_kernel launch", e);
+  return WANB200_OK;
+}
+
+}  // namespace wanb200

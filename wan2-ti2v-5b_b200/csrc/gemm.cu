@@ -1,0 +1,358 @@
+// Persistent tcgen05 GEMM with fused epilogues:  D[M,N] = epi(A[M,K] . W[N,K]^T).
+//
+// The projections of the Wan2.2 DiT block (`_lin` / `_mm`, models/fast_dit.py:103-109, on
+// nn.Linear weights [out, in]): fused QKV (3072 -> 9216), self/cross out-projection,
+// cross-q, FFN up (3072 -> 14336, GELU-tanh) and FFN down (14336 -> 3072, gate + residual).
+//
+// Tile 128 x 256 x 64, 4-stage TMA ring (48 KB / stage), fp32 accumulators in TMEM, two
+// accumulator buffers (2 x 256 columns) so the epilogue of tile t overlaps the main loop of
+// tile t+1.  One CTA per SM, tiles strided over the persistent grid, N fastest so the CTAs
+// running together share A rows and the weight matrix stays L2-resident.
+//
+// Warp roles (192 threads):
+//   warp 0      TMA producer (one lane)
+//   warp 1      TMEM allocator + UMMA issuer (one lane)
+//   warps 2..5  epilogue: warp w drains TMEM lanes 32*(w%4)..+31 (= tile rows), 32 columns
+//               per tcgen05.ld, applies the epilogue in fp32 and stores bf16.
+#include "common.cuh"
+#include "internal.h"
+
+namespace wanb200 {
+
+constexpr int GBM = 128, GBN = 256, GBK = 64, GSTAGES = 4;
+constexpr int G_A_BYTES = GBM * GBK * 2;  // 16 KB
+constexpr int G_B_BYTES = GBN * GBK * 2;  // 32 KB
+constexpr int G_STAGE_BYTES = G_A_BYTES + G_B_BYTES;
+constexpr int G_TILE_BYTES = GSTAGES * G_STAGE_BYTES;
+constexpr int G_SMEM_BYTES = G_TILE_BYTES + 256 + 1024;  // barriers + alignment slack
+constexpr uint32_t G_TMEM_COLS = 512;
+
+struct GemmArgs {
+  __nv_bfloat16* d;
+  int64_t ldd;
+  int M, N, K;
+  const __nv_bfloat16* bias;
+  const __nv_bfloat16* residual;
+  int64_t ldr;
+  const __nv_bfloat16* gate_mod;
+  const float* gate_e0;
+  int64_t gate_frame_stride;
+  int seq_len, tokens_per_frame;
+  float* rowss;
+  int ss_section, ss_nsections;
+  int* err;
+};
+
+template <int EPI>
+__device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v, int row, int col0, float& ss_acc,
+                                                    int& ss_sec) {
+  if constexpr (EPI != WANB200_EPI_NONE) {
+    const uint4* bp = reinterpret_cast<const uint4*>(a.bias + col0);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float b[8];
+      unpack_bf16x8(__ldg(bp + q), b);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[q * 8 + i] += b[i];
+    }
+  }
+  if constexpr (EPI == WANB200_EPI_BIAS_GELU) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
+  }
+  if constexpr (EPI == WANB200_EPI_BIAS_GATE_RES || EPI == WANB200_EPI_BIAS_RES) {
+    if (row < a.M) {
+      const uint4* rp = reinterpret_cast<const uint4*>(a.residual + (int64_t)row * a.ldr + col0);
+      if constexpr (EPI == WANB200_EPI_BIAS_GATE_RES) {
+        const int f = (row % a.seq_len) / a.tokens_per_frame;
+        const float4* ep = reinterpret_cast<const float4*>(a.gate_e0 + (int64_t)f * a.gate_frame_stride + col0);
+        const uint4* mp = reinterpret_cast<const uint4*>(a.gate_mod + col0);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float r[8], g[8];
+          unpack_bf16x8(rp[q], r);
+          unpack_bf16x8(__ldg(mp + q), g);
+          const float4 e_lo = __ldg(ep + 2 * q), e_hi = __ldg(ep + 2 * q + 1);
+          g[0] += e_lo.x; g[1] += e_lo.y; g[2] += e_lo.z; g[3] += e_lo.w;
+          g[4] += e_hi.x; g[5] += e_hi.y; g[6] += e_hi.z; g[7] += e_hi.w;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[q * 8 + i] = r[i] + v[q * 8 + i] * g[i];
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float r[8];
+          unpack_bf16x8(rp[q], r);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[q * 8 + i] += r[i];
+        }
+      }
+    }
+  }
+  if constexpr (EPI == WANB200_EPI_BIAS_SUMSQ) {
+    const int sec = col0 / a.ss_section;
+    if (sec != ss_sec) {
+      if (ss_sec >= 0 && ss_sec < a.ss_nsections && row < a.M) atomicAdd(a.rowss + (int64_t)ss_sec * a.M + row, ss_acc);
+      ss_acc = 0.f;
+      ss_sec = sec;
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) ss_acc = fmaf(v[i], v[i], ss_acc);
+  }
+  if (row < a.M) {
+    uint4* dp = reinterpret_cast<uint4*>(a.d + (int64_t)row * a.ldd + col0);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 u;
+      u.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
+      u.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
+      u.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
+      u.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
+      dp[q] = u;
+    }
+  }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(192, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const GemmArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  const uint32_t tiles = smem_u32(smem);
+  uint8_t* meta = smem + G_TILE_BYTES;
+  const uint32_t full0 = smem_u32(meta);           // GSTAGES x 8
+  const uint32_t empty0 = full0 + 8 * GSTAGES;     // GSTAGES x 8
+  const uint32_t tfull0 = empty0 + 8 * GSTAGES;    // 2 x 8
+  const uint32_t tempty0 = tfull0 + 16;            // 2 x 8
+  const uint32_t done_bar = tempty0 + 16;          // 8
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(meta + 8 * (2 * GSTAGES + 5));
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* err = args.err;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < GSTAGES; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull0 + 8 * b, 1);
+      mbar_init(tempty0 + 8 * b, 128);
+    }
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), G_TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_n = (args.N + GBN - 1) / GBN;
+  const int num_tiles = ((args.M + GBM - 1) / GBM) * num_n;
+  const int kblocks = args.K / GBK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0, issued = 0, last_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        const int m0 = (tile / num_n) * GBM, n0 = (tile % num_n) * GBN;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, abort_flag, err, kErrTimeoutGemmProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t a_dst = tiles + stage * G_STAGE_BYTES;
+          mbar_expect_tx(full0 + 8 * stage, G_STAGE_BYTES);
+          tma_load_2d(a_dst, &tmA, full0 + 8 * stage, kb * GBK, m0);
+          tma_load_2d(a_dst + G_A_BYTES, &tmB, full0 + 8 * stage, kb * GBK, n0);
+          issued |= 1u << stage;
+          last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == GSTAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {  // let every load in flight land before the CTA's shared memory goes away
+        for (int s = 0; s < GSTAGES; ++s)
+          if ((issued >> s) & 1) mbar_drain(full0 + 8 * s, (last_phase >> s) & 1, err);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(GBM, GBN, false, false);
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        if (!mbar_wait(tempty0 + 8 * acc, acc_phase ^ 1, abort_flag, err, kErrTimeoutGemmMma)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * GBN;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(full0 + 8 * stage, phase, abort_flag, err, kErrTimeoutGemmMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = tiles + stage * G_STAGE_BYTES;
+          const uint32_t b_addr = a_addr + G_A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < GBK / 16; ++kk) {
+            umma_bf16(d_tmem, sw128_desc(a_addr + kk * 32, 16, 1024), sw128_desc(b_addr + kk * 32, 16, 1024), idesc,
+                      (kb | kk) != 0);
+          }
+          umma_commit(empty0 + 8 * stage);
+          if (++stage == GSTAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(tfull0 + 8 * acc);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      // every UMMA issued by this thread has completed once done_bar flips
+      umma_commit(done_bar);
+      mbar_drain(done_bar, 0, err);
+    }
+  } else {
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      if (!mbar_wait_warp(tfull0 + 8 * acc, acc_phase, abort_flag, err, kErrTimeoutGemmEpilogue)) break;
+      tc_fence_after();
+      const int m0 = (tile / num_n) * GBM, n0 = (tile % num_n) * GBN;
+      const int row = m0 + r;
+      const uint32_t t_row = tmem_base + (uint32_t(quad * 32) << 16) + acc * GBN;
+      float ss_acc = 0.f;
+      int ss_sec = -1;
+#pragma unroll 1
+      for (int c = 0; c < GBN / 32; ++c) {
+        const int col0 = n0 + c * 32;
+        if (col0 >= args.N) break;  // warp-uniform
+        float v[32];
+        tmem_ld32(t_row + c * 32, v);
+        gemm_epilogue_chunk<EPI>(args, v, row, col0, ss_acc, ss_sec);
+      }
+      if constexpr (EPI == WANB200_EPI_BIAS_SUMSQ) {
+        if (ss_sec >= 0 && ss_sec < args.ss_nsections && row < args.M)
+          atomicAdd(args.rowss + (int64_t)ss_sec * args.M + row, ss_acc);
+      }
+      tc_fence_before();
+      mbar_arrive(tempty0 + 8 * acc);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, G_TMEM_COLS);
+}
+
+// ------------------------------------------------------------------ host launcher
+template <int EPI>
+static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& ga, int grid, cudaStream_t st) {
+  static bool attr_set[kMaxDevices] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(gemm_bf16_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM_BYTES);
+    if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(gemm)", e);
+    attr_set[dev] = true;
+  }
+  gemm_bf16_kernel<EPI><<<grid, 192, G_SMEM_BYTES, st>>>(ta, tb, ga);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error("gemm_bf16_kernel launch", e);
+  return WANB200_OK;
+}
+
+int gemm_bf16(const wanb200_gemm_params* p, cudaStream_t st) {
+  if (!p) return set_error(WANB200_EINVAL, "gemm: null params");
+  if (!p->a || !p->w || !p->d) return set_error(WANB200_EINVAL, "gemm: null a/w/d");
+  if (p->M <= 0 || p->N <= 0 || p->K <= 0) return set_error(WANB200_EINVAL, "gemm: M, N, K must be positive");
+  if (p->K % GBK) return set_error(WANB200_EINVAL, "gemm: K must be a multiple of 64");
+  if (p->N % 32) return set_error(WANB200_EINVAL, "gemm: N must be a multiple of 32");
+  if (p->M > INT32_MAX / 2 || p->N > INT32_MAX / 2 || p->K > INT32_MAX / 2)
+    return set_error(WANB200_EINVAL, "gemm: dimension too large");
+  if (p->lda < p->K || p->ldw < p->K || p->ldd < p->N || (p->lda % 8) || (p->ldw % 8) || (p->ldd % 8))
+    return set_error(WANB200_EINVAL, "gemm: leading dims must be >= the row length and multiples of 8");
+  if (!aligned16(p->a) || !aligned16(p->w) || !aligned16(p->d))
+    return set_error(WANB200_EINVAL, "gemm: a/w/d must be 16-byte aligned");
+  const int epi = p->epilogue;
+  if (epi < WANB200_EPI_NONE || epi > WANB200_EPI_BIAS_SUMSQ) return set_error(WANB200_EINVAL, "gemm: bad epilogue");
+  if (epi != WANB200_EPI_NONE && (!p->bias || !aligned16(p->bias)))
+    return set_error(WANB200_EINVAL, "gemm: epilogue needs a 16-byte aligned bias");
+  if (epi == WANB200_EPI_BIAS_GATE_RES || epi == WANB200_EPI_BIAS_RES) {
+    if (!p->residual || !aligned16(p->residual) || p->ldr < p->N || (p->ldr % 8))
+      return set_error(WANB200_EINVAL, "gemm: residual epilogue needs an aligned residual with ldr >= N, ldr % 8 == 0");
+  }
+  if (epi == WANB200_EPI_BIAS_GATE_RES) {
+    if (!p->gate_mod || !p->gate_e0 || !aligned16(p->gate_mod) || !aligned16(p->gate_e0) ||
+        (p->gate_frame_stride % 4) || p->seq_len <= 0 || p->tokens_per_frame <= 0 || p->seq_len > INT32_MAX ||
+        p->tokens_per_frame > INT32_MAX)
+      return set_error(WANB200_EINVAL, "gemm: gate epilogue needs gate_mod, gate_e0, seq_len, tokens_per_frame");
+  }
+  if (epi == WANB200_EPI_BIAS_SUMSQ) {
+    if (!p->rowss || p->ss_section <= 0 || (p->ss_section % 32) || p->ss_nsections <= 0 || p->ss_section > INT32_MAX)
+      return set_error(WANB200_EINVAL, "gemm: sumsq epilogue needs rowss and a section width that is a multiple of 32");
+  }
+
+  int* err = device_error_word();
+  if (!err) return WANB200_ECUDA;
+  CUtensorMap ta, tb;
+  int rc = make_tmap_2d(&ta, p->a, p->K, p->M, p->lda, GBK, GBM);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tb, p->w, p->K, p->N, p->ldw, GBK, GBN);
+  if (rc) return rc;
+
+  GemmArgs ga;
+  ga.d = reinterpret_cast<__nv_bfloat16*>(p->d);
+  ga.ldd = p->ldd;
+  ga.M = (int)p->M;
+  ga.N = (int)p->N;
+  ga.K = (int)p->K;
+  ga.bias = reinterpret_cast<const __nv_bfloat16*>(p->bias);
+  ga.residual = reinterpret_cast<const __nv_bfloat16*>(p->residual);
+  ga.ldr = p->ldr;
+  ga.gate_mod = reinterpret_cast<const __nv_bfloat16*>(p->gate_mod);
+  ga.gate_e0 = p->gate_e0;
+  ga.gate_frame_stride = p->gate_frame_stride;
+  ga.seq_len = (int)(p->seq_len > 0 ? p->seq_len : 1);
+  ga.tokens_per_frame = (int)(p->tokens_per_frame > 0 ? p->tokens_per_frame : 1);
+  ga.rowss = p->rowss;
+  ga.ss_section = (int)(p->ss_section > 0 ? p->ss_section : 1);
+  ga.ss_nsections = p->ss_nsections;
+  ga.err = err;
+
+  const int64_t tiles = ((p->M + GBM - 1) / GBM) * ((p->N + GBN - 1) / GBN);
+  const int grid = (int)std::min<int64_t>(tiles, num_sms());
+  switch (epi) {
+    case WANB200_EPI_NONE: return launch_gemm<WANB200_EPI_NONE>(ta, tb, ga, grid, st);
+    case WANB200_EPI_BIAS: return launch_gemm<WANB200_EPI_BIAS>(ta, tb, ga, grid, st);
+    case WANB200_EPI_BIAS_GELU: return launch_gemm<WANB200_EPI_BIAS_GELU>(ta, tb, ga, grid, st);
+    case WANB200_EPI_BIAS_GATE_RES: return launch_gemm<WANB200_EPI_BIAS_GATE_RES>(ta, tb, ga, grid, st);
+    case WANB200_EPI_BIAS_RES: return launch_gemm<WANB200_EPI_BIAS_RES>(ta, tb, ga, grid, st);
+    default: return launch_gemm<WANB200_EPI_BIAS_SUMSQ>(ta, tb, ga, grid, st);
+  }
+}
+
+}  // namespace wanb200

@@ -1,0 +1,42 @@
+// Host-side helpers shared by the launchers (not part of the public C ABI).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <algorithm>
+
+#include "../../include/wanb200.h"
+
+namespace wanb200 {
+
+constexpr int kMaxDevices = 64;
+
+// Record a message for wanb200_last_error() and return `code`.
+int set_error(int code, const char* msg);
+int set_cuda_error(const char* what, cudaError_t e);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Per-device int in global memory that kernels write error codes into (allocated once per
+// device on first use; nullptr + last error set on failure).
+int* device_error_word();
+int num_sms();
+
+// 2-D / 4-D bf16 TMA descriptors with 128-byte swizzle and zero fill out of bounds.
+//   2-D: dims {inner, outer}, row stride `ld` elements, box {box_inner, box_outer}.
+//   4-D: dims d[0..3] (d[0] innermost, contiguous), strides s[1..3] in elements, box b[0..3].
+int make_tmap_2d(CUtensorMap* m, const void* base, int64_t inner, int64_t outer, int64_t ld, int box_inner,
+                 int box_outer);
+int make_tmap_4d(CUtensorMap* m, const void* base, const int64_t dims[4], const int64_t strides[4],
+                 const int box[4]);
+
+// Launchers (one per public entry point).
+int gemm_bf16(const wanb200_gemm_params* p, cudaStream_t st);
+int attn_fwd(const wanb200_attn_params* p, cudaStream_t st);
+int layernorm(const wanb200_ln_params* p, cudaStream_t st);
+int qk_norm_rope(const wanb200_qknorm_params* p, cudaStream_t st);
+int bias_gate_residual(const wanb200_residual_params* p, cudaStream_t st);
+
+}  // namespace wanb200

@@ -1,0 +1,107 @@
+"""ctypes binding of libwanb200.so (the C ABI declared in include/wanb200.h).
+
+The library is loaded from this directory only; there is no fallback implementation.  If it
+is missing or a CUDA device is absent, every op raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libwanb200.so")
+
+c_void_p, c_int64, c_int, c_float = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float
+c_float_p = ctypes.POINTER(ctypes.c_float)
+
+EPI_NONE, EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_GATE_RES, EPI_BIAS_RES, EPI_BIAS_SUMSQ = range(6)
+LN_MODULATE, LN_AFFINE = 0, 1
+
+
+class GemmParams(ctypes.Structure):
+    _fields_ = [("a", c_void_p), ("lda", c_int64), ("w", c_void_p), ("ldw", c_int64), ("d", c_void_p),
+                ("ldd", c_int64), ("M", c_int64), ("N", c_int64), ("K", c_int64), ("epilogue", c_int),
+                ("bias", c_void_p), ("residual", c_void_p), ("ldr", c_int64), ("gate_mod", c_void_p),
+                ("gate_e0", c_void_p), ("gate_frame_stride", c_int64), ("seq_len", c_int64),
+                ("tokens_per_frame", c_int64), ("rowss", c_void_p), ("ss_section", c_int64),
+                ("ss_nsections", c_int)]
+
+
+class AttnParams(ctypes.Structure):
+    _fields_ = [("q", c_void_p), ("q_tok_stride", c_int64), ("q_batch_stride", c_int64),
+                ("k", c_void_p), ("k_tok_stride", c_int64), ("k_batch_stride", c_int64),
+                ("v", c_void_p), ("v_tok_stride", c_int64), ("v_batch_stride", c_int64),
+                ("o", c_void_p), ("o_tok_stride", c_int64), ("o_batch_stride", c_int64),
+                ("batch", c_int64), ("heads", c_int64), ("q_len", c_int64), ("kv_len", c_int64),
+                ("head_dim", c_int64), ("softmax_scale", c_float)]
+
+
+class LnParams(ctypes.Structure):
+    _fields_ = [("x", c_void_p), ("out", c_void_p), ("rows", c_int64), ("dim", c_int64), ("eps", c_float),
+                ("mode", c_int), ("modulation", c_void_p), ("e0", c_void_p), ("e0_frame_stride", c_int64),
+                ("shift_idx", c_int), ("scale_idx", c_int), ("seq_len", c_int64), ("tokens_per_frame", c_int64),
+                ("weight", c_void_p), ("bias", c_void_p), ("zero_buf", c_void_p), ("zero_count", c_int64)]
+
+
+class QkNormParams(ctypes.Structure):
+    _fields_ = [("x", c_void_p), ("ld", c_int64), ("rows", c_int64), ("nsections", c_int),
+                ("col0", c_int64 * 2), ("width", c_int64), ("ss", c_void_p * 2), ("gamma", c_void_p * 2),
+                ("inv_dim", c_float), ("eps", c_float), ("rope", c_int), ("cos", c_void_p), ("sin", c_void_p),
+                ("seq_len", c_int64)]
+
+
+class ResidualParams(ctypes.Structure):
+    _fields_ = [("out", c_void_p), ("residual", c_void_p), ("y", c_void_p), ("rows", c_int64), ("dim", c_int64),
+                ("bias", c_void_p), ("gate_mod", c_void_p), ("gate_e0", c_void_p), ("gate_frame_stride", c_int64),
+                ("seq_len", c_int64), ("tokens_per_frame", c_int64)]
+
+
+EXPORTS = ("wanb200_gemm_bf16", "wanb200_attn_fwd", "wanb200_layernorm", "wanb200_qk_norm_rope",
+           "wanb200_bias_gate_residual", "wanb200_last_error", "wanb200_device_error", "wanb200_version")
+
+_lock = threading.Lock()
+_lib = None
+
+
+class WanB200Error(RuntimeError):
+    pass
+
+
+def load():
+    """Load (once) and return the ctypes handle; raises if the library was not built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise WanB200Error(f"{LIB_PATH} is missing: build it with `python wan2-ti2v-5b_b200/build.py` "
+                                   "(there is no fallback implementation)")
+            lib = ctypes.CDLL(LIB_PATH)
+            lib.wanb200_gemm_bf16.argtypes = [ctypes.POINTER(GemmParams), c_void_p]
+            lib.wanb200_attn_fwd.argtypes = [ctypes.POINTER(AttnParams), c_void_p]
+            lib.wanb200_layernorm.argtypes = [ctypes.POINTER(LnParams), c_void_p]
+            lib.wanb200_qk_norm_rope.argtypes = [ctypes.POINTER(QkNormParams), c_void_p]
+            lib.wanb200_bias_gate_residual.argtypes = [ctypes.POINTER(ResidualParams), c_void_p]
+            for fn in ("wanb200_gemm_bf16", "wanb200_attn_fwd", "wanb200_layernorm", "wanb200_qk_norm_rope",
+                       "wanb200_bias_gate_residual"):
+                getattr(lib, fn).restype = c_int
+            lib.wanb200_last_error.restype = ctypes.c_char_p
+            lib.wanb200_last_error.argtypes = []
+            lib.wanb200_device_error.argtypes = [c_int]
+            lib.wanb200_device_error.restype = c_int
+            lib.wanb200_version.restype = c_int
+            _lib = lib
+    return _lib
+
+
+def check(rc: int, what: str):
+    if rc != 0:
+        msg = load().wanb200_last_error().decode(errors="replace")
+        raise WanB200Error(f"{what} failed ({rc}): {msg}")
+
+
+def device_error(reset: bool = False) -> int:
+    """Device-side error word of the current device (synchronizes)."""
+    return load().wanb200_device_error(1 if reset else 0)

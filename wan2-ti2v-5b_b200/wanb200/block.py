@@ -1,0 +1,189 @@
+"""The DiT block forward on the B200 kernels, behind the reference's per-block call signature.
+
+`FastBlock.forward(x, e, cos, sin, ck, cv) -> x` is `_FastBlock.forward` of
+models/fast_dit.py:270-311 (one WanAttentionBlock, batched CFG, per-frame modulation, TP by
+heads with in-graph all-reduces).  `FastCrossKV.forward(context) -> (ck, cv)` is
+`_FastCrossKV` (fast_dit.py:464-477), run once per generation.
+
+Op sequence of one block (N = B*L tokens, C = 3072, C_l = C / TP, F_l = 14336 / TP):
+   1  h   = LN1(x) * (1 + scale) + shift                    layernorm (also zeroes the Σx² slots)
+   2  qkv = h W_qkv^T + b, Σq², Σk² per row                 tcgen05 GEMM, SUMSQ epilogue
+      [TP: all-reduce Σq², Σk²]
+   3  q,k = RoPE(x * rsqrt(Σ/C + eps) * γ)                   qk_norm_rope (in place)
+   4  y   = softmax(q k^T / sqrt(d)) v                       flash attention
+   5  x1  = x + (y W_o^T + b_o) * gate2                      GEMM, GATE_RES epilogue
+      [TP: GEMM partial -> all-reduce -> bias_gate_residual]
+   6  h   = LN3_affine(x1)
+   7  qc  = h W_cq^T + b, Σqc²                              GEMM, SUMSQ  [TP: all-reduce Σ]
+   8  qc  = qc * rsqrt(Σ/C + eps) * γ                        qk_norm_rope (no rotation)
+   9  y   = attention(qc, ck, cv)                            flash attention over 512 keys
+  10  x1 += y W_co^T + b_co                                  GEMM, RES epilogue [TP: AR path]
+  11  h   = LN2(x1) * (1 + scale) + shift
+  12  f   = gelu_tanh(h W_1^T + b_1)                         GEMM, GELU epilogue
+  13  x1 += (f W_2^T + b_2) * gate5                          GEMM, GATE_RES  [TP: AR path]
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import _lib as L
+from . import ops
+from .weights import BlockWeights
+
+BF16 = torch.bfloat16
+
+
+class Workspace:
+    """Scratch activations of one block forward, allocated once per (device, token count)."""
+
+    def __init__(self, n_tok: int, dim: int, local_dim: int, ffn_local: int, device, tp: bool):
+        kw = dict(device=device, dtype=BF16)
+        self.h = torch.empty(n_tok, dim, **kw)
+        self.qkv = torch.empty(n_tok, 3 * local_dim, **kw)
+        self.y = torch.empty(n_tok, local_dim, **kw)
+        self.cq = torch.empty(n_tok, local_dim, **kw)
+        self.f = torch.empty(n_tok, ffn_local, **kw)
+        self.ss = torch.empty(3, n_tok, device=device, dtype=torch.float32)
+        self.part = torch.empty(n_tok, dim, **kw) if tp else None
+
+
+_WS = {}
+
+
+def workspace(n_tok, w: BlockWeights, device, tp: bool) -> Workspace:
+    key = (str(device), n_tok, w.dim, w.local_dim, w.ffn_local, tp)
+    ws = _WS.get(key)
+    if ws is None:
+        ws = _WS[key] = Workspace(n_tok, w.dim, w.local_dim, w.ffn_local, device, tp)
+    return ws
+
+
+def clear_workspaces():
+    _WS.clear()
+
+
+class FastBlock:
+    """One WanAttentionBlock (models/fast_dit.py:260-311) on libwanb200.
+
+    weights: BlockWeights of this TP rank; num_frames: latent frames F (the modulation row of
+    token l is frame l // (L / F)); tp_group: torch.distributed group of the TP ranks (None or
+    size 1 = single GPU).
+    """
+
+    def __init__(self, weights: BlockWeights, num_frames: int, tp_group=None, eps: float = 1e-6):
+        self.w = weights
+        self.num_frames = num_frames
+        self.tp_group = tp_group
+        self.tp = weights.tp_size > 1
+        self.eps = eps
+
+    def _all_reduce(self, t):
+        if self.tp:
+            dist.all_reduce(t, group=self.tp_group)
+
+    def forward(self, x, e, cos, sin, ck, cv):
+        """x [B, L, C] bf16; e [1, F, 6, C] per-frame time projection (any float dtype);
+        cos/sin [1, L, 1, 64] fp32; ck/cv [B, Lc, H_local, 128] bf16 -> new x [B, L, C] bf16."""
+        w = self.w
+        B, Lx, C = x.shape
+        nf = self.num_frames
+        if Lx % nf:
+            raise ValueError(f"sequence length {Lx} is not a multiple of {nf} frames")
+        tpf = Lx // nf
+        N, Cl, nl = B * Lx, w.local_dim, w.local_heads
+        frames = (Lx, tpf)
+        xf = x.reshape(N, C)
+        if not xf.is_contiguous():
+            xf = xf.contiguous()
+        e0 = e.reshape(-1, 6, C)
+        if e0.dtype != torch.float32 or not e0.is_contiguous():
+            e0 = e0.float().contiguous()
+        if e0.shape[0] != nf:
+            raise ValueError(f"e has {e0.shape[0]} frames, expected {nf}")
+        cos2 = cos.reshape(Lx, -1)
+        sin2 = sin.reshape(Lx, -1)
+        if cos2.dtype != torch.float32 or not cos2.is_contiguous():
+            cos2, sin2 = cos2.float().contiguous(), sin2.float().contiguous()
+        ws = workspace(N, w, x.device, self.tp)
+        mod = w.modulation
+
+        # -- self-attention
+        ops.layernorm_modulate(xf, mod, e0, 0, 1, frames, out=ws.h, eps=self.eps, zero=ws.ss)
+        ops.linear(ws.h, w.w_qkv, w.b_qkv, epilogue=L.EPI_BIAS_SUMSQ, out=ws.qkv, rowss=ws.ss,
+                   ss_section=Cl, ss_nsections=2)
+        self._all_reduce(ws.ss[0:2])
+        ops.qk_norm_rope(ws.qkv, [(0, ws.ss[0], w.g_q), (Cl, ws.ss[1], w.g_k)], Cl, C, eps=self.eps,
+                         cos=cos2, sin=sin2, seq_len=Lx)
+        q = ws.qkv[:, :Cl].view(B, Lx, nl, 128)
+        k = ws.qkv[:, Cl:2 * Cl].view(B, Lx, nl, 128)
+        v = ws.qkv[:, 2 * Cl:].view(B, Lx, nl, 128)
+        ops.attention(q, k, v, out=ws.y.view(B, Lx, nl, 128))
+        x1 = torch.empty_like(xf)
+        gate2 = (mod[2], e0[:, 2, :])
+        if self.tp:
+            ops.linear(ws.y, w.w_o, None, epilogue=L.EPI_NONE, out=ws.part)
+            self._all_reduce(ws.part)
+            ops.bias_gate_residual(xf, ws.part, w.b_o, gate=gate2, frames=frames, out=x1)
+        else:
+            ops.linear(ws.y, w.w_o, w.b_o, epilogue=L.EPI_BIAS_GATE_RES, out=x1, residual=xf, gate=gate2,
+                       frames=frames)
+
+        # -- cross-attention (ck/cv cached per generation)
+        ops.layernorm_affine(x1, w.ln3_w, w.ln3_b, out=ws.h, eps=self.eps)
+        ops.linear(ws.h, w.w_cq, w.b_cq, epilogue=L.EPI_BIAS_SUMSQ, out=ws.cq, rowss=ws.ss[2],
+                   ss_section=Cl, ss_nsections=1)
+        self._all_reduce(ws.ss[2])
+        ops.qk_norm_rope(ws.cq, [(0, ws.ss[2], w.g_cq)], Cl, C, eps=self.eps)
+        ops.attention(ws.cq.view(B, Lx, nl, 128), ck, cv, out=ws.y.view(B, Lx, nl, 128))
+        if self.tp:
+            ops.linear(ws.y, w.w_co, None, epilogue=L.EPI_NONE, out=ws.part)
+            self._all_reduce(ws.part)
+            ops.bias_gate_residual(x1, ws.part, w.b_co, out=x1)
+        else:
+            ops.linear(ws.y, w.w_co, w.b_co, epilogue=L.EPI_BIAS_RES, out=x1, residual=x1)
+
+        # -- FFN
+        ops.layernorm_modulate(x1, mod, e0, 3, 4, frames, out=ws.h, eps=self.eps)
+        ops.linear(ws.h, w.w1, w.b1, epilogue=L.EPI_BIAS_GELU, out=ws.f)
+        gate5 = (mod[5], e0[:, 5, :])
+        if self.tp:
+            ops.linear(ws.f, w.w2, None, epilogue=L.EPI_NONE, out=ws.part)
+            self._all_reduce(ws.part)
+            ops.bias_gate_residual(x1, ws.part, w.b2, gate=gate5, frames=frames, out=x1)
+        else:
+            ops.linear(ws.f, w.w2, w.b2, epilogue=L.EPI_BIAS_GATE_RES, out=x1, residual=x1, gate=gate5,
+                       frames=frames)
+        return x1.view(B, Lx, C)
+
+    __call__ = forward
+
+    # kernel launches per forward (for the bench's gpu_launches count)
+    @property
+    def launches(self) -> int:
+        return 13 if not self.tp else 16
+
+
+class FastCrossKV:
+    """A block's cross-attention K (RMS-normed over all heads) and V from the text context,
+    once per generation (models/fast_dit.py:464-477)."""
+
+    def __init__(self, weights: BlockWeights, tp_group=None, eps: float = 1e-6):
+        self.w, self.tp_group, self.eps = weights, tp_group, eps
+
+    def forward(self, context):
+        """context [B, Lc, C] bf16 -> ck, cv [B, Lc, H_local, 128] bf16 (views of one buffer)."""
+        w = self.w
+        B, Lc, C = context.shape
+        N, Cl = B * Lc, w.local_dim
+        ctx = context.reshape(N, C).to(BF16).contiguous()
+        ss = torch.zeros(N, device=context.device, dtype=torch.float32)
+        kv = ops.linear(ctx, w.w_ckv, w.b_ckv, epilogue=L.EPI_BIAS_SUMSQ, rowss=ss, ss_section=Cl, ss_nsections=1)
+        if w.tp_size > 1:
+            dist.all_reduce(ss, group=self.tp_group)
+        ops.qk_norm_rope(kv, [(0, ss, w.g_ck)], Cl, C, eps=self.eps)
+        ck = kv[:, :Cl].view(B, Lc, w.local_heads, 128)
+        cv = kv[:, Cl:].view(B, Lc, w.local_heads, 128)
+        return ck, cv
+
+    __call__ = forward

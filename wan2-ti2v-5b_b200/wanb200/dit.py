@@ -1,0 +1,170 @@
+"""FastWanDiT on the B200 kernels: the denoise-step driver around the 30 block ops.
+
+Mirrors `FastWanDiT` of models/fast_dit.py:561-697:
+    fast = FastWanDiT(model, grid=(F, H/2, W/2), guide_scale=5.0, device=dev)
+    fast.set_context(ctx_cond, ctx_null)     # [1, 512, 4096] each, once per prompt
+    noise_pred = fast(latent, t)             # latent [48, F, H, W], t scalar -> [48, F, H, W]
+
+`model` is either a reference `WanModel` (any object with `.state_dict()` and the WanModel
+config attributes) or a `(WanSpec, state_dict)` pair.  Batched CFG: cond and uncond run as a
+batch of 2 through every block.  With `tp_group` of size T > 1 each rank holds 24/T heads and
+1/T of the FFN, and the block ops all-reduce over the group (TP by heads, as the reference's
+`shard_model_tp`, models/tp_utils.py:378-458).
+
+The time / text / patch embeddings and the head are small (about 1% of the step) and run as
+fp32 torch ops on the GPU around the block kernels.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+
+from .block import FastBlock, FastCrossKV
+from .weights import BlockWeights, WanSpec, block_state
+
+BF16 = torch.bfloat16
+
+
+def rope_params(max_seq_len: int, dim: int, theta: float = 10000.0) -> torch.Tensor:
+    """[max_seq_len, dim/2] angles (wan/modules/rope_neuron.py:14-24)."""
+    inv = 1.0 / torch.pow(theta, torch.arange(0, dim, 2).float().div(dim))
+    return torch.outer(torch.arange(max_seq_len).float(), inv)
+
+
+def model_freqs(head_dim: int) -> torch.Tensor:
+    d = head_dim
+    return torch.cat([rope_params(1024, d - 4 * (d // 6)), rope_params(1024, 2 * (d // 6)),
+                      rope_params(1024, 2 * (d // 6))], dim=1)
+
+
+def rope_tables(grid, head_dim: int, device):
+    """cos/sin [1, L, 1, d/2] fp32 for a (F, H, W) token grid (models/fast_dit.py:548-558)."""
+    f, h, w = grid
+    c = head_dim // 2
+    fr = model_freqs(head_dim).split([c - 2 * (c // 3), c // 3, c // 3], dim=1)
+    ang = torch.cat([fr[0][:f].view(f, 1, 1, -1).expand(f, h, w, -1),
+                     fr[1][:h].view(1, h, 1, -1).expand(f, h, w, -1),
+                     fr[2][:w].view(1, 1, w, -1).expand(f, h, w, -1)], dim=-1).reshape(1, f * h * w, 1, c)
+    return torch.cos(ang).to(device), torch.sin(ang).to(device)
+
+
+def sinusoidal_embedding_1d(dim: int, position: torch.Tensor) -> torch.Tensor:
+    """(wan/modules/model.py:15-25) in float64."""
+    half = dim // 2
+    position = position.type(torch.float64)
+    s = torch.outer(position, torch.pow(10000, -torch.arange(half).to(position).div(half)))
+    return torch.cat([torch.cos(s), torch.sin(s)], dim=1)
+
+
+def _spec_and_state(model):
+    if isinstance(model, tuple):
+        return model
+    sd = model.state_dict()
+    spec = WanSpec(dim=model.dim, ffn_dim=model.ffn_dim, num_heads=model.num_heads, num_layers=len(model.blocks),
+                   freq_dim=model.freq_dim, text_dim=model.text_dim, in_dim=model.in_dim, out_dim=model.out_dim,
+                   patch_size=tuple(model.patch_size), text_len=model.text_len, eps=model.eps)
+    return spec, sd
+
+
+class FastWanDiT:
+    def __init__(self, model, grid, guide_scale, device, tp_group=None, num_layers=None):
+        spec, sd = _spec_and_state(model)
+        self.spec = spec
+        self.grid = tuple(int(g) for g in grid)
+        self.num_frames = self.grid[0]
+        self.seq_len = self.grid[0] * self.grid[1] * self.grid[2]
+        self.guide_scale = float(guide_scale)
+        self.device = torch.device(device)
+        self.tp_group = tp_group
+        tp = dist.get_world_size(tp_group) if (tp_group is not None and dist.is_initialized()) else 1
+        rank = dist.get_rank(tp_group) if tp > 1 else 0
+        self.tp_size, self.tp_rank = tp, rank
+        self.cos, self.sin = rope_tables(self.grid, spec.head_dim, self.device)
+        nl = spec.num_layers if num_layers is None else num_layers
+
+        def f32(k):
+            return sd[k].to(device=self.device, dtype=torch.float32)
+
+        self.emb = {k: f32(k) for k in sd if not k.startswith("blocks.")}
+        self.block_weights = [BlockWeights(block_state(sd, i), spec.num_heads, self.device, rank, tp)
+                              for i in range(nl)]
+        self.blocks = [FastBlock(w, self.num_frames, tp_group, spec.eps) for w in self.block_weights]
+        self.cross_kv = [FastCrossKV(w, tp_group, spec.eps) for w in self.block_weights]
+        self.context = None
+
+    # ------------------------------------------------------------------ embeddings (torch, fp32)
+    def set_context(self, ctx_cond, ctx_null):
+        """Text embedding + every block's cross K/V, once per prompt (fast_dit.py:658-664)."""
+        m = self.emb
+        ctx = torch.cat([ctx_cond.reshape(1, -1, ctx_cond.shape[-1]), ctx_null.reshape(1, -1, ctx_null.shape[-1])])
+        ctx = ctx.to(self.device, torch.float32)
+        h = F.gelu(F.linear(ctx, m["text_embedding.0.weight"], m["text_embedding.0.bias"]), approximate="tanh")
+        context = F.linear(h, m["text_embedding.2.weight"], m["text_embedding.2.bias"]).to(BF16)
+        self.context = [kv(context) for kv in self.cross_kv]
+
+    def time_embed(self, t):
+        """Per-frame embedding, frame 0 (the image frame) at t=0 (fast_dit.py:677-687).
+        Returns e [1, F, C] fp32 and e0 [F, 6, C] fp32."""
+        m = self.emb
+        tf = torch.full((self.num_frames,), float(t), dtype=torch.float64)
+        tf[0] = 0.0
+        s = sinusoidal_embedding_1d(self.spec.freq_dim, tf).float().to(self.device).unsqueeze(0)
+        e = F.linear(F.silu(F.linear(s, m["time_embedding.0.weight"], m["time_embedding.0.bias"])),
+                     m["time_embedding.2.weight"], m["time_embedding.2.bias"])
+        e0 = F.linear(F.silu(e), m["time_projection.1.weight"], m["time_projection.1.bias"])
+        return e, e0.reshape(self.num_frames, 6, self.spec.dim).contiguous()
+
+    def patch(self, latent):
+        """Conv3d patchify (stride = kernel) as one fp32 matmul -> x [2, L, C] bf16."""
+        m = self.emb
+        C_in, Fr, H, W = latent.shape
+        p, q, r = self.spec.patch_size
+        lat = latent.to(self.device, torch.float32)
+        x = lat.view(C_in, Fr // p, p, H // q, q, W // r, r).permute(1, 3, 5, 0, 2, 4, 6)
+        x = x.reshape(-1, C_in * p * q * r)
+        wt = m["patch_embedding.weight"].reshape(self.spec.dim, -1)
+        x = torch.addmm(m["patch_embedding.bias"], x, wt.t())
+        return x.to(BF16).unsqueeze(0).expand(2, -1, -1).contiguous()
+
+    def head(self, x, e):
+        """LN + 2-way modulation + Linear, unpatchify, CFG combine (fast_dit.py:480-505)."""
+        m = self.emb
+        f, h, w = self.grid
+        p, q, r = self.spec.patch_size
+        c = self.spec.out_dim
+        B, Lx, C = x.shape
+        mod = (m["head.modulation"].unsqueeze(0) + e.unsqueeze(2))  # [1, F, 2, C]
+        xn = F.layer_norm(x.float(), (C,), eps=self.spec.eps).view(B, f, Lx // f, C)
+        xn = (xn * (1 + mod[:, :, 1].unsqueeze(2)) + mod[:, :, 0].unsqueeze(2)).view(B, Lx, C)
+        y = F.linear(xn, m["head.head.weight"], m["head.head.bias"])
+        y = y.view(B, f, h, w, p, q, r, c).permute(0, 7, 1, 4, 2, 5, 3, 6).reshape(B, c, f * p, h * q, w * r)
+        return y[1] + self.guide_scale * (y[0] - y[1])
+
+    # ------------------------------------------------------------------ step
+    def forward_blocks(self, x, e0):
+        for blk, (ck, cv) in zip(self.blocks, self.context):
+            x = blk(x, e0, self.cos, self.sin, ck, cv)
+        return x
+
+    def __call__(self, latent, t):
+        if self.context is None:
+            raise RuntimeError("call set_context() first")
+        e, e0 = self.time_embed(t)
+        x = self.patch(latent)
+        x = self.forward_blocks(x, e0)
+        return self.head(x, e)
+
+    @property
+    def launches_per_step(self) -> int:
+        return sum(b.launches for b in self.blocks)
+
+
+def block_flops(n_tok: int, seq_len: int, dim: int = 3072, ffn: int = 14336, heads: int = 24, ctx_len: int = 512,
+                batch: int = 2) -> dict:
+    """Algorithmic FLOPs of one block (the roofline basis): GEMMs N(12C^2 + 4 C F), self-attention
+    4 B H L^2 d, cross-attention 4 B H L Lc d."""
+    d = dim // heads
+    gemm = 2 * n_tok * (6 * dim * dim + 2 * dim * ffn)
+    return {"gemm": gemm, "self_attn": 4 * batch * heads * seq_len * seq_len * d,
+            "cross_attn": 4 * batch * heads * seq_len * ctx_len * d}

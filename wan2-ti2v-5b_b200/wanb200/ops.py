@@ -1,0 +1,184 @@
+"""Torch-facing wrappers of the libwanb200 entry points.
+
+Each function takes CUDA tensors, checks dtype / layout on the host, fills the C parameter
+struct and launches on the current torch stream.  There is no eager fallback: a missing
+library or a non-CUDA tensor raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import _lib as L
+
+BF16 = torch.bfloat16
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _need(cond: bool, msg: str):
+    if not cond:
+        raise ValueError(msg)
+
+
+def _cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise L.WanB200Error("libwanb200 ops need CUDA tensors (no CPU fallback)")
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+def _rows(t: torch.Tensor, name: str):
+    _need(t.dim() == 2 and t.stride(1) == 1, f"{name} must be 2-D with unit column stride")
+    return t.stride(0)
+
+
+# ---------------------------------------------------------------------------- GEMM
+def linear(a, w, bias=None, *, epilogue=L.EPI_BIAS, out=None, residual=None, gate=None, frames=None,
+           rowss=None, ss_section=0, ss_nsections=0):
+    """out[M, N] = epilogue(a[M, K] @ w[N, K]^T) on tcgen05 (see include/wanb200.h).
+
+    gate: (gate_mod [N] bf16, gate_e0 [F, N] fp32 view with unit column stride) for EPI_BIAS_GATE_RES.
+    frames: (seq_len, tokens_per_frame) mapping a row to its latent frame.
+    rowss: fp32 [ss_nsections, M] accumulators for EPI_BIAS_SUMSQ (must be zeroed first).
+    """
+    _cuda(a, w, bias, out, residual, rowss)
+    _need(a.dtype == BF16 and w.dtype == BF16, "linear: a and w must be bf16")
+    lda, ldw = _rows(a, "a"), _rows(w, "w")
+    M, K = a.shape
+    N = w.shape[0]
+    _need(w.shape[1] == K, f"linear: a is [*, {K}] but w is {tuple(w.shape)}")
+    if out is None:
+        out = torch.empty(M, N, dtype=BF16, device=a.device)
+    ldd = _rows(out, "out")
+    p = L.GemmParams()
+    p.a, p.lda, p.w, p.ldw, p.d, p.ldd = _p(a), lda, _p(w), ldw, _p(out), ldd
+    p.M, p.N, p.K, p.epilogue = M, N, K, epilogue
+    p.bias = _p(bias)
+    if residual is not None:
+        p.residual, p.ldr = _p(residual), _rows(residual, "residual")
+    if gate is not None:
+        gm, ge = gate
+        _need(gm.dtype == BF16 and ge.dtype == torch.float32 and ge.stride(-1) == 1, "linear: bad gate tensors")
+        p.gate_mod, p.gate_e0, p.gate_frame_stride = _p(gm), _p(ge), ge.stride(0)
+    if frames is not None:
+        p.seq_len, p.tokens_per_frame = frames
+    if rowss is not None:
+        _need(rowss.dtype == torch.float32, "linear: rowss must be fp32")
+        p.rowss, p.ss_section, p.ss_nsections = _p(rowss), ss_section, ss_nsections
+    L.check(L.load().wanb200_gemm_bf16(ctypes.byref(p), _stream(a)), "wanb200_gemm_bf16")
+    return out
+
+
+# ---------------------------------------------------------------------------- attention
+def attention(q, k, v, out=None, softmax_scale=None):
+    """o = softmax(q k^T * scale) v on [B, L, H, 128] tensors (head stride 128, unit d stride)."""
+    _cuda(q, k, v, out)
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _need(t.dtype == BF16 and t.dim() == 4 and t.shape[-1] == 128 and t.stride(3) == 1 and t.stride(2) == 128,
+              f"attention: {name} must be bf16 [B, L, H, 128] with head stride 128")
+    B, Lq, H, D = q.shape
+    _need(k.shape[0] == B and k.shape[2] == H and v.shape == k.shape, "attention: q/k/v shape mismatch")
+    if out is None:
+        out = torch.empty(B, Lq, H, D, dtype=BF16, device=q.device)
+    _need(out.stride(3) == 1 and out.stride(2) == 128, "attention: out must have head stride 128")
+    p = L.AttnParams()
+    p.q, p.q_tok_stride, p.q_batch_stride = _p(q), q.stride(1), q.stride(0)
+    p.k, p.k_tok_stride, p.k_batch_stride = _p(k), k.stride(1), k.stride(0)
+    p.v, p.v_tok_stride, p.v_batch_stride = _p(v), v.stride(1), v.stride(0)
+    p.o, p.o_tok_stride, p.o_batch_stride = _p(out), out.stride(1), out.stride(0)
+    p.batch, p.heads, p.q_len, p.kv_len, p.head_dim = B, H, Lq, k.shape[1], D
+    p.softmax_scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(D)
+    L.check(L.load().wanb200_attn_fwd(ctypes.byref(p), _stream(q)), "wanb200_attn_fwd")
+    return out
+
+
+# ---------------------------------------------------------------------------- norms
+def layernorm_modulate(x, modulation, e0, shift_idx, scale_idx, frames, out=None, eps=1e-6, zero=None):
+    """LN(x) * (1 + scale[f]) + shift[f]; modulation [6, C] bf16, e0 [F, 6, C] fp32."""
+    _cuda(x, modulation, e0, out, zero)
+    _need(x.dtype == BF16 and x.is_contiguous() and x.dim() == 2, "layernorm: x must be contiguous bf16 [M, C]")
+    _need(e0.dtype == torch.float32 and e0.is_contiguous() and modulation.dtype == BF16, "layernorm: bad mod tensors")
+    M, C = x.shape
+    if out is None:
+        out = torch.empty_like(x)
+    p = L.LnParams()
+    p.x, p.out, p.rows, p.dim, p.eps, p.mode = _p(x), _p(out), M, C, eps, L.LN_MODULATE
+    p.modulation, p.e0, p.e0_frame_stride = _p(modulation), _p(e0), 6 * C
+    p.shift_idx, p.scale_idx = shift_idx, scale_idx
+    p.seq_len, p.tokens_per_frame = frames
+    if zero is not None:
+        p.zero_buf, p.zero_count = _p(zero), zero.numel()
+    L.check(L.load().wanb200_layernorm(ctypes.byref(p), _stream(x)), "wanb200_layernorm")
+    return out
+
+
+def layernorm_affine(x, weight, bias, out=None, eps=1e-6, zero=None):
+    _cuda(x, weight, bias, out, zero)
+    _need(x.dtype == BF16 and x.is_contiguous() and x.dim() == 2, "layernorm: x must be contiguous bf16 [M, C]")
+    M, C = x.shape
+    if out is None:
+        out = torch.empty_like(x)
+    p = L.LnParams()
+    p.x, p.out, p.rows, p.dim, p.eps, p.mode = _p(x), _p(out), M, C, eps, L.LN_AFFINE
+    p.weight, p.bias = _p(weight), _p(bias)
+    if zero is not None:
+        p.zero_buf, p.zero_count = _p(zero), zero.numel()
+    L.check(L.load().wanb200_layernorm(ctypes.byref(p), _stream(x)), "wanb200_layernorm")
+    return out
+
+
+def qk_norm_rope(x, sections, width, global_dim, eps=1e-6, cos=None, sin=None, seq_len=0):
+    """In place on x [M, ld]: for each (col0, ss [M] fp32, gamma [width] bf16) section,
+    x[:, col0:col0+width] = RoPE(x * rsqrt(ss/global_dim + eps) * gamma) (RoPE if cos given)."""
+    _cuda(x, cos, sin)
+    ld = _rows(x, "x")
+    p = L.QkNormParams()
+    p.x, p.ld, p.rows, p.nsections, p.width = _p(x), ld, x.shape[0], len(sections), width
+    for i, (c0, ss, g) in enumerate(sections):
+        _cuda(ss, g)
+        _need(ss.dtype == torch.float32 and g.dtype == BF16, "qk_norm_rope: ss fp32, gamma bf16")
+        p.col0[i], p.ss[i], p.gamma[i] = c0, _p(ss), _p(g)
+    p.inv_dim, p.eps = 1.0 / global_dim, eps
+    if cos is not None:
+        _need(cos.dtype == torch.float32 and cos.is_contiguous() and sin.is_contiguous(), "qk_norm_rope: bad tables")
+        p.rope, p.cos, p.sin, p.seq_len = 1, _p(cos), _p(sin), seq_len
+    L.check(L.load().wanb200_qk_norm_rope(ctypes.byref(p), _stream(x)), "wanb200_qk_norm_rope")
+    return x
+
+
+def bias_gate_residual(residual, y, bias, gate=None, frames=None, out=None):
+    """out = residual + (y + bias) * gate[f]  (or residual + y + bias without gate)."""
+    _cuda(residual, y, bias, out)
+    _need(residual.is_contiguous() and y.is_contiguous() and residual.shape == y.shape, "bias_gate_residual: layout")
+    M, C = residual.shape
+    if out is None:
+        out = torch.empty_like(residual)
+    p = L.ResidualParams()
+    p.out, p.residual, p.y, p.rows, p.dim, p.bias = _p(out), _p(residual), _p(y), M, C, _p(bias)
+    if gate is not None:
+        gm, ge = gate
+        p.gate_mod, p.gate_e0, p.gate_frame_stride = _p(gm), _p(ge), ge.stride(0)
+        p.seq_len, p.tokens_per_frame = frames
+    L.check(L.load().wanb200_bias_gate_residual(ctypes.byref(p), _stream(residual)), "wanb200_bias_gate_residual")
+    return out
+
+
+# ---------------------------------------------------------------------------- torch.library ops
+# The attention seam of the reference (`fn(q, k, v) -> o`, models/fast_dit.py:186-255) as a
+# custom op with a fake kernel, so the device path can sit under torch.compile / CUDA graphs.
+@torch.library.custom_op("wanb200::attn", mutates_args=())
+def attn_op(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, softmax_scale: float) -> torch.Tensor:
+    return attention(q, k, v, softmax_scale=softmax_scale)
+
+
+@attn_op.register_fake
+def _(q, k, v, softmax_scale):
+    return torch.empty(q.shape[0], q.shape[1], q.shape[2], q.shape[3], dtype=q.dtype, device=q.device)
