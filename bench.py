@@ -1,0 +1,334 @@
+#!/usr/bin/env python
+"""Benchmark of the north-star path: seconds per 30-layer DiT denoise step of Wan2.2-TI2V-5B at
+7854 tokens (latent grid 21x17x22, 704x544x81 video) with batched CFG (batch 2), on N B200s
+of one node (TP = N by heads; N = 1 runs the whole step on one GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1)
+
+Prints one JSON line on rank 0.  `value` is device time per step (CUDA events, inputs resident
+in HBM, max over ranks); `e2e` is the same step through the public `FastWanDiT.__call__` with
+the latent copied from pinned host memory and the noise prediction copied back every step.
+Weights are seeded N(0, 0.02) bf16 with the TI2V-5B shapes, the text context is seeded, so
+`data` is synthetic.  `--impl reference` times the CPU oracle (the reference's fp32 block math,
+ref_fp32.block_fwd restated in oracle/dit_ref.py) on this host's cores instead.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "wan2-ti2v-5b_b200"))
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+METRIC = "DiT s/step @7854 tok CFG=2 at 1/2/4/8 B200; self-attn TFLOP/s vs bf16 peak"
+GRID = (21, 17, 22)
+LATENT = (48, 21, 34, 44)
+GUIDE = 5.0
+T_STEP = 999.0
+CFG_BATCH = 2
+CTX_LEN, TEXT_DIM = 512, 4096
+
+# DRAM traffic per launch of the dominant kernel from one ncu capture (dram__bytes_read.sum +
+# dram__bytes_write.sum), keyed by kernel class; None until captured.  The capture command and
+# its figures are in profiles/ (gemm_ffn_up_l7854.txt).
+NCU_TRAFFIC_PER_LAUNCH = {}
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d["bf16_tflops_sustained"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = str(gpu_index)
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", self.idx], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        sms, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sms.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sms:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sms)}
+
+
+def init_dist(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}; launch N>1 under torchrun")
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def max_over_ranks(x, world, device):
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def cpu_block_sample(threads=None):
+    """One block of config 2 (B=2, L=7854, dim 3072) through the fp32 CPU oracle; returns seconds."""
+    from oracle import dit_ref as R
+    from wanb200.weights import TI2V_5B, random_block_state
+    torch.set_num_threads(threads or os.cpu_count() or 1)
+    spec = TI2V_5B
+    sd = {k: v.float() for k, v in random_block_state(spec, 0).items()}
+    g = torch.Generator().manual_seed(1)
+    Lx = GRID[0] * GRID[1] * GRID[2]
+    x = torch.randn(CFG_BATCH, Lx, spec.dim, generator=g)
+    e0 = torch.randn(1, GRID[0], 6, spec.dim, generator=g) * 0.1
+    ctx = torch.randn(CFG_BATCH, CTX_LEN, spec.dim, generator=g)
+    cos, sin = R.rope_tables(R.model_freqs(spec.head_dim), GRID, spec.head_dim)
+    ck, cv = R.cross_kv(sd, ctx, spec.num_heads)
+    with torch.no_grad():
+        t0 = time.perf_counter()
+        R.block_fwd(sd, x, e0, cos, sin, ck, cv, GRID[0], spec.num_heads)
+        return time.perf_counter() - t0
+
+
+def cpu_info():
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_reference(args):
+    """Reference arm: the reference's block math (fp32, CPU) on the host cores, rank 0 only."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    torch.set_grad_enabled(False)
+    threads = os.cpu_count() or 1
+    layers = 30
+    for _ in range(args.warmup):
+        cpu_block_sample(threads)
+    times = [cpu_block_sample(threads) for _ in range(args.steps)]
+    per_step = statistics.mean(times) * layers
+    line = {
+        "impl": "reference", "metric": METRIC, "value": per_step, "unit": "s/step", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config2: 30-layer Wan2.2-TI2V-5B DiT step, 7854 tokens (21x17x22), CFG batch 2",
+                   "global_batch": CFG_BATCH, "seq_len": GRID[0] * GRID[1] * GRID[2],
+                   "parallelism": "cpu", "inputs_larger_than_l2": True},
+        "cpu_baseline": {"value": per_step, "unit": "s/step", "cores": threads, "kind": "port",
+                         "sample": f"1 of 30 blocks per step (B=2, L=7854, dim 3072), fp32 oracle "
+                                   f"(ref_fp32.block_fwd restated), x30; host: {cpu_info()}"},
+        "e2e": {"value": per_step, "unit": "s/step", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    world, rank, local = init_dist(args.gpus)
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    torch.set_grad_enabled(False)
+    from wanb200 import FastWanDiT, TI2V_5B, random_model_state
+    from wanb200 import ops
+    from wanb200.dit import block_flops
+
+    spec = TI2V_5B
+    layers = args.layers
+    sd = random_model_state(spec, seed=0, device=device, num_layers=layers)
+    tp_group = dist.group.WORLD if world > 1 else None
+    fast = FastWanDiT((spec, sd), GRID, GUIDE, device, tp_group=tp_group, num_layers=layers)
+    del sd
+    g = torch.Generator(device=device).manual_seed(123)
+    ctx = torch.randn(CTX_LEN, TEXT_DIM, generator=g, device=device)
+    ctx_null = torch.randn(CTX_LEN, TEXT_DIM, generator=g, device=device)
+    fast.set_context(ctx, ctx_null)
+    latent_host = torch.randn(LATENT, generator=torch.Generator().manual_seed(7)).pin_memory()
+    latent_dev = latent_host.to(device)
+    out_host = torch.empty(LATENT, dtype=torch.float32).pin_memory()
+    stream = torch.cuda.current_stream(device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(device)
+
+    for _ in range(args.warmup):
+        fast(latent_dev, T_STEP)
+    barrier()
+
+    # ---- device-timed steps (inputs resident), per-kernel events inside the timed region
+    timer = ops.KernelTimer()
+    ops.set_timer(timer)
+    clocks = ClockSampler(local if "CUDA_VISIBLE_DEVICES" not in os.environ else
+                          os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local])
+    clocks.start()
+    launches0 = ops.launch_count
+    barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        out = fast(latent_dev, T_STEP)
+    t1.record(stream)
+    barrier()
+    launches = ops.launch_count - launches0
+    ops.set_timer(None)
+    step_s = max_over_ranks(t0.elapsed_time(t1) / 1e3 / args.steps, world, device)
+    clk = clocks.stop()
+    kern = timer.summary()
+
+    # ---- end to end through the public call: pinned H2D of the latent, D2H of the prediction
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        lat = latent_host.to(device, non_blocking=True)
+        out = fast(lat, T_STEP)
+        out_host.copy_(out, non_blocking=True)
+    e1.record(stream)
+    barrier()
+    e2e_s = max_over_ranks(e0.elapsed_time(e1) / 1e3 / args.steps, world, device)
+    assert torch.isfinite(out_host).all()
+
+    if rank != 0:
+        if world > 1:
+            dist.barrier(device_ids=[local])
+            dist.destroy_process_group()
+        return
+
+    peaks = measured_peaks()
+    # dominant kernel class by device time
+    dom = max(kern, key=lambda k: kern[k][1])
+    n, ms, work = kern[dom]
+    hbm_kinds = {"layernorm", "qk_norm_rope", "bias_gate_residual"}
+    if dom in hbm_kinds:
+        achieved = work / (ms / 1e3) / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s"}
+    else:
+        achieved = work / (ms / 1e3) / 1e12
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s"}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof["kernel"] = {"gemm": "gemm_bf16_kernel (all projection GEMMs)", "attn_self": "attn_fwd_kernel (self)",
+                      "attn_cross": "attn_fwd_kernel (cross)"}.get(dom, dom)
+    roof["peak_kind"] = f"{peaks['source']} {'sustained bf16' if roof['bound'] == 'tensor' else 'HBM copy'}"
+    roof["launches"] = n
+    roof["work_per_launch"] = work / n
+    tr = NCU_TRAFFIC_PER_LAUNCH.get(dom)
+    roof["traffic"] = tr
+    per_kernel = {k: {"launches": v[0], "ms": v[1], "share": v[1] / sum(x[1] for x in kern.values()),
+                      ("tflops" if k not in hbm_kinds else "gbs"):
+                          (v[2] / (v[1] / 1e3) / (1e12 if k not in hbm_kinds else 1e9))} for k, v in kern.items()}
+    sa = kern.get("attn_self")
+    self_attn = None
+    if sa:
+        tf = sa[2] / (sa[1] / 1e3) / 1e12
+        self_attn = {"tflops": tf, "frac_of_burst_peak": tf / peaks["bf16_tflops"],
+                     "frac_of_sustained_peak": tf / peaks["bf16_tflops_sustained"], "ms_per_launch": sa[1] / sa[0]}
+
+    fl = block_flops(CFG_BATCH * GRID[0] * GRID[1] * GRID[2], GRID[0] * GRID[1] * GRID[2])
+    step_flops = layers * sum(fl.values())
+    line = {
+        "metric": METRIC, "value": step_s, "unit": "s/step", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": False, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) bf16 weights, seeded context/latent)",
+        "config": {"workload": f"config2: {layers}-layer Wan2.2-TI2V-5B DiT step, 7854 tokens (21x17x22), CFG batch 2",
+                   "global_batch": CFG_BATCH, "seq_len": GRID[0] * GRID[1] * GRID[2],
+                   "parallelism": f"tp{world}", "layers": layers, "inputs_larger_than_l2": True,
+                   "l2_note": "each step streams ~9.8 GB of weights, far above the 126 MB L2"},
+        "e2e": {"value": e2e_s, "unit": "s/step", "h2d_bytes_per_step": latent_host.numel() * 4,
+                "d2h_bytes_per_step": out_host.numel() * 4},
+        "gpu_launches": launches,
+        "roofline": roof,
+        "self_attn": self_attn,
+        "step_tflops": step_flops / step_s / 1e12,
+        "kernels": per_kernel,
+        "clocks": clk,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        t_blk = cpu_block_sample()
+        line["cpu_baseline"] = {"value": t_blk * 30, "unit": "s/step", "cores": torch.get_num_threads(),
+                                "kind": "port",
+                                "sample": f"1 of 30 blocks (B=2, L=7854, dim 3072) through the fp32 oracle, x30; "
+                                          f"host: {cpu_info()}"}
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--layers", type=int, default=30, help="blocks per step (30 for the bench line)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -118,7 +118,7 @@ class FastBlock:
         q = ws.qkv[:, :Cl].view(B, Lx, nl, 128)
         k = ws.qkv[:, Cl:2 * Cl].view(B, Lx, nl, 128)
         v = ws.qkv[:, 2 * Cl:].view(B, Lx, nl, 128)
-        ops.attention(q, k, v, out=ws.y.view(B, Lx, nl, 128))
+        ops.attention(q, k, v, out=ws.y.view(B, Lx, nl, 128), kind="attn_self")
         x1 = torch.empty_like(xf)
         gate2 = (mod[2], e0[:, 2, :])
         if self.tp:
@@ -135,7 +135,7 @@ class FastBlock:
                    ss_section=Cl, ss_nsections=1)
         self._all_reduce(ws.ss[2])
         ops.qk_norm_rope(ws.cq, [(0, ws.ss[2], w.g_cq)], Cl, C, eps=self.eps)
-        ops.attention(ws.cq.view(B, Lx, nl, 128), ck, cv, out=ws.y.view(B, Lx, nl, 128))
+        ops.attention(ws.cq.view(B, Lx, nl, 128), ck, cv, out=ws.y.view(B, Lx, nl, 128), kind="attn_cross")
         if self.tp:
             ops.linear(ws.y, w.w_co, None, epilogue=L.EPI_NONE, out=ws.part)
             self._all_reduce(ws.part)

@@ -16,6 +16,56 @@ from . import _lib as L
 BF16 = torch.bfloat16
 
 
+class KernelTimer:
+    """Optional per-launch CUDA-event timing of the ops below, by kernel class.
+
+    While installed with `set_timer`, every op records an event pair on the launching stream
+    and its algorithmic work (FLOPs for tensor-core kernels, bytes for HBM-bound ones).
+    `summary()` synchronizes and returns {kind: (launches, total_ms, total_work)}.
+    """
+
+    def __init__(self):
+        self.records = []
+
+    def begin(self, t):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(torch.cuda.current_stream(t.device))
+        return ev
+
+    def end(self, t, start, kind, work):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(torch.cuda.current_stream(t.device))
+        self.records.append((kind, start, ev, work))
+
+    def summary(self):
+        torch.cuda.synchronize()
+        out = {}
+        for kind, s, e, work in self.records:
+            n, ms, w = out.get(kind, (0, 0.0, 0.0))
+            out[kind] = (n + 1, ms + s.elapsed_time(e), w + work)
+        return out
+
+
+_timer = None
+launch_count = 0
+
+
+def set_timer(timer):
+    global _timer
+    _timer = timer
+
+
+def _launch(t, kind, work, fn):
+    global launch_count
+    launch_count += 1
+    if _timer is None:
+        return fn()
+    s = _timer.begin(t)
+    rc = fn()
+    _timer.end(t, s, kind, work)
+    return rc
+
+
 def _stream(t: torch.Tensor) -> int:
     return torch.cuda.current_stream(t.device).cuda_stream
 
@@ -73,12 +123,14 @@ def linear(a, w, bias=None, *, epilogue=L.EPI_BIAS, out=None, residual=None, gat
     if rowss is not None:
         _need(rowss.dtype == torch.float32, "linear: rowss must be fp32")
         p.rowss, p.ss_section, p.ss_nsections = _p(rowss), ss_section, ss_nsections
-    L.check(L.load().wanb200_gemm_bf16(ctypes.byref(p), _stream(a)), "wanb200_gemm_bf16")
+    lib = L.load()
+    L.check(_launch(a, "gemm", 2.0 * M * N * K, lambda: lib.wanb200_gemm_bf16(ctypes.byref(p), _stream(a))),
+            "wanb200_gemm_bf16")
     return out
 
 
 # ---------------------------------------------------------------------------- attention
-def attention(q, k, v, out=None, softmax_scale=None):
+def attention(q, k, v, out=None, softmax_scale=None, kind="attn"):
     """o = softmax(q k^T * scale) v on [B, L, H, 128] tensors (head stride 128, unit d stride)."""
     _cuda(q, k, v, out)
     for name, t in (("q", q), ("k", k), ("v", v)):
@@ -96,7 +148,9 @@ def attention(q, k, v, out=None, softmax_scale=None):
     p.o, p.o_tok_stride, p.o_batch_stride = _p(out), out.stride(1), out.stride(0)
     p.batch, p.heads, p.q_len, p.kv_len, p.head_dim = B, H, Lq, k.shape[1], D
     p.softmax_scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(D)
-    L.check(L.load().wanb200_attn_fwd(ctypes.byref(p), _stream(q)), "wanb200_attn_fwd")
+    lib = L.load()
+    flops = 4.0 * B * H * Lq * k.shape[1] * D
+    L.check(_launch(q, kind, flops, lambda: lib.wanb200_attn_fwd(ctypes.byref(p), _stream(q))), "wanb200_attn_fwd")
     return out
 
 
@@ -116,7 +170,9 @@ def layernorm_modulate(x, modulation, e0, shift_idx, scale_idx, frames, out=None
     p.seq_len, p.tokens_per_frame = frames
     if zero is not None:
         p.zero_buf, p.zero_count = _p(zero), zero.numel()
-    L.check(L.load().wanb200_layernorm(ctypes.byref(p), _stream(x)), "wanb200_layernorm")
+    lib = L.load()
+    L.check(_launch(x, "layernorm", 4.0 * M * C, lambda: lib.wanb200_layernorm(ctypes.byref(p), _stream(x))),
+            "wanb200_layernorm")
     return out
 
 
@@ -131,7 +187,9 @@ def layernorm_affine(x, weight, bias, out=None, eps=1e-6, zero=None):
     p.weight, p.bias = _p(weight), _p(bias)
     if zero is not None:
         p.zero_buf, p.zero_count = _p(zero), zero.numel()
-    L.check(L.load().wanb200_layernorm(ctypes.byref(p), _stream(x)), "wanb200_layernorm")
+    lib = L.load()
+    L.check(_launch(x, "layernorm", 4.0 * M * C, lambda: lib.wanb200_layernorm(ctypes.byref(p), _stream(x))),
+            "wanb200_layernorm")
     return out
 
 
@@ -150,7 +208,10 @@ def qk_norm_rope(x, sections, width, global_dim, eps=1e-6, cos=None, sin=None, s
     if cos is not None:
         _need(cos.dtype == torch.float32 and cos.is_contiguous() and sin.is_contiguous(), "qk_norm_rope: bad tables")
         p.rope, p.cos, p.sin, p.seq_len = 1, _p(cos), _p(sin), seq_len
-    L.check(L.load().wanb200_qk_norm_rope(ctypes.byref(p), _stream(x)), "wanb200_qk_norm_rope")
+    lib = L.load()
+    nbytes = 4.0 * x.shape[0] * width * len(sections) + 4.0 * x.shape[0] * len(sections)
+    L.check(_launch(x, "qk_norm_rope", nbytes, lambda: lib.wanb200_qk_norm_rope(ctypes.byref(p), _stream(x))),
+            "wanb200_qk_norm_rope")
     return x
 
 
@@ -167,7 +228,10 @@ def bias_gate_residual(residual, y, bias, gate=None, frames=None, out=None):
         gm, ge = gate
         p.gate_mod, p.gate_e0, p.gate_frame_stride = _p(gm), _p(ge), ge.stride(0)
         p.seq_len, p.tokens_per_frame = frames
-    L.check(L.load().wanb200_bias_gate_residual(ctypes.byref(p), _stream(residual)), "wanb200_bias_gate_residual")
+    lib = L.load()
+    L.check(_launch(residual, "bias_gate_residual", 6.0 * M * C,
+                    lambda: lib.wanb200_bias_gate_residual(ctypes.byref(p), _stream(residual))),
+            "wanb200_bias_gate_residual")
     return out
 
 
