@@ -1,0 +1,104 @@
+"""Single-kernel timing at the block's shapes (CUDA events, inputs larger than L2).
+
+    python -m wanb200.kernel_bench gemm --M 15708 --N 14336 --K 3072 --epi gelu [--iters 20]
+    python -m wanb200.kernel_bench attn --B 2 --H 24 --Lq 7854 --Lk 7854 [--iters 20]
+    python -m wanb200.kernel_bench ln --M 15708 --C 3072
+
+(run from wan2-ti2v-5b_b200/ or with it on sys.path).  Prints one JSON line with the mean
+time per launch and the algorithmic TFLOP/s or GB/s.  Used for sweeps and as the small-case
+command under ncu.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from . import _lib as L
+from . import ops
+
+EPIS = {"none": L.EPI_NONE, "bias": L.EPI_BIAS, "gelu": L.EPI_BIAS_GELU, "gate_res": L.EPI_BIAS_GATE_RES,
+        "res": L.EPI_BIAS_RES, "sumsq": L.EPI_BIAS_SUMSQ}
+
+
+def _time(fn, iters, warmup=3):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def bench_gemm(a):
+    dev = "cuda"
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(a.M, a.K, generator=g, device=dev).to(torch.bfloat16)
+    w = (torch.randn(a.N, a.K, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    b = torch.zeros(a.N, device=dev, dtype=torch.bfloat16)
+    out = torch.empty(a.M, a.N, device=dev, dtype=torch.bfloat16)
+    epi = EPIS[a.epi]
+    kw = {}
+    if epi in (L.EPI_BIAS_GATE_RES, L.EPI_BIAS_RES):
+        kw["residual"] = torch.zeros_like(out)
+    if epi == L.EPI_BIAS_GATE_RES:
+        kw["gate"] = (torch.zeros(a.N, device=dev, dtype=torch.bfloat16), torch.ones(21, 6 * a.N, device=dev)[:, :a.N])
+        kw["frames"] = (a.M, max(1, a.M // 21))
+    if epi == L.EPI_BIAS_SUMSQ:
+        kw["rowss"] = torch.zeros(2, a.M, device=dev)
+        kw["ss_section"], kw["ss_nsections"] = a.N // 3, 2
+    ms = _time(lambda: ops.linear(x, w, b if epi else None, epilogue=epi, out=out, **kw), a.iters)
+    L.check(0, "")
+    return {"kernel": "gemm", "M": a.M, "N": a.N, "K": a.K, "epi": a.epi, "ms": ms,
+            "tflops": 2 * a.M * a.N * a.K / ms / 1e9}
+
+
+def bench_attn(a):
+    dev = "cuda"
+    g = torch.Generator(device=dev).manual_seed(0)
+    q = torch.randn(a.B, a.Lq, a.H, 128, generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn(a.B, a.Lk, a.H, 128, generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn(a.B, a.Lk, a.H, 128, generator=g, device=dev).to(torch.bfloat16)
+    o = torch.empty_like(q)
+    ms = _time(lambda: ops.attention(q, k, v, out=o), a.iters)
+    return {"kernel": "attn", "B": a.B, "H": a.H, "Lq": a.Lq, "Lk": a.Lk, "ms": ms,
+            "tflops": 4 * a.B * a.H * a.Lq * a.Lk * 128 / ms / 1e9}
+
+
+def bench_ln(a):
+    dev = "cuda"
+    x = torch.randn(a.M, a.C, device=dev).to(torch.bfloat16)
+    mod = torch.zeros(6, a.C, device=dev, dtype=torch.bfloat16)
+    e0 = torch.zeros(21, 6, a.C, device=dev)
+    out = torch.empty_like(x)
+    ms = _time(lambda: ops.layernorm_modulate(x, mod, e0, 0, 1, (a.M, max(1, a.M // 21)), out=out), a.iters)
+    return {"kernel": "layernorm_modulate", "M": a.M, "C": a.C, "ms": ms, "gbs": 4 * a.M * a.C / ms / 1e6}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("kind", choices=["gemm", "attn", "ln"])
+    ap.add_argument("--M", type=int, default=15708)
+    ap.add_argument("--N", type=int, default=14336)
+    ap.add_argument("--K", type=int, default=3072)
+    ap.add_argument("--C", type=int, default=3072)
+    ap.add_argument("--epi", default="gelu", choices=sorted(EPIS))
+    ap.add_argument("--B", type=int, default=2)
+    ap.add_argument("--H", type=int, default=24)
+    ap.add_argument("--Lq", type=int, default=7854)
+    ap.add_argument("--Lk", type=int, default=7854)
+    ap.add_argument("--iters", type=int, default=20)
+    a = ap.parse_args()
+    torch.cuda.set_device(0)
+    r = {"gemm": bench_gemm, "attn": bench_attn, "ln": bench_ln}[a.kind](a)
+    r["device_error"] = L.device_error(reset=True)
+    print(json.dumps(r), flush=True)
+
+
+if __name__ == "__main__":
+    main()
