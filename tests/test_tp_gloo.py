@@ -1,0 +1,118 @@
+"""Tensor-parallel decomposition on CPU ranks (gloo, world size 2 and 4).
+
+Each rank slices the block with the product's `BlockWeights` (the reference's
+`shard_model_tp` pattern, models/tp_utils.py:378-458), runs its share with the CPU
+restatement `oracle.tp_ref.block_fwd_tp` (same all-reduce points as `FastBlock`'s TP branch)
+and must reproduce the unsharded oracle block.  A second test checks that a collective whose
+peer has gone away fails with an error inside the process-group timeout instead of hanging.
+"""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from conftest import PKG_DIR, ROOT
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _setup(rank, world, port, timeout_s=60):
+    import datetime
+    import sys
+    for p in (ROOT, PKG_DIR):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=timeout_s))
+
+
+def _tp_worker(rank, world, port, q):
+    try:
+        _setup(rank, world, port)
+        torch.set_num_threads(1)
+        from oracle import dit_ref as R
+        from oracle.tp_ref import block_fwd_tp
+        from wanb200 import BlockWeights, WanSpec, random_block_state
+        spec = WanSpec(dim=512, ffn_dim=1024, num_heads=4)
+        grid = (2, 3, 4)
+        B, L, Lc = 2, 24, 16
+        sd = random_block_state(spec, 5)
+        g = torch.Generator().manual_seed(9)
+        x = torch.randn(B, L, spec.dim, generator=g)
+        e0 = torch.randn(1, grid[0], 6, spec.dim, generator=g) * 0.1
+        ctx = torch.randn(B, Lc, spec.dim, generator=g)
+        cos, sin = R.rope_tables(R.model_freqs(128), grid, 128)
+        p32 = {k: v.float() for k, v in sd.items()}
+        ck, cv = R.cross_kv(p32, ctx, spec.num_heads)  # all heads
+        w = BlockWeights(sd, spec.num_heads, "cpu", rank, world)
+        hs = slice(rank * w.local_heads, (rank + 1) * w.local_heads)
+        y = block_fwd_tp(w, x, e0, cos, sin, ck[:, :, hs].contiguous(), cv[:, :, hs].contiguous(), grid[0],
+                         lambda t: dist.all_reduce(t))
+        y_ref = R.block_fwd(p32, x, e0, cos, sin, ck, cv, grid[0], spec.num_heads)
+        q.put((rank, R.rel_rms(y, y_ref)))
+    except Exception as ex:  # pragma: no cover - reported to the parent
+        q.put((rank, repr(ex)))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_decomposition_matches_unsharded_oracle(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_tp_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(world):
+        assert isinstance(res[r], float), res[r]
+        assert res[r] < 1e-5, (r, res[r])
+
+
+def _lost_peer_worker(rank, world, port, q):
+    try:
+        _setup(rank, world, port, timeout_s=5)
+        t = torch.ones(4)
+        dist.all_reduce(t)  # both ranks take part
+        if rank == 1:
+            q.put((rank, "left"))
+            q.close()
+            q.join_thread()  # flush the message before leaving
+            os._exit(0)  # leaves between steps, nothing in flight
+        try:
+            dist.all_reduce(t)  # the peer is gone: must raise, not hang
+            q.put((rank, "no error"))
+        except Exception as ex:
+            q.put((rank, "raised:" + type(ex).__name__))
+    except Exception as ex:  # pragma: no cover
+        q.put((rank, repr(ex)))
+
+
+def test_collective_with_lost_peer_raises_instead_of_hanging():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_lost_peer_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    assert res[1] == "left"
+    assert res[0].startswith("raised:"), res[0]

@@ -31,7 +31,7 @@ struct LnArgs {
 //     shift/scale[f, c] = modulation[idx, c] + e0[f, idx, c] (fast_dit.py:276-277).
 //   MODE 1 (affine): norm3 = WanLayerNorm(elementwise_affine=True) (model.py:207-209).
 template <int MODE, int NVEC>
-__global__ void __launch_bounds__(256) layernorm_kernel(const LnArgs a) {
+__global__ void __launch_bounds__(256, 2) layernorm_kernel(const LnArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < a.zero_count;
        i += (int64_t)gridDim.x * blockDim.x)
@@ -39,15 +39,16 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const LnArgs a) {
   const int64_t row = (int64_t)blockIdx.x * 8 + warp;
   if (row >= a.rows) return;
   const uint4* xr = reinterpret_cast<const uint4*>(a.x + row * a.dim);
-  float x[NVEC][8];
+  uint4 xv[NVEC];  // the row stays packed (bf16) in registers: half the footprint of fp32
+#pragma unroll
+  for (int i = 0; i < NVEC; ++i) xv[i] = __ldg(xr + i * 32 + lane);
   float sum = 0.f;
 #pragma unroll
   for (int i = 0; i < NVEC; ++i) {
-    {
-      unpack_bf16x8(__ldg(xr + i * 32 + lane), x[i]);
+    float x[8];
+    unpack_bf16x8(xv[i], x);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) sum += x[i][k];
-    }
+    for (int k = 0; k < 8; ++k) sum += x[k];
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
@@ -55,12 +56,12 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const LnArgs a) {
   float var = 0.f;
 #pragma unroll
   for (int i = 0; i < NVEC; ++i) {
-    {
+    float x[8];
+    unpack_bf16x8(xv[i], x);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const float d = x[i][k] - mean;
-        var = fmaf(d, d, var);
-      }
+    for (int k = 0; k < 8; ++k) {
+      const float d = x[k] - mean;
+      var = fmaf(d, d, var);
     }
   }
 #pragma unroll
@@ -79,7 +80,8 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const LnArgs a) {
   for (int i = 0; i < NVEC; ++i) {
     {
       const int col = (i * 32 + lane) * 8;
-      float y[8];
+      float x[8], y[8];
+      unpack_bf16x8(xv[i], x);
       if constexpr (MODE == 0) {
         float ms[8], mc[8];
         unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.modulation + (int64_t)a.shift_idx * a.dim + col)), ms);
@@ -91,13 +93,13 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const LnArgs a) {
         const float sh[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
         const float sc[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
 #pragma unroll
-        for (int k = 0; k < 8; ++k) y[k] = fmaf((x[i][k] - mean) * rstd, 1.f + (mc[k] + sc[k]), ms[k] + sh[k]);
+        for (int k = 0; k < 8; ++k) y[k] = fmaf((x[k] - mean) * rstd, 1.f + (mc[k] + sc[k]), ms[k] + sh[k]);
       } else {
         float w[8], bb[8];
         unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.weight + col)), w);
         unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.bias + col)), bb);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) y[k] = fmaf((x[i][k] - mean) * rstd, w[k], bb[k]);
+        for (int k = 0; k < 8; ++k) y[k] = fmaf((x[k] - mean) * rstd, w[k], bb[k]);
       }
       uint4 u;
       u.x = pack_bf16x2(y[0], y[1]);

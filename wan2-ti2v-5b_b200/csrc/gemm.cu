@@ -43,6 +43,22 @@ struct GemmArgs {
   int* err;
 };
 
+// Grouped rasterisation: tiles are numbered in groups of G_GROUP_M row-blocks; inside a group
+// the row-block index runs fastest.  The ~148 tiles in flight then cover ~16 row-blocks x ~9
+// column-blocks, so the A rows of the group stay L2-resident while W is streamed once per
+// group (instead of once per row-block with a plain row-major order).
+constexpr int G_GROUP_M = 16;
+
+__device__ __forceinline__ void tile_origin(int tile, int num_m, int num_n, int& m0, int& n0) {
+  const int per_group = G_GROUP_M * num_n;
+  const int g = tile / per_group;
+  const int first_m = g * G_GROUP_M;
+  const int gm = min(num_m - first_m, G_GROUP_M);
+  const int r = tile - g * per_group;
+  m0 = (first_m + r % gm) * GBM;
+  n0 = (r / gm) * GBN;
+}
+
 template <int EPI>
 __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v, int row, int col0, float& ss_acc,
                                                     int& ss_sec) {
@@ -159,7 +175,8 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   const int num_n = (args.N + GBN - 1) / GBN;
-  const int num_tiles = ((args.M + GBM - 1) / GBM) * num_n;
+  const int num_m = (args.M + GBM - 1) / GBM;
+  const int num_tiles = num_m * num_n;
   const int kblocks = args.K / GBK;
 
   if (warp == 0) {
@@ -168,7 +185,8 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t phase = 0, issued = 0, last_phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
-        const int m0 = (tile / num_n) * GBM, n0 = (tile % num_n) * GBN;
+        int m0, n0;
+        tile_origin(tile, num_m, num_n, m0, n0);
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, abort_flag, err, kErrTimeoutGemmProducer)) {
             ok = false;
@@ -237,7 +255,8 @@ __global__ void __launch_bounds__(192, 1)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       if (!mbar_wait_warp(tfull0 + 8 * acc, acc_phase, abort_flag, err, kErrTimeoutGemmEpilogue)) break;
       tc_fence_after();
-      const int m0 = (tile / num_n) * GBM, n0 = (tile % num_n) * GBN;
+      int m0, n0;
+      tile_origin(tile, num_m, num_n, m0, n0);
       const int row = m0 + r;
       const uint32_t t_row = tmem_base + (uint32_t(quad * 32) << 16) + acc * GBN;
       float ss_acc = 0.f;
