@@ -36,9 +36,8 @@ T_STEP = 999.0
 CFG_BATCH = 2
 CTX_LEN, TEXT_DIM = 512, 4096
 
-# DRAM traffic per launch of the dominant kernel from one ncu capture (dram__bytes_read.sum +
-# dram__bytes_write.sum), keyed by kernel class; None until captured.  The capture command and
-# its figures are in profiles/ (gemm_ffn_up_l7854.txt).
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per launch at config 2, by kernel
+# role, from ncu captures summarised in profiles/ (command lines there).
 NCU_TRAFFIC_PER_LAUNCH = {}
 
 
@@ -254,27 +253,38 @@ def run_ours(args):
         return
 
     peaks = measured_peaks()
-    # dominant kernel class by device time
-    dom = max(kern, key=lambda k: kern[k][1])
-    n, ms, work = kern[dom]
     hbm_kinds = {"layernorm", "qk_norm_rope", "bias_gate_residual"}
-    if dom in hbm_kinds:
-        achieved = work / (ms / 1e3) / 1e9
-        roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s"}
-    else:
-        achieved = work / (ms / 1e3) / 1e12
-        roof = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s"}
-    roof["frac"] = roof["achieved"] / roof["peak"]
-    roof["kernel"] = {"gemm": "gemm_bf16_kernel (all projection GEMMs)", "attn_self": "attn_fwd_kernel (self)",
-                      "attn_cross": "attn_fwd_kernel (cross)"}.get(dom, dom)
-    roof["peak_kind"] = f"{peaks['source']} {'sustained bf16' if roof['bound'] == 'tensor' else 'HBM copy'}"
-    roof["launches"] = n
-    roof["work_per_launch"] = work / n
-    tr = NCU_TRAFFIC_PER_LAUNCH.get(dom)
-    roof["traffic"] = tr
-    per_kernel = {k: {"launches": v[0], "ms": v[1], "share": v[1] / sum(x[1] for x in kern.values()),
+    total_ms = sum(x[1] for x in kern.values())
+    per_kernel = {k: {"launches": v[0], "ms": v[1], "share": v[1] / total_ms,
                       ("tflops" if k not in hbm_kinds else "gbs"):
                           (v[2] / (v[1] / 1e3) / (1e12 if k not in hbm_kinds else 1e9))} for k, v in kern.items()}
+    g_all = [v for k, v in kern.items() if k.startswith("gemm")]
+    if g_all:
+        gms, gw = sum(v[1] for v in g_all), sum(v[2] for v in g_all)
+        per_kernel["gemm_all"] = {"launches": sum(v[0] for v in g_all), "ms": gms, "share": gms / total_ms,
+                                  "tflops": gw / (gms / 1e3) / 1e12}
+    # the dominant kernel: the single kernel (by role) with the largest device time
+    dom = max(kern, key=lambda k: kern[k][1])
+    n, ms, work = kern[dom]
+    if dom in hbm_kinds:
+        achieved = work / n / (ms / n / 1e3) / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s"}
+    else:
+        achieved = work / n / (ms / n / 1e3) / 1e12
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s"}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof["kernel"] = ("attn_fwd_kernel (" + dom[5:] + ")") if dom.startswith("attn") else (
+        "gemm_bf16_kernel (" + dom[5:] + ")" if dom.startswith("gemm") else dom)
+    roof["peak_kind"] = f"{peaks['source']} {'sustained bf16' if roof['bound'] == 'tensor' else 'HBM copy'}"
+    if roof["bound"] == "tensor":
+        roof["frac_of_burst_peak"] = roof["achieved"] / peaks["bf16_tflops"]
+    roof["launches"] = n
+    roof["ms_per_launch"] = ms / n
+    roof["work_per_launch"] = work / n
+    tr = NCU_TRAFFIC_PER_LAUNCH.get(dom)
+    roof["traffic"] = tr[0] if tr else None
+    if tr:
+        roof["traffic_note"] = tr[1]
     sa = kern.get("attn_self")
     self_attn = None
     if sa:

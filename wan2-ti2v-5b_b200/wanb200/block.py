@@ -111,7 +111,7 @@ class FastBlock:
         # -- self-attention
         ops.layernorm_modulate(xf, mod, e0, 0, 1, frames, out=ws.h, eps=self.eps, zero=ws.ss)
         ops.linear(ws.h, w.w_qkv, w.b_qkv, epilogue=L.EPI_BIAS_SUMSQ, out=ws.qkv, rowss=ws.ss,
-                   ss_section=Cl, ss_nsections=2)
+                   ss_section=Cl, ss_nsections=2, kind="gemm_qkv")
         self._all_reduce(ws.ss[0:2])
         ops.qk_norm_rope(ws.qkv, [(0, ws.ss[0], w.g_q), (Cl, ws.ss[1], w.g_k)], Cl, C, eps=self.eps,
                          cos=cos2, sin=sin2, seq_len=Lx)
@@ -122,38 +122,38 @@ class FastBlock:
         x1 = torch.empty_like(xf)
         gate2 = (mod[2], e0[:, 2, :])
         if self.tp:
-            ops.linear(ws.y, w.w_o, None, epilogue=L.EPI_NONE, out=ws.part)
+            ops.linear(ws.y, w.w_o, None, epilogue=L.EPI_NONE, out=ws.part, kind="gemm_o")
             self._all_reduce(ws.part)
             ops.bias_gate_residual(xf, ws.part, w.b_o, gate=gate2, frames=frames, out=x1)
         else:
             ops.linear(ws.y, w.w_o, w.b_o, epilogue=L.EPI_BIAS_GATE_RES, out=x1, residual=xf, gate=gate2,
-                       frames=frames)
+                       frames=frames, kind="gemm_o")
 
         # -- cross-attention (ck/cv cached per generation)
         ops.layernorm_affine(x1, w.ln3_w, w.ln3_b, out=ws.h, eps=self.eps)
         ops.linear(ws.h, w.w_cq, w.b_cq, epilogue=L.EPI_BIAS_SUMSQ, out=ws.cq, rowss=ws.ss[2],
-                   ss_section=Cl, ss_nsections=1)
+                   ss_section=Cl, ss_nsections=1, kind="gemm_cross_q")
         self._all_reduce(ws.ss[2])
         ops.qk_norm_rope(ws.cq, [(0, ws.ss[2], w.g_cq)], Cl, C, eps=self.eps)
         ops.attention(ws.cq.view(B, Lx, nl, 128), ck, cv, out=ws.y.view(B, Lx, nl, 128), kind="attn_cross")
         if self.tp:
-            ops.linear(ws.y, w.w_co, None, epilogue=L.EPI_NONE, out=ws.part)
+            ops.linear(ws.y, w.w_co, None, epilogue=L.EPI_NONE, out=ws.part, kind="gemm_cross_o")
             self._all_reduce(ws.part)
             ops.bias_gate_residual(x1, ws.part, w.b_co, out=x1)
         else:
-            ops.linear(ws.y, w.w_co, w.b_co, epilogue=L.EPI_BIAS_RES, out=x1, residual=x1)
+            ops.linear(ws.y, w.w_co, w.b_co, epilogue=L.EPI_BIAS_RES, out=x1, residual=x1, kind="gemm_cross_o")
 
         # -- FFN
         ops.layernorm_modulate(x1, mod, e0, 3, 4, frames, out=ws.h, eps=self.eps)
-        ops.linear(ws.h, w.w1, w.b1, epilogue=L.EPI_BIAS_GELU, out=ws.f)
+        ops.linear(ws.h, w.w1, w.b1, epilogue=L.EPI_BIAS_GELU, out=ws.f, kind="gemm_ffn_up")
         gate5 = (mod[5], e0[:, 5, :])
         if self.tp:
-            ops.linear(ws.f, w.w2, None, epilogue=L.EPI_NONE, out=ws.part)
+            ops.linear(ws.f, w.w2, None, epilogue=L.EPI_NONE, out=ws.part, kind="gemm_ffn_down")
             self._all_reduce(ws.part)
             ops.bias_gate_residual(x1, ws.part, w.b2, gate=gate5, frames=frames, out=x1)
         else:
             ops.linear(ws.f, w.w2, w.b2, epilogue=L.EPI_BIAS_GATE_RES, out=x1, residual=x1, gate=gate5,
-                       frames=frames)
+                       frames=frames, kind="gemm_ffn_down")
         return x1.view(B, Lx, C)
 
     __call__ = forward
@@ -178,7 +178,8 @@ class FastCrossKV:
         N, Cl = B * Lc, w.local_dim
         ctx = context.reshape(N, C).to(BF16).contiguous()
         ss = torch.zeros(N, device=context.device, dtype=torch.float32)
-        kv = ops.linear(ctx, w.w_ckv, w.b_ckv, epilogue=L.EPI_BIAS_SUMSQ, rowss=ss, ss_section=Cl, ss_nsections=1)
+        kv = ops.linear(ctx, w.w_ckv, w.b_ckv, epilogue=L.EPI_BIAS_SUMSQ, rowss=ss, ss_section=Cl, ss_nsections=1,
+                        kind="gemm_cross_kv")
         if w.tp_size > 1:
             dist.all_reduce(ss, group=self.tp_group)
         ops.qk_norm_rope(kv, [(0, ss, w.g_ck)], Cl, C, eps=self.eps)

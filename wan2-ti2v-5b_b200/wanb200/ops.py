@@ -92,7 +92,7 @@ def _rows(t: torch.Tensor, name: str):
 
 # ---------------------------------------------------------------------------- GEMM
 def linear(a, w, bias=None, *, epilogue=L.EPI_BIAS, out=None, residual=None, gate=None, frames=None,
-           rowss=None, ss_section=0, ss_nsections=0):
+           rowss=None, ss_section=0, ss_nsections=0, kind="gemm"):
     """out[M, N] = epilogue(a[M, K] @ w[N, K]^T) on tcgen05 (see include/wanb200.h).
 
     gate: (gate_mod [N] bf16, gate_e0 [F, N] fp32 view with unit column stride) for EPI_BIAS_GATE_RES.
@@ -124,7 +124,7 @@ def linear(a, w, bias=None, *, epilogue=L.EPI_BIAS, out=None, residual=None, gat
         _need(rowss.dtype == torch.float32, "linear: rowss must be fp32")
         p.rowss, p.ss_section, p.ss_nsections = _p(rowss), ss_section, ss_nsections
     lib = L.load()
-    L.check(_launch(a, "gemm", 2.0 * M * N * K, lambda: lib.wanb200_gemm_bf16(ctypes.byref(p), _stream(a))),
+    L.check(_launch(a, kind, 2.0 * M * N * K, lambda: lib.wanb200_gemm_bf16(ctypes.byref(p), _stream(a))),
             "wanb200_gemm_bf16")
     return out
 
