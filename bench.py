@@ -192,8 +192,10 @@ def run_ours(args):
     spec = TI2V_5B
     layers = args.layers
     sd = random_model_state(spec, seed=0, device=device, num_layers=layers)
-    tp_group = dist.group.WORLD if world > 1 else None
-    fast = FastWanDiT((spec, sd), GRID, GUIDE, device, tp_group=tp_group, num_layers=layers)
+    from wanb200.parallel import make_layout
+    lay = make_layout(args.layout)
+    fast = FastWanDiT((spec, sd), GRID, GUIDE, device, cfg_group=lay.cfg_group, pair_group=lay.pair_group,
+                      tp_group=lay.tp_group, num_layers=layers)
     del sd
     g = torch.Generator(device=device).manual_seed(123)
     ctx = torch.randn(CTX_LEN, TEXT_DIM, generator=g, device=device)
@@ -300,7 +302,7 @@ def run_ours(args):
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) bf16 weights, seeded context/latent)",
         "config": {"workload": f"config2: {layers}-layer Wan2.2-TI2V-5B DiT step, 7854 tokens (21x17x22), CFG batch 2",
                    "global_batch": CFG_BATCH, "seq_len": GRID[0] * GRID[1] * GRID[2],
-                   "parallelism": f"tp{world}", "layers": layers, "inputs_larger_than_l2": True,
+                   "parallelism": lay.describe(world), "layers": layers, "inputs_larger_than_l2": True,
                    "l2_note": "each step streams ~9.8 GB of weights, far above the 126 MB L2"},
         "e2e": {"value": e2e_s, "unit": "s/step", "h2d_bytes_per_step": latent_host.numel() * 4,
                 "d2h_bytes_per_step": out_host.numel() * 4},
@@ -329,6 +331,9 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--layout", default="auto", choices=["auto", "tp", "cfg"],
+                    help="N>1: tp = TP over all N ranks (batched CFG); cfg = CFG-parallel groups of N/2 "
+                         "(TP inside each); auto = cfg for even N")
     ap.add_argument("--layers", type=int, default=30, help="blocks per step (30 for the bench line)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

@@ -78,6 +78,14 @@ def _worker(rank, world, port, q):
         fast.set_context(mg["ctx"].to(dev), mg["ctx_null"].to(dev))
         pred = fast(lat.to(dev), mg["t"])
         out["step_vs_reference"] = R.rel_rms(pred.float().cpu(), mg["noise_pred"])
+        # ---- the same step CFG-parallel: rank 0 = cond, rank 1 = uncond, pair all-reduce at the head
+        from wanb200.parallel import make_layout
+        lay = make_layout("cfg")
+        fc = FastWanDiT((sp, mg["state_dict"]), (lat.shape[1], lat.shape[2] // 2, lat.shape[3] // 2), mg["guide"],
+                        dev, cfg_group=lay.cfg_group, pair_group=lay.pair_group, tp_group=lay.tp_group)
+        fc.set_context(mg["ctx"].to(dev), mg["ctx_null"].to(dev))
+        pc = fc(lat.to(dev), mg["t"])
+        out["cfgpar_vs_reference"] = R.rel_rms(pc.float().cpu(), mg["noise_pred"])
         out["device_error"] = device_error(reset=True)
         q.put((rank, out))
     except Exception as ex:  # reported to the parent
@@ -104,6 +112,7 @@ def test_tp2_block_and_step():
         assert isinstance(res[r], dict), res[r]
         assert res[r]["device_error"] == 0
         assert res[r]["step_vs_reference"] < 5e-2, res[r]
+        assert res[r]["cfgpar_vs_reference"] < 5e-2, res[r]
     print("tp2:", res[0])
     assert res[0]["tp_vs_tp1"] < 1e-2
     assert res[0]["tp_vs_oracle"] < 2e-2

@@ -116,3 +116,38 @@ def test_collective_with_lost_peer_raises_instead_of_hanging():
             p.kill()
     assert res[1] == "left"
     assert res[0].startswith("raised:"), res[0]
+
+
+def _layout_worker(rank, world, port, q):
+    try:
+        _setup(rank, world, port)
+        from wanb200.parallel import make_layout
+        lay = make_layout("cfg")
+        t = torch.tensor([float(rank)])
+        dist.all_reduce(t, group=lay.tp_group)
+        p = torch.tensor([float(rank)])
+        dist.all_reduce(p, group=lay.pair_group)
+        q.put((rank, (lay.cfg_group, lay.tp_size, float(t), float(p), lay.describe(world))))
+    except Exception as ex:  # pragma: no cover
+        q.put((rank, repr(ex)))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def test_cfg_parallel_layout_groups():
+    """4 ranks: CFG groups {0,1} (cond) and {2,3} (uncond) with TP 2 inside, pairs {0,2}, {1,3}
+    (the reference's CFG-parallel split, inference_neuron_ti2v.py:241-274)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_layout_worker, args=(r, 4, port, q)) for r in range(4)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=30)
+    assert res[0] == (0, 2, 1.0, 2.0, "cfg2xtp2"), res[0]
+    assert res[1] == (0, 2, 1.0, 4.0, "cfg2xtp2"), res[1]
+    assert res[2] == (1, 2, 5.0, 2.0, "cfg2xtp2"), res[2]
+    assert res[3] == (1, 2, 5.0, 4.0, "cfg2xtp2"), res[3]

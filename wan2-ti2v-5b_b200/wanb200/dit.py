@@ -6,10 +6,15 @@ Mirrors `FastWanDiT` of models/fast_dit.py:561-697:
     noise_pred = fast(latent, t)             # latent [48, F, H, W], t scalar -> [48, F, H, W]
 
 `model` is either a reference `WanModel` (any object with `.state_dict()` and the WanModel
-config attributes) or a `(WanSpec, state_dict)` pair.  Batched CFG: cond and uncond run as a
-batch of 2 through every block.  With `tp_group` of size T > 1 each rank holds 24/T heads and
-1/T of the FFN, and the block ops all-reduce over the group (TP by heads, as the reference's
-`shard_model_tp`, models/tp_utils.py:378-458).
+config attributes) or a `(WanSpec, state_dict)` pair.
+
+Layouts (as the reference's):
+  * batched CFG (`cfg_group=None`): cond and uncond run as a batch of 2 through every block;
+  * CFG-parallel (`cfg_group=0/1`, inference_neuron_ti2v.py:241-274): this rank's group runs
+    only the cond (0) or uncond (1) branch at batch 1, and the head sums w * pred over
+    `pair_group` (the same TP rank of the other group), w = g or 1 - g (fast_dit.py:508-524);
+  * TP inside a group (`tp_group` of size T > 1): each rank holds 24/T heads and 1/T of the
+    FFN, and the block ops all-reduce over the group (`shard_model_tp`, tp_utils.py:378-458).
 
 The time / text / patch embeddings and the head are small (about 1% of the step) and run as
 fp32 torch ops on the GPU around the block kernels.
@@ -68,7 +73,8 @@ def _spec_and_state(model):
 
 
 class FastWanDiT:
-    def __init__(self, model, grid, guide_scale, device, tp_group=None, num_layers=None):
+    def __init__(self, model, grid, guide_scale, device, cfg_group=None, pair_group=None, tp_group=None,
+                 num_layers=None):
         spec, sd = _spec_and_state(model)
         self.spec = spec
         self.grid = tuple(int(g) for g in grid)
@@ -77,6 +83,11 @@ class FastWanDiT:
         self.guide_scale = float(guide_scale)
         self.device = torch.device(device)
         self.tp_group = tp_group
+        if cfg_group not in (None, 0, 1):
+            raise ValueError("cfg_group must be None, 0 (cond) or 1 (uncond)")
+        self.cfg_group, self.pair_group = cfg_group, pair_group
+        self.batch = 2 if cfg_group is None else 1
+        self.cfg_w = None if cfg_group is None else (self.guide_scale if cfg_group == 0 else 1.0 - self.guide_scale)
         tp = dist.get_world_size(tp_group) if (tp_group is not None and dist.is_initialized()) else 1
         rank = dist.get_rank(tp_group) if tp > 1 else 0
         self.tp_size, self.tp_rank = tp, rank
@@ -97,7 +108,12 @@ class FastWanDiT:
     def set_context(self, ctx_cond, ctx_null):
         """Text embedding + every block's cross K/V, once per prompt (fast_dit.py:658-664)."""
         m = self.emb
-        ctx = torch.cat([ctx_cond.reshape(1, -1, ctx_cond.shape[-1]), ctx_null.reshape(1, -1, ctx_null.shape[-1])])
+        cond = ctx_cond.reshape(1, -1, ctx_cond.shape[-1])
+        null = ctx_null.reshape(1, -1, ctx_null.shape[-1])
+        if self.cfg_group is None:
+            ctx = torch.cat([cond, null])
+        else:
+            ctx = cond if self.cfg_group == 0 else null
         ctx = ctx.to(self.device, torch.float32)
         h = F.gelu(F.linear(ctx, m["text_embedding.0.weight"], m["text_embedding.0.bias"]), approximate="tanh")
         context = F.linear(h, m["text_embedding.2.weight"], m["text_embedding.2.bias"]).to(BF16)
@@ -125,7 +141,7 @@ class FastWanDiT:
         x = x.reshape(-1, C_in * p * q * r)
         wt = m["patch_embedding.weight"].reshape(self.spec.dim, -1)
         x = torch.addmm(m["patch_embedding.bias"], x, wt.t())
-        return x.to(BF16).unsqueeze(0).expand(2, -1, -1).contiguous()
+        return x.to(BF16).unsqueeze(0).expand(self.batch, -1, -1).contiguous()
 
     def head(self, x, e):
         """LN + 2-way modulation + Linear, unpatchify, CFG combine (fast_dit.py:480-505)."""
@@ -139,7 +155,13 @@ class FastWanDiT:
         xn = (xn * (1 + mod[:, :, 1].unsqueeze(2)) + mod[:, :, 0].unsqueeze(2)).view(B, Lx, C)
         y = F.linear(xn, m["head.head.weight"], m["head.head.bias"])
         y = y.view(B, f, h, w, p, q, r, c).permute(0, 7, 1, 4, 2, 5, 3, 6).reshape(B, c, f * p, h * q, w * r)
-        return y[1] + self.guide_scale * (y[0] - y[1])
+        if self.cfg_group is None:
+            return y[1] + self.guide_scale * (y[0] - y[1])
+        # CFG-parallel: uncond + g (cond - uncond) = g * cond + (1 - g) * uncond, summed over the pair
+        out = (y[0] * self.cfg_w).contiguous()
+        if self.pair_group is not None:
+            dist.all_reduce(out, group=self.pair_group)
+        return out
 
     # ------------------------------------------------------------------ step
     def forward_blocks(self, x, e0):
