@@ -17,7 +17,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -51,53 +50,63 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock, max clock and clock-event (throttle) reasons of this rank's GPU, read through
+    NVML every 20 ms from a background thread while the timed region runs (read-only queries)."""
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
 
-    def __init__(self, gpu_index):
-        self.idx = str(gpu_index)
-        self.proc = None
-        self.lines = []
+    def __init__(self, torch_device_index):
+        self.idx = torch_device_index
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self.error = None
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200", "-i", self.idx], stdout=subprocess.PIPE,
-                                         stderr=subprocess.DEVNULL, text=True)
-            threading.Thread(target=self._read, daemon=True).start()
-        except OSError:
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            try:
+                nvml_idx = torch.cuda._get_nvml_device_index(self.idx)
+            except Exception:
+                nvml_idx = self.idx
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(nvml_idx)
+            self._nv = pynvml
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM))
+            self._bits = [(n, getattr(pynvml, c)) for n, c in self.REASONS]
+        except Exception as ex:  # no NVML: report no samples
+            self.error = repr(ex)
+            return
+        self._thread = threading.Thread(target=self._run, daemon=True)
+        self._thread.start()
 
-    def _read(self):
-        for ln in self.proc.stdout:
-            self.lines.append(ln.strip())
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(float(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                for n, bit in self._bits:
+                    if r & bit:
+                        self.reasons.add(n)
+            except Exception as ex:
+                self.error = repr(ex)
+                return
+            time.sleep(0.02)
 
     def stop(self):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-        sms, mx, reasons = [], None, set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for ln in self.lines:
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sms.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sms:
-            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sms)}
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=2)
+        out = {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+               "reasons": sorted(self.reasons), "samples": len(self.samples), "source": "nvml, 20 ms"}
+        if self.error:
+            out["error"] = self.error
+        return out
 
 
 def init_dist(n_gpus):
@@ -218,8 +227,7 @@ def run_ours(args):
     # ---- device-timed steps (inputs resident), per-kernel events inside the timed region
     timer = ops.KernelTimer()
     ops.set_timer(timer)
-    clocks = ClockSampler(local if "CUDA_VISIBLE_DEVICES" not in os.environ else
-                          os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local])
+    clocks = ClockSampler(local)
     clocks.start()
     launches0 = ops.launch_count
     barrier()

@@ -42,7 +42,8 @@ extern "C" {
  *                             (the sum of squares of `_tp_rms_qk` 138-140 / `_tp_rms` 158)
  *   WANB200_EPI_NONE          d = acc (row-parallel partial sum before the TP all-reduce, 127)
  * gate[f, n] = gate_mod[n] + gate_e0[f * gate_frame_stride + n] (modulation + e0 chunk,
- * fast_dit.py:276-277), frame(row) = (row % seq_len) / tokens_per_frame.
+ * fast_dit.py:276-277), frame(row) = ((row + row_offset) % seq_len) / tokens_per_frame
+ * (row_offset: index of row 0 in the flattened token sequence, for a token shard).
  * Limits: K % 64 == 0, N % 32 == 0, lda/ldw/ldd/ldr % 8 == 0, 16-byte aligned pointers.
  * d may alias residual (in place). */
 #define WANB200_EPI_NONE 0
@@ -62,7 +63,7 @@ typedef struct wanb200_gemm_params {
   const void* residual; int64_t ldr;               /* [M, N] bf16 for *_RES */
   const void* gate_mod;                            /* [N] bf16 for GATE_RES */
   const float* gate_e0; int64_t gate_frame_stride; /* e0 row of frame 0, stride between frames */
-  int64_t seq_len, tokens_per_frame;               /* frame(row) for GATE_RES */
+  int64_t seq_len, tokens_per_frame, row_offset;   /* frame(row) for GATE_RES */
   float* rowss; int64_t ss_section; int ss_nsections; /* SUMSQ: [ss_nsections, M] fp32, pre-zeroed */
 } wanb200_gemm_params;
 
@@ -105,7 +106,7 @@ typedef struct wanb200_ln_params {
   const void* modulation;                 /* [6, dim] bf16 */
   const float* e0; int64_t e0_frame_stride; /* [F, 6, dim] fp32 -> frame stride 6*dim */
   int shift_idx, scale_idx;
-  int64_t seq_len, tokens_per_frame;
+  int64_t seq_len, tokens_per_frame, row_offset;
   const void* weight; const void* bias;   /* [dim] bf16 for AFFINE */
   float* zero_buf; int64_t zero_count;
 } wanb200_ln_params;
@@ -140,7 +141,7 @@ typedef struct wanb200_residual_params {
   void* out; const void* residual; const void* y; int64_t rows, dim;
   const void* bias;
   const void* gate_mod; const float* gate_e0; int64_t gate_frame_stride;
-  int64_t seq_len, tokens_per_frame;
+  int64_t seq_len, tokens_per_frame, row_offset;
 } wanb200_residual_params;
 
 int wanb200_bias_gate_residual(const wanb200_residual_params* p, void* stream);
@@ -152,6 +153,10 @@ const char* wanb200_last_error(void);
 int wanb200_device_error(int reset);
 /* Library version, e.g. 100 for 0.1.0. */
 int wanb200_version(void);
+/* sizeof of the parameter structs in declaration order (gemm, attn, ln, qknorm, residual)
+ * written to out[0..n); returns the number of structs.  Lets a binding detect a library built
+ * from a different header. */
+int wanb200_struct_sizes(int64_t* out, int n);
 
 #ifdef __cplusplus
 }

@@ -61,3 +61,45 @@ def block_fwd_tp(w, x, e0, cos, sin, ck, cv, nf: int, all_reduce):
     part = F.linear(F.gelu(F.linear(h, f["w1"], f["b1"]), approximate="tanh"), f["w2"])
     all_reduce(part)
     return x + gate(part + f["b2"], e[5])
+
+
+def block_fwd_sp(w, xs, e0, cos, sin, ck, cv, seq_len: int, nf: int, rank: int, world: int, all_gather,
+                 reduce_scatter, all_reduce):
+    """One rank's share of the sequence-parallel block (`_FastBlockSP` with local all-head
+    cross-attention, models/fast_dit.py:314-389), batch 1, fp32 CPU, in the op order of
+    `wanb200.block.FastBlockSP`.  xs [S, C] is the rank's shard of the zero-padded tokens;
+    ck/cv [1, Lc, H, d] all heads; w built with local_cross=True.  Returns the new shard."""
+    f = {k: getattr(w, k).float().cpu() for k in ("modulation", "w_qkv", "b_qkv", "g_q", "g_k", "w_o", "b_o", "ln3_w",
+                                                   "ln3_b", "w_cq", "b_cq", "g_cq", "w_co", "b_co", "w1", "b1",
+                                                   "w2", "b2")}
+    S, C = xs.shape
+    Cl, nl, H = w.local_dim, w.local_heads, w.cross_heads
+    L = seq_len
+    tpf = L // nf
+    frame = ((torch.arange(S) + rank * S) % L) // tpf  # per-row frame of the shard
+    em = f["modulation"].reshape(1, 6, C) + e0[0]       # [F, 6, C]
+    et = em[frame]                                      # [S, 6, C]
+
+    h = F.layer_norm(xs, (C,), eps=EPS) * (1 + et[:, 1]) + et[:, 0]
+    hf = all_gather(h)                                  # [T*S, C]
+    qkv = F.linear(hf, f["w_qkv"], f["b_qkv"])
+    q, k, v = qkv[:, :Cl], qkv[:, Cl:2 * Cl], qkv[:, 2 * Cl:]
+    ss = torch.stack([q.pow(2).sum(-1), k.pow(2).sum(-1)])
+    all_reduce(ss)
+    q = q * torch.rsqrt(ss[0] / C + EPS).unsqueeze(-1) * f["g_q"]
+    k = k * torch.rsqrt(ss[1] / C + EPS).unsqueeze(-1) * f["g_k"]
+    q = rope(q[:L].reshape(1, L, nl, 128), cos, sin)
+    k = rope(k[:L].reshape(1, L, nl, 128), cos, sin)
+    y = attn(q, k, v[:L].reshape(1, L, nl, 128)).reshape(L, Cl)
+    y = torch.cat([y, y.new_zeros(hf.shape[0] - L, Cl)])
+    part = reduce_scatter(F.linear(y, f["w_o"]))       # [S, C]
+    xs = xs + (part + f["b_o"]) * et[:, 2]
+    h = F.layer_norm(xs, (C,), f["ln3_w"], f["ln3_b"], eps=EPS)
+    qc = F.linear(h, f["w_cq"], f["b_cq"])
+    qc = qc * torch.rsqrt(qc.pow(2).mean(-1, keepdim=True) + EPS) * f["g_cq"]
+    yc = attn(qc.reshape(1, S, H, 128), ck, cv).reshape(S, C)
+    xs = xs + F.linear(yc, f["w_co"], f["b_co"])
+    h = F.layer_norm(xs, (C,), eps=EPS) * (1 + et[:, 4]) + et[:, 3]
+    hf = all_gather(h)
+    part = reduce_scatter(F.linear(F.gelu(F.linear(hf, f["w1"], f["b1"]), approximate="tanh"), f["w2"]))
+    return xs + (part + f["b2"]) * et[:, 5]

@@ -1,0 +1,147 @@
+"""Sequence-parallel block (token-sharded residual + local all-head cross-attention) on
+B200s over NCCL.
+
+* 2 GPUs: `FastBlockSP` at TP=2, batch 1, on a config-0-sized block (7854-token grid cut to
+  6x12x15) against the TP=1 device block and the fp32 oracle;
+* 4 GPUs: the two-layer golden step in the CFG-parallel 2 x (SP+TP 2) layout against the
+  reference's own ref_fp32.main() output.
+Each test is skipped on boxes with fewer GPUs."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from conftest import PKG_DIR, ROOT
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _init(rank, world, port):
+    import datetime
+    import sys
+    for p in (ROOT, PKG_DIR):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    return dev
+
+
+def _block_worker(rank, world, port, q):
+    try:
+        dev = _init(rank, world, port)
+        from oracle import dit_ref as R
+        from wanb200 import BlockWeights, FastBlock, FastCrossKV, WanSpec, device_error, random_block_state
+        from wanb200.block import FastBlockSP
+        from wanb200.dit import rope_tables
+        spec = WanSpec()
+        grid = (6, 12, 15)
+        L = 1080
+        sd = random_block_state(spec, 21)
+        g = torch.Generator().manual_seed(22)
+        x = torch.randn(1, L, spec.dim, generator=g).to(torch.bfloat16)
+        e0 = torch.randn(1, grid[0], 6, spec.dim, generator=g) * 0.1
+        ctx = torch.randn(1, 512, spec.dim, generator=g).to(torch.bfloat16)
+        cos, sin = rope_tables(grid, 128, dev)
+        w = BlockWeights(sd, spec.num_heads, dev, rank, world, local_cross=True)
+        ck, cv = FastCrossKV(w)(ctx.to(dev))
+        S = -(-L // world)
+        xp = torch.cat([x[0], x.new_zeros(S * world - L, spec.dim)]).to(dev)
+        ys = FastBlockSP(w, L, grid[0], dist.group.WORLD)(xp[rank * S:(rank + 1) * S].contiguous(), e0.to(dev),
+                                                         cos, sin, ck, cv)
+        full = torch.empty(S * world, spec.dim, dtype=ys.dtype, device=dev)
+        dist.all_gather_into_tensor(full, ys)
+        out = {"device_error": device_error(reset=True)}
+        if rank == 0:
+            y = full[:L].float().cpu()
+            w1 = BlockWeights(sd, spec.num_heads, dev)
+            ck1, cv1 = FastCrossKV(w1)(ctx.to(dev))
+            y1 = FastBlock(w1, grid[0])(x.to(dev), e0.to(dev), cos, sin, ck1, cv1)[0].float().cpu()
+            out["sp_vs_tp1"] = R.rel_rms(y, y1)
+            p32 = {k: v.float() for k, v in sd.items()}
+            cosr, sinr = R.rope_tables(R.model_freqs(128), grid, 128)
+            ckr, cvr = R.cross_kv(p32, ctx.float(), spec.num_heads)
+            y_ref = R.block_fwd(p32, x.float(), e0, cosr, sinr, ckr, cvr, grid[0], spec.num_heads)[0]
+            out["sp_vs_oracle"] = R.rel_rms(y, y_ref)
+        q.put((rank, out))
+    except Exception:
+        import traceback
+        q.put((rank, traceback.format_exc()))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def _step_worker(rank, world, port, q):
+    try:
+        dev = _init(rank, world, port)
+        from oracle import dit_ref as R
+        from wanb200 import FastWanDiT, WanSpec, device_error
+        from wanb200.parallel import make_layout
+        mg = torch.load(os.path.join(ROOT, "tests", "golden", "model_small.pt"), weights_only=False)
+        cfg = mg["cfg"]
+        sp = WanSpec(dim=cfg["dim"], ffn_dim=cfg["ffn_dim"], num_heads=cfg["num_heads"],
+                     num_layers=cfg["num_layers"], freq_dim=cfg["freq_dim"], text_dim=cfg["text_dim"],
+                     in_dim=cfg["in_dim"], out_dim=cfg["out_dim"], text_len=cfg["text_len"])
+        lat = mg["latent"]
+        lay = make_layout("cfg")
+        fc = FastWanDiT((sp, mg["state_dict"]), (lat.shape[1], lat.shape[2] // 2, lat.shape[3] // 2), mg["guide"],
+                        dev, cfg_group=lay.cfg_group, pair_group=lay.pair_group, tp_group=lay.tp_group)
+        assert fc.sp
+        fc.set_context(mg["ctx"].to(dev), mg["ctx_null"].to(dev))
+        pred = fc(lat.to(dev), mg["t"])
+        q.put((rank, {"step_vs_reference": R.rel_rms(pred.float().cpu(), mg["noise_pred"]),
+                      "device_error": device_error(reset=True)}))
+    except Exception:
+        import traceback
+        q.put((rank, traceback.format_exc()))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def _run(target, world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=target, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=600) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+    for r in range(world):
+        assert isinstance(res[r], dict), res[r]
+        assert res[r]["device_error"] == 0
+    return res
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_sp_block_tp2():
+    res = _run(_block_worker, 2)
+    print("sp2:", res[0])
+    assert res[0]["sp_vs_tp1"] < 1e-2
+    assert res[0]["sp_vs_oracle"] < 2e-2
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 4, reason="needs 4 GPUs")
+def test_cfg_parallel_sp_step_4gpu():
+    res = _run(_step_worker, 4)
+    print("cfg2xsp2:", res)
+    for r in range(4):
+        assert res[r]["step_vs_reference"] < 5e-2, res[r]

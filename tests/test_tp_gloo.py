@@ -147,7 +147,70 @@ def test_cfg_parallel_layout_groups():
     res = dict(q.get(timeout=120) for _ in procs)
     for p in procs:
         p.join(timeout=30)
-    assert res[0] == (0, 2, 1.0, 2.0, "cfg2xtp2"), res[0]
-    assert res[1] == (0, 2, 1.0, 4.0, "cfg2xtp2"), res[1]
-    assert res[2] == (1, 2, 5.0, 2.0, "cfg2xtp2"), res[2]
-    assert res[3] == (1, 2, 5.0, 4.0, "cfg2xtp2"), res[3]
+    assert res[0] == (0, 2, 1.0, 2.0, "cfg2x(sp+tp)2"), res[0]
+    assert res[1] == (0, 2, 1.0, 4.0, "cfg2x(sp+tp)2"), res[1]
+    assert res[2] == (1, 2, 5.0, 2.0, "cfg2x(sp+tp)2"), res[2]
+    assert res[3] == (1, 2, 5.0, 4.0, "cfg2x(sp+tp)2"), res[3]
+
+
+def _sp_worker(rank, world, port, q):
+    try:
+        _setup(rank, world, port)
+        torch.set_num_threads(1)
+        from oracle import dit_ref as R
+        from oracle.tp_ref import block_fwd_sp
+        from wanb200 import BlockWeights, WanSpec, random_block_state
+        spec = WanSpec(dim=512, ffn_dim=1024, num_heads=4)
+        grid = (2, 3, 5)
+        L, Lc = 30, 16  # 30 tokens over `world` ranks: padded when world does not divide 30
+        sd = random_block_state(spec, 6)
+        g = torch.Generator().manual_seed(10)
+        x = torch.randn(1, L, spec.dim, generator=g)
+        e0 = torch.randn(1, grid[0], 6, spec.dim, generator=g) * 0.1
+        ctx = torch.randn(1, Lc, spec.dim, generator=g)
+        cos, sin = R.rope_tables(R.model_freqs(128), grid, 128)
+        p32 = {k: v.float() for k, v in sd.items()}
+        ck, cv = R.cross_kv(p32, ctx, spec.num_heads)
+        y_ref = R.block_fwd(p32, x, e0, cos, sin, ck, cv, grid[0], spec.num_heads)[0]
+        S = -(-L // world)
+        xp = torch.cat([x[0], x.new_zeros(S * world - L, spec.dim)])
+        xs = xp[rank * S:(rank + 1) * S].contiguous()
+        w = BlockWeights(sd, spec.num_heads, "cpu", rank, world, local_cross=True)
+
+        def ag(t):
+            out = [torch.empty_like(t) for _ in range(world)]
+            dist.all_gather(out, t.contiguous())
+            return torch.cat(out)
+
+        def rs(t):
+            t = t.contiguous()
+            dist.all_reduce(t)
+            return t[rank * S:(rank + 1) * S]
+
+        ys = block_fwd_sp(w, xs, e0, cos, sin, ck, cv, L, grid[0], rank, world, ag, rs, lambda t: dist.all_reduce(t))
+        y = ag(ys)[:L]
+        q.put((rank, R.rel_rms(y, y_ref)))
+    except Exception as ex:  # pragma: no cover
+        import traceback
+        q.put((rank, traceback.format_exc()))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_sequence_parallel_decomposition_matches_unsharded_oracle(world):
+    """Token-sharded residual + all-gather / reduce-scatter around the TP GEMMs + local
+    all-head cross-attention (the reference's _FastBlockSP with full_cross) == one block."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_sp_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(world):
+        assert isinstance(res[r], float), res[r]
+        assert res[r] < 1e-5, (r, res[r])

@@ -157,4 +157,12 @@ int wanb200_device_error(int reset) {
 
 int wanb200_version(void) { return 100; }
 
+int wanb200_struct_sizes(int64_t* out, int n) {
+  const int64_t sizes[5] = {(int64_t)sizeof(wanb200_gemm_params), (int64_t)sizeof(wanb200_attn_params),
+                            (int64_t)sizeof(wanb200_ln_params), (int64_t)sizeof(wanb200_qknorm_params),
+                            (int64_t)sizeof(wanb200_residual_params)};
+  for (int i = 0; i < n && i < 5; ++i) out[i] = sizes[i];
+  return 5;
+}
+
 }  // extern "C"

@@ -18,7 +18,7 @@ struct LnArgs {
   const float* e0;
   int64_t e0_frame_stride;
   int shift_idx, scale_idx;
-  int64_t seq_len, tokens_per_frame;
+  int64_t seq_len, tokens_per_frame, row_offset;
   const __nv_bfloat16* weight;
   const __nv_bfloat16* bias;
   float* zero_buf;
@@ -71,7 +71,7 @@ __global__ void __launch_bounds__(256, 2) layernorm_kernel(const LnArgs a) {
   const float* shp = nullptr;
   const float* scp = nullptr;
   if constexpr (MODE == 0) {
-    const int64_t f = (row % a.seq_len) / a.tokens_per_frame;
+    const int64_t f = ((row + a.row_offset) % a.seq_len) / a.tokens_per_frame;
     shp = a.e0 + f * a.e0_frame_stride + (int64_t)a.shift_idx * a.dim;
     scp = a.e0 + f * a.e0_frame_stride + (int64_t)a.scale_idx * a.dim;
   }
@@ -156,6 +156,7 @@ int layernorm(const wanb200_ln_params* p, cudaStream_t st) {
   a.scale_idx = p->scale_idx;
   a.seq_len = p->seq_len > 0 ? p->seq_len : 1;
   a.tokens_per_frame = p->tokens_per_frame > 0 ? p->tokens_per_frame : 1;
+  a.row_offset = p->row_offset;
   a.weight = reinterpret_cast<const __nv_bfloat16*>(p->weight);
   a.bias = reinterpret_cast<const __nv_bfloat16*>(p->bias);
   a.zero_buf = p->zero_buf;
@@ -275,7 +276,7 @@ struct ResArgs {
   const __nv_bfloat16* bias;
   const __nv_bfloat16* gate_mod;
   const float* gate_e0;
-  int64_t gate_frame_stride, seq_len, tokens_per_frame;
+  int64_t gate_frame_stride, seq_len, tokens_per_frame, row_offset;
 };
 
 // Thread = 8 channels of one row.  `x + _gate(y + b, e[k])` / `x + (y + b)` after the TP
@@ -294,7 +295,7 @@ __global__ void __launch_bounds__(256) bias_gate_residual_kernel(const ResArgs a
   if constexpr (GATE) {
     float g[8];
     unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.gate_mod + col)), g);
-    const float* e = a.gate_e0 + ((row % a.seq_len) / a.tokens_per_frame) * a.gate_frame_stride + col;
+    const float* e = a.gate_e0 + (((row + a.row_offset) % a.seq_len) / a.tokens_per_frame) * a.gate_frame_stride + col;
     const float4 e0 = __ldg(reinterpret_cast<const float4*>(e)), e1 = __ldg(reinterpret_cast<const float4*>(e + 4));
     g[0] += e0.x; g[1] += e0.y; g[2] += e0.z; g[3] += e0.w;
     g[4] += e1.x; g[5] += e1.y; g[6] += e1.z; g[7] += e1.w;
@@ -335,6 +336,7 @@ int bias_gate_residual(const wanb200_residual_params* p, cudaStream_t st) {
   a.gate_frame_stride = p->gate_frame_stride;
   a.seq_len = p->seq_len > 0 ? p->seq_len : 1;
   a.tokens_per_frame = p->tokens_per_frame > 0 ? p->tokens_per_frame : 1;
+  a.row_offset = p->row_offset;
   const int64_t blocks = (p->rows * (p->dim / 8) + 255) / 256;
   if (blocks > INT32_MAX) return set_error(WANB200_EINVAL, "bias_gate_residual: too large");
   if (gate)

@@ -38,6 +38,7 @@ struct GemmArgs {
   const float* gate_e0;
   int64_t gate_frame_stride;
   int seq_len, tokens_per_frame;
+  int64_t row_offset;
   float* rowss;
   int ss_section, ss_nsections;
   int* err;
@@ -80,7 +81,7 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v,
     if (row < a.M) {
       const uint4* rp = reinterpret_cast<const uint4*>(a.residual + (int64_t)row * a.ldr + col0);
       if constexpr (EPI == WANB200_EPI_BIAS_GATE_RES) {
-        const int f = (row % a.seq_len) / a.tokens_per_frame;
+        const int f = (int)(((int64_t)row + a.row_offset) % a.seq_len) / a.tokens_per_frame;
         const float4* ep = reinterpret_cast<const float4*>(a.gate_e0 + (int64_t)f * a.gate_frame_stride + col0);
         const uint4* mp = reinterpret_cast<const uint4*>(a.gate_mod + col0);
 #pragma unroll
@@ -357,6 +358,7 @@ int gemm_bf16(const wanb200_gemm_params* p, cudaStream_t st) {
   ga.gate_frame_stride = p->gate_frame_stride;
   ga.seq_len = (int)(p->seq_len > 0 ? p->seq_len : 1);
   ga.tokens_per_frame = (int)(p->tokens_per_frame > 0 ? p->tokens_per_frame : 1);
+  ga.row_offset = p->row_offset;
   ga.rowss = p->rowss;
   ga.ss_section = (int)(p->ss_section > 0 ? p->ss_section : 1);
   ga.ss_nsections = p->ss_nsections;

@@ -24,7 +24,7 @@ class GemmParams(ctypes.Structure):
                 ("ldd", c_int64), ("M", c_int64), ("N", c_int64), ("K", c_int64), ("epilogue", c_int),
                 ("bias", c_void_p), ("residual", c_void_p), ("ldr", c_int64), ("gate_mod", c_void_p),
                 ("gate_e0", c_void_p), ("gate_frame_stride", c_int64), ("seq_len", c_int64),
-                ("tokens_per_frame", c_int64), ("rowss", c_void_p), ("ss_section", c_int64),
+                ("tokens_per_frame", c_int64), ("row_offset", c_int64), ("rowss", c_void_p), ("ss_section", c_int64),
                 ("ss_nsections", c_int)]
 
 
@@ -41,6 +41,7 @@ class LnParams(ctypes.Structure):
     _fields_ = [("x", c_void_p), ("out", c_void_p), ("rows", c_int64), ("dim", c_int64), ("eps", c_float),
                 ("mode", c_int), ("modulation", c_void_p), ("e0", c_void_p), ("e0_frame_stride", c_int64),
                 ("shift_idx", c_int), ("scale_idx", c_int), ("seq_len", c_int64), ("tokens_per_frame", c_int64),
+                ("row_offset", c_int64),
                 ("weight", c_void_p), ("bias", c_void_p), ("zero_buf", c_void_p), ("zero_count", c_int64)]
 
 
@@ -54,11 +55,12 @@ class QkNormParams(ctypes.Structure):
 class ResidualParams(ctypes.Structure):
     _fields_ = [("out", c_void_p), ("residual", c_void_p), ("y", c_void_p), ("rows", c_int64), ("dim", c_int64),
                 ("bias", c_void_p), ("gate_mod", c_void_p), ("gate_e0", c_void_p), ("gate_frame_stride", c_int64),
-                ("seq_len", c_int64), ("tokens_per_frame", c_int64)]
+                ("seq_len", c_int64), ("tokens_per_frame", c_int64), ("row_offset", c_int64)]
 
 
 EXPORTS = ("wanb200_gemm_bf16", "wanb200_attn_fwd", "wanb200_layernorm", "wanb200_qk_norm_rope",
-           "wanb200_bias_gate_residual", "wanb200_last_error", "wanb200_device_error", "wanb200_version")
+           "wanb200_bias_gate_residual", "wanb200_last_error", "wanb200_device_error", "wanb200_version",
+           "wanb200_struct_sizes")
 
 _lock = threading.Lock()
 _lib = None
@@ -92,6 +94,14 @@ def load():
             lib.wanb200_device_error.argtypes = [c_int]
             lib.wanb200_device_error.restype = c_int
             lib.wanb200_version.restype = c_int
+            lib.wanb200_struct_sizes.argtypes = [ctypes.POINTER(c_int64), c_int]
+            lib.wanb200_struct_sizes.restype = c_int
+            sizes = (c_int64 * 5)()
+            lib.wanb200_struct_sizes(sizes, 5)
+            want = [ctypes.sizeof(c) for c in (GemmParams, AttnParams, LnParams, QkNormParams, ResidualParams)]
+            if list(sizes) != want:
+                raise WanB200Error(f"{LIB_PATH} was built from a different include/wanb200.h (struct sizes "
+                                   f"{list(sizes)} vs {want}); rebuild it with `python wan2-ti2v-5b_b200/build.py`")
             _lib = lib
     return _lib
 

@@ -172,19 +172,129 @@ class FastCrossKV:
         self.w, self.tp_group, self.eps = weights, tp_group, eps
 
     def forward(self, context):
-        """context [B, Lc, C] bf16 -> ck, cv [B, Lc, H_local, 128] bf16 (views of one buffer)."""
+        """context [B, Lc, C] bf16 -> ck, cv [B, Lc, H_x, 128] bf16 (views of one buffer); H_x is
+        this rank's heads, or all heads when the weights keep the cross-attention whole."""
         w = self.w
         B, Lc, C = context.shape
-        N, Cl = B * Lc, w.local_dim
+        N, Cl, nh = B * Lc, w.cross_dim, w.cross_heads
         ctx = context.reshape(N, C).to(BF16).contiguous()
         ss = torch.zeros(N, device=context.device, dtype=torch.float32)
         kv = ops.linear(ctx, w.w_ckv, w.b_ckv, epilogue=L.EPI_BIAS_SUMSQ, rowss=ss, ss_section=Cl, ss_nsections=1,
                         kind="gemm_cross_kv")
-        if w.tp_size > 1:
+        if w.tp_size > 1 and not w.local_cross:
             dist.all_reduce(ss, group=self.tp_group)
         ops.qk_norm_rope(kv, [(0, ss, w.g_ck)], Cl, C, eps=self.eps)
-        ck = kv[:, :Cl].view(B, Lc, w.local_heads, 128)
-        cv = kv[:, Cl:].view(B, Lc, w.local_heads, 128)
+        ck = kv[:, :Cl].view(B, Lc, nh, 128)
+        cv = kv[:, Cl:].view(B, Lc, nh, 128)
         return ck, cv
 
     __call__ = forward
+
+
+class SPWorkspace:
+    """Scratch of the sequence-parallel block for (device, shard rows S, TP size T)."""
+
+    def __init__(self, S: int, T: int, dim: int, local_dim: int, ffn_local: int, device):
+        Np = S * T
+        kw = dict(device=device, dtype=BF16)
+        self.h_s = torch.empty(S, dim, **kw)
+        self.hf = torch.empty(Np, dim, **kw)
+        self.qkv = torch.empty(Np, 3 * local_dim, **kw)
+        self.y = torch.zeros(Np, local_dim, **kw)  # rows past the real tokens stay zero
+        self.part = torch.empty(Np, dim, **kw)
+        self.part_s = torch.empty(S, dim, **kw)
+        self.cq = torch.empty(S, dim, **kw)
+        self.yc = torch.empty(S, dim, **kw)
+        self.f = torch.empty(Np, ffn_local, **kw)
+        self.ss = torch.empty(2, Np, device=device, dtype=torch.float32)
+        self.ssc = torch.empty(S, device=device, dtype=torch.float32)
+
+
+_SPWS = {}
+
+
+class FastBlockSP:
+    """One WanAttentionBlock with a token-sharded residual stream inside the TP group and local
+    all-head cross-attention: `_FastBlockSP.forward(xs, e, oh, cos, sin, ck, cv)` of
+    models/fast_dit.py:314-389 with `full_cross` (372-377), batch 1 (CFG-parallel).
+
+    The residual xs [S, C] is rank r's shard (rows r*S .. r*S+S-1) of the flattened tokens,
+    zero-padded to T*S rows.  Before the column-parallel QKV / FFN-up GEMMs the normed shard is
+    all-gathered; after the row-parallel O / FFN-down GEMMs the partial sums are
+    reduce-scattered back to the shard (the bytes of the all-reduce they replace), so the norms,
+    gates and residual adds run on S rows.  Cross-attention runs on the shard with all 24 heads
+    and whole weights (BlockWeights(local_cross=True)) and needs no collective.  The per-token
+    modulation row comes from the global token index (row offset r*S) instead of the
+    reference's one-hot matmul.
+    """
+
+    def __init__(self, weights: BlockWeights, seq_len: int, num_frames: int, tp_group, eps: float = 1e-6):
+        assert weights.local_cross, "the sequence-parallel block needs BlockWeights(local_cross=True)"
+        self.w, self.L, self.num_frames, self.tp_group, self.eps = weights, seq_len, num_frames, tp_group, eps
+        self.T, self.rank = weights.tp_size, weights.tp_rank
+
+    def _ws(self, S, device):
+        w = self.w
+        key = (str(device), S, self.T, w.dim, w.local_dim, w.ffn_local)
+        ws = _SPWS.get(key)
+        if ws is None:
+            ws = _SPWS[key] = SPWorkspace(S, self.T, w.dim, w.local_dim, w.ffn_local, device)
+        return ws
+
+    def forward(self, xs, e, cos, sin, ck, cv):
+        """xs [S, C] bf16 shard; e [1, F, 6, C]; cos/sin [1, L, 1, 64] fp32; ck/cv [1, Lc, 24, 128]."""
+        w, Lx, nf, g = self.w, self.L, self.num_frames, self.tp_group
+        S, C = xs.shape
+        N, Cl, nl = Lx, w.local_dim, w.local_heads  # batch 1
+        tpf = Lx // nf
+        frames_s = (Lx, tpf, self.rank * S)
+        e0 = e.reshape(-1, 6, C)
+        if e0.dtype != torch.float32 or not e0.is_contiguous():
+            e0 = e0.float().contiguous()
+        cos2, sin2 = cos.reshape(Lx, -1), sin.reshape(Lx, -1)
+        if cos2.dtype != torch.float32 or not cos2.is_contiguous():
+            cos2, sin2 = cos2.float().contiguous(), sin2.float().contiguous()
+        ws = self._ws(S, xs.device)
+        mod = w.modulation
+
+        # -- self-attention: LN on the shard, all-gather, column-parallel QKV on all tokens
+        ops.layernorm_modulate(xs, mod, e0, 0, 1, frames_s, out=ws.h_s, eps=self.eps, zero=ws.ss)
+        dist.all_gather_into_tensor(ws.hf, ws.h_s, group=g)
+        ops.linear(ws.hf, w.w_qkv, w.b_qkv, epilogue=L.EPI_BIAS_SUMSQ, out=ws.qkv, rowss=ws.ss,
+                   ss_section=Cl, ss_nsections=2, kind="gemm_qkv")
+        dist.all_reduce(ws.ss, group=g)
+        ops.qk_norm_rope(ws.qkv, [(0, ws.ss[0], w.g_q), (Cl, ws.ss[1], w.g_k)], Cl, C, eps=self.eps,
+                         cos=cos2, sin=sin2, seq_len=Lx)
+        q = ws.qkv[:N, :Cl].view(1, Lx, nl, 128)
+        k = ws.qkv[:N, Cl:2 * Cl].view(1, Lx, nl, 128)
+        v = ws.qkv[:N, 2 * Cl:].view(1, Lx, nl, 128)
+        ops.attention(q, k, v, out=ws.y[:N].view(1, Lx, nl, 128), kind="attn_self")
+        ops.linear(ws.y, w.w_o, None, epilogue=L.EPI_NONE, out=ws.part, kind="gemm_o")
+        dist.reduce_scatter_tensor(ws.part_s, ws.part, group=g)
+        x1 = torch.empty_like(xs)
+        ops.bias_gate_residual(xs, ws.part_s, w.b_o, gate=(mod[2], e0[:, 2, :]), frames=frames_s, out=x1)
+
+        # -- cross-attention on the shard, all heads, no collective
+        ops.layernorm_affine(x1, w.ln3_w, w.ln3_b, out=ws.h_s, eps=self.eps, zero=ws.ssc)
+        ops.linear(ws.h_s, w.w_cq, w.b_cq, epilogue=L.EPI_BIAS_SUMSQ, out=ws.cq, rowss=ws.ssc, ss_section=C,
+                   ss_nsections=1, kind="gemm_cross_q")
+        ops.qk_norm_rope(ws.cq, [(0, ws.ssc, w.g_cq)], C, C, eps=self.eps)
+        H = w.cross_heads
+        ops.attention(ws.cq.view(1, S, H, 128), ck, cv, out=ws.yc.view(1, S, H, 128), kind="attn_cross")
+        ops.linear(ws.yc, w.w_co, w.b_co, epilogue=L.EPI_BIAS_RES, out=x1, residual=x1, kind="gemm_cross_o")
+
+        # -- FFN: LN on the shard, all-gather, column/row-parallel GEMMs, reduce-scatter
+        ops.layernorm_modulate(x1, mod, e0, 3, 4, frames_s, out=ws.h_s, eps=self.eps)
+        dist.all_gather_into_tensor(ws.hf, ws.h_s, group=g)
+        ops.linear(ws.hf, w.w1, w.b1, epilogue=L.EPI_BIAS_GELU, out=ws.f, kind="gemm_ffn_up")
+        ops.linear(ws.f, w.w2, None, epilogue=L.EPI_NONE, out=ws.part, kind="gemm_ffn_down")
+        dist.reduce_scatter_tensor(ws.part_s, ws.part, group=g)
+        ops.bias_gate_residual(x1, ws.part_s, w.b2, gate=(mod[5], e0[:, 5, :]), frames=frames_s, out=x1)
+        return x1
+
+    __call__ = forward
+
+    @property
+    def launches(self) -> int:
+        return 15
+

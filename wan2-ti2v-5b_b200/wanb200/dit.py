@@ -25,7 +25,7 @@ import torch
 import torch.distributed as dist
 import torch.nn.functional as F
 
-from .block import FastBlock, FastCrossKV
+from .block import FastBlock, FastBlockSP, FastCrossKV
 from .weights import BlockWeights, WanSpec, block_state
 
 BF16 = torch.bfloat16
@@ -74,7 +74,10 @@ def _spec_and_state(model):
 
 class FastWanDiT:
     def __init__(self, model, grid, guide_scale, device, cfg_group=None, pair_group=None, tp_group=None,
-                 num_layers=None):
+                 num_layers=None, seq_parallel=None):
+        """seq_parallel: token-sharded residual inside the TP group with local all-head
+        cross-attention (`_FastBlockSP`, fast_dit.py:314-389); default on for CFG-parallel with
+        TP > 1 (batch 1), the reference's best layout."""
         spec, sd = _spec_and_state(model)
         self.spec = spec
         self.grid = tuple(int(g) for g in grid)
@@ -98,9 +101,18 @@ class FastWanDiT:
             return sd[k].to(device=self.device, dtype=torch.float32)
 
         self.emb = {k: f32(k) for k in sd if not k.startswith("blocks.")}
-        self.block_weights = [BlockWeights(block_state(sd, i), spec.num_heads, self.device, rank, tp)
-                              for i in range(nl)]
-        self.blocks = [FastBlock(w, self.num_frames, tp_group, spec.eps) for w in self.block_weights]
+        if seq_parallel is None:
+            seq_parallel = cfg_group is not None and tp > 1
+        if seq_parallel and (self.batch != 1 or tp == 1):
+            raise ValueError("seq_parallel needs CFG-parallel (batch 1) and a TP group of size > 1")
+        self.sp = seq_parallel
+        self.block_weights = [BlockWeights(block_state(sd, i), spec.num_heads, self.device, rank, tp,
+                                           local_cross=seq_parallel) for i in range(nl)]
+        if seq_parallel:
+            self.blocks = [FastBlockSP(w, self.seq_len, self.num_frames, tp_group, spec.eps)
+                           for w in self.block_weights]
+        else:
+            self.blocks = [FastBlock(w, self.num_frames, tp_group, spec.eps) for w in self.block_weights]
         self.cross_kv = [FastCrossKV(w, tp_group, spec.eps) for w in self.block_weights]
         self.context = None
 
@@ -169,12 +181,32 @@ class FastWanDiT:
             x = blk(x, e0, self.cos, self.sin, ck, cv)
         return x
 
+    def shard(self, x):
+        """[B, L, C] -> this rank's [S, C] rows of the flattened tokens, zero-padded to T*S."""
+        B, Lx, C = x.shape
+        N, T = B * Lx, self.tp_size
+        S = -(-N // T)
+        flat = x.reshape(N, C)
+        if S * T != N:
+            flat = torch.cat([flat, flat.new_zeros(S * T - N, C)])
+        return flat[self.tp_rank * S:(self.tp_rank + 1) * S].contiguous()
+
+    def unshard(self, xs):
+        """All-gather the token shards back to [B, L, C]."""
+        S, C = xs.shape
+        full = torch.empty(S * self.tp_size, C, dtype=xs.dtype, device=xs.device)
+        dist.all_gather_into_tensor(full, xs, group=self.tp_group)
+        return full[:self.batch * self.seq_len].view(self.batch, self.seq_len, C)
+
     def __call__(self, latent, t):
         if self.context is None:
             raise RuntimeError("call set_context() first")
         e, e0 = self.time_embed(t)
         x = self.patch(latent)
-        x = self.forward_blocks(x, e0)
+        if self.sp:
+            x = self.unshard(self.forward_blocks(self.shard(x), e0))
+        else:
+            x = self.forward_blocks(x, e0)
         return self.head(x, e)
 
     @property

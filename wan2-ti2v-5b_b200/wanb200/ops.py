@@ -85,6 +85,13 @@ def _p(t):
     return None if t is None else t.data_ptr()
 
 
+def _set_frames(p, frames):
+    """frames = (seq_len, tokens_per_frame[, row_offset]): row r belongs to latent frame
+    ((r + row_offset) % seq_len) // tokens_per_frame."""
+    p.seq_len, p.tokens_per_frame = frames[0], frames[1]
+    p.row_offset = frames[2] if len(frames) > 2 else 0
+
+
 def _rows(t: torch.Tensor, name: str):
     _need(t.dim() == 2 and t.stride(1) == 1, f"{name} must be 2-D with unit column stride")
     return t.stride(0)
@@ -119,7 +126,7 @@ def linear(a, w, bias=None, *, epilogue=L.EPI_BIAS, out=None, residual=None, gat
         _need(gm.dtype == BF16 and ge.dtype == torch.float32 and ge.stride(-1) == 1, "linear: bad gate tensors")
         p.gate_mod, p.gate_e0, p.gate_frame_stride = _p(gm), _p(ge), ge.stride(0)
     if frames is not None:
-        p.seq_len, p.tokens_per_frame = frames
+        _set_frames(p, frames)
     if rowss is not None:
         _need(rowss.dtype == torch.float32, "linear: rowss must be fp32")
         p.rowss, p.ss_section, p.ss_nsections = _p(rowss), ss_section, ss_nsections
@@ -167,7 +174,7 @@ def layernorm_modulate(x, modulation, e0, shift_idx, scale_idx, frames, out=None
     p.x, p.out, p.rows, p.dim, p.eps, p.mode = _p(x), _p(out), M, C, eps, L.LN_MODULATE
     p.modulation, p.e0, p.e0_frame_stride = _p(modulation), _p(e0), 6 * C
     p.shift_idx, p.scale_idx = shift_idx, scale_idx
-    p.seq_len, p.tokens_per_frame = frames
+    _set_frames(p, frames)
     if zero is not None:
         p.zero_buf, p.zero_count = _p(zero), zero.numel()
     lib = L.load()
@@ -227,7 +234,7 @@ def bias_gate_residual(residual, y, bias, gate=None, frames=None, out=None):
     if gate is not None:
         gm, ge = gate
         p.gate_mod, p.gate_e0, p.gate_frame_stride = _p(gm), _p(ge), ge.stride(0)
-        p.seq_len, p.tokens_per_frame = frames
+        _set_frames(p, frames)
     lib = L.load()
     L.check(_launch(residual, "bias_gate_residual", 6.0 * M * C,
                     lambda: lib.wanb200_bias_gate_residual(ctypes.byref(p), _stream(residual))),

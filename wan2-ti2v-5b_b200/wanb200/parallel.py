@@ -25,7 +25,7 @@ class Layout:
     def describe(self, world: int) -> str:
         if self.cfg_group is None:
             return f"tp{world}"
-        return "cfg2" if self.tp_size == 1 else f"cfg2xtp{self.tp_size}"
+        return "cfg2" if self.tp_size == 1 else f"cfg2x(sp+tp){self.tp_size}"
 
 
 def make_layout(kind: str = "auto") -> Layout:

@@ -103,7 +103,11 @@ def block_state(sd: dict, i: int) -> dict:
 class BlockWeights:
     """One block's parameters on `device` in bf16, sliced for TP rank `tp_rank` of `tp_size`."""
 
-    def __init__(self, sd: dict, num_heads: int, device, tp_rank: int = 0, tp_size: int = 1):
+    def __init__(self, sd: dict, num_heads: int, device, tp_rank: int = 0, tp_size: int = 1,
+                 local_cross: bool = False):
+        """local_cross: keep the cross-attention weights whole (all heads) on every rank, for the
+        sequence-parallel block whose cross-attention runs on the rank's token shard without
+        collectives (the reference's `full_cross`, models/fast_dit.py:372-377)."""
         C = sd["self_attn.q.weight"].shape[1]
         assert num_heads % tp_size == 0, f"{num_heads} heads do not split over {tp_size} ranks"
         d = C // num_heads
@@ -132,10 +136,14 @@ class BlockWeights:
         self.g_q, self.g_k = g(f"{sa}.norm_q.weight", hs), g(f"{sa}.norm_k.weight", hs)
         self.w_o, self.b_o = g(f"{sa}.o.weight", hs, col=True), g(f"{sa}.o.bias")
         self.ln3_w, self.ln3_b = g("norm3.weight"), g("norm3.bias")
-        self.w_cq, self.b_cq, self.g_cq = g(f"{ca}.q.weight", hs), g(f"{ca}.q.bias", hs), g(f"{ca}.norm_q.weight", hs)
-        self.w_ckv = torch.cat([g(f"{ca}.k.weight", hs), g(f"{ca}.v.weight", hs)]).contiguous()
-        self.b_ckv = torch.cat([g(f"{ca}.k.bias", hs), g(f"{ca}.v.bias", hs)]).contiguous()
-        self.g_ck = g(f"{ca}.norm_k.weight", hs)
-        self.w_co, self.b_co = g(f"{ca}.o.weight", hs, col=True), g(f"{ca}.o.bias")
+        self.local_cross = local_cross
+        cs = None if local_cross else hs
+        self.cross_heads = num_heads if local_cross else nl
+        self.cross_dim = C if local_cross else Cl
+        self.w_cq, self.b_cq, self.g_cq = g(f"{ca}.q.weight", cs), g(f"{ca}.q.bias", cs), g(f"{ca}.norm_q.weight", cs)
+        self.w_ckv = torch.cat([g(f"{ca}.k.weight", cs), g(f"{ca}.v.weight", cs)]).contiguous()
+        self.b_ckv = torch.cat([g(f"{ca}.k.bias", cs), g(f"{ca}.v.bias", cs)]).contiguous()
+        self.g_ck = g(f"{ca}.norm_k.weight", cs)
+        self.w_co, self.b_co = g(f"{ca}.o.weight", cs, col=True), g(f"{ca}.o.bias")
         self.w1, self.b1 = g("ffn.0.weight", fs), g("ffn.0.bias", fs)
         self.w2, self.b2 = g("ffn.2.weight", fs, col=True), g("ffn.2.bias")
