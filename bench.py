@@ -204,7 +204,7 @@ def run_ours(args):
     from wanb200.parallel import make_layout
     lay = make_layout(args.layout)
     fast = FastWanDiT((spec, sd), GRID, GUIDE, device, cfg_group=lay.cfg_group, pair_group=lay.pair_group,
-                      tp_group=lay.tp_group, num_layers=layers)
+                      tp_group=lay.tp_group, num_layers=layers, comm=args.comm)
     del sd
     g = torch.Generator(device=device).manual_seed(123)
     ctx = torch.randn(CTX_LEN, TEXT_DIM, generator=g, device=device)
@@ -310,7 +310,8 @@ def run_ours(args):
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) bf16 weights, seeded context/latent)",
         "config": {"workload": f"config2: {layers}-layer Wan2.2-TI2V-5B DiT step, 7854 tokens (21x17x22), CFG batch 2",
                    "global_batch": CFG_BATCH, "seq_len": GRID[0] * GRID[1] * GRID[2],
-                   "parallelism": lay.describe(world), "layers": layers, "inputs_larger_than_l2": True,
+                   "parallelism": lay.describe(world) + (f", {args.comm} collectives" if fast.sp else ""),
+                   "layers": layers, "inputs_larger_than_l2": True,
                    "l2_note": "each step streams ~9.8 GB of weights, far above the 126 MB L2"},
         "e2e": {"value": e2e_s, "unit": "s/step", "h2d_bytes_per_step": latent_host.numel() * 4,
                 "d2h_bytes_per_step": out_host.numel() * 4},
@@ -339,6 +340,8 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--comm", default="peer", choices=["peer", "nccl"],
+                    help="sequence-parallel collectives: fused into the kernels over NVLink peer memory, or NCCL")
     ap.add_argument("--layout", default="auto", choices=["auto", "tp", "cfg"],
                     help="N>1: tp = TP over all N ranks (batched CFG); cfg = CFG-parallel groups of N/2 "
                          "(TP inside each); auto = cfg for even N")

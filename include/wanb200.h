@@ -41,6 +41,11 @@ extern "C" {
  *   WANB200_EPI_BIAS_SUMSQ    d = acc + bias; rowss[s*M + row] += sum over section s of d^2
  *                             (the sum of squares of `_tp_rms_qk` 138-140 / `_tp_rms` 158)
  *   WANB200_EPI_NONE          d = acc (row-parallel partial sum before the TP all-reduce, 127)
+ *   WANB200_EPI_SCATTER       the reduce-scatter half of that all-reduce, fused: row r of acc is
+ *                             stored (bf16, over NVLink) into the inbox of its owner o = r / shard_rows,
+ *                             peer_out[o] + ((src_rank * shard_rows) + r - o * shard_rows) * ldd;
+ *                             d is unused.  The owner sums the slices (wanb200_bias_gate_residual
+ *                             with nsum) after a wanb200_peer_barrier.
  * gate[f, n] = gate_mod[n] + gate_e0[f * gate_frame_stride + n] (modulation + e0 chunk,
  * fast_dit.py:276-277), frame(row) = ((row + row_offset) % seq_len) / tokens_per_frame
  * (row_offset: index of row 0 in the flattened token sequence, for a token shard).
@@ -52,6 +57,8 @@ extern "C" {
 #define WANB200_EPI_BIAS_GATE_RES 3
 #define WANB200_EPI_BIAS_RES 4
 #define WANB200_EPI_BIAS_SUMSQ 5
+#define WANB200_EPI_SCATTER 6
+#define WANB200_MAX_PEERS 8
 
 typedef struct wanb200_gemm_params {
   const void* a; int64_t lda;      /* [M, K] bf16 */
@@ -65,6 +72,7 @@ typedef struct wanb200_gemm_params {
   const float* gate_e0; int64_t gate_frame_stride; /* e0 row of frame 0, stride between frames */
   int64_t seq_len, tokens_per_frame, row_offset;   /* frame(row) for GATE_RES */
   float* rowss; int64_t ss_section; int ss_nsections; /* SUMSQ: [ss_nsections, M] fp32, pre-zeroed */
+  void* peer_out[WANB200_MAX_PEERS]; int npeers; int src_rank; int64_t shard_rows; /* SCATTER */
 } wanb200_gemm_params;
 
 int wanb200_gemm_bf16(const wanb200_gemm_params* p, void* stream);
@@ -109,6 +117,9 @@ typedef struct wanb200_ln_params {
   int64_t seq_len, tokens_per_frame, row_offset;
   const void* weight; const void* bias;   /* [dim] bf16 for AFFINE */
   float* zero_buf; int64_t zero_count;
+  /* all-gather fused into the norm: when npush > 0 every output row is also stored at
+   * push_out[p] + (push_row0 + row) * dim for p < npush (peer-mapped buffers; out may be NULL) */
+  void* push_out[WANB200_MAX_PEERS]; int npush; int64_t push_row0;
 } wanb200_ln_params;
 
 int wanb200_layernorm(const wanb200_ln_params* p, void* stream);
@@ -135,16 +146,27 @@ int wanb200_qk_norm_rope(const wanb200_qknorm_params* p, void* stream);
  * out = residual + y + bias                        (gate_mod == NULL)
  * The tail of `_row_linear` + `_gate` + residual (fast_dit.py:126-131, 179-181, 294, 305, 311)
  * when the projection is row-parallel: y is the all-reduced partial sum (the GEMM ran with
- * WANB200_EPI_NONE).  All tensors [rows, dim] contiguous; out may alias residual.
+ * WANB200_EPI_NONE; or the nsum inbox slices a WANB200_EPI_SCATTER GEMM wrote).  All tensors
+ * [rows, dim] contiguous; out may alias residual.
  * Limits: dim % 8 == 0. */
 typedef struct wanb200_residual_params {
   void* out; const void* residual; const void* y; int64_t rows, dim;
   const void* bias;
   const void* gate_mod; const float* gate_e0; int64_t gate_frame_stride;
   int64_t seq_len, tokens_per_frame, row_offset;
+  int nsum; int64_t y_slice_stride; /* y = sum of nsum slices y + s * y_slice_stride (0/1: y alone) */
 } wanb200_residual_params;
 
 int wanb200_bias_gate_residual(const wanb200_residual_params* p, void* stream);
+
+/* ---------------------------------------------------------------- peer barrier
+ * Barrier of the `world` ranks of a TP group over NVLink peer memory, the synchronisation step
+ * of the fused collectives above.  flags[p] points to rank p's int32[world] flag array
+ * (peer-mapped).  This rank stores `epoch` into flags[p][rank] for every p (system-scope
+ * release after a system-scope fence), then waits (system-scope acquire) until its own
+ * flags[rank][s] >= epoch for every s.  Every rank calls it with the same increasing epochs.
+ * The wait is bounded (2 s); on timeout the device error word is set and the kernel returns. */
+int wanb200_peer_barrier(int* const* flags, int rank, int world, int epoch, void* stream);
 
 /* ---------------------------------------------------------------- status */
 const char* wanb200_last_error(void);

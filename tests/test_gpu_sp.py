@@ -42,7 +42,7 @@ def _init(rank, world, port):
     return dev
 
 
-def _block_worker(rank, world, port, q):
+def _block_worker(rank, world, port, q, comm_kind):
     try:
         dev = _init(rank, world, port)
         from oracle import dit_ref as R
@@ -62,11 +62,18 @@ def _block_worker(rank, world, port, q):
         ck, cv = FastCrossKV(w)(ctx.to(dev))
         S = -(-L // world)
         xp = torch.cat([x[0], x.new_zeros(S * world - L, spec.dim)]).to(dev)
-        ys = FastBlockSP(w, L, grid[0], dist.group.WORLD)(xp[rank * S:(rank + 1) * S].contiguous(), e0.to(dev),
-                                                         cos, sin, ck, cv)
+        comm = None
+        if comm_kind == "peer":
+            from wanb200.comm import PeerComm
+            comm = PeerComm(dist.group.WORLD, S, spec.dim, dev)
+        blk = FastBlockSP(w, L, grid[0], dist.group.WORLD, comm=comm)
+        xs = xp[rank * S:(rank + 1) * S].contiguous()
+        ys = blk(xs, e0.to(dev), cos, sin, ck, cv)
+        ys2 = blk(xs, e0.to(dev), cos, sin, ck, cv)  # the buffers and barrier epochs are reused
         full = torch.empty(S * world, spec.dim, dtype=ys.dtype, device=dev)
         dist.all_gather_into_tensor(full, ys)
-        out = {"device_error": device_error(reset=True)}
+        out = {"device_error": device_error(reset=True),
+               "repeat": float((ys.float() - ys2.float()).abs().max())}
         if rank == 0:
             y = full[:L].float().cpu()
             w1 = BlockWeights(sd, spec.num_heads, dev)
@@ -115,11 +122,11 @@ def _step_worker(rank, world, port, q):
             dist.destroy_process_group()
 
 
-def _run(target, world):
+def _run(target, world, *extra):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=target, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=target, args=(r, world, port, q) + extra) for r in range(world)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=600) for _ in procs)
@@ -132,11 +139,16 @@ def _run(target, world):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_sp_block_tp2():
-    res = _run(_block_worker, 2)
-    print("sp2:", res[0])
+@pytest.mark.parametrize("comm_kind", ["nccl", "peer"])
+def test_sp_block_tp2(comm_kind):
+    """comm_kind "peer": the all-gathers / reduce-scatters run inside the LayerNorm (row push) and
+    the row-parallel GEMM epilogue (inbox scatter) over NVLink peer memory, with peer barriers."""
+    res = _run(_block_worker, 2, comm_kind)
+    print(f"sp2[{comm_kind}]:", res[0])
     assert res[0]["sp_vs_tp1"] < 1e-2
     assert res[0]["sp_vs_oracle"] < 2e-2
+    for r in range(2):
+        assert res[r]["repeat"] < 0.1, res[r]  # only the fp32 atomics of the norm sums may differ
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 4, reason="needs 4 GPUs")

@@ -138,6 +138,10 @@ int wanb200_bias_gate_residual(const wanb200_residual_params* p, void* stream) {
   return bias_gate_residual(p, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int wanb200_peer_barrier(int* const* flags, int rank, int world, int epoch, void* stream) {
+  return peer_barrier(flags, rank, world, epoch, reinterpret_cast<cudaStream_t>(stream));
+}
+
 const char* wanb200_last_error(void) { return t_last_error.c_str(); }
 
 int wanb200_device_error(int reset) {

@@ -25,6 +25,7 @@ enum DevError : int {
   kErrTimeoutAttnMma = 202,
   kErrTimeoutAttnSoftmax = 203,
   kErrTimeoutDrain = 301,
+  kErrTimeoutPeerBarrier = 401,
 };
 
 // 2 s: far above any legitimate wait (a whole 30-layer step is ~0.2 s).

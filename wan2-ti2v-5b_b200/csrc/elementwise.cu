@@ -23,6 +23,9 @@ struct LnArgs {
   const __nv_bfloat16* bias;
   float* zero_buf;
   int64_t zero_count;
+  __nv_bfloat16* push_out[WANB200_MAX_PEERS];
+  int npush;
+  int64_t push_row0;
 };
 
 // One warp per row: lane l holds the 16-byte vectors at columns (i*32 + l)*8, i < dim/256.
@@ -30,7 +33,7 @@ struct LnArgs {
 //     `_modulate` (models/fast_dit.py:172-176): y * (1 + scale[f]) + shift[f] with
 //     shift/scale[f, c] = modulation[idx, c] + e0[f, idx, c] (fast_dit.py:276-277).
 //   MODE 1 (affine): norm3 = WanLayerNorm(elementwise_affine=True) (model.py:207-209).
-template <int MODE, int NVEC>
+template <int MODE, int NVEC, bool PUSH>
 __global__ void __launch_bounds__(256, 2) layernorm_kernel(const LnArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < a.zero_count;
@@ -75,7 +78,7 @@ __global__ void __launch_bounds__(256, 2) layernorm_kernel(const LnArgs a) {
     shp = a.e0 + f * a.e0_frame_stride + (int64_t)a.shift_idx * a.dim;
     scp = a.e0 + f * a.e0_frame_stride + (int64_t)a.scale_idx * a.dim;
   }
-  uint4* outr = reinterpret_cast<uint4*>(a.out + row * a.dim);
+  uint4* outr = a.out ? reinterpret_cast<uint4*>(a.out + row * a.dim) : nullptr;
 #pragma unroll
   for (int i = 0; i < NVEC; ++i) {
     {
@@ -106,27 +109,36 @@ __global__ void __launch_bounds__(256, 2) layernorm_kernel(const LnArgs a) {
       u.y = pack_bf16x2(y[2], y[3]);
       u.z = pack_bf16x2(y[4], y[5]);
       u.w = pack_bf16x2(y[6], y[7]);
-      outr[i * 32 + lane] = u;
+      if (!PUSH || outr) outr[i * 32 + lane] = u;
+#pragma unroll
+      for (int p = 0; p < (PUSH ? WANB200_MAX_PEERS : 0); ++p)  // all-gather fused into the norm: push the row to every rank
+        if (p < a.npush)
+        reinterpret_cast<uint4*>(a.push_out[p] + (a.push_row0 + row) * a.dim)[i * 32 + lane] = u;
     }
   }
 }
 
-template <int MODE>
+template <int MODE, bool PUSH>
 static void launch_ln(int nvec, const LnArgs& a, unsigned blocks, cudaStream_t st) {
   switch (nvec) {
 #define WANB200_LN_CASE(n) \
-  case n: layernorm_kernel<MODE, n><<<blocks, 256, 0, st>>>(a); break;
+  case n: layernorm_kernel<MODE, n, PUSH><<<blocks, 256, 0, st>>>(a); break;
     WANB200_LN_CASE(1) WANB200_LN_CASE(2) WANB200_LN_CASE(3) WANB200_LN_CASE(4) WANB200_LN_CASE(5)
     WANB200_LN_CASE(6) WANB200_LN_CASE(7) WANB200_LN_CASE(8) WANB200_LN_CASE(9) WANB200_LN_CASE(10)
     WANB200_LN_CASE(11) WANB200_LN_CASE(12) WANB200_LN_CASE(13) WANB200_LN_CASE(14) WANB200_LN_CASE(15)
-    default: layernorm_kernel<MODE, 16><<<blocks, 256, 0, st>>>(a); break;
+    default: layernorm_kernel<MODE, 16, PUSH><<<blocks, 256, 0, st>>>(a); break;
 #undef WANB200_LN_CASE
   }
 }
 
 int layernorm(const wanb200_ln_params* p, cudaStream_t st) {
   if (!p) return set_error(WANB200_EINVAL, "layernorm: null params");
-  if (!p->x || !p->out) return set_error(WANB200_EINVAL, "layernorm: null x/out");
+  if (!p->x || (!p->out && p->npush <= 0)) return set_error(WANB200_EINVAL, "layernorm: null x/out");
+  if (p->npush < 0 || p->npush > WANB200_MAX_PEERS || p->push_row0 < 0)
+    return set_error(WANB200_EINVAL, "layernorm: npush must be 0..8 and push_row0 >= 0");
+  for (int i = 0; i < p->npush; ++i)
+    if (!p->push_out[i] || !aligned16(p->push_out[i]))
+      return set_error(WANB200_EINVAL, "layernorm: push_out pointers must be non-null and 16-byte aligned");
   if (p->rows <= 0 || p->dim <= 0 || p->dim % 256 || p->dim > 256 * LN_MAX_VEC)
     return set_error(WANB200_EINVAL, "layernorm: dim must be a positive multiple of 256, at most 4096");
   if (!aligned16(p->x) || !aligned16(p->out)) return set_error(WANB200_EINVAL, "layernorm: x/out must be 16-byte aligned");
@@ -161,13 +173,18 @@ int layernorm(const wanb200_ln_params* p, cudaStream_t st) {
   a.bias = reinterpret_cast<const __nv_bfloat16*>(p->bias);
   a.zero_buf = p->zero_buf;
   a.zero_count = p->zero_count;
+  for (int i = 0; i < WANB200_MAX_PEERS; ++i)
+    a.push_out[i] = reinterpret_cast<__nv_bfloat16*>(i < p->npush ? p->push_out[i] : nullptr);
+  a.npush = p->npush;
+  a.push_row0 = p->push_row0;
   const int64_t blocks = (p->rows + 7) / 8;
   if (blocks > INT32_MAX) return set_error(WANB200_EINVAL, "layernorm: too many rows");
   const int nvec = a.dim / 256;
+  const bool push = a.npush > 0;
   if (p->mode == WANB200_LN_MODULATE)
-    launch_ln<0>(nvec, a, (unsigned)blocks, st);
+    push ? launch_ln<0, true>(nvec, a, (unsigned)blocks, st) : launch_ln<0, false>(nvec, a, (unsigned)blocks, st);
   else
-    launch_ln<1>(nvec, a, (unsigned)blocks, st);
+    push ? launch_ln<1, true>(nvec, a, (unsigned)blocks, st) : launch_ln<1, false>(nvec, a, (unsigned)blocks, st);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error("layernorm_kernel launch", e);
   return WANB200_OK;
@@ -277,6 +294,8 @@ struct ResArgs {
   const __nv_bfloat16* gate_mod;
   const float* gate_e0;
   int64_t gate_frame_stride, seq_len, tokens_per_frame, row_offset;
+  int nsum;
+  int64_t y_slice_stride;
 };
 
 // Thread = 8 channels of one row.  `x + _gate(y + b, e[k])` / `x + (y + b)` after the TP
@@ -291,6 +310,12 @@ __global__ void __launch_bounds__(256) bias_gate_residual_kernel(const ResArgs a
   float r[8], y[8], b[8];
   unpack_bf16x8(*reinterpret_cast<const uint4*>(a.residual + row * a.dim + col), r);
   unpack_bf16x8(*reinterpret_cast<const uint4*>(a.y + row * a.dim + col), y);
+  for (int s = 1; s < a.nsum; ++s) {  // the inbox slices of a fused reduce-scatter
+    float t[8];
+    unpack_bf16x8(*reinterpret_cast<const uint4*>(a.y + s * a.y_slice_stride + row * a.dim + col), t);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) y[k] += t[k];
+  }
   unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.bias + col)), b);
   if constexpr (GATE) {
     float g[8];
@@ -337,6 +362,8 @@ int bias_gate_residual(const wanb200_residual_params* p, cudaStream_t st) {
   a.seq_len = p->seq_len > 0 ? p->seq_len : 1;
   a.tokens_per_frame = p->tokens_per_frame > 0 ? p->tokens_per_frame : 1;
   a.row_offset = p->row_offset;
+  a.nsum = p->nsum;
+  a.y_slice_stride = p->y_slice_stride;
   const int64_t blocks = (p->rows * (p->dim / 8) + 255) / 256;
   if (blocks > INT32_MAX) return set_error(WANB200_EINVAL, "bias_gate_residual: too large");
   if (gate)

@@ -19,13 +19,25 @@
 
 namespace wanb200 {
 
-constexpr int GBM = 128, GBN = 256, GBK = 64, GSTAGES = 4;
+constexpr int GBM = 128, GBN = 256, GBK = 64;
 constexpr int G_A_BYTES = GBM * GBK * 2;  // 16 KB
 constexpr int G_B_BYTES = GBN * GBK * 2;  // 32 KB
 constexpr int G_STAGE_BYTES = G_A_BYTES + G_B_BYTES;
-constexpr int G_TILE_BYTES = GSTAGES * G_STAGE_BYTES;
-constexpr int G_SMEM_BYTES = G_TILE_BYTES + 256 + 1024;  // barriers + alignment slack
 constexpr uint32_t G_TMEM_COLS = 512;
+
+// Shared-memory plan per epilogue.  The scatter epilogue (reduce-scatter fused into the GEMM)
+// stages each warp's 32 x 256 output rows in shared memory so that every remote store is one
+// coalesced 512-byte row segment (16-byte stores per thread scattered over rows run at a
+// fraction of the NVLink bandwidth); it gives up one pipeline stage for the staging buffer.
+template <int EPI>
+struct GemmCfg {
+  static constexpr int STAGES = EPI == WANB200_EPI_SCATTER ? 3 : 4;
+  static constexpr int STAGING_ROW = GBN * 2 + 16;  // padded: the 16-byte row writes of a warp hit distinct banks
+  static constexpr int STAGING = EPI == WANB200_EPI_SCATTER ? 4 * 32 * STAGING_ROW : 0;
+  static constexpr int TILES = STAGES * G_STAGE_BYTES;
+  static constexpr int META = TILES + STAGING;
+  static constexpr int SMEM = META + 256 + 1024;  // barriers + alignment slack
+};
 
 struct GemmArgs {
   __nv_bfloat16* d;
@@ -41,8 +53,22 @@ struct GemmArgs {
   int64_t row_offset;
   float* rowss;
   int ss_section, ss_nsections;
+  __nv_bfloat16* peer_out[WANB200_MAX_PEERS];
+  int npeers, src_rank;
+  int64_t shard_rows;
   int* err;
 };
+
+// Row r's destination for the fused reduce-scatter: the inbox slice of this source rank on the
+// rank that owns r (a uniform select instead of a dynamically indexed parameter array).
+__device__ __forceinline__ __nv_bfloat16* scatter_row_ptr(const GemmArgs& a, int row) {
+  const int o = (int)((int64_t)row / a.shard_rows);
+  __nv_bfloat16* base = a.peer_out[0];
+#pragma unroll
+  for (int i = 1; i < WANB200_MAX_PEERS; ++i)
+    if (o == i) base = a.peer_out[i];
+  return base + ((int64_t)a.src_rank * a.shard_rows + row - (int64_t)o * a.shard_rows) * a.ldd;
+}
 
 // Grouped rasterisation: tiles are numbered in groups of G_GROUP_M row-blocks; inside a group
 // the row-block index runs fastest.  The ~148 tiles in flight then cover ~16 row-blocks x ~9
@@ -63,7 +89,7 @@ __device__ __forceinline__ void tile_origin(int tile, int num_m, int num_n, int&
 template <int EPI>
 __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v, int row, int col0, float& ss_acc,
                                                     int& ss_sec) {
-  if constexpr (EPI != WANB200_EPI_NONE) {
+  if constexpr (EPI != WANB200_EPI_NONE && EPI != WANB200_EPI_SCATTER) {
     const uint4* bp = reinterpret_cast<const uint4*>(a.bias + col0);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
@@ -117,7 +143,12 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v,
     for (int i = 0; i < 32; ++i) ss_acc = fmaf(v[i], v[i], ss_acc);
   }
   if (row < a.M) {
-    uint4* dp = reinterpret_cast<uint4*>(a.d + (int64_t)row * a.ldd + col0);
+    __nv_bfloat16* drow;
+    if constexpr (EPI == WANB200_EPI_SCATTER)
+      drow = scatter_row_ptr(a, row);
+    else
+      drow = a.d + (int64_t)row * a.ldd;
+    uint4* dp = reinterpret_cast<uint4*>(drow + col0);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       uint4 u;
@@ -138,7 +169,8 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   const uint32_t tiles = smem_u32(smem);
-  uint8_t* meta = smem + G_TILE_BYTES;
+  constexpr int GSTAGES = GemmCfg<EPI>::STAGES;
+  uint8_t* meta = smem + GemmCfg<EPI>::META;
   const uint32_t full0 = smem_u32(meta);           // GSTAGES x 8
   const uint32_t empty0 = full0 + 8 * GSTAGES;     // GSTAGES x 8
   const uint32_t tfull0 = empty0 + 8 * GSTAGES;    // 2 x 8
@@ -262,13 +294,39 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t t_row = tmem_base + (uint32_t(quad * 32) << 16) + acc * GBN;
       float ss_acc = 0.f;
       int ss_sec = -1;
+      if constexpr (EPI == WANB200_EPI_SCATTER) {
+        // stage this warp's 32 rows (lane = row), then write each row as one 512-byte segment
+        constexpr int SR = GemmCfg<EPI>::STAGING_ROW;
+        uint8_t* stg = smem + GemmCfg<EPI>::TILES + quad * 32 * SR;
+        const int ncols = min(GBN, args.N - n0);  // multiple of 32
 #pragma unroll 1
-      for (int c = 0; c < GBN / 32; ++c) {
-        const int col0 = n0 + c * 32;
-        if (col0 >= args.N) break;  // warp-uniform
-        float v[32];
-        tmem_ld32(t_row + c * 32, v);
-        gemm_epilogue_chunk<EPI>(args, v, row, col0, ss_acc, ss_sec);
+        for (int c = 0; c < ncols / 32; ++c) {
+          float v[32];
+          tmem_ld32(t_row + c * 32, v);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<uint4*>(stg + lane * SR + c * 64 + q * 16) =
+                make_uint4(pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]), pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]),
+                           pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]), pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]));
+        }
+        __syncwarp();
+#pragma unroll 1
+        for (int rr = 0; rr < 32; ++rr) {
+          const int orow = m0 + quad * 32 + rr;
+          if (orow < args.M && lane * 8 < ncols)
+            *reinterpret_cast<uint4*>(scatter_row_ptr(args, orow) + n0 + lane * 8) =
+                *reinterpret_cast<const uint4*>(stg + rr * SR + lane * 16);
+        }
+        __syncwarp();
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < GBN / 32; ++c) {
+          const int col0 = n0 + c * 32;
+          if (col0 >= args.N) break;  // warp-uniform
+          float v[32];
+          tmem_ld32(t_row + c * 32, v);
+          gemm_epilogue_chunk<EPI>(args, v, row, col0, ss_acc, ss_sec);
+        }
       }
       if constexpr (EPI == WANB200_EPI_BIAS_SUMSQ) {
         if (ss_sec >= 0 && ss_sec < args.ss_nsections && row < args.M)
@@ -295,11 +353,11 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmA
   cudaGetDevice(&dev);
   if (!attr_set[dev]) {
     cudaError_t e =
-        cudaFuncSetAttribute(gemm_bf16_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM_BYTES);
+        cudaFuncSetAttribute(gemm_bf16_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<EPI>::SMEM);
     if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(gemm)", e);
     attr_set[dev] = true;
   }
-  gemm_bf16_kernel<EPI><<<grid, 192, G_SMEM_BYTES, st>>>(ta, tb, ga);
+  gemm_bf16_kernel<EPI><<<grid, 192, GemmCfg<EPI>::SMEM, st>>>(ta, tb, ga);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error("gemm_bf16_kernel launch", e);
   return WANB200_OK;
@@ -307,7 +365,10 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmA
 
 int gemm_bf16(const wanb200_gemm_params* p, cudaStream_t st) {
   if (!p) return set_error(WANB200_EINVAL, "gemm: null params");
-  if (!p->a || !p->w || !p->d) return set_error(WANB200_EINVAL, "gemm: null a/w/d");
+  const int epi = p->epilogue;
+  if (epi < WANB200_EPI_NONE || epi > WANB200_EPI_SCATTER) return set_error(WANB200_EINVAL, "gemm: bad epilogue");
+  const bool scatter = epi == WANB200_EPI_SCATTER;
+  if (!p->a || !p->w || (!p->d && !scatter)) return set_error(WANB200_EINVAL, "gemm: null a/w/d");
   if (p->M <= 0 || p->N <= 0 || p->K <= 0) return set_error(WANB200_EINVAL, "gemm: M, N, K must be positive");
   if (p->K % GBK) return set_error(WANB200_EINVAL, "gemm: K must be a multiple of 64");
   if (p->N % 32) return set_error(WANB200_EINVAL, "gemm: N must be a multiple of 32");
@@ -315,12 +376,18 @@ int gemm_bf16(const wanb200_gemm_params* p, cudaStream_t st) {
     return set_error(WANB200_EINVAL, "gemm: dimension too large");
   if (p->lda < p->K || p->ldw < p->K || p->ldd < p->N || (p->lda % 8) || (p->ldw % 8) || (p->ldd % 8))
     return set_error(WANB200_EINVAL, "gemm: leading dims must be >= the row length and multiples of 8");
-  if (!aligned16(p->a) || !aligned16(p->w) || !aligned16(p->d))
+  if (!aligned16(p->a) || !aligned16(p->w) || (!scatter && !aligned16(p->d)))
     return set_error(WANB200_EINVAL, "gemm: a/w/d must be 16-byte aligned");
-  const int epi = p->epilogue;
-  if (epi < WANB200_EPI_NONE || epi > WANB200_EPI_BIAS_SUMSQ) return set_error(WANB200_EINVAL, "gemm: bad epilogue");
-  if (epi != WANB200_EPI_NONE && (!p->bias || !aligned16(p->bias)))
+  if (epi != WANB200_EPI_NONE && !scatter && (!p->bias || !aligned16(p->bias)))
     return set_error(WANB200_EINVAL, "gemm: epilogue needs a 16-byte aligned bias");
+  if (scatter) {
+    if (p->npeers < 1 || p->npeers > WANB200_MAX_PEERS || p->src_rank < 0 || p->src_rank >= p->npeers ||
+        p->shard_rows <= 0 || p->M > (int64_t)p->npeers * p->shard_rows)
+      return set_error(WANB200_EINVAL, "gemm: scatter needs 1..8 peers, a valid src_rank and M <= npeers*shard_rows");
+    for (int i = 0; i < p->npeers; ++i)
+      if (!p->peer_out[i] || !aligned16(p->peer_out[i]))
+        return set_error(WANB200_EINVAL, "gemm: scatter peer_out pointers must be non-null and 16-byte aligned");
+  }
   if (epi == WANB200_EPI_BIAS_GATE_RES || epi == WANB200_EPI_BIAS_RES) {
     if (!p->residual || !aligned16(p->residual) || p->ldr < p->N || (p->ldr % 8))
       return set_error(WANB200_EINVAL, "gemm: residual epilogue needs an aligned residual with ldr >= N, ldr % 8 == 0");
@@ -362,6 +429,11 @@ int gemm_bf16(const wanb200_gemm_params* p, cudaStream_t st) {
   ga.rowss = p->rowss;
   ga.ss_section = (int)(p->ss_section > 0 ? p->ss_section : 1);
   ga.ss_nsections = p->ss_nsections;
+  for (int i = 0; i < WANB200_MAX_PEERS; ++i)
+    ga.peer_out[i] = reinterpret_cast<__nv_bfloat16*>(i < p->npeers ? p->peer_out[i] : p->peer_out[0]);
+  ga.npeers = p->npeers;
+  ga.src_rank = p->src_rank;
+  ga.shard_rows = p->shard_rows > 0 ? p->shard_rows : 1;
   ga.err = err;
 
   const int64_t tiles = ((p->M + GBM - 1) / GBM) * ((p->N + GBN - 1) / GBN);
@@ -372,6 +444,7 @@ int gemm_bf16(const wanb200_gemm_params* p, cudaStream_t st) {
     case WANB200_EPI_BIAS_GELU: return launch_gemm<WANB200_EPI_BIAS_GELU>(ta, tb, ga, grid, st);
     case WANB200_EPI_BIAS_GATE_RES: return launch_gemm<WANB200_EPI_BIAS_GATE_RES>(ta, tb, ga, grid, st);
     case WANB200_EPI_BIAS_RES: return launch_gemm<WANB200_EPI_BIAS_RES>(ta, tb, ga, grid, st);
+    case WANB200_EPI_SCATTER: return launch_gemm<WANB200_EPI_SCATTER>(ta, tb, ga, grid, st);
     default: return launch_gemm<WANB200_EPI_BIAS_SUMSQ>(ta, tb, ga, grid, st);
   }
 }

@@ -15,7 +15,8 @@ LIB_PATH = os.path.join(_HERE, "libwanb200.so")
 c_void_p, c_int64, c_int, c_float = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float
 c_float_p = ctypes.POINTER(ctypes.c_float)
 
-EPI_NONE, EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_GATE_RES, EPI_BIAS_RES, EPI_BIAS_SUMSQ = range(6)
+EPI_NONE, EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_GATE_RES, EPI_BIAS_RES, EPI_BIAS_SUMSQ, EPI_SCATTER = range(7)
+MAX_PEERS = 8
 LN_MODULATE, LN_AFFINE = 0, 1
 
 
@@ -25,7 +26,8 @@ class GemmParams(ctypes.Structure):
                 ("bias", c_void_p), ("residual", c_void_p), ("ldr", c_int64), ("gate_mod", c_void_p),
                 ("gate_e0", c_void_p), ("gate_frame_stride", c_int64), ("seq_len", c_int64),
                 ("tokens_per_frame", c_int64), ("row_offset", c_int64), ("rowss", c_void_p), ("ss_section", c_int64),
-                ("ss_nsections", c_int)]
+                ("ss_nsections", c_int), ("peer_out", c_void_p * 8), ("npeers", c_int), ("src_rank", c_int),
+                ("shard_rows", c_int64)]
 
 
 class AttnParams(ctypes.Structure):
@@ -42,7 +44,8 @@ class LnParams(ctypes.Structure):
                 ("mode", c_int), ("modulation", c_void_p), ("e0", c_void_p), ("e0_frame_stride", c_int64),
                 ("shift_idx", c_int), ("scale_idx", c_int), ("seq_len", c_int64), ("tokens_per_frame", c_int64),
                 ("row_offset", c_int64),
-                ("weight", c_void_p), ("bias", c_void_p), ("zero_buf", c_void_p), ("zero_count", c_int64)]
+                ("weight", c_void_p), ("bias", c_void_p), ("zero_buf", c_void_p), ("zero_count", c_int64),
+                ("push_out", c_void_p * 8), ("npush", c_int), ("push_row0", c_int64)]
 
 
 class QkNormParams(ctypes.Structure):
@@ -55,12 +58,13 @@ class QkNormParams(ctypes.Structure):
 class ResidualParams(ctypes.Structure):
     _fields_ = [("out", c_void_p), ("residual", c_void_p), ("y", c_void_p), ("rows", c_int64), ("dim", c_int64),
                 ("bias", c_void_p), ("gate_mod", c_void_p), ("gate_e0", c_void_p), ("gate_frame_stride", c_int64),
-                ("seq_len", c_int64), ("tokens_per_frame", c_int64), ("row_offset", c_int64)]
+                ("seq_len", c_int64), ("tokens_per_frame", c_int64), ("row_offset", c_int64), ("nsum", c_int),
+                ("y_slice_stride", c_int64)]
 
 
 EXPORTS = ("wanb200_gemm_bf16", "wanb200_attn_fwd", "wanb200_layernorm", "wanb200_qk_norm_rope",
            "wanb200_bias_gate_residual", "wanb200_last_error", "wanb200_device_error", "wanb200_version",
-           "wanb200_struct_sizes")
+           "wanb200_struct_sizes", "wanb200_peer_barrier")
 
 _lock = threading.Lock()
 _lib = None
@@ -96,6 +100,8 @@ def load():
             lib.wanb200_version.restype = c_int
             lib.wanb200_struct_sizes.argtypes = [ctypes.POINTER(c_int64), c_int]
             lib.wanb200_struct_sizes.restype = c_int
+            lib.wanb200_peer_barrier.argtypes = [ctypes.POINTER(c_void_p), c_int, c_int, c_int, c_void_p]
+            lib.wanb200_peer_barrier.restype = c_int
             sizes = (c_int64 * 5)()
             lib.wanb200_struct_sizes(sizes, 5)
             want = [ctypes.sizeof(c) for c in (GemmParams, AttnParams, LnParams, QkNormParams, ResidualParams)]

@@ -228,10 +228,36 @@ class FastBlockSP:
     reference's one-hot matmul.
     """
 
-    def __init__(self, weights: BlockWeights, seq_len: int, num_frames: int, tp_group, eps: float = 1e-6):
+    def __init__(self, weights: BlockWeights, seq_len: int, num_frames: int, tp_group, eps: float = 1e-6,
+                 comm=None):
+        """comm: a wanb200.comm.PeerComm of the group to run the all-gathers / reduce-scatters
+        fused into the LayerNorm and GEMM kernels over NVLink peer memory; None = NCCL."""
         assert weights.local_cross, "the sequence-parallel block needs BlockWeights(local_cross=True)"
         self.w, self.L, self.num_frames, self.tp_group, self.eps = weights, seq_len, num_frames, tp_group, eps
         self.T, self.rank = weights.tp_size, weights.tp_rank
+        self.comm = comm
+
+    def _ln_gather(self, xs, mod, e0, shift, scale, frames, ws, zero=None):
+        """LN + modulation of the shard, all-gathered to [T*S, C]; returns the gathered buffer."""
+        if self.comm is not None:
+            ops.layernorm_modulate(xs, mod, e0, shift, scale, frames, out=None, eps=self.eps, zero=zero,
+                                   push=self.comm.push)
+            self.comm.barrier()
+            return self.comm.hf
+        ops.layernorm_modulate(xs, mod, e0, shift, scale, frames, out=ws.h_s, eps=self.eps, zero=zero)
+        dist.all_gather_into_tensor(ws.hf, ws.h_s, group=self.tp_group)
+        return ws.hf
+
+    def _rowpar_residual(self, a, wmat, bias, residual, gate, frames, out, ws, kind):
+        """out = residual + (reduce_scatter(a @ wmat^T) + bias) * gate (row-parallel projection)."""
+        if self.comm is not None:
+            ops.linear(a, wmat, None, epilogue=L.EPI_SCATTER, scatter=self.comm.scatter, kind=kind)
+            self.comm.barrier()
+            return ops.bias_gate_residual(residual, self.comm.inbox, bias, gate=gate, frames=frames, out=out,
+                                          nsum=self.T)
+        ops.linear(a, wmat, None, epilogue=L.EPI_NONE, out=ws.part, kind=kind)
+        dist.reduce_scatter_tensor(ws.part_s, ws.part, group=self.tp_group)
+        return ops.bias_gate_residual(residual, ws.part_s, bias, gate=gate, frames=frames, out=out)
 
     def _ws(self, S, device):
         w = self.w
@@ -258,9 +284,8 @@ class FastBlockSP:
         mod = w.modulation
 
         # -- self-attention: LN on the shard, all-gather, column-parallel QKV on all tokens
-        ops.layernorm_modulate(xs, mod, e0, 0, 1, frames_s, out=ws.h_s, eps=self.eps, zero=ws.ss)
-        dist.all_gather_into_tensor(ws.hf, ws.h_s, group=g)
-        ops.linear(ws.hf, w.w_qkv, w.b_qkv, epilogue=L.EPI_BIAS_SUMSQ, out=ws.qkv, rowss=ws.ss,
+        hf = self._ln_gather(xs, mod, e0, 0, 1, frames_s, ws, zero=ws.ss)
+        ops.linear(hf, w.w_qkv, w.b_qkv, epilogue=L.EPI_BIAS_SUMSQ, out=ws.qkv, rowss=ws.ss,
                    ss_section=Cl, ss_nsections=2, kind="gemm_qkv")
         dist.all_reduce(ws.ss, group=g)
         ops.qk_norm_rope(ws.qkv, [(0, ws.ss[0], w.g_q), (Cl, ws.ss[1], w.g_k)], Cl, C, eps=self.eps,
@@ -269,10 +294,8 @@ class FastBlockSP:
         k = ws.qkv[:N, Cl:2 * Cl].view(1, Lx, nl, 128)
         v = ws.qkv[:N, 2 * Cl:].view(1, Lx, nl, 128)
         ops.attention(q, k, v, out=ws.y[:N].view(1, Lx, nl, 128), kind="attn_self")
-        ops.linear(ws.y, w.w_o, None, epilogue=L.EPI_NONE, out=ws.part, kind="gemm_o")
-        dist.reduce_scatter_tensor(ws.part_s, ws.part, group=g)
         x1 = torch.empty_like(xs)
-        ops.bias_gate_residual(xs, ws.part_s, w.b_o, gate=(mod[2], e0[:, 2, :]), frames=frames_s, out=x1)
+        self._rowpar_residual(ws.y, w.w_o, w.b_o, xs, (mod[2], e0[:, 2, :]), frames_s, x1, ws, "gemm_o")
 
         # -- cross-attention on the shard, all heads, no collective
         ops.layernorm_affine(x1, w.ln3_w, w.ln3_b, out=ws.h_s, eps=self.eps, zero=ws.ssc)
@@ -284,12 +307,9 @@ class FastBlockSP:
         ops.linear(ws.yc, w.w_co, w.b_co, epilogue=L.EPI_BIAS_RES, out=x1, residual=x1, kind="gemm_cross_o")
 
         # -- FFN: LN on the shard, all-gather, column/row-parallel GEMMs, reduce-scatter
-        ops.layernorm_modulate(x1, mod, e0, 3, 4, frames_s, out=ws.h_s, eps=self.eps)
-        dist.all_gather_into_tensor(ws.hf, ws.h_s, group=g)
-        ops.linear(ws.hf, w.w1, w.b1, epilogue=L.EPI_BIAS_GELU, out=ws.f, kind="gemm_ffn_up")
-        ops.linear(ws.f, w.w2, None, epilogue=L.EPI_NONE, out=ws.part, kind="gemm_ffn_down")
-        dist.reduce_scatter_tensor(ws.part_s, ws.part, group=g)
-        ops.bias_gate_residual(x1, ws.part_s, w.b2, gate=(mod[5], e0[:, 5, :]), frames=frames_s, out=x1)
+        hf = self._ln_gather(x1, mod, e0, 3, 4, frames_s, ws)
+        ops.linear(hf, w.w1, w.b1, epilogue=L.EPI_BIAS_GELU, out=ws.f, kind="gemm_ffn_up")
+        self._rowpar_residual(ws.f, w.w2, w.b2, x1, (mod[5], e0[:, 5, :]), frames_s, x1, ws, "gemm_ffn_down")
         return x1
 
     __call__ = forward

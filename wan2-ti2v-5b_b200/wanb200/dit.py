@@ -74,10 +74,12 @@ def _spec_and_state(model):
 
 class FastWanDiT:
     def __init__(self, model, grid, guide_scale, device, cfg_group=None, pair_group=None, tp_group=None,
-                 num_layers=None, seq_parallel=None):
+                 num_layers=None, seq_parallel=None, comm="peer"):
         """seq_parallel: token-sharded residual inside the TP group with local all-head
         cross-attention (`_FastBlockSP`, fast_dit.py:314-389); default on for CFG-parallel with
-        TP > 1 (batch 1), the reference's best layout."""
+        TP > 1 (batch 1), the reference's best layout.  comm: how the sequence-parallel block
+        all-gathers / reduce-scatters: "peer" = fused into the LayerNorm / GEMM kernels over NVLink
+        peer memory (wanb200.comm), "nccl" = torch.distributed collectives."""
         spec, sd = _spec_and_state(model)
         self.spec = spec
         self.grid = tuple(int(g) for g in grid)
@@ -108,8 +110,15 @@ class FastWanDiT:
         self.sp = seq_parallel
         self.block_weights = [BlockWeights(block_state(sd, i), spec.num_heads, self.device, rank, tp,
                                            local_cross=seq_parallel) for i in range(nl)]
+        self.comm = None
         if seq_parallel:
-            self.blocks = [FastBlockSP(w, self.seq_len, self.num_frames, tp_group, spec.eps)
+            if comm == "peer":
+                from .comm import PeerComm
+                S = -(-self.batch * self.seq_len // tp)
+                self.comm = PeerComm(tp_group, S, spec.dim, self.device)
+            elif comm != "nccl":
+                raise ValueError("comm must be 'peer' or 'nccl'")
+            self.blocks = [FastBlockSP(w, self.seq_len, self.num_frames, tp_group, spec.eps, comm=self.comm)
                            for w in self.block_weights]
         else:
             self.blocks = [FastBlock(w, self.num_frames, tp_group, spec.eps) for w in self.block_weights]

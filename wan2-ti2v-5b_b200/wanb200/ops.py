@@ -99,7 +99,7 @@ def _rows(t: torch.Tensor, name: str):
 
 # ---------------------------------------------------------------------------- GEMM
 def linear(a, w, bias=None, *, epilogue=L.EPI_BIAS, out=None, residual=None, gate=None, frames=None,
-           rowss=None, ss_section=0, ss_nsections=0, kind="gemm"):
+           rowss=None, ss_section=0, ss_nsections=0, kind="gemm", scatter=None):
     """out[M, N] = epilogue(a[M, K] @ w[N, K]^T) on tcgen05 (see include/wanb200.h).
 
     gate: (gate_mod [N] bf16, gate_e0 [F, N] fp32 view with unit column stride) for EPI_BIAS_GATE_RES.
@@ -112,9 +112,9 @@ def linear(a, w, bias=None, *, epilogue=L.EPI_BIAS, out=None, residual=None, gat
     M, K = a.shape
     N = w.shape[0]
     _need(w.shape[1] == K, f"linear: a is [*, {K}] but w is {tuple(w.shape)}")
-    if out is None:
+    if out is None and scatter is None:
         out = torch.empty(M, N, dtype=BF16, device=a.device)
-    ldd = _rows(out, "out")
+    ldd = _rows(out, "out") if out is not None else N  # scatter: rows land in the peers' inboxes
     p = L.GemmParams()
     p.a, p.lda, p.w, p.ldw, p.d, p.ldd = _p(a), lda, _p(w), ldw, _p(out), ldd
     p.M, p.N, p.K, p.epilogue = M, N, K, epilogue
@@ -130,6 +130,12 @@ def linear(a, w, bias=None, *, epilogue=L.EPI_BIAS, out=None, residual=None, gat
     if rowss is not None:
         _need(rowss.dtype == torch.float32, "linear: rowss must be fp32")
         p.rowss, p.ss_section, p.ss_nsections = _p(rowss), ss_section, ss_nsections
+    if scatter is not None:  # (peer inbox pointers, this rank, rows per shard)
+        ptrs, src, shard_rows = scatter
+        _need(epilogue == L.EPI_SCATTER and 1 <= len(ptrs) <= L.MAX_PEERS, "linear: bad scatter")
+        for i, q in enumerate(ptrs):
+            p.peer_out[i] = q
+        p.npeers, p.src_rank, p.shard_rows = len(ptrs), src, shard_rows
     lib = L.load()
     L.check(_launch(a, kind, 2.0 * M * N * K, lambda: lib.wanb200_gemm_bf16(ctypes.byref(p), _stream(a))),
             "wanb200_gemm_bf16")
@@ -162,15 +168,27 @@ def attention(q, k, v, out=None, softmax_scale=None, kind="attn"):
 
 
 # ---------------------------------------------------------------------------- norms
-def layernorm_modulate(x, modulation, e0, shift_idx, scale_idx, frames, out=None, eps=1e-6, zero=None):
+def _set_push(p, push):
+    """push = (peer buffer pointers, first row): also store the output rows into every peer buffer
+    at rows first_row.. (the all-gather fused into the norm)."""
+    if push is not None:
+        ptrs, row0 = push
+        _need(1 <= len(ptrs) <= L.MAX_PEERS, "layernorm: bad push")
+        for i, q in enumerate(ptrs):
+            p.push_out[i] = q
+        p.npush, p.push_row0 = len(ptrs), row0
+
+
+def layernorm_modulate(x, modulation, e0, shift_idx, scale_idx, frames, out=None, eps=1e-6, zero=None, push=None):
     """LN(x) * (1 + scale[f]) + shift[f]; modulation [6, C] bf16, e0 [F, 6, C] fp32."""
     _cuda(x, modulation, e0, out, zero)
     _need(x.dtype == BF16 and x.is_contiguous() and x.dim() == 2, "layernorm: x must be contiguous bf16 [M, C]")
     _need(e0.dtype == torch.float32 and e0.is_contiguous() and modulation.dtype == BF16, "layernorm: bad mod tensors")
     M, C = x.shape
-    if out is None:
+    if out is None and push is None:
         out = torch.empty_like(x)
     p = L.LnParams()
+    _set_push(p, push)
     p.x, p.out, p.rows, p.dim, p.eps, p.mode = _p(x), _p(out), M, C, eps, L.LN_MODULATE
     p.modulation, p.e0, p.e0_frame_stride = _p(modulation), _p(e0), 6 * C
     p.shift_idx, p.scale_idx = shift_idx, scale_idx
@@ -222,15 +240,19 @@ def qk_norm_rope(x, sections, width, global_dim, eps=1e-6, cos=None, sin=None, s
     return x
 
 
-def bias_gate_residual(residual, y, bias, gate=None, frames=None, out=None):
-    """out = residual + (y + bias) * gate[f]  (or residual + y + bias without gate)."""
+def bias_gate_residual(residual, y, bias, gate=None, frames=None, out=None, nsum=1):
+    """out = residual + (y + bias) * gate[f]  (or residual + y + bias without gate).
+    nsum > 1: y is [nsum * M, C] (the inbox of a fused reduce-scatter) and its nsum slices of M
+    rows are summed first."""
     _cuda(residual, y, bias, out)
-    _need(residual.is_contiguous() and y.is_contiguous() and residual.shape == y.shape, "bias_gate_residual: layout")
     M, C = residual.shape
+    _need(residual.is_contiguous() and y.is_contiguous() and tuple(y.shape) == (nsum * M, C),
+          "bias_gate_residual: layout")
     if out is None:
         out = torch.empty_like(residual)
     p = L.ResidualParams()
     p.out, p.residual, p.y, p.rows, p.dim, p.bias = _p(out), _p(residual), _p(y), M, C, _p(bias)
+    p.nsum, p.y_slice_stride = nsum, M * C
     if gate is not None:
         gm, ge = gate
         p.gate_mod, p.gate_e0, p.gate_frame_stride = _p(gm), _p(ge), ge.stride(0)
@@ -240,6 +262,14 @@ def bias_gate_residual(residual, y, bias, gate=None, frames=None, out=None):
                     lambda: lib.wanb200_bias_gate_residual(ctypes.byref(p), _stream(residual))),
             "wanb200_bias_gate_residual")
     return out
+
+
+def peer_barrier(flag_ptrs, rank, epoch, device):
+    """Barrier of the TP group over NVLink peer memory (include/wanb200.h, wanb200_peer_barrier)."""
+    arr = (ctypes.c_void_p * len(flag_ptrs))(*flag_ptrs)
+    lib = L.load()
+    st = torch.cuda.current_stream(device).cuda_stream
+    L.check(lib.wanb200_peer_barrier(arr, rank, len(flag_ptrs), epoch, st), "wanb200_peer_barrier")
 
 
 # ---------------------------------------------------------------------------- torch.library ops
