@@ -93,9 +93,16 @@ typedef struct wanb200_attn_params {
   void* o; int64_t o_tok_stride, o_batch_stride;
   int64_t batch, heads, q_len, kv_len, head_dim;
   float softmax_scale;
+  /* split-KV (flash-decoding style) for grids that fill the SMs in few waves: kv_splits CTAs
+   * per query tile each take a contiguous range of key tiles and write unnormalised partials
+   * (workspace, wanb200_attn_workspace_bytes() bytes) that a merge kernel combines.  0 or 1 =
+   * no split; wanb200_attn_kv_splits() gives the split count the library would pick. */
+  int kv_splits; void* workspace; int64_t workspace_bytes;
 } wanb200_attn_params;
 
 int wanb200_attn_fwd(const wanb200_attn_params* p, void* stream);
+int64_t wanb200_attn_workspace_bytes(int64_t batch, int64_t heads, int64_t q_len, int kv_splits);
+int wanb200_attn_kv_splits(int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len);
 
 /* ---------------------------------------------------------------- LayerNorm (+ modulation)
  * mode WANB200_LN_MODULATE: out = LN(x) * (1 + scale[frame]) + shift[frame]

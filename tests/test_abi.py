@@ -16,7 +16,7 @@ HEADER = os.path.join(ROOT, "include", "wanb200.h")
 
 def header_functions():
     src = open(HEADER).read()
-    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(wanb200_\w+)\s*\(", src, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int64_t|int|const char\*)\s+(wanb200_\w+)\s*\(", src, re.M)))
 
 
 def test_library_exports_every_declared_function():

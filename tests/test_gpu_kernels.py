@@ -112,6 +112,26 @@ def test_attention_vs_sdpa(B, H, Lq, Lk):
     assert rel(o, sdpa_ref(q, k, v)) < 1e-2
 
 
+@pytest.mark.parametrize("B,H,Lq,Lk,splits", [(1, 6, 1000, 7854, 3), (2, 3, 300, 1080, 2), (1, 2, 200, 77, 1),
+                                              (1, 4, 257, 513, 3), (2, 2, 128, 1100, 3)])
+def test_attention_split_kv(B, H, Lq, Lk, splits):
+    """Split-KV: each CTA covers a contiguous range of key tiles, writes unnormalised partials,
+    and the merge kernel combines them (ragged last split included)."""
+    q, k, v = randn(B, Lq, H, 128, seed=41), randn(B, Lk, H, 128, seed=42), randn(B, Lk, H, 128, seed=43)
+    o = ops.attention(q, k, v, kv_splits=splits)
+    ref = sdpa_ref(q, k, v)
+    assert rel(o, ref) < 1e-2
+    o1 = ops.attention(q, k, v, kv_splits=1)
+    assert rel(o, o1.float()) < 1e-2
+
+
+def test_attention_split_kv_rejects_empty_split():
+    q = randn(1, 128, 1, 128, seed=44)
+    k = randn(1, 300, 1, 128, seed=45)  # 3 key tiles
+    with pytest.raises(L.WanB200Error, match="kv_splits"):
+        ops.attention(q, k, k, kv_splits=4)
+
+
 def test_attention_fused_qkv_layout_and_scaled_scores():
     """q, k, v as column slices of one [B*L, 3*H*128] buffer (the QKV GEMM output); RMS-normed
     inputs with a gain of 3 so the scores are large (softmax far from uniform)."""

@@ -126,6 +126,14 @@ int wanb200_attn_fwd(const wanb200_attn_params* p, void* stream) {
   return attn_fwd(p, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int64_t wanb200_attn_workspace_bytes(int64_t batch, int64_t heads, int64_t q_len, int kv_splits) {
+  return attn_workspace_bytes(batch, heads, q_len, kv_splits);
+}
+
+int wanb200_attn_kv_splits(int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len) {
+  return attn_kv_splits(batch, heads, q_len, kv_len);
+}
+
 int wanb200_layernorm(const wanb200_ln_params* p, void* stream) {
   return layernorm(p, reinterpret_cast<cudaStream_t>(stream));
 }

@@ -45,8 +45,15 @@ constexpr float A_RESCALE_THRESHOLD = 8.0f;  // log2 units
 struct AttnArgs {
   __nv_bfloat16* o;
   int64_t o_tok_stride, o_batch_stride;
-  int Lq, Lk;
+  int Lq, Lk, heads;
   float scale_log2;
+  // split-KV: CTA blockIdx.x = q_pair * kv_splits + split covers key tiles
+  // [split * kv_tiles_per_split, ...); with kv_splits > 1 it writes its unnormalised O and
+  // (running max, row sum) to o_part / ml_part and attn_combine_kernel merges the splits.
+  int kv_splits, kv_tiles_per_split;
+  float* o_part;   // [kv_splits, B*H*Lq, 128]
+  float* ml_part;  // [kv_splits, B*H*Lq, 2]
+  int64_t part_rows;  // B*H*Lq
   int* err;
 };
 
@@ -71,8 +78,10 @@ __global__ void __launch_bounds__(A_THREADS, 1)
   int* err = args.err;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int q0 = blockIdx.x * 2 * ABM, h = blockIdx.y, b = blockIdx.z;
-  const int nkv = (args.Lk + ABN - 1) / ABN;
+  const int split = blockIdx.x % args.kv_splits;
+  const int q0 = (blockIdx.x / args.kv_splits) * 2 * ABM, h = blockIdx.y, b = blockIdx.z;
+  const int kv0 = split * args.kv_tiles_per_split;  // first key tile of this CTA
+  const int nkv = min((args.Lk + ABN - 1) / ABN - kv0, args.kv_tiles_per_split);  // >= 1 (host)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -123,8 +132,8 @@ __global__ void __launch_bounds__(A_THREADS, 1)
         const void* map = (i & 1) ? static_cast<const void*>(&tmV) : static_cast<const void*>(&tmK);
         const uint32_t dst = sbase + A_OFF_R + slot * A_TILE;
         mbar_expect_tx(kv_full + 8 * slot, A_TILE);
-        tma_load_4d(dst, map, kv_full + 8 * slot, 0, h, (i >> 1) * ABN, b);
-        tma_load_4d(dst + A_BLK, map, kv_full + 8 * slot, 64, h, (i >> 1) * ABN, b);
+        tma_load_4d(dst, map, kv_full + 8 * slot, 0, h, (kv0 + (i >> 1)) * ABN, b);
+        tma_load_4d(dst + A_BLK, map, kv_full + 8 * slot, 64, h, (kv0 + (i >> 1)) * ABN, b);
         issued |= 1u << slot;
         last_ph = (last_ph & ~(1u << slot)) | (ph << slot);
       }
@@ -214,7 +223,7 @@ __global__ void __launch_bounds__(A_THREADS, 1)
       for (int c = 0; c < ABN / 32; ++c) tmem_ld32_nowait(t_s + c * 32, sr + c * 32);
       tmem_wait_ld();
       float* s = reinterpret_cast<float*>(sr);
-      const int kbase = j * ABN;
+      const int kbase = (kv0 + j) * ABN;
       if (kbase + ABN > args.Lk) {  // CTA-uniform: mask the key tail
 #pragma unroll
         for (int k = 0; k < ABN; ++k)
@@ -272,7 +281,23 @@ __global__ void __launch_bounds__(A_THREADS, 1)
       if (lane == 0) mbar_arrive(p_full + 8 * t);
     }
     if (ok) ok = mbar_wait_warp(o_done + 8 * t, 0, abort_flag, err, kErrTimeoutAttnSoftmax);
-    if (ok) {
+    if (ok && args.kv_splits > 1) {
+      // partial result of this key range: unnormalised O, running max (log2 units), row sum
+      tc_fence_after();
+      const int qrow = q0 + t * ABM + r;
+      const int64_t prow = (int64_t)split * args.part_rows + ((int64_t)b * args.heads + h) * args.Lq + qrow;
+      float4* dst = reinterpret_cast<float4*>(args.o_part + prow * AD);
+#pragma unroll
+      for (int c = 0; c < AD / 32; ++c) {
+        float o[32];
+        tmem_ld32(t_o + c * 32, o);
+        if (qrow < args.Lq) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) dst[c * 8 + q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+        }
+      }
+      if (qrow < args.Lq) *reinterpret_cast<float2*>(args.ml_part + prow * 2) = make_float2(m_used, l_run);
+    } else if (ok) {
       tc_fence_after();
       const int qrow = q0 + t * ABM + r;
       const float inv_l = 1.f / l_run;
@@ -303,7 +328,42 @@ __global__ void __launch_bounds__(A_THREADS, 1)
   if (warp == 9) tmem_dealloc(tmem_base, A_TMEM_COLS);
 }
 
+// Merge of the split-KV partials: one warp per (batch, head, query row), lane l owns head
+// dimensions 4l..4l+3.  O = sum_s 2^(m_s - m) O_s / sum_s 2^(m_s - m) l_s with m = max_s m_s.
+__global__ void __launch_bounds__(256) attn_combine_kernel(const AttnArgs a) {
+  const int64_t w = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (w >= a.part_rows) return;
+  const int q = (int)(w % a.Lq);
+  const int64_t bh = w / a.Lq;
+  const int h = (int)(bh % a.heads), b = (int)(bh / a.heads);
+  float m = -INFINITY;
+  for (int s = 0; s < a.kv_splits; ++s) m = fmaxf(m, a.ml_part[(s * a.part_rows + w) * 2]);
+  float l = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s = 0; s < a.kv_splits; ++s) {
+    const float2 ml = *reinterpret_cast<const float2*>(a.ml_part + (s * a.part_rows + w) * 2);
+    const float wgt = ex2_approx(ml.x - m);
+    l = fmaf(wgt, ml.y, l);
+    const float4 o = reinterpret_cast<const float4*>(a.o_part + (s * a.part_rows + w) * AD)[lane];
+    acc.x = fmaf(wgt, o.x, acc.x);
+    acc.y = fmaf(wgt, o.y, acc.y);
+    acc.z = fmaf(wgt, o.z, acc.z);
+    acc.w = fmaf(wgt, o.w, acc.w);
+  }
+  const float inv = 1.f / l;
+  uint2 u;
+  u.x = pack_bf16x2(acc.x * inv, acc.y * inv);
+  u.y = pack_bf16x2(acc.z * inv, acc.w * inv);
+  *reinterpret_cast<uint2*>(a.o + (int64_t)b * a.o_batch_stride + (int64_t)q * a.o_tok_stride + (int64_t)h * AD +
+                            lane * 4) = u;
+}
+
 // ------------------------------------------------------------------ host launcher
+int64_t attn_workspace_bytes(int64_t batch, int64_t heads, int64_t q_len, int kv_splits) {
+  return kv_splits > 1 ? (int64_t)kv_splits * batch * heads * q_len * (AD + 2) * 4 : 0;
+}
+
 int attn_fwd(const wanb200_attn_params* p, cudaStream_t st) {
   if (!p) return set_error(WANB200_EINVAL, "attn: null params");
   if (!p->q || !p->k || !p->v || !p->o) return set_error(WANB200_EINVAL, "attn: null q/k/v/o");
@@ -324,8 +384,23 @@ int attn_fwd(const wanb200_attn_params* p, cudaStream_t st) {
     return set_error(WANB200_EINVAL, "attn: q/k/v/o must be 16-byte aligned");
   if (!(p->softmax_scale > 0.f)) return set_error(WANB200_EINVAL, "attn: softmax_scale must be positive");
 
+  wanb200_attn_params pp = *p;  // kv_splits 0 means 1 (no split)
+  if (pp.kv_splits == 0) pp.kv_splits = 1;
+  p = &pp;
+  if (p->kv_splits < 1 || p->kv_splits > 64) return set_error(WANB200_EINVAL, "attn: kv_splits must be 0..64");
+  const int nkv = (int)((p->kv_len + ABN - 1) / ABN);
+  const int per = (nkv + p->kv_splits - 1) / p->kv_splits;
+  if ((int64_t)(p->kv_splits - 1) * per >= nkv)
+    return set_error(WANB200_EINVAL, "attn: kv_splits leaves a split without key tiles (use attn_kv_splits)");
+  const int64_t need = attn_workspace_bytes(p->batch, p->heads, p->q_len, p->kv_splits);
+  if (need > 0 && (!p->workspace || !aligned16(p->workspace) || p->workspace_bytes < need))
+    return set_error(WANB200_EINVAL, "attn: kv_splits > 1 needs a 16-byte aligned workspace of wanb200_attn_workspace_bytes()");
   int* err = device_error_word();
   if (!err) return WANB200_ECUDA;
+  return attn_launch(p, err, st);
+}
+
+int attn_launch(const wanb200_attn_params* p, int* err, cudaStream_t st) {
   CUtensorMap tq, tk, tv;
   const int box[4] = {64, 1, ABM, 1};
   {
@@ -349,7 +424,13 @@ int attn_fwd(const wanb200_attn_params* p, cudaStream_t st) {
   aa.o_batch_stride = p->o_batch_stride;
   aa.Lq = (int)p->q_len;
   aa.Lk = (int)p->kv_len;
+  aa.heads = (int)p->heads;
   aa.scale_log2 = p->softmax_scale * 1.4426950408889634f;
+  aa.kv_splits = p->kv_splits;
+  aa.kv_tiles_per_split = (int)(((p->kv_len + ABN - 1) / ABN + p->kv_splits - 1) / p->kv_splits);
+  aa.part_rows = p->batch * p->heads * p->q_len;
+  aa.o_part = reinterpret_cast<float*>(p->workspace);
+  aa.ml_part = aa.o_part ? aa.o_part + (int64_t)p->kv_splits * aa.part_rows * AD : nullptr;
   aa.err = err;
 
   static bool attr_set[kMaxDevices] = {};
@@ -360,11 +441,41 @@ int attn_fwd(const wanb200_attn_params* p, cudaStream_t st) {
     if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(attn)", e);
     attr_set[dev] = true;
   }
-  dim3 grid((unsigned)((p->q_len + 2 * ABM - 1) / (2 * ABM)), (unsigned)p->heads, (unsigned)p->batch);
+  const int64_t gx = ((p->q_len + 2 * ABM - 1) / (2 * ABM)) * p->kv_splits;
+  if (gx > INT32_MAX) return set_error(WANB200_EINVAL, "attn: grid too large");
+  dim3 grid((unsigned)gx, (unsigned)p->heads, (unsigned)p->batch);
   attn_fwd_kernel<<<grid, A_THREADS, A_SMEM_BYTES, st>>>(tq, tk, tv, aa);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error("attn_fwd_kernel launch", e);
+  if (p->kv_splits > 1) {
+    attn_combine_kernel<<<(unsigned)((aa.part_rows + 7) / 8), 256, 0, st>>>(aa);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return set_cuda_error("attn_combine_kernel launch", e);
+  }
   return WANB200_OK;
 }
+
+int attn_kv_splits(int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len) {
+  // Wave-quantisation model: a CTA with all key tiles costs 1, a split one 1/s + 0.04 (its
+  // prologue / epilogue), the merge pass is ignored.  Pick s in 1..4 with the smallest
+  // makespan ceil(units*s / SMs) * cost(s); s is capped so that no split is empty.
+  const int64_t units = ((q_len + 2 * ABM - 1) / (2 * ABM)) * heads * batch;
+  const int nkv = (int)((kv_len + ABN - 1) / ABN);
+  const int sms = num_sms();
+  int best = 1;
+  double best_t = 1e300;
+  for (int s = 1; s <= 4; ++s) {
+    const int per = (nkv + s - 1) / s;
+    if ((int64_t)(s - 1) * per >= nkv) break;
+    const double waves = (double)((units * s + sms - 1) / sms);
+    const double t = waves * (1.0 / s + (s > 1 ? 0.04 : 0.0));
+    if (t < best_t - 1e-9) {
+      best_t = t;
+      best = s;
+    }
+  }
+  return best;
+}
+
 
 }  // namespace wanb200

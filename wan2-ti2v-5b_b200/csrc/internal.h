@@ -35,6 +35,9 @@ int make_tmap_4d(CUtensorMap* m, const void* base, const int64_t dims[4], const 
 // Launchers (one per public entry point).
 int gemm_bf16(const wanb200_gemm_params* p, cudaStream_t st);
 int attn_fwd(const wanb200_attn_params* p, cudaStream_t st);
+int attn_launch(const wanb200_attn_params* p, int* err, cudaStream_t st);  // validated params
+int64_t attn_workspace_bytes(int64_t batch, int64_t heads, int64_t q_len, int kv_splits);
+int attn_kv_splits(int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len);
 int layernorm(const wanb200_ln_params* p, cudaStream_t st);
 int qk_norm_rope(const wanb200_qknorm_params* p, cudaStream_t st);
 int bias_gate_residual(const wanb200_residual_params* p, cudaStream_t st);

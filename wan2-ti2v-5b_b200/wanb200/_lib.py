@@ -36,7 +36,8 @@ class AttnParams(ctypes.Structure):
                 ("v", c_void_p), ("v_tok_stride", c_int64), ("v_batch_stride", c_int64),
                 ("o", c_void_p), ("o_tok_stride", c_int64), ("o_batch_stride", c_int64),
                 ("batch", c_int64), ("heads", c_int64), ("q_len", c_int64), ("kv_len", c_int64),
-                ("head_dim", c_int64), ("softmax_scale", c_float)]
+                ("head_dim", c_int64), ("softmax_scale", c_float), ("kv_splits", c_int), ("workspace", c_void_p),
+                ("workspace_bytes", c_int64)]
 
 
 class LnParams(ctypes.Structure):
@@ -64,7 +65,8 @@ class ResidualParams(ctypes.Structure):
 
 EXPORTS = ("wanb200_gemm_bf16", "wanb200_attn_fwd", "wanb200_layernorm", "wanb200_qk_norm_rope",
            "wanb200_bias_gate_residual", "wanb200_last_error", "wanb200_device_error", "wanb200_version",
-           "wanb200_struct_sizes", "wanb200_peer_barrier")
+           "wanb200_struct_sizes", "wanb200_peer_barrier", "wanb200_attn_workspace_bytes",
+           "wanb200_attn_kv_splits")
 
 _lock = threading.Lock()
 _lib = None
@@ -102,6 +104,10 @@ def load():
             lib.wanb200_struct_sizes.restype = c_int
             lib.wanb200_peer_barrier.argtypes = [ctypes.POINTER(c_void_p), c_int, c_int, c_int, c_void_p]
             lib.wanb200_peer_barrier.restype = c_int
+            lib.wanb200_attn_workspace_bytes.argtypes = [c_int64, c_int64, c_int64, c_int]
+            lib.wanb200_attn_workspace_bytes.restype = c_int64
+            lib.wanb200_attn_kv_splits.argtypes = [c_int64, c_int64, c_int64, c_int64]
+            lib.wanb200_attn_kv_splits.restype = c_int
             sizes = (c_int64 * 5)()
             lib.wanb200_struct_sizes(sizes, 5)
             want = [ctypes.sizeof(c) for c in (GemmParams, AttnParams, LnParams, QkNormParams, ResidualParams)]

@@ -143,8 +143,22 @@ def linear(a, w, bias=None, *, epilogue=L.EPI_BIAS, out=None, residual=None, gat
 
 
 # ---------------------------------------------------------------------------- attention
-def attention(q, k, v, out=None, softmax_scale=None, kind="attn"):
-    """o = softmax(q k^T * scale) v on [B, L, H, 128] tensors (head stride 128, unit d stride)."""
+_WORKSPACES = {}
+
+
+def _workspace(device, nbytes):
+    """A per-device scratch buffer of at least nbytes (grown on demand, reused by every launch on
+    the stream; launches on one stream are ordered, so reuse is safe)."""
+    key = str(device)
+    ws = _WORKSPACES.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = _WORKSPACES[key] = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    return ws
+
+
+def attention(q, k, v, out=None, softmax_scale=None, kind="attn", kv_splits=None):
+    """o = softmax(q k^T * scale) v on [B, L, H, 128] tensors (head stride 128, unit d stride).
+    kv_splits: None = the library's choice for the grid size, 1 = no split."""
     _cuda(q, k, v, out)
     for name, t in (("q", q), ("k", k), ("v", v)):
         _need(t.dtype == BF16 and t.dim() == 4 and t.shape[-1] == 128 and t.stride(3) == 1 and t.stride(2) == 128,
@@ -162,6 +176,11 @@ def attention(q, k, v, out=None, softmax_scale=None, kind="attn"):
     p.batch, p.heads, p.q_len, p.kv_len, p.head_dim = B, H, Lq, k.shape[1], D
     p.softmax_scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(D)
     lib = L.load()
+    splits = kv_splits if kv_splits is not None else lib.wanb200_attn_kv_splits(B, H, Lq, k.shape[1])
+    p.kv_splits = splits
+    if splits > 1:
+        nbytes = lib.wanb200_attn_workspace_bytes(B, H, Lq, splits)
+        p.workspace, p.workspace_bytes = _workspace(q.device, nbytes).data_ptr(), nbytes
     flops = 4.0 * B * H * Lq * k.shape[1] * D
     L.check(_launch(q, kind, flops, lambda: lib.wanb200_attn_fwd(ctypes.byref(p), _stream(q))), "wanb200_attn_fwd")
     return out
