@@ -101,6 +101,20 @@ typedef struct wanb200_attn_params {
 } wanb200_attn_params;
 
 int wanb200_attn_fwd(const wanb200_attn_params* p, void* stream);
+/* Allocation-free variant of wanb200_attn_fwd (no counterpart in the reference, which has no C
+ * boundary).  For callers that cannot have a library allocate device memory: applications that
+ * give all GPU memory to their own pool or allocator (an allocation behind their back fails or
+ * escapes their accounting) and latency-critical loops that avoid cudaMalloc / cudaFree because
+ * those can block on the device.  It takes the same parameters (workspace ignored) and calls no
+ * allocating routine: the split-KV partials live in a fixed 16 MiB array inside the library,
+ * which every GPU that loads the library holds until the process exits.  Shapes whose partials
+ * need more (kv_splits * batch * heads * q_len * 520 bytes > 16 MiB) are rejected with
+ * WANB200_EINVAL; kv_splits 0 or 1 needs none.  The first call on a device resolves the array's
+ * device address (cudaGetSymbolAddress) with that device current; make that first call before
+ * any stream capture.  All calls on a device share the array: calls that overlap on the GPU
+ * (unordered streams) race.  Deadline expiries inside its kernels go to the error word read by
+ * wanb200_device_error() when another entry point has already created it on this device. */
+int wanb200_attn_fwd_noalloc(const wanb200_attn_params* p, void* stream);
 int64_t wanb200_attn_workspace_bytes(int64_t batch, int64_t heads, int64_t q_len, int kv_splits);
 int wanb200_attn_kv_splits(int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len);
 

@@ -53,6 +53,13 @@ int* device_error_word() {
   return g_err_word[dev];
 }
 
+int* device_error_word_if_present() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lk(g_mu);
+  return g_err_word[dev];
+}
+
 int num_sms() {
   int dev = 0;
   cudaGetDevice(&dev);
@@ -124,6 +131,10 @@ int wanb200_gemm_bf16(const wanb200_gemm_params* p, void* stream) {
 
 int wanb200_attn_fwd(const wanb200_attn_params* p, void* stream) {
   return attn_fwd(p, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int wanb200_attn_fwd_noalloc(const wanb200_attn_params* p, void* stream) {
+  return attn_fwd_noalloc(p, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int64_t wanb200_attn_workspace_bytes(int64_t batch, int64_t heads, int64_t q_len, int kv_splits) {

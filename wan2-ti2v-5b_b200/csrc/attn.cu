@@ -24,6 +24,8 @@
 // Warp roles (320 threads): warps 0-3 softmax of tile 0, warps 4-7 softmax of tile 1 (thread
 // row = TMEM lane), warp 8 TMA producer, warp 9 TMEM allocator + UMMA issuer.  K and V tiles
 // stream through one 3-slot ring (K_0, V_0, K_1, V_1, ...).
+#include <mutex>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -477,5 +479,99 @@ int attn_kv_splits(int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len) 
   return best;
 }
 
+
+}  // namespace wanb200
+
+namespace wanb200 {
+
+// ------------------------------------------------------------------ allocation-free variant
+// Some callers cannot let a library allocate device memory: applications that hand all GPU memory
+// to their own pool or allocator at start-up (an allocation behind their back either fails for
+// lack of memory or escapes their accounting), and latency-critical loops that must not pay for
+// cudaMalloc / cudaFree, which can block on the device.  wanb200_attn_fwd_noalloc serves them: it
+// keeps the split-KV partials in the fixed-size array below instead of a caller-provided or
+// library-allocated workspace, and calls no allocating routine.
+//
+// The array is part of the library image, so every GPU that loads the library holds it until the
+// process exits.  All calls on a device share it and it keeps the last call's contents; every
+// call overwrites the partials it reads, so nothing has to start at zero.  Calls that overlap on
+// the GPU (different streams, no ordering between them) race on the array.
+constexpr int64_t kNoAllocScratchBytes = int64_t(16) << 20;  // 16 MiB
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+// Deadline word for the kernels of this variant when the library's per-device error word (which
+// the other entry points allocate on first use) does not exist yet.
+static __device__ int g_noalloc_status;
+
+struct NoAllocDevice {
+  void* scratch = nullptr;
+  int* status = nullptr;
+};
+static NoAllocDevice g_noalloc_dev[kMaxDevices];
+static std::mutex g_noalloc_mu;
+
+// Device addresses of the file-scope arrays for the current device.  In host code the array names
+// only stand in for the symbols; the address a kernel may use comes from cudaGetSymbolAddress,
+// resolved once per device, with that device current, on the first call.
+static int noalloc_setup(NoAllocDevice* out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_cuda_error("cudaGetDevice", e);
+  if (dev < 0 || dev >= kMaxDevices) return set_error(WANB200_EINVAL, "device index out of range");
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  NoAllocDevice& d = g_noalloc_dev[dev];
+  if (!d.scratch) {
+    void* scratch = nullptr;
+    void* status = nullptr;
+    e = cudaGetSymbolAddress(&scratch, g_noalloc_scratch);
+    if (e != cudaSuccess) return set_cuda_error("cudaGetSymbolAddress(static attention workspace)", e);
+    e = cudaGetSymbolAddress(&status, g_noalloc_status);
+    if (e != cudaSuccess) return set_cuda_error("cudaGetSymbolAddress(static status word)", e);
+    d.status = static_cast<int*>(status);
+    d.scratch = scratch;
+  }
+  *out = d;
+  return WANB200_OK;
+}
+
+int attn_fwd_noalloc(const wanb200_attn_params* p, cudaStream_t st) {
+  if (!p) return set_error(WANB200_EINVAL, "attn_noalloc: null params");
+  if (!p->q || !p->k || !p->v || !p->o) return set_error(WANB200_EINVAL, "attn_noalloc: null q/k/v/o");
+  if (p->head_dim != AD) return set_error(WANB200_EINVAL, "attn_noalloc: head_dim must be 128");
+  if (p->batch <= 0 || p->heads <= 0 || p->q_len <= 0 || p->kv_len <= 0)
+    return set_error(WANB200_EINVAL, "attn_noalloc: batch, heads, q_len, kv_len must be positive");
+  if (p->batch > 65535 || p->heads > 65535 || p->q_len > (int64_t)INT32_MAX - 2 * ABM ||
+      p->kv_len > (int64_t)INT32_MAX - ABN)
+    return set_error(WANB200_EINVAL, "attn_noalloc: batch/heads/lengths too large");
+  const int64_t strides[8] = {p->q_tok_stride, p->q_batch_stride, p->k_tok_stride, p->k_batch_stride,
+                              p->v_tok_stride, p->v_batch_stride, p->o_tok_stride, p->o_batch_stride};
+  for (int i = 0; i < 8; ++i)
+    if (strides[i] <= 0 || strides[i] % 8)
+      return set_error(WANB200_EINVAL, "attn_noalloc: strides must be positive multiples of 8");
+  if (p->q_tok_stride < p->heads * AD || p->k_tok_stride < p->heads * AD || p->v_tok_stride < p->heads * AD ||
+      p->o_tok_stride < p->heads * AD)
+    return set_error(WANB200_EINVAL, "attn_noalloc: token stride smaller than heads*128");
+  if (!aligned16(p->q) || !aligned16(p->k) || !aligned16(p->v) || !aligned16(p->o))
+    return set_error(WANB200_EINVAL, "attn_noalloc: q/k/v/o must be 16-byte aligned");
+  if (!(p->softmax_scale > 0.f)) return set_error(WANB200_EINVAL, "attn_noalloc: softmax_scale must be positive");
+  wanb200_attn_params pp = *p;
+  if (pp.kv_splits == 0) pp.kv_splits = 1;
+  if (pp.kv_splits < 1 || pp.kv_splits > 64) return set_error(WANB200_EINVAL, "attn_noalloc: kv_splits must be 0..64");
+  const int nkv = (int)((pp.kv_len + ABN - 1) / ABN);
+  const int per = (nkv + pp.kv_splits - 1) / pp.kv_splits;
+  if ((int64_t)(pp.kv_splits - 1) * per >= nkv)
+    return set_error(WANB200_EINVAL, "attn_noalloc: kv_splits leaves a split without key tiles");
+  const int64_t need = attn_workspace_bytes(pp.batch, pp.heads, pp.q_len, pp.kv_splits);
+  if (need > kNoAllocScratchBytes)
+    return set_error(WANB200_EINVAL,
+                     "attn_noalloc: the split-KV partials need more than the fixed 16 MiB static workspace "
+                     "(kv_splits * batch * heads * q_len * 520 bytes); use fewer splits or wanb200_attn_fwd");
+  NoAllocDevice d;
+  const int rc = noalloc_setup(&d);
+  if (rc) return rc;
+  pp.workspace = d.scratch;
+  pp.workspace_bytes = kNoAllocScratchBytes;
+  int* err = device_error_word_if_present();
+  return attn_launch(&pp, err ? err : d.status, st);
+}
 
 }  // namespace wanb200

@@ -22,6 +22,9 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // Per-device int in global memory that kernels write error codes into (allocated once per
 // device on first use; nullptr + last error set on failure).
 int* device_error_word();
+// The error word of the current device if some entry point already created it, else nullptr
+// (never allocates).
+int* device_error_word_if_present();
 int num_sms();
 
 // 2-D / 4-D bf16 TMA descriptors with 128-byte swizzle and zero fill out of bounds.
@@ -36,6 +39,7 @@ int make_tmap_4d(CUtensorMap* m, const void* base, const int64_t dims[4], const 
 int gemm_bf16(const wanb200_gemm_params* p, cudaStream_t st);
 int attn_fwd(const wanb200_attn_params* p, cudaStream_t st);
 int attn_launch(const wanb200_attn_params* p, int* err, cudaStream_t st);  // validated params
+int attn_fwd_noalloc(const wanb200_attn_params* p, cudaStream_t st);
 int64_t attn_workspace_bytes(int64_t batch, int64_t heads, int64_t q_len, int kv_splits);
 int attn_kv_splits(int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len);
 int layernorm(const wanb200_ln_params* p, cudaStream_t st);

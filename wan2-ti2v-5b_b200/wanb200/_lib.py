@@ -66,7 +66,7 @@ class ResidualParams(ctypes.Structure):
 EXPORTS = ("wanb200_gemm_bf16", "wanb200_attn_fwd", "wanb200_layernorm", "wanb200_qk_norm_rope",
            "wanb200_bias_gate_residual", "wanb200_last_error", "wanb200_device_error", "wanb200_version",
            "wanb200_struct_sizes", "wanb200_peer_barrier", "wanb200_attn_workspace_bytes",
-           "wanb200_attn_kv_splits")
+           "wanb200_attn_kv_splits", "wanb200_attn_fwd_noalloc")
 
 _lock = threading.Lock()
 _lib = None
@@ -108,6 +108,8 @@ def load():
             lib.wanb200_attn_workspace_bytes.restype = c_int64
             lib.wanb200_attn_kv_splits.argtypes = [c_int64, c_int64, c_int64, c_int64]
             lib.wanb200_attn_kv_splits.restype = c_int
+            lib.wanb200_attn_fwd_noalloc.argtypes = [ctypes.POINTER(AttnParams), c_void_p]
+            lib.wanb200_attn_fwd_noalloc.restype = c_int
             sizes = (c_int64 * 5)()
             lib.wanb200_struct_sizes(sizes, 5)
             want = [ctypes.sizeof(c) for c in (GemmParams, AttnParams, LnParams, QkNormParams, ResidualParams)]
