@@ -231,9 +231,14 @@ __global__ void __launch_bounds__(A_THREADS, 1)
         for (int k = 0; k < ABN; ++k)
           if (kbase + k >= args.Lk) s[k] = -INFINITY;
       }
-      float mx = s[0];
+      // row max with 8 independent partial maxima (a single chain of 127 dependent FMNMX would
+      // dominate the warp's latency; two softmax warps per sub-partition cannot hide it)
+      float m8[8];
 #pragma unroll
-      for (int k = 1; k < ABN; ++k) mx = fmaxf(mx, s[k]);
+      for (int k = 0; k < 8; ++k) m8[k] = s[k];
+#pragma unroll
+      for (int k = 8; k < ABN; ++k) m8[k & 7] = fmaxf(m8[k & 7], s[k]);
+      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
       const float m_cand = mx * sl2;
       const bool need = m_cand > m_used + A_RESCALE_THRESHOLD;
       const bool any_need = __any_sync(0xffffffffu, need);
@@ -245,7 +250,7 @@ __global__ void __launch_bounds__(A_THREADS, 1)
         m_used = m_new;
       }
       const float neg = -m_used;
-      float rowsum = 0.f;
+      float r8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // 8 partial row sums (short dependency chains)
 #pragma unroll
       for (int c = 0; c < ABN / 32; ++c) {
         uint32_t pk[16];
@@ -253,7 +258,7 @@ __global__ void __launch_bounds__(A_THREADS, 1)
         for (int k = 0; k < 32; k += 2) {
           const float p0 = ex2_approx(fmaf(s[c * 32 + k], sl2, neg));
           const float p1 = ex2_approx(fmaf(s[c * 32 + k + 1], sl2, neg));
-          rowsum += p0 + p1;
+          r8[(k >> 1) & 7] += p0 + p1;
           pk[k >> 1] = pack_bf16x2(p0, p1);
         }
         uint8_t* rowp = pbuf + (c >> 1) * A_BLK + (r >> 3) * 1024 + (r & 7) * 128;
@@ -264,7 +269,7 @@ __global__ void __launch_bounds__(A_THREADS, 1)
               make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
         }
       }
-      l_run += rowsum;
+      l_run += ((r8[0] + r8[1]) + (r8[2] + r8[3])) + ((r8[4] + r8[5]) + (r8[6] + r8[7]));
       // Rescale O_t (rare).  PV_t(j-1) has completed (see the ordering note above) and PV_t(j)
       // is not issued before this warpgroup's p_full arrival below.
       if (any_need && j > 0) {
