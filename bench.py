@@ -208,7 +208,7 @@ def run_ours(args):
     from wanb200.parallel import make_layout
     lay = make_layout(args.layout)
     fast = FastWanDiT((spec, sd), GRID, GUIDE, device, cfg_group=lay.cfg_group, pair_group=lay.pair_group,
-                      tp_group=lay.tp_group, num_layers=layers, comm=args.comm)
+                      tp_group=lay.tp_group, num_layers=layers, comm=args.comm, sp_group=lay.sp_group)
     del sd
     g = torch.Generator(device=device).manual_seed(123)
     ctx = torch.randn(CTX_LEN, TEXT_DIM, generator=g, device=device)
@@ -267,7 +267,7 @@ def run_ours(args):
         return
 
     peaks = measured_peaks()
-    hbm_kinds = {"layernorm", "qk_norm_rope", "bias_gate_residual"}
+    hbm_kinds = {"layernorm", "qk_norm_rope", "bias_gate_residual", "kv_gather", "peer_barrier"}
     total_ms = sum(x[1] for x in kern.values())
     per_kernel = {k: {"launches": v[0], "ms": v[1], "share": v[1] / total_ms,
                       ("tflops" if k not in hbm_kinds else "gbs"):
@@ -314,7 +314,8 @@ def run_ours(args):
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) bf16 weights, seeded context/latent)",
         "config": {"workload": f"config2: {layers}-layer Wan2.2-TI2V-5B DiT step, 7854 tokens (21x17x22), CFG batch 2",
                    "global_batch": CFG_BATCH, "seq_len": GRID[0] * GRID[1] * GRID[2],
-                   "parallelism": lay.describe(world) + (f", {args.comm} collectives" if fast.sp else ""),
+                   "parallelism": lay.describe(world) + (f", {args.comm} collectives"
+                                                          if (fast.sp or fast.kv_gather is not None) else ""),
                    "layers": layers, "inputs_larger_than_l2": True,
                    "l2_note": "each step streams ~9.8 GB of weights, far above the 126 MB L2"},
         "e2e": {"value": e2e_s, "unit": "s/step", "h2d_bytes_per_step": latent_host.numel() * 4,
@@ -346,9 +347,11 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--comm", default="peer", choices=["peer", "nccl"],
                     help="sequence-parallel collectives: fused into the kernels over NVLink peer memory, or NCCL")
-    ap.add_argument("--layout", default="auto", choices=["auto", "tp", "cfg"],
+    ap.add_argument("--layout", default="auto", choices=["auto", "tp", "cfg", "sp", "cfgsp", "cfgsptp"],
                     help="N>1: tp = TP over all N ranks (batched CFG); cfg = CFG-parallel groups of N/2 "
-                         "(TP inside each); auto = cfg for even N")
+                         "(token-sharded TP inside each); sp = Q-local sequence parallelism over all N ranks "
+                         "(batched CFG, K/V all-gather); cfgsp = CFG-parallel groups of N/2 with Q-local SP "
+                         "inside; cfgsptp = CFG-parallel groups of SP2 x TP(N/4); auto = cfg for even N")
     ap.add_argument("--layers", type=int, default=30, help="blocks per step (30 for the bench line)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

@@ -47,8 +47,11 @@ extern "C" {
  *                             d is unused.  The owner sums the slices (wanb200_bias_gate_residual
  *                             with nsum) after a wanb200_peer_barrier.
  * gate[f, n] = gate_mod[n] + gate_e0[f * gate_frame_stride + n] (modulation + e0 chunk,
- * fast_dit.py:276-277), frame(row) = ((row + row_offset) % seq_len) / tokens_per_frame
- * (row_offset: index of row 0 in the flattened token sequence, for a token shard).
+ * fast_dit.py:276-277), frame(row) = (token(row) % seq_len) / tokens_per_frame with
+ * token(row) = (rows_per_seq > 0 ? row % rows_per_seq : row) + row_offset.
+ * For a whole sequence row_offset = rows_per_seq = 0; for a token shard of the flattened
+ * sequence row_offset is the index of row 0; for a [batch, shard] buffer holding tokens
+ * row_offset .. row_offset + rows_per_seq - 1 of every batch element, rows_per_seq = shard.
  * Limits: K % 64 == 0, N % 32 == 0, lda/ldw/ldd/ldr % 8 == 0, 16-byte aligned pointers.
  * d may alias residual (in place). */
 #define WANB200_EPI_NONE 0
@@ -70,7 +73,7 @@ typedef struct wanb200_gemm_params {
   const void* residual; int64_t ldr;               /* [M, N] bf16 for *_RES */
   const void* gate_mod;                            /* [N] bf16 for GATE_RES */
   const float* gate_e0; int64_t gate_frame_stride; /* e0 row of frame 0, stride between frames */
-  int64_t seq_len, tokens_per_frame, row_offset;   /* frame(row) for GATE_RES */
+  int64_t seq_len, tokens_per_frame, row_offset, rows_per_seq; /* frame(row) for GATE_RES */
   float* rowss; int64_t ss_section; int ss_nsections; /* SUMSQ: [ss_nsections, M] fp32, pre-zeroed */
   void* peer_out[WANB200_MAX_PEERS]; int npeers; int src_rank; int64_t shard_rows; /* SCATTER */
 } wanb200_gemm_params;
@@ -135,7 +138,7 @@ typedef struct wanb200_ln_params {
   const void* modulation;                 /* [6, dim] bf16 */
   const float* e0; int64_t e0_frame_stride; /* [F, 6, dim] fp32 -> frame stride 6*dim */
   int shift_idx, scale_idx;
-  int64_t seq_len, tokens_per_frame, row_offset;
+  int64_t seq_len, tokens_per_frame, row_offset, rows_per_seq; /* frame(row) as for the GEMM */
   const void* weight; const void* bias;   /* [dim] bf16 for AFFINE */
   float* zero_buf; int64_t zero_count;
   /* all-gather fused into the norm: when npush > 0 every output row is also stored at
@@ -174,7 +177,7 @@ typedef struct wanb200_residual_params {
   void* out; const void* residual; const void* y; int64_t rows, dim;
   const void* bias;
   const void* gate_mod; const float* gate_e0; int64_t gate_frame_stride;
-  int64_t seq_len, tokens_per_frame, row_offset;
+  int64_t seq_len, tokens_per_frame, row_offset, rows_per_seq; /* frame(row) as for the GEMM */
   int nsum; int64_t y_slice_stride; /* y = sum of nsum slices y + s * y_slice_stride (0/1: y alone) */
 } wanb200_residual_params;
 
@@ -189,6 +192,26 @@ int wanb200_bias_gate_residual(const wanb200_residual_params* p, void* stream);
  * The wait is bounded (2 s); on timeout the device error word is set and the kernel returns. */
 int wanb200_peer_barrier(int* const* flags, int rank, int world, int epoch, void* stream);
 
+/* ---------------------------------------------------------------- shard gather (push)
+ * The K/V all-gather of sequence-parallel self-attention: `WanSelfAttentionSP.forward`
+ * (models/dit_attention_sp.py:88-99) all-gathers the normed, rotated k and v of every rank's
+ * query shard over the attn-sp group (`ps.all_gather_into_tensor`, parallel_state.py) so each
+ * rank attends its own queries to all keys.  Here the owner of a shard stores it into every
+ * rank's gathered buffer over NVLink: row i < valid_rows of batch element b of the shard,
+ * src + (b * shard_rows + i) * src_ld (width bf16), goes to
+ * dst[p] + b * dst_batch_stride + (dst_row0 + i) * dst_ld for every p < ndst (peer-mapped
+ * buffers, this rank's own included; rows >= valid_rows are the padding of the last shard and
+ * are not sent).  Every rank calls wanb200_peer_barrier before it reads the gathered rows.
+ * Limits: width % 8 == 0, src_ld, dst_ld, dst_batch_stride % 8 == 0, 16-byte aligned pointers. */
+typedef struct wanb200_shard_gather_params {
+  const void* src; int64_t src_ld;
+  int64_t batch, shard_rows, valid_rows, width;
+  void* dst[WANB200_MAX_PEERS]; int ndst;
+  int64_t dst_ld, dst_batch_stride, dst_row0;
+} wanb200_shard_gather_params;
+
+int wanb200_shard_gather(const wanb200_shard_gather_params* p, void* stream);
+
 /* ---------------------------------------------------------------- status */
 const char* wanb200_last_error(void);
 /* Device-side error word of the current device: 0 or a code (a bounded wait expired inside a
@@ -196,7 +219,7 @@ const char* wanb200_last_error(void);
 int wanb200_device_error(int reset);
 /* Library version, e.g. 100 for 0.1.0. */
 int wanb200_version(void);
-/* sizeof of the parameter structs in declaration order (gemm, attn, ln, qknorm, residual)
+/* sizeof of the parameter structs in declaration order (gemm, attn, ln, qknorm, residual, shard_gather)
  * written to out[0..n); returns the number of structs.  Lets a binding detect a library built
  * from a different header. */
 int wanb200_struct_sizes(int64_t* out, int n);

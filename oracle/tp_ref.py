@@ -8,7 +8,9 @@ The reference shards the block by heads (models/tp_utils.py:378-458) and all-red
 `block_fwd_tp` runs one rank's share of that on the CPU in fp32, from the rank's
 `wanb200.BlockWeights` slices, with a caller-supplied `all_reduce` (gloo in the tests), in the
 same op order as `wanb200.block.FastBlock`'s TP branch.  Summed over ranks it must equal the
-unsharded `dit_ref.block_fwd`.
+unsharded `dit_ref.block_fwd`.  `block_fwd_sp` restates the token-sharded residual layout
+(`_FastBlockSP`) and `block_fwd_qsp` the Q-local sequence-parallel one (local queries, K/V
+all-gathered, TP inside) the same way.
 """
 from __future__ import annotations
 
@@ -102,4 +104,48 @@ def block_fwd_sp(w, xs, e0, cos, sin, ck, cv, seq_len: int, nf: int, rank: int, 
     h = F.layer_norm(xs, (C,), eps=EPS) * (1 + et[:, 4]) + et[:, 3]
     hf = all_gather(h)
     part = reduce_scatter(F.linear(F.gelu(F.linear(hf, f["w1"], f["b1"]), approximate="tanh"), f["w2"]))
+    return xs + (part + f["b2"]) * et[:, 5]
+
+
+def block_fwd_qsp(w, xs, e0, cos, sin, ck, cv, seq_len: int, nf: int, rank: int, sp: int, gather_kv, all_reduce):
+    """One rank's share of the Q-local sequence-parallel block (`WanSelfAttentionSP`,
+    models/dit_attention_sp.py:25-152, for the whole block) with TP inside, fp32 CPU, in the op
+    order of `wanb200.block.FastBlock` with a KVGather.  xs [B, S, C] holds tokens
+    rank*S .. rank*S + S - 1 of every batch element (the last shard zero-padded); cos/sin
+    [1, sp*S, 1, 64] (zero-padded); ck/cv [B, Lc, n_local, d]; gather_kv([B, S, W]) ->
+    [B, sp*S, W] concatenates the shards of the SP group; all_reduce sums over the TP group."""
+    f = {k: getattr(w, k).float().cpu() for k in ("modulation", "w_qkv", "b_qkv", "g_q", "g_k", "w_o", "b_o", "ln3_w",
+                                                   "ln3_b", "w_cq", "b_cq", "g_cq", "w_co", "b_co", "w1", "b1",
+                                                   "w2", "b2")}
+    B, S, C = xs.shape
+    Cl, nl = w.local_dim, w.local_heads
+    L = seq_len
+    tpf = L // nf
+    frame = ((torch.arange(S) + rank * S) % L) // tpf   # frame of each shard row (padding wraps)
+    et = (f["modulation"].reshape(1, 6, C) + e0[0])[frame]  # [S, 6, C]
+    c, s = cos[:, rank * S:(rank + 1) * S], sin[:, rank * S:(rank + 1) * S]
+
+    h = F.layer_norm(xs, (C,), eps=EPS) * (1 + et[:, 1]) + et[:, 0]
+    qkv = F.linear(h, f["w_qkv"], f["b_qkv"])
+    q, k, v = qkv[..., :Cl], qkv[..., Cl:2 * Cl], qkv[..., 2 * Cl:]
+    ss = torch.stack([q.pow(2).sum(-1), k.pow(2).sum(-1)])
+    all_reduce(ss)
+    q = rope((q * torch.rsqrt(ss[0] / C + EPS).unsqueeze(-1) * f["g_q"]).reshape(B, S, nl, 128), c, s)
+    k = rope((k * torch.rsqrt(ss[1] / C + EPS).unsqueeze(-1) * f["g_k"]).reshape(B, S, nl, 128), c, s)
+    kv = gather_kv(torch.cat([k.reshape(B, S, Cl), v], dim=-1))[:, :L]  # [B, L, 2*Cl]
+    y = attn(q, kv[..., :Cl].reshape(B, L, nl, 128), kv[..., Cl:].reshape(B, L, nl, 128)).reshape(B, S, Cl)
+    part = F.linear(y, f["w_o"])
+    all_reduce(part)
+    xs = xs + (part + f["b_o"]) * et[:, 2]
+    h = F.layer_norm(xs, (C,), f["ln3_w"], f["ln3_b"], eps=EPS)
+    qc = F.linear(h, f["w_cq"], f["b_cq"])
+    ssc = qc.pow(2).sum(-1)
+    all_reduce(ssc)
+    qc = (qc * torch.rsqrt(ssc / C + EPS).unsqueeze(-1) * f["g_cq"]).reshape(B, S, nl, 128)
+    part = F.linear(attn(qc, ck, cv).reshape(B, S, Cl), f["w_co"])
+    all_reduce(part)
+    xs = xs + part + f["b_co"]
+    h = F.layer_norm(xs, (C,), eps=EPS) * (1 + et[:, 4]) + et[:, 3]
+    part = F.linear(F.gelu(F.linear(h, f["w1"], f["b1"]), approximate="tanh"), f["w2"])
+    all_reduce(part)
     return xs + (part + f["b2"]) * et[:, 5]

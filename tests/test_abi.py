@@ -35,6 +35,7 @@ STRUCTS = {
     "wanb200_ln_params": L.LnParams,
     "wanb200_qknorm_params": L.QkNormParams,
     "wanb200_residual_params": L.ResidualParams,
+    "wanb200_shard_gather_params": L.ShardGatherParams,
 }
 
 
@@ -134,6 +135,34 @@ def test_layernorm_and_qknorm_reject_bad_args_on_host():
     r.rows, r.dim = 4, 12
     rc, msg = _rc_msg(lib.wanb200_bias_gate_residual, r)
     assert rc == -1 and "dim % 8" in msg
+
+
+def test_frame_index_and_shard_gather_reject_bad_args_on_host():
+    lib = L.load()
+    r = L.ResidualParams()
+    r.out = r.residual = r.y = r.bias = r.gate_mod = r.gate_e0 = 64
+    r.rows, r.dim, r.seq_len, r.tokens_per_frame = 4, 16, 8, 2
+    r.rows_per_seq = -1
+    rc, msg = _rc_msg(lib.wanb200_bias_gate_residual, r)
+    assert rc == -1 and "rows_per_seq" in msg
+    g = L.ShardGatherParams()
+    g.src, g.src_ld, g.batch, g.shard_rows, g.valid_rows, g.width = 64, 256, 2, 10, 10, 256
+    g.dst[0], g.ndst, g.dst_ld, g.dst_batch_stride, g.dst_row0 = 128, 1, 256, 256 * 40, 0
+    g.valid_rows = 11  # more valid rows than the shard holds
+    rc, msg = _rc_msg(lib.wanb200_shard_gather, g)
+    assert rc == -1 and "valid_rows" in msg
+    g.valid_rows, g.width = 10, 250
+    rc, msg = _rc_msg(lib.wanb200_shard_gather, g)
+    assert rc == -1 and "width % 8" in msg
+    g.width, g.ndst = 256, 9
+    rc, msg = _rc_msg(lib.wanb200_shard_gather, g)
+    assert rc == -1 and "ndst" in msg
+    g.ndst, g.dst_batch_stride = 1, 256 * 5  # batch 1 would overwrite batch 0's rows
+    rc, msg = _rc_msg(lib.wanb200_shard_gather, g)
+    assert rc == -1 and "dst_batch_stride" in msg
+    g.dst_batch_stride, g.dst[0] = 256 * 40, 72  # destination not 16-byte aligned
+    rc, msg = _rc_msg(lib.wanb200_shard_gather, g)
+    assert rc == -1 and "aligned" in msg
 
 
 def test_ops_refuse_cpu_tensors():

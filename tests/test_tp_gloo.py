@@ -214,3 +214,118 @@ def test_sequence_parallel_decomposition_matches_unsharded_oracle(world):
     for r in range(world):
         assert isinstance(res[r], float), res[r]
         assert res[r] < 1e-5, (r, res[r])
+
+
+def _qsp_worker(rank, world, port, q, tp):
+    try:
+        _setup(rank, world, port)
+        torch.set_num_threads(1)
+        from oracle import dit_ref as R
+        from oracle.tp_ref import block_fwd_qsp
+        from wanb200 import BlockWeights, WanSpec, random_block_state
+        sp = world // tp
+        # contiguous TP groups, SP groups strided across them (parallel_state.py's tp / attn-sp)
+        tp_groups = [dist.new_group(list(range(j * tp, (j + 1) * tp))) for j in range(sp)]
+        sp_groups = [dist.new_group([i + j * tp for j in range(sp)]) for i in range(tp)]
+        tp_group, sp_group = tp_groups[rank // tp], sp_groups[rank % tp]
+        sp_rank, tp_rank = rank // tp, rank % tp
+        spec = WanSpec(dim=512, ffn_dim=1024, num_heads=4)
+        grid = (2, 3, 5)
+        L, Lc, B = 30, 16, 2  # 30 tokens over 4 SP ranks: shards of 8, the last one padded by 2
+        sd = random_block_state(spec, 7)
+        g = torch.Generator().manual_seed(11)
+        x = torch.randn(B, L, spec.dim, generator=g)
+        e0 = torch.randn(1, grid[0], 6, spec.dim, generator=g) * 0.1
+        ctx = torch.randn(B, Lc, spec.dim, generator=g)
+        cos, sin = R.rope_tables(R.model_freqs(128), grid, 128)
+        p32 = {k: v.float() for k, v in sd.items()}
+        ck, cv = R.cross_kv(p32, ctx, spec.num_heads)
+        y_ref = R.block_fwd(p32, x, e0, cos, sin, ck, cv, grid[0], spec.num_heads)
+        S = -(-L // sp)
+        pad = S * sp - L
+        xs = torch.cat([x, x.new_zeros(B, pad, spec.dim)], dim=1)[:, sp_rank * S:(sp_rank + 1) * S].contiguous()
+        cosp = torch.cat([cos, cos.new_zeros(1, pad, 1, 64)], dim=1)
+        sinp = torch.cat([sin, sin.new_zeros(1, pad, 1, 64)], dim=1)
+        w = BlockWeights(sd, spec.num_heads, "cpu", tp_rank, tp)
+        nl = w.local_heads
+        ckl = ck[:, :, tp_rank * nl:(tp_rank + 1) * nl].contiguous()
+        cvl = cv[:, :, tp_rank * nl:(tp_rank + 1) * nl].contiguous()
+
+        def gather(t):
+            out = [torch.empty_like(t) for _ in range(sp)]
+            dist.all_gather(out, t.contiguous(), group=sp_group)
+            return torch.cat(out, dim=1)
+
+        def ar(t):
+            if tp > 1:
+                dist.all_reduce(t, group=tp_group)
+
+        ys = block_fwd_qsp(w, xs, e0, cosp, sinp, ckl, cvl, L, grid[0], sp_rank, sp, gather, ar)
+        y = gather(ys)[:, :L]
+        q.put((rank, R.rel_rms(y, y_ref)))
+    except Exception:  # pragma: no cover
+        import traceback
+        q.put((rank, traceback.format_exc()))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,tp", [(2, 1), (4, 1), (4, 2)])
+def test_qlocal_sequence_parallel_decomposition_matches_unsharded_oracle(world, tp):
+    """Whole block on each rank's token shard (batch 2), K/V all-gathered over the SP group for
+    the local queries, TP inside (the reference's WanSelfAttentionSP layout) == one block."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_qsp_worker, args=(r, world, port, q, tp)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(world):
+        assert isinstance(res[r], float), res[r]
+        assert res[r] < 1e-5, (r, res[r])
+
+
+def _qsp_layout_worker(rank, world, port, q, kind):
+    try:
+        _setup(rank, world, port)
+        from wanb200.parallel import make_layout
+        lay = make_layout(kind)
+        t = torch.tensor([float(rank)])
+        dist.all_reduce(t, group=lay.sp_group)
+        p = torch.tensor([float(rank)])
+        if lay.pair_group is not None:
+            dist.all_reduce(p, group=lay.pair_group)
+        q.put((rank, (lay.cfg_group, lay.sp_size, lay.tp_size, float(t), float(p), lay.describe(world))))
+    except Exception as ex:  # pragma: no cover
+        q.put((rank, repr(ex)))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("kind", ["sp", "cfgsp", "cfgsptp"])
+def test_qlocal_layout_groups(kind):
+    """4 ranks: "sp" = one SP group of all ranks; "cfgsp" / "cfgsptp" (TP 1 at 4 ranks) = CFG
+    groups {0,1} and {2,3} each one SP group, pairs {0,2}, {1,3}."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_qsp_layout_worker, args=(r, 4, port, q, kind)) for r in range(4)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=30)
+    if kind == "sp":
+        for r in range(4):
+            assert res[r] == (None, 4, 1, 6.0, float(r), "sp4"), res[r]
+        return
+    name = "cfg2xsp2" if kind == "cfgsp" else "cfg2xsp2xtp1"
+    assert res[0] == (0, 2, 1, 1.0, 2.0, name), res[0]
+    assert res[1] == (0, 2, 1, 1.0, 4.0, name), res[1]
+    assert res[2] == (1, 2, 1, 5.0, 2.0, name), res[2]
+    assert res[3] == (1, 2, 1, 5.0, 4.0, name), res[3]

@@ -161,6 +161,10 @@ int wanb200_peer_barrier(int* const* flags, int rank, int world, int epoch, void
   return peer_barrier(flags, rank, world, epoch, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int wanb200_shard_gather(const wanb200_shard_gather_params* p, void* stream) {
+  return shard_gather(p, reinterpret_cast<cudaStream_t>(stream));
+}
+
 const char* wanb200_last_error(void) { return t_last_error.c_str(); }
 
 int wanb200_device_error(int reset) {
@@ -181,11 +185,11 @@ int wanb200_device_error(int reset) {
 int wanb200_version(void) { return 100; }
 
 int wanb200_struct_sizes(int64_t* out, int n) {
-  const int64_t sizes[5] = {(int64_t)sizeof(wanb200_gemm_params), (int64_t)sizeof(wanb200_attn_params),
+  const int64_t sizes[6] = {(int64_t)sizeof(wanb200_gemm_params), (int64_t)sizeof(wanb200_attn_params),
                             (int64_t)sizeof(wanb200_ln_params), (int64_t)sizeof(wanb200_qknorm_params),
-                            (int64_t)sizeof(wanb200_residual_params)};
-  for (int i = 0; i < n && i < 5; ++i) out[i] = sizes[i];
-  return 5;
+                            (int64_t)sizeof(wanb200_residual_params), (int64_t)sizeof(wanb200_shard_gather_params)};
+  for (int i = 0; i < n && i < 6; ++i) out[i] = sizes[i];
+  return 6;
 }
 
 }  // extern "C"

@@ -274,4 +274,14 @@ __device__ __forceinline__ float gelu_tanh(float x) {
   return 0.5f * x * (1.0f + t);
 }
 
+// Latent frame of buffer row `row` (the index of its per-frame modulation row):
+// token = (rows_per_seq > 0 ? row % rows_per_seq : row) + row_offset, frame = (token % seq_len) /
+// tokens_per_frame.  rows_per_seq > 0 describes a [batch, rows_per_seq] buffer holding tokens
+// row_offset .. row_offset + rows_per_seq - 1 of every batch element (a sequence shard).
+__device__ __forceinline__ int64_t frame_of_row(int64_t row, int64_t rows_per_seq, int64_t row_offset,
+                                                int64_t seq_len, int64_t tokens_per_frame) {
+  const int64_t tok = (rows_per_seq > 0 ? row % rows_per_seq : row) + row_offset;
+  return (tok % seq_len) / tokens_per_frame;
+}
+
 }  // namespace wanb200

@@ -18,7 +18,7 @@ struct LnArgs {
   const float* e0;
   int64_t e0_frame_stride;
   int shift_idx, scale_idx;
-  int64_t seq_len, tokens_per_frame, row_offset;
+  int64_t seq_len, tokens_per_frame, row_offset, rows_per_seq;
   const __nv_bfloat16* weight;
   const __nv_bfloat16* bias;
   float* zero_buf;
@@ -74,7 +74,7 @@ __global__ void __launch_bounds__(256, 2) layernorm_kernel(const LnArgs a) {
   const float* shp = nullptr;
   const float* scp = nullptr;
   if constexpr (MODE == 0) {
-    const int64_t f = ((row + a.row_offset) % a.seq_len) / a.tokens_per_frame;
+    const int64_t f = frame_of_row(row, a.rows_per_seq, a.row_offset, a.seq_len, a.tokens_per_frame);
     shp = a.e0 + f * a.e0_frame_stride + (int64_t)a.shift_idx * a.dim;
     scp = a.e0 + f * a.e0_frame_stride + (int64_t)a.scale_idx * a.dim;
   }
@@ -145,8 +145,9 @@ int layernorm(const wanb200_ln_params* p, cudaStream_t st) {
   if (p->mode == WANB200_LN_MODULATE) {
     if (!p->modulation || !p->e0 || !aligned16(p->modulation) || !aligned16(p->e0) || p->e0_frame_stride % 4 ||
         p->shift_idx < 0 || p->shift_idx > 5 || p->scale_idx < 0 || p->scale_idx > 5 || p->seq_len <= 0 ||
-        p->tokens_per_frame <= 0)
-      return set_error(WANB200_EINVAL, "layernorm: modulate mode needs modulation, e0, indices, seq_len, tokens_per_frame");
+        p->tokens_per_frame <= 0 || p->row_offset < 0 || p->rows_per_seq < 0)
+      return set_error(WANB200_EINVAL, "layernorm: modulate mode needs modulation, e0, indices, seq_len, tokens_per_frame "
+                                       "(row_offset, rows_per_seq >= 0)");
   } else if (p->mode == WANB200_LN_AFFINE) {
     if (!p->weight || !p->bias || !aligned16(p->weight) || !aligned16(p->bias))
       return set_error(WANB200_EINVAL, "layernorm: affine mode needs 16-byte aligned weight and bias");
@@ -169,6 +170,7 @@ int layernorm(const wanb200_ln_params* p, cudaStream_t st) {
   a.seq_len = p->seq_len > 0 ? p->seq_len : 1;
   a.tokens_per_frame = p->tokens_per_frame > 0 ? p->tokens_per_frame : 1;
   a.row_offset = p->row_offset;
+  a.rows_per_seq = p->rows_per_seq;
   a.weight = reinterpret_cast<const __nv_bfloat16*>(p->weight);
   a.bias = reinterpret_cast<const __nv_bfloat16*>(p->bias);
   a.zero_buf = p->zero_buf;
@@ -293,7 +295,7 @@ struct ResArgs {
   const __nv_bfloat16* bias;
   const __nv_bfloat16* gate_mod;
   const float* gate_e0;
-  int64_t gate_frame_stride, seq_len, tokens_per_frame, row_offset;
+  int64_t gate_frame_stride, seq_len, tokens_per_frame, row_offset, rows_per_seq;
   int nsum;
   int64_t y_slice_stride;
 };
@@ -320,7 +322,8 @@ __global__ void __launch_bounds__(256) bias_gate_residual_kernel(const ResArgs a
   if constexpr (GATE) {
     float g[8];
     unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.gate_mod + col)), g);
-    const float* e = a.gate_e0 + (((row + a.row_offset) % a.seq_len) / a.tokens_per_frame) * a.gate_frame_stride + col;
+    const float* e = a.gate_e0 +
+                     frame_of_row(row, a.rows_per_seq, a.row_offset, a.seq_len, a.tokens_per_frame) * a.gate_frame_stride + col;
     const float4 e0 = __ldg(reinterpret_cast<const float4*>(e)), e1 = __ldg(reinterpret_cast<const float4*>(e + 4));
     g[0] += e0.x; g[1] += e0.y; g[2] += e0.z; g[3] += e0.w;
     g[4] += e1.x; g[5] += e1.y; g[6] += e1.z; g[7] += e1.w;
@@ -347,8 +350,9 @@ int bias_gate_residual(const wanb200_residual_params* p, cudaStream_t st) {
     return set_error(WANB200_EINVAL, "bias_gate_residual: pointers must be 16-byte aligned");
   const bool gate = p->gate_mod != nullptr;
   if (gate && (!p->gate_e0 || !aligned16(p->gate_mod) || !aligned16(p->gate_e0) || p->gate_frame_stride % 4 ||
-               p->seq_len <= 0 || p->tokens_per_frame <= 0))
-    return set_error(WANB200_EINVAL, "bias_gate_residual: gate needs gate_e0, seq_len, tokens_per_frame");
+               p->seq_len <= 0 || p->tokens_per_frame <= 0 || p->row_offset < 0 || p->rows_per_seq < 0))
+    return set_error(WANB200_EINVAL, "bias_gate_residual: gate needs gate_e0, seq_len, tokens_per_frame "
+                                     "(row_offset, rows_per_seq >= 0)");
   ResArgs a;
   a.out = reinterpret_cast<__nv_bfloat16*>(p->out);
   a.residual = reinterpret_cast<const __nv_bfloat16*>(p->residual);
@@ -362,6 +366,7 @@ int bias_gate_residual(const wanb200_residual_params* p, cudaStream_t st) {
   a.seq_len = p->seq_len > 0 ? p->seq_len : 1;
   a.tokens_per_frame = p->tokens_per_frame > 0 ? p->tokens_per_frame : 1;
   a.row_offset = p->row_offset;
+  a.rows_per_seq = p->rows_per_seq;
   a.nsum = p->nsum;
   a.y_slice_stride = p->y_slice_stride;
   const int64_t blocks = (p->rows * (p->dim / 8) + 255) / 256;

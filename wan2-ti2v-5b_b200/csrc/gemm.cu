@@ -50,7 +50,7 @@ struct GemmArgs {
   const float* gate_e0;
   int64_t gate_frame_stride;
   int seq_len, tokens_per_frame;
-  int64_t row_offset;
+  int64_t row_offset, rows_per_seq;
   float* rowss;
   int ss_section, ss_nsections;
   __nv_bfloat16* peer_out[WANB200_MAX_PEERS];
@@ -107,7 +107,7 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v,
     if (row < a.M) {
       const uint4* rp = reinterpret_cast<const uint4*>(a.residual + (int64_t)row * a.ldr + col0);
       if constexpr (EPI == WANB200_EPI_BIAS_GATE_RES) {
-        const int f = (int)(((int64_t)row + a.row_offset) % a.seq_len) / a.tokens_per_frame;
+        const int f = (int)frame_of_row(row, a.rows_per_seq, a.row_offset, a.seq_len, a.tokens_per_frame);
         const float4* ep = reinterpret_cast<const float4*>(a.gate_e0 + (int64_t)f * a.gate_frame_stride + col0);
         const uint4* mp = reinterpret_cast<const uint4*>(a.gate_mod + col0);
 #pragma unroll
@@ -395,8 +395,9 @@ int gemm_bf16(const wanb200_gemm_params* p, cudaStream_t st) {
   if (epi == WANB200_EPI_BIAS_GATE_RES) {
     if (!p->gate_mod || !p->gate_e0 || !aligned16(p->gate_mod) || !aligned16(p->gate_e0) ||
         (p->gate_frame_stride % 4) || p->seq_len <= 0 || p->tokens_per_frame <= 0 || p->seq_len > INT32_MAX ||
-        p->tokens_per_frame > INT32_MAX)
-      return set_error(WANB200_EINVAL, "gemm: gate epilogue needs gate_mod, gate_e0, seq_len, tokens_per_frame");
+        p->tokens_per_frame > INT32_MAX || p->row_offset < 0 || p->rows_per_seq < 0)
+      return set_error(WANB200_EINVAL, "gemm: gate epilogue needs gate_mod, gate_e0, seq_len, tokens_per_frame "
+                                       "(row_offset, rows_per_seq >= 0)");
   }
   if (epi == WANB200_EPI_BIAS_SUMSQ) {
     if (!p->rowss || p->ss_section <= 0 || (p->ss_section % 32) || p->ss_nsections <= 0 || p->ss_section > INT32_MAX)
@@ -426,6 +427,7 @@ int gemm_bf16(const wanb200_gemm_params* p, cudaStream_t st) {
   ga.seq_len = (int)(p->seq_len > 0 ? p->seq_len : 1);
   ga.tokens_per_frame = (int)(p->tokens_per_frame > 0 ? p->tokens_per_frame : 1);
   ga.row_offset = p->row_offset;
+  ga.rows_per_seq = p->rows_per_seq;
   ga.rowss = p->rowss;
   ga.ss_section = (int)(p->ss_section > 0 ? p->ss_section : 1);
   ga.ss_nsections = p->ss_nsections;

@@ -46,5 +46,6 @@ int layernorm(const wanb200_ln_params* p, cudaStream_t st);
 int qk_norm_rope(const wanb200_qknorm_params* p, cudaStream_t st);
 int bias_gate_residual(const wanb200_residual_params* p, cudaStream_t st);
 int peer_barrier(int* const* flags, int rank, int world, int epoch, cudaStream_t st);
+int shard_gather(const wanb200_shard_gather_params* p, cudaStream_t st);
 
 }  // namespace wanb200

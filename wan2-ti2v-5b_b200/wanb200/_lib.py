@@ -25,7 +25,8 @@ class GemmParams(ctypes.Structure):
                 ("ldd", c_int64), ("M", c_int64), ("N", c_int64), ("K", c_int64), ("epilogue", c_int),
                 ("bias", c_void_p), ("residual", c_void_p), ("ldr", c_int64), ("gate_mod", c_void_p),
                 ("gate_e0", c_void_p), ("gate_frame_stride", c_int64), ("seq_len", c_int64),
-                ("tokens_per_frame", c_int64), ("row_offset", c_int64), ("rowss", c_void_p), ("ss_section", c_int64),
+                ("tokens_per_frame", c_int64), ("row_offset", c_int64), ("rows_per_seq", c_int64), ("rowss", c_void_p),
+                ("ss_section", c_int64),
                 ("ss_nsections", c_int), ("peer_out", c_void_p * 8), ("npeers", c_int), ("src_rank", c_int),
                 ("shard_rows", c_int64)]
 
@@ -44,7 +45,7 @@ class LnParams(ctypes.Structure):
     _fields_ = [("x", c_void_p), ("out", c_void_p), ("rows", c_int64), ("dim", c_int64), ("eps", c_float),
                 ("mode", c_int), ("modulation", c_void_p), ("e0", c_void_p), ("e0_frame_stride", c_int64),
                 ("shift_idx", c_int), ("scale_idx", c_int), ("seq_len", c_int64), ("tokens_per_frame", c_int64),
-                ("row_offset", c_int64),
+                ("row_offset", c_int64), ("rows_per_seq", c_int64),
                 ("weight", c_void_p), ("bias", c_void_p), ("zero_buf", c_void_p), ("zero_count", c_int64),
                 ("push_out", c_void_p * 8), ("npush", c_int), ("push_row0", c_int64)]
 
@@ -59,14 +60,21 @@ class QkNormParams(ctypes.Structure):
 class ResidualParams(ctypes.Structure):
     _fields_ = [("out", c_void_p), ("residual", c_void_p), ("y", c_void_p), ("rows", c_int64), ("dim", c_int64),
                 ("bias", c_void_p), ("gate_mod", c_void_p), ("gate_e0", c_void_p), ("gate_frame_stride", c_int64),
-                ("seq_len", c_int64), ("tokens_per_frame", c_int64), ("row_offset", c_int64), ("nsum", c_int),
+                ("seq_len", c_int64), ("tokens_per_frame", c_int64), ("row_offset", c_int64), ("rows_per_seq", c_int64),
+                ("nsum", c_int),
                 ("y_slice_stride", c_int64)]
+
+
+class ShardGatherParams(ctypes.Structure):
+    _fields_ = [("src", c_void_p), ("src_ld", c_int64), ("batch", c_int64), ("shard_rows", c_int64),
+                ("valid_rows", c_int64), ("width", c_int64), ("dst", c_void_p * 8), ("ndst", c_int),
+                ("dst_ld", c_int64), ("dst_batch_stride", c_int64), ("dst_row0", c_int64)]
 
 
 EXPORTS = ("wanb200_gemm_bf16", "wanb200_attn_fwd", "wanb200_layernorm", "wanb200_qk_norm_rope",
            "wanb200_bias_gate_residual", "wanb200_last_error", "wanb200_device_error", "wanb200_version",
            "wanb200_struct_sizes", "wanb200_peer_barrier", "wanb200_attn_workspace_bytes",
-           "wanb200_attn_kv_splits", "wanb200_attn_fwd_noalloc")
+           "wanb200_attn_kv_splits", "wanb200_attn_fwd_noalloc", "wanb200_shard_gather")
 
 _lock = threading.Lock()
 _lib = None
@@ -92,8 +100,9 @@ def load():
             lib.wanb200_layernorm.argtypes = [ctypes.POINTER(LnParams), c_void_p]
             lib.wanb200_qk_norm_rope.argtypes = [ctypes.POINTER(QkNormParams), c_void_p]
             lib.wanb200_bias_gate_residual.argtypes = [ctypes.POINTER(ResidualParams), c_void_p]
+            lib.wanb200_shard_gather.argtypes = [ctypes.POINTER(ShardGatherParams), c_void_p]
             for fn in ("wanb200_gemm_bf16", "wanb200_attn_fwd", "wanb200_layernorm", "wanb200_qk_norm_rope",
-                       "wanb200_bias_gate_residual"):
+                       "wanb200_bias_gate_residual", "wanb200_shard_gather"):
                 getattr(lib, fn).restype = c_int
             lib.wanb200_last_error.restype = ctypes.c_char_p
             lib.wanb200_last_error.argtypes = []
@@ -110,10 +119,11 @@ def load():
             lib.wanb200_attn_kv_splits.restype = c_int
             lib.wanb200_attn_fwd_noalloc.argtypes = [ctypes.POINTER(AttnParams), c_void_p]
             lib.wanb200_attn_fwd_noalloc.restype = c_int
-            sizes = (c_int64 * 5)()
-            lib.wanb200_struct_sizes(sizes, 5)
-            want = [ctypes.sizeof(c) for c in (GemmParams, AttnParams, LnParams, QkNormParams, ResidualParams)]
-            if list(sizes) != want:
+            structs = (GemmParams, AttnParams, LnParams, QkNormParams, ResidualParams, ShardGatherParams)
+            sizes = (c_int64 * len(structs))()
+            n = lib.wanb200_struct_sizes(sizes, len(structs))
+            want = [ctypes.sizeof(c) for c in structs]
+            if n != len(structs) or list(sizes) != want:
                 raise WanB200Error(f"{LIB_PATH} was built from a different include/wanb200.h (struct sizes "
                                    f"{list(sizes)} vs {want}); rebuild it with `python wan2-ti2v-5b_b200/build.py`")
             _lib = lib

@@ -71,12 +71,17 @@ class FastBlock:
     size 1 = single GPU).
     """
 
-    def __init__(self, weights: BlockWeights, num_frames: int, tp_group=None, eps: float = 1e-6):
+    def __init__(self, weights: BlockWeights, num_frames: int, tp_group=None, eps: float = 1e-6, sp=None):
+        """sp: a wanb200.comm.KVGather of the sequence-parallel group for Q-local self-attention
+        (`WanSelfAttentionSP`, models/dit_attention_sp.py:25-152): x then holds the tokens
+        sp.rank*S .. sp.rank*S + S - 1 of every batch element, every op runs on those rows, and
+        only K/V are gathered from the group.  None = x holds whole sequences."""
         self.w = weights
         self.num_frames = num_frames
         self.tp_group = tp_group
         self.tp = weights.tp_size > 1
         self.eps = eps
+        self.sp = sp
 
     def _all_reduce(self, t):
         if self.tp:
@@ -85,14 +90,18 @@ class FastBlock:
     def forward(self, x, e, cos, sin, ck, cv):
         """x [B, L, C] bf16; e [1, F, 6, C] per-frame time projection (any float dtype);
         cos/sin [1, L, 1, 64] fp32; ck/cv [B, Lc, H_local, 128] bf16 -> new x [B, L, C] bf16."""
-        w = self.w
-        B, Lx, C = x.shape
+        w, sp = self.w, self.sp
+        B, Lx, C = x.shape  # Lx: rows per batch element held here (the shard length under sp)
         nf = self.num_frames
-        if Lx % nf:
-            raise ValueError(f"sequence length {Lx} is not a multiple of {nf} frames")
-        tpf = Lx // nf
+        L_seq = sp.L if sp is not None else Lx
+        if L_seq % nf:
+            raise ValueError(f"sequence length {L_seq} is not a multiple of {nf} frames")
+        if sp is not None and (Lx != sp.S or B != sp.B):
+            raise ValueError(f"x is [{B}, {Lx}, C]; the sequence-parallel group expects [{sp.B}, {sp.S}, C]")
+        tpf = L_seq // nf
         N, Cl, nl = B * Lx, w.local_dim, w.local_heads
-        frames = (Lx, tpf)
+        row0 = sp.rank * sp.S if sp is not None else 0
+        frames = (L_seq, tpf, row0, Lx) if sp is not None else (Lx, tpf)
         xf = x.reshape(N, C)
         if not xf.is_contiguous():
             xf = xf.contiguous()
@@ -101,8 +110,11 @@ class FastBlock:
             e0 = e0.float().contiguous()
         if e0.shape[0] != nf:
             raise ValueError(f"e has {e0.shape[0]} frames, expected {nf}")
-        cos2 = cos.reshape(Lx, -1)
-        sin2 = sin.reshape(Lx, -1)
+        cos2 = cos.reshape(-1, cos.shape[-1])
+        sin2 = sin.reshape(-1, sin.shape[-1])
+        if cos2.shape[0] < row0 + Lx:
+            raise ValueError(f"RoPE tables have {cos2.shape[0]} rows, need {row0 + Lx} (pad them to SP * S rows)")
+        cos2, sin2 = cos2[row0:row0 + Lx], sin2[row0:row0 + Lx]
         if cos2.dtype != torch.float32 or not cos2.is_contiguous():
             cos2, sin2 = cos2.float().contiguous(), sin2.float().contiguous()
         ws = workspace(N, w, x.device, self.tp)
@@ -116,8 +128,13 @@ class FastBlock:
         ops.qk_norm_rope(ws.qkv, [(0, ws.ss[0], w.g_q), (Cl, ws.ss[1], w.g_k)], Cl, C, eps=self.eps,
                          cos=cos2, sin=sin2, seq_len=Lx)
         q = ws.qkv[:, :Cl].view(B, Lx, nl, 128)
-        k = ws.qkv[:, Cl:2 * Cl].view(B, Lx, nl, 128)
-        v = ws.qkv[:, 2 * Cl:].view(B, Lx, nl, 128)
+        if sp is None:
+            k = ws.qkv[:, Cl:2 * Cl].view(B, Lx, nl, 128)
+            v = ws.qkv[:, 2 * Cl:].view(B, Lx, nl, 128)
+        else:  # Q-local: this shard's queries against the whole sequence's keys
+            kv = sp.gather(ws.qkv[:, Cl:])[:, :L_seq]
+            k = kv[:, :, :Cl].unflatten(2, (nl, 128))
+            v = kv[:, :, Cl:].unflatten(2, (nl, 128))
         ops.attention(q, k, v, out=ws.y.view(B, Lx, nl, 128), kind="attn_self")
         x1 = torch.empty_like(xf)
         gate2 = (mod[2], e0[:, 2, :])
@@ -161,7 +178,10 @@ class FastBlock:
     # kernel launches per forward (for the bench's gpu_launches count)
     @property
     def launches(self) -> int:
-        return 13 if not self.tp else 16
+        n = 13 if not self.tp else 16
+        if self.sp is not None and self.sp.comm == "peer":
+            n += 2  # shard gather + peer barrier
+        return n
 
 
 class FastCrossKV:

@@ -66,3 +66,82 @@ class PeerComm:
     def scatter(self):
         """`scatter=` argument of ops.linear for the row-parallel GEMMs."""
         return (self.inbox_ptrs, self.rank, self.S)
+
+
+class KVGather:
+    """The gathered K/V of a sequence-parallel group (Q-local self-attention).
+
+    `WanSelfAttentionSP` (models/dit_attention_sp.py:25-152) keeps each rank's L/SP query
+    tokens local and all-gathers the normed, rotated K and V over the attn-sp group before the
+    attention (88-99).  Here every rank holds the tokens rank*S .. rank*S + S - 1 of each batch
+    element (S = ceil(L / SP); the last shard is zero-padded), and `gather(kv)` returns
+    [batch, SP*S, width] with rows 0 .. L-1 the whole sequence's k | v columns.
+      comm="peer": the owner of each shard pushes it into every rank's buffer over NVLink
+        (wanb200_shard_gather) followed by a peer barrier.  Two buffers alternate by call, so a
+        rank that runs ahead writes the buffer its slower peers finished reading one call ago
+        (they passed the previous barrier after that read).
+      comm="nccl": torch.distributed.all_gather_into_tensor per batch element.
+    Every rank must call gather() the same number of times in the same order.
+    """
+
+    def __init__(self, group, batch: int, seq_len: int, width: int, device, comm: str = "peer"):
+        self.group = group
+        self.T = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.B, self.L, self.width = batch, seq_len, width
+        self.S = -(-seq_len // self.T)
+        self.valid = max(0, min(self.S, seq_len - self.rank * self.S))
+        self.device = torch.device(device)
+        self.comm = comm
+        rows = self.T * self.S
+        self.calls = 0
+        if comm == "peer":
+            import torch.distributed._symmetric_memory as symm_mem
+            name = group.group_name
+            try:
+                symm_mem.enable_symm_mem_for_group(name)
+            except Exception:
+                pass
+            self.bufs, self.ptrs, self._handles = [], [], []
+            for _ in range(2):
+                t = symm_mem.empty((batch, rows, width), dtype=BF16, device=self.device)
+                h = symm_mem.rendezvous(t, name)
+                off = t.data_ptr() - int(h.buffer_ptrs[self.rank])
+                ptrs = [int(p) + off for p in h.buffer_ptrs]
+                # start with the next rank so the ranks' first stores go to different GPUs
+                self.ptrs.append([ptrs[(self.rank + 1 + i) % self.T] for i in range(self.T)])
+                self.bufs.append(t)
+                self._handles.append(h)
+            self.flags = symm_mem.empty((self.T,), dtype=torch.int32, device=self.device)
+            hf = symm_mem.rendezvous(self.flags, name)
+            foff = self.flags.data_ptr() - int(hf.buffer_ptrs[self.rank])
+            self.flag_ptrs = [int(p) + foff for p in hf.buffer_ptrs]
+            self._handles.append(hf)
+            self.flags.zero_()
+            self.epoch = 0
+        elif comm == "nccl":
+            self.bufs = [torch.empty(batch, rows, width, dtype=BF16, device=self.device)]
+            self.stage = torch.empty(batch, self.S, width, dtype=BF16, device=self.device)
+        else:
+            raise ValueError("comm must be 'peer' or 'nccl'")
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=group)
+
+    def gather(self, kv: torch.Tensor) -> torch.Tensor:
+        """kv: [batch * S, width] bf16 with unit column stride (this rank's shard, e.g. the k | v
+        columns of the QKV buffer) -> the gathered [batch, SP*S, width] buffer."""
+        if self.comm == "peer":
+            i = self.calls % 2
+            self.calls += 1
+            row_elems = self.T * self.S * self.width
+            ops.shard_gather(kv, self.B, self.S, self.valid, self.ptrs[i], self.width, row_elems,
+                             self.rank * self.S, self.device)
+            self.epoch += 1
+            ops.peer_barrier(self.flag_ptrs, self.rank, self.epoch, self.device)
+            return self.bufs[i]
+        self.calls += 1
+        self.stage.view(self.B * self.S, self.width).copy_(kv[:self.B * self.S])
+        out = self.bufs[0]
+        for b in range(self.B):
+            dist.all_gather_into_tensor(out[b], self.stage[b], group=self.group)
+        return out

@@ -74,12 +74,16 @@ def _spec_and_state(model):
 
 class FastWanDiT:
     def __init__(self, model, grid, guide_scale, device, cfg_group=None, pair_group=None, tp_group=None,
-                 num_layers=None, seq_parallel=None, comm="peer"):
+                 num_layers=None, seq_parallel=None, comm="peer", sp_group=None):
         """seq_parallel: token-sharded residual inside the TP group with local all-head
         cross-attention (`_FastBlockSP`, fast_dit.py:314-389); default on for CFG-parallel with
-        TP > 1 (batch 1), the reference's best layout.  comm: how the sequence-parallel block
-        all-gathers / reduce-scatters: "peer" = fused into the LayerNorm / GEMM kernels over NVLink
-        peer memory (wanb200.comm), "nccl" = torch.distributed collectives."""
+        TP > 1 (batch 1) and no sp_group, the reference's best layout.
+        sp_group: Q-local sequence parallelism (`WanSelfAttentionSP`, dit_attention_sp.py:25-152)
+        over this group: each rank runs every block on ceil(L / SP) tokens of each batch element
+        and gathers only the normed, rotated K/V of the group (TP inside, by tp_group, as usual);
+        the head runs on the token shard and its 4*48-wide output is gathered.
+        comm: how the sequence-parallel collectives run: "peer" = fused into the kernels /
+        pushed over NVLink peer memory (wanb200.comm), "nccl" = torch.distributed collectives."""
         spec, sd = _spec_and_state(model)
         self.spec = spec
         self.grid = tuple(int(g) for g in grid)
@@ -103,11 +107,24 @@ class FastWanDiT:
             return sd[k].to(device=self.device, dtype=torch.float32)
 
         self.emb = {k: f32(k) for k in sd if not k.startswith("blocks.")}
+        spn = dist.get_world_size(sp_group) if (sp_group is not None and dist.is_initialized()) else 1
+        self.sp_size = spn
+        self.sp_rank = dist.get_rank(sp_group) if spn > 1 else 0
+        self.sp_group = sp_group if spn > 1 else None
         if seq_parallel is None:
-            seq_parallel = cfg_group is not None and tp > 1
-        if seq_parallel and (self.batch != 1 or tp == 1):
-            raise ValueError("seq_parallel needs CFG-parallel (batch 1) and a TP group of size > 1")
+            seq_parallel = cfg_group is not None and tp > 1 and spn == 1
+        if seq_parallel and (self.batch != 1 or tp == 1 or spn > 1):
+            raise ValueError("seq_parallel needs CFG-parallel (batch 1), a TP group of size > 1 and no sp_group")
         self.sp = seq_parallel
+        self.kv_gather = None
+        if spn > 1:
+            from .comm import KVGather
+            self.kv_gather = KVGather(sp_group, self.batch, self.seq_len, 2 * spec.dim // tp, self.device, comm)
+            S = self.kv_gather.S
+            pad = spn * S - self.seq_len
+            if pad:  # the padded rows of the last shard rotate by zeros (they are never read back)
+                self.cos = torch.cat([self.cos, self.cos.new_zeros(1, pad, 1, self.cos.shape[-1])], dim=1)
+                self.sin = torch.cat([self.sin, self.sin.new_zeros(1, pad, 1, self.sin.shape[-1])], dim=1)
         self.block_weights = [BlockWeights(block_state(sd, i), spec.num_heads, self.device, rank, tp,
                                            local_cross=seq_parallel) for i in range(nl)]
         self.comm = None
@@ -121,7 +138,8 @@ class FastWanDiT:
             self.blocks = [FastBlockSP(w, self.seq_len, self.num_frames, tp_group, spec.eps, comm=self.comm)
                            for w in self.block_weights]
         else:
-            self.blocks = [FastBlock(w, self.num_frames, tp_group, spec.eps) for w in self.block_weights]
+            self.blocks = [FastBlock(w, self.num_frames, tp_group, spec.eps, sp=self.kv_gather)
+                           for w in self.block_weights]
         self.cross_kv = [FastCrossKV(w, tp_group, spec.eps) for w in self.block_weights]
         self.context = None
 
@@ -164,17 +182,28 @@ class FastWanDiT:
         x = torch.addmm(m["patch_embedding.bias"], x, wt.t())
         return x.to(BF16).unsqueeze(0).expand(self.batch, -1, -1).contiguous()
 
+    def head_tokens(self, x, e, row0=0):
+        """LN + 2-way modulation + Linear of `_FastHead` (fast_dit.py:480-505) per token:
+        x [B, n, C] holds tokens row0 .. row0 + n - 1 -> [B, n, 4*48] fp32."""
+        m = self.emb
+        B, n, C = x.shape
+        tpf = self.seq_len // self.num_frames
+        frame = (torch.arange(row0, row0 + n, device=x.device) // tpf).clamp_(max=self.num_frames - 1)
+        mod = (m["head.modulation"].unsqueeze(0) + e.unsqueeze(2))[0, frame]  # [n, 2, C]
+        xn = F.layer_norm(x.float(), (C,), eps=self.spec.eps)
+        xn = xn * (1 + mod[:, 1]) + mod[:, 0]
+        return F.linear(xn, m["head.head.weight"], m["head.head.bias"])
+
     def head(self, x, e):
         """LN + 2-way modulation + Linear, unpatchify, CFG combine (fast_dit.py:480-505)."""
-        m = self.emb
+        return self.combine(self.head_tokens(x, e))
+
+    def combine(self, y):
+        """Unpatchify [B, L, 4*48] and combine the CFG branches."""
         f, h, w = self.grid
         p, q, r = self.spec.patch_size
         c = self.spec.out_dim
-        B, Lx, C = x.shape
-        mod = (m["head.modulation"].unsqueeze(0) + e.unsqueeze(2))  # [1, F, 2, C]
-        xn = F.layer_norm(x.float(), (C,), eps=self.spec.eps).view(B, f, Lx // f, C)
-        xn = (xn * (1 + mod[:, :, 1].unsqueeze(2)) + mod[:, :, 0].unsqueeze(2)).view(B, Lx, C)
-        y = F.linear(xn, m["head.head.weight"], m["head.head.bias"])
+        B = y.shape[0]
         y = y.view(B, f, h, w, p, q, r, c).permute(0, 7, 1, 4, 2, 5, 3, 6).reshape(B, c, f * p, h * q, w * r)
         if self.cfg_group is None:
             return y[1] + self.guide_scale * (y[0] - y[1])
@@ -207,11 +236,31 @@ class FastWanDiT:
         dist.all_gather_into_tensor(full, xs, group=self.tp_group)
         return full[:self.batch * self.seq_len].view(self.batch, self.seq_len, C)
 
+    def shard_q(self, x):
+        """[B, L, C] -> this rank's Q-local shard [B, S, C] (tokens sp_rank*S .., zero-padded)."""
+        B, Lx, C = x.shape
+        S = self.kv_gather.S
+        r0 = self.sp_rank * S
+        xs = x.new_zeros(B, S, C)
+        n = max(0, min(S, Lx - r0))
+        xs[:, :n] = x[:, r0:r0 + n]
+        return xs
+
+    def gather_q(self, ys):
+        """All-gather the per-shard head outputs [B, S, D] of the SP group -> [B, L, D]."""
+        B, S, D = ys.shape
+        full = torch.empty(self.sp_size, B, S, D, dtype=ys.dtype, device=ys.device)
+        dist.all_gather_into_tensor(full, ys.contiguous(), group=self.sp_group)
+        return full.permute(1, 0, 2, 3).reshape(B, self.sp_size * S, D)[:, :self.seq_len]
+
     def __call__(self, latent, t):
         if self.context is None:
             raise RuntimeError("call set_context() first")
         e, e0 = self.time_embed(t)
         x = self.patch(latent)
+        if self.kv_gather is not None:
+            xs = self.forward_blocks(self.shard_q(x), e0)
+            return self.combine(self.gather_q(self.head_tokens(xs, e, self.sp_rank * self.kv_gather.S)))
         if self.sp:
             x = self.unshard(self.forward_blocks(self.shard(x), e0))
         else:

@@ -86,10 +86,12 @@ def _p(t):
 
 
 def _set_frames(p, frames):
-    """frames = (seq_len, tokens_per_frame[, row_offset]): row r belongs to latent frame
-    ((r + row_offset) % seq_len) // tokens_per_frame."""
+    """frames = (seq_len, tokens_per_frame[, row_offset[, rows_per_seq]]): row r holds token
+    t = (r % rows_per_seq if rows_per_seq else r) + row_offset of its sequence and belongs to
+    latent frame (t % seq_len) // tokens_per_frame."""
     p.seq_len, p.tokens_per_frame = frames[0], frames[1]
     p.row_offset = frames[2] if len(frames) > 2 else 0
+    p.rows_per_seq = frames[3] if len(frames) > 3 else 0
 
 
 def _rows(t: torch.Tensor, name: str):
@@ -283,12 +285,41 @@ def bias_gate_residual(residual, y, bias, gate=None, frames=None, out=None, nsum
     return out
 
 
+class _OnDevice:
+    """Stands in for a tensor in `_launch` where an op has none: only `.device` is read."""
+
+    def __init__(self, device):
+        self.device = torch.device(device)
+
+
 def peer_barrier(flag_ptrs, rank, epoch, device):
     """Barrier of the TP group over NVLink peer memory (include/wanb200.h, wanb200_peer_barrier)."""
     arr = (ctypes.c_void_p * len(flag_ptrs))(*flag_ptrs)
     lib = L.load()
     st = torch.cuda.current_stream(device).cuda_stream
-    L.check(lib.wanb200_peer_barrier(arr, rank, len(flag_ptrs), epoch, st), "wanb200_peer_barrier")
+    L.check(_launch(_OnDevice(device), "peer_barrier", 0.0,
+                    lambda: lib.wanb200_peer_barrier(arr, rank, len(flag_ptrs), epoch, st)), "wanb200_peer_barrier")
+
+
+def shard_gather(src, batch, shard_rows, valid_rows, dst_ptrs, dst_ld, dst_batch_stride, dst_row0, device):
+    """Push this rank's shard rows into every gathered buffer (include/wanb200.h,
+    wanb200_shard_gather).  src: [batch * shard_rows, width] bf16 view with unit column stride
+    (e.g. the k|v columns of the QKV buffer); dst_ptrs: device addresses of the gathered buffers
+    (peer-mapped), all with row stride dst_ld and batch stride dst_batch_stride elements."""
+    _cuda(src)
+    _need(src.dtype == BF16, "shard_gather: src must be bf16")
+    _need(src.shape[0] >= batch * shard_rows, "shard_gather: src has fewer than batch * shard_rows rows")
+    p = L.ShardGatherParams()
+    p.src, p.src_ld = src.data_ptr(), _rows(src, "src")
+    p.batch, p.shard_rows, p.valid_rows, p.width = batch, shard_rows, valid_rows, src.shape[1]
+    for i, ptr in enumerate(dst_ptrs):
+        p.dst[i] = ptr
+    p.ndst = len(dst_ptrs)
+    p.dst_ld, p.dst_batch_stride, p.dst_row0 = dst_ld, dst_batch_stride, dst_row0
+    lib = L.load()
+    nbytes = 2.0 * batch * valid_rows * src.shape[1] * (1 + len(dst_ptrs))  # local read + one write per rank
+    L.check(_launch(src, "kv_gather", nbytes, lambda: lib.wanb200_shard_gather(ctypes.byref(p), _stream(src))),
+            "wanb200_shard_gather")
 
 
 # ---------------------------------------------------------------------------- torch.library ops
