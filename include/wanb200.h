@@ -76,6 +76,8 @@ typedef struct wanb200_gemm_params {
   int64_t seq_len, tokens_per_frame, row_offset, rows_per_seq; /* frame(row) for GATE_RES */
   float* rowss; int64_t ss_section; int ss_nsections; /* SUMSQ: [ss_nsections, M] fp32, pre-zeroed */
   void* peer_out[WANB200_MAX_PEERS]; int npeers; int src_rank; int64_t shard_rows; /* SCATTER */
+  int tile_n;  /* tile width along N: 0 = the library's choice (fills the SMs' last wave), else a
+                * multiple of 32 in 64..256 (for tuning; results do not depend on it) */
 } wanb200_gemm_params;
 
 int wanb200_gemm_bf16(const wanb200_gemm_params* p, void* stream);

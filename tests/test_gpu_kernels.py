@@ -78,6 +78,37 @@ def test_gemm_gate_residual(inplace):
     assert rel(out, ref) < 4e-3
 
 
+@pytest.mark.parametrize("tile_n", [64, 96, 128, 160, 192, 224, 256, 0])
+def test_gemm_tile_widths(tile_n):
+    """Every tile width along N (ragged last column tile included) gives the same product; the
+    sums of squares of sections that straddle tiles add up across tiles."""
+    M, K, Cl = 300, 192, 224
+    N = 3 * Cl  # 672: not a multiple of most tile widths
+    a, w, b = randn(M, K, seed=51), randn(N, K, scale=0.05, seed=52), randn(N, scale=0.1, seed=53)
+    ss = torch.zeros(2, M, device=DEV)
+    out = ops.linear(a, w, b, epilogue=L.EPI_BIAS_SUMSQ, rowss=ss, ss_section=Cl, ss_nsections=2, tile_n=tile_n)
+    ref = a.float() @ w.float().t() + b.float()
+    assert rel(out, ref) < 4e-3
+    ref_ss = torch.stack([ref[:, :Cl].pow(2).sum(1), ref[:, Cl:2 * Cl].pow(2).sum(1)])
+    assert rel(ss, ref_ss) < 1e-3
+
+
+def test_gemm_gate_residual_on_a_sequence_shard():
+    """rows_per_seq / row_offset: a [2, S] buffer holding tokens 40 .. 40+S-1 of each sequence."""
+    Lx, nf, S, off = 180, 6, 70, 40
+    M, N, K = 2 * S, 256, 128
+    a, w, b = randn(M, K, seed=54), randn(N, K, scale=0.05, seed=55), randn(N, scale=0.1, seed=56)
+    res = randn(M, N, seed=57)
+    mod = randn(6, N, scale=0.1, seed=58)
+    e0 = torch.randn(nf, 6, N, device=DEV) * 0.1
+    out = ops.linear(a, w, b, epilogue=L.EPI_BIAS_GATE_RES, residual=res, gate=(mod[2], e0[:, 2, :]),
+                     frames=(Lx, Lx // nf, off, S), tile_n=128)
+    frame = ((torch.arange(M, device=DEV) % S) + off) // (Lx // nf)
+    g = mod[2].float() + e0[frame, 2, :]
+    ref = res.float() + (a.float() @ w.float().t() + b.float()) * g
+    assert rel(out, ref) < 4e-3
+
+
 def test_gemm_residual():
     M, N, K = 333, 256, 128
     a, w, b, res = randn(M, K, seed=14), randn(N, K, scale=0.05, seed=15), randn(N, seed=16), randn(M, N, seed=17)
@@ -123,6 +154,16 @@ def test_attention_split_kv(B, H, Lq, Lk, splits):
     assert rel(o, ref) < 1e-2
     o1 = ops.attention(q, k, v, kv_splits=1)
     assert rel(o, o1.float()) < 1e-2
+
+
+def test_attention_split_choice():
+    """The library's split count: none for short key ranges (cross-attention over 512 keys) or
+    grids that already fill the SMs in many waves; a split for few-wave grids over long keys."""
+    lib = L.load()
+    assert lib.wanb200_attn_kv_splits(1, 24, 7854, 512) == 1     # cross-attention, batch 1
+    assert lib.wanb200_attn_kv_splits(2, 24, 7854, 7854) == 1    # config-2 self-attention
+    assert lib.wanb200_attn_kv_splits(1, 24, 1964, 7854) > 1     # Q-local shard of 4
+    assert lib.wanb200_attn_kv_splits(1, 6, 7854, 7854) > 1      # TP 4, batch 1
 
 
 def test_attention_split_kv_rejects_empty_split():

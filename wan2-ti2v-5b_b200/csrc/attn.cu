@@ -463,9 +463,10 @@ int attn_launch(const wanb200_attn_params* p, int* err, cudaStream_t st) {
 }
 
 int attn_kv_splits(int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len) {
-  // Wave-quantisation model: a CTA with all key tiles costs 1, a split one 1/s + 0.04 (its
-  // prologue / epilogue), the merge pass is ignored.  Pick s in 1..4 with the smallest
-  // makespan ceil(units*s / SMs) * cost(s); s is capped so that no split is empty.
+  // Wave-quantisation model in key-tile units: a CTA costs the key tiles of its split plus a
+  // fixed 1.5 (Q load, output epilogue) plus 2.5 when split (fp32 partial stores and the merge
+  // pass).  Pick s in 1..4 with the smallest makespan ceil(units*s / SMs) * cost(s); s is capped
+  // so that no split is empty.  Short key ranges (cross-attention over 512 keys) stay unsplit.
   const int64_t units = ((q_len + 2 * ABM - 1) / (2 * ABM)) * heads * batch;
   const int nkv = (int)((kv_len + ABN - 1) / ABN);
   const int sms = num_sms();
@@ -475,7 +476,7 @@ int attn_kv_splits(int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len) 
     const int per = (nkv + s - 1) / s;
     if ((int64_t)(s - 1) * per >= nkv) break;
     const double waves = (double)((units * s + sms - 1) / sms);
-    const double t = waves * (1.0 / s + (s > 1 ? 0.04 : 0.0));
+    const double t = waves * ((double)per + 1.5 + (s > 1 ? 2.5 : 0.0));
     if (t < best_t - 1e-9) {
       best_t = t;
       best = s;

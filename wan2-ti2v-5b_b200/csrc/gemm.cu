@@ -4,10 +4,11 @@
 // nn.Linear weights [out, in]): fused QKV (3072 -> 9216), self/cross out-projection,
 // cross-q, FFN up (3072 -> 14336, GELU-tanh) and FFN down (14336 -> 3072, gate + residual).
 //
-// Tile 128 x 256 x 64, 4-stage TMA ring (48 KB / stage), fp32 accumulators in TMEM, two
-// accumulator buffers (2 x 256 columns) so the epilogue of tile t overlaps the main loop of
-// tile t+1.  One CTA per SM, tiles strided over the persistent grid, N fastest so the CTAs
-// running together share A rows and the weight matrix stays L2-resident.
+// Tile 128 x BN x 64 with BN <= 256 chosen per launch (a multiple of 32; 256 unless a narrower
+// tile fills the last wave of the persistent grid better), 4-stage TMA ring (up to 48 KB per
+// stage), fp32 accumulators in TMEM, two accumulator buffers (2 x 256 columns) so the epilogue
+// of tile t overlaps the main loop of tile t+1.  One CTA per SM, tiles strided over the
+// persistent grid in grouped order so the CTAs running together share A rows and W.
 //
 // Warp roles (192 threads):
 //   warp 0      TMA producer (one lane)
@@ -56,6 +57,7 @@ struct GemmArgs {
   __nv_bfloat16* peer_out[WANB200_MAX_PEERS];
   int npeers, src_rank;
   int64_t shard_rows;
+  int bn;  // tile width along N: multiple of 32, <= GBN
   int* err;
 };
 
@@ -76,14 +78,14 @@ __device__ __forceinline__ __nv_bfloat16* scatter_row_ptr(const GemmArgs& a, int
 // group (instead of once per row-block with a plain row-major order).
 constexpr int G_GROUP_M = 16;
 
-__device__ __forceinline__ void tile_origin(int tile, int num_m, int num_n, int& m0, int& n0) {
+__device__ __forceinline__ void tile_origin(int tile, int num_m, int num_n, int bn, int& m0, int& n0) {
   const int per_group = G_GROUP_M * num_n;
   const int g = tile / per_group;
   const int first_m = g * G_GROUP_M;
   const int gm = min(num_m - first_m, G_GROUP_M);
   const int r = tile - g * per_group;
   m0 = (first_m + r % gm) * GBM;
-  n0 = (r / gm) * GBN;
+  n0 = (r / gm) * bn;
 }
 
 template <int EPI>
@@ -207,7 +209,8 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int num_n = (args.N + GBN - 1) / GBN;
+  const int bn = args.bn;
+  const int num_n = (args.N + bn - 1) / bn;
   const int num_m = (args.M + GBM - 1) / GBM;
   const int num_tiles = num_m * num_n;
   const int kblocks = args.K / GBK;
@@ -219,14 +222,14 @@ __global__ void __launch_bounds__(192, 1)
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
         int m0, n0;
-        tile_origin(tile, num_m, num_n, m0, n0);
+        tile_origin(tile, num_m, num_n, bn, m0, n0);
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, abort_flag, err, kErrTimeoutGemmProducer)) {
             ok = false;
             break;
           }
           const uint32_t a_dst = tiles + stage * G_STAGE_BYTES;
-          mbar_expect_tx(full0 + 8 * stage, G_STAGE_BYTES);
+          mbar_expect_tx(full0 + 8 * stage, G_A_BYTES + bn * GBK * 2);
           tma_load_2d(a_dst, &tmA, full0 + 8 * stage, kb * GBK, m0);
           tma_load_2d(a_dst + G_A_BYTES, &tmB, full0 + 8 * stage, kb * GBK, n0);
           issued |= 1u << stage;
@@ -244,7 +247,7 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(GBM, GBN, false, false);
+      const uint32_t idesc = idesc_bf16_f32(GBM, bn, false, false);
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
@@ -289,7 +292,7 @@ __global__ void __launch_bounds__(192, 1)
       if (!mbar_wait_warp(tfull0 + 8 * acc, acc_phase, abort_flag, err, kErrTimeoutGemmEpilogue)) break;
       tc_fence_after();
       int m0, n0;
-      tile_origin(tile, num_m, num_n, m0, n0);
+      tile_origin(tile, num_m, num_n, bn, m0, n0);
       const int row = m0 + r;
       const uint32_t t_row = tmem_base + (uint32_t(quad * 32) << 16) + acc * GBN;
       float ss_acc = 0.f;
@@ -298,7 +301,7 @@ __global__ void __launch_bounds__(192, 1)
         // stage this warp's 32 rows (lane = row), then write each row as one 512-byte segment
         constexpr int SR = GemmCfg<EPI>::STAGING_ROW;
         uint8_t* stg = smem + GemmCfg<EPI>::TILES + quad * 32 * SR;
-        const int ncols = min(GBN, args.N - n0);  // multiple of 32
+        const int ncols = min(bn, args.N - n0);  // multiple of 32
 #pragma unroll 1
         for (int c = 0; c < ncols / 32; ++c) {
           float v[32];
@@ -320,7 +323,7 @@ __global__ void __launch_bounds__(192, 1)
         __syncwarp();
       } else {
 #pragma unroll 1
-        for (int c = 0; c < GBN / 32; ++c) {
+        for (int c = 0; c < bn / 32; ++c) {
           const int col0 = n0 + c * 32;
           if (col0 >= args.N) break;  // warp-uniform
           float v[32];
@@ -363,6 +366,25 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmA
   return WANB200_OK;
 }
 
+// Tile width along N for a launch: the candidate (multiples of 32 from 256 down to 128) with the
+// smallest makespan waves * (BN + c), waves = ceil(tiles / SMs) over the persistent grid.  c
+// stands for the per-tile cost that does not shrink with BN (the A tile loads, the accumulator
+// hand-off); it keeps BN at 256 unless a narrower tile removes a mostly empty last wave.
+static int choose_tile_n(int64_t M, int64_t N, int sms) {
+  const int64_t num_m = (M + GBM - 1) / GBM;
+  int best = GBN;
+  double best_t = 1e300;
+  for (int bn = GBN; bn >= 128; bn -= 32) {
+    const int64_t tiles = num_m * ((N + bn - 1) / bn);
+    const double t = (double)((tiles + sms - 1) / sms) * (bn + 64.0);
+    if (t < best_t - 1e-9) {
+      best_t = t;
+      best = bn;
+    }
+  }
+  return best;
+}
+
 int gemm_bf16(const wanb200_gemm_params* p, cudaStream_t st) {
   if (!p) return set_error(WANB200_EINVAL, "gemm: null params");
   const int epi = p->epilogue;
@@ -399,6 +421,8 @@ int gemm_bf16(const wanb200_gemm_params* p, cudaStream_t st) {
       return set_error(WANB200_EINVAL, "gemm: gate epilogue needs gate_mod, gate_e0, seq_len, tokens_per_frame "
                                        "(row_offset, rows_per_seq >= 0)");
   }
+  if (p->tile_n != 0 && (p->tile_n < 64 || p->tile_n > GBN || p->tile_n % 32))
+    return set_error(WANB200_EINVAL, "gemm: tile_n must be 0 (library's choice) or a multiple of 32 in 64..256");
   if (epi == WANB200_EPI_BIAS_SUMSQ) {
     if (!p->rowss || p->ss_section <= 0 || (p->ss_section % 32) || p->ss_nsections <= 0 || p->ss_section > INT32_MAX)
       return set_error(WANB200_EINVAL, "gemm: sumsq epilogue needs rowss and a section width that is a multiple of 32");
@@ -406,10 +430,12 @@ int gemm_bf16(const wanb200_gemm_params* p, cudaStream_t st) {
 
   int* err = device_error_word();
   if (!err) return WANB200_ECUDA;
+  const int sms = num_sms();
+  const int bn = p->tile_n ? p->tile_n : choose_tile_n(p->M, p->N, sms);
   CUtensorMap ta, tb;
   int rc = make_tmap_2d(&ta, p->a, p->K, p->M, p->lda, GBK, GBM);
   if (rc) return rc;
-  rc = make_tmap_2d(&tb, p->w, p->K, p->N, p->ldw, GBK, GBN);
+  rc = make_tmap_2d(&tb, p->w, p->K, p->N, p->ldw, GBK, bn);
   if (rc) return rc;
 
   GemmArgs ga;
@@ -436,10 +462,11 @@ int gemm_bf16(const wanb200_gemm_params* p, cudaStream_t st) {
   ga.npeers = p->npeers;
   ga.src_rank = p->src_rank;
   ga.shard_rows = p->shard_rows > 0 ? p->shard_rows : 1;
+  ga.bn = bn;
   ga.err = err;
 
-  const int64_t tiles = ((p->M + GBM - 1) / GBM) * ((p->N + GBN - 1) / GBN);
-  const int grid = (int)std::min<int64_t>(tiles, num_sms());
+  const int64_t tiles = ((p->M + GBM - 1) / GBM) * ((p->N + bn - 1) / bn);
+  const int grid = (int)std::min<int64_t>(tiles, sms);
   switch (epi) {
     case WANB200_EPI_NONE: return launch_gemm<WANB200_EPI_NONE>(ta, tb, ga, grid, st);
     case WANB200_EPI_BIAS: return launch_gemm<WANB200_EPI_BIAS>(ta, tb, ga, grid, st);

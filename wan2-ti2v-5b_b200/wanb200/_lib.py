@@ -28,7 +28,7 @@ class GemmParams(ctypes.Structure):
                 ("tokens_per_frame", c_int64), ("row_offset", c_int64), ("rows_per_seq", c_int64), ("rowss", c_void_p),
                 ("ss_section", c_int64),
                 ("ss_nsections", c_int), ("peer_out", c_void_p * 8), ("npeers", c_int), ("src_rank", c_int),
-                ("shard_rows", c_int64)]
+                ("shard_rows", c_int64), ("tile_n", c_int)]
 
 
 class AttnParams(ctypes.Structure):

@@ -52,9 +52,8 @@ def bench_gemm(a):
     if epi == L.EPI_BIAS_SUMSQ:
         kw["rowss"] = torch.zeros(2, a.M, device=dev)
         kw["ss_section"], kw["ss_nsections"] = a.N // 3, 2
-    ms = _time(lambda: ops.linear(x, w, b if epi else None, epilogue=epi, out=out, **kw), a.iters)
-    L.check(0, "")
-    return {"kernel": "gemm", "M": a.M, "N": a.N, "K": a.K, "epi": a.epi, "ms": ms,
+    ms = _time(lambda: ops.linear(x, w, b if epi else None, epilogue=epi, out=out, tile_n=a.tile_n, **kw), a.iters)
+    return {"kernel": "gemm", "M": a.M, "N": a.N, "K": a.K, "epi": a.epi, "tile_n": a.tile_n, "ms": ms,
             "tflops": 2 * a.M * a.N * a.K / ms / 1e9}
 
 
@@ -93,6 +92,7 @@ def main():
     ap.add_argument("--Lq", type=int, default=7854)
     ap.add_argument("--Lk", type=int, default=7854)
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--tile-n", type=int, default=0, help="gemm tile width along N (0 = the library's choice)")
     a = ap.parse_args()
     torch.cuda.set_device(0)
     r = {"gemm": bench_gemm, "attn": bench_attn, "ln": bench_ln}[a.kind](a)

@@ -101,8 +101,10 @@ def _rows(t: torch.Tensor, name: str):
 
 # ---------------------------------------------------------------------------- GEMM
 def linear(a, w, bias=None, *, epilogue=L.EPI_BIAS, out=None, residual=None, gate=None, frames=None,
-           rowss=None, ss_section=0, ss_nsections=0, kind="gemm", scatter=None):
+           rowss=None, ss_section=0, ss_nsections=0, kind="gemm", scatter=None, tile_n=0):
     """out[M, N] = epilogue(a[M, K] @ w[N, K]^T) on tcgen05 (see include/wanb200.h).
+
+    tile_n: width of the output tile along N (0 = the library's choice; 64..256, multiple of 32).
 
     gate: (gate_mod [N] bf16, gate_e0 [F, N] fp32 view with unit column stride) for EPI_BIAS_GATE_RES.
     frames: (seq_len, tokens_per_frame) mapping a row to its latent frame.
@@ -120,6 +122,7 @@ def linear(a, w, bias=None, *, epilogue=L.EPI_BIAS, out=None, residual=None, gat
     p = L.GemmParams()
     p.a, p.lda, p.w, p.ldw, p.d, p.ldd = _p(a), lda, _p(w), ldw, _p(out), ldd
     p.M, p.N, p.K, p.epilogue = M, N, K, epilogue
+    p.tile_n = tile_n
     p.bias = _p(bias)
     if residual is not None:
         p.residual, p.ldr = _p(residual), _rows(residual, "residual")
