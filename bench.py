@@ -1,14 +1,17 @@
 #!/usr/bin/env python
 """Benchmark of the north-star path: seconds per 30-layer DiT denoise step of Wan2.2-TI2V-5B at
-7854 tokens (latent grid 21x17x22, 704x544x81 video) with batched CFG (batch 2), on N B200s
-of one node (TP = N by heads; N = 1 runs the whole step on one GPU).
+7854 tokens (latent grid 21x17x22, 704x544x81 video) with CFG (cond + uncond), on N B200s of
+one node.  N = 1 runs the whole step (batch 2) on one GPU; N > 1 uses --layout (default: CFG
+groups of N/2 GPUs with Q-local sequence parallelism inside, see wanb200.parallel).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--layout L]
     torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1)
 
 Prints one JSON line on rank 0.  `value` is device time per step (CUDA events, inputs resident
-in HBM, max over ranks); `e2e` is the same step through the public `FastWanDiT.__call__` with
-the latent copied from pinned host memory and the noise prediction copied back every step.
+in HBM, max over ranks, no per-launch instrumentation); `kernels` and `roofline` come from a
+second pass over the same steps with a CUDA-event pair around every launch; `e2e` is the same
+step through the public `FastWanDiT.__call__` with the latent copied from pinned host memory
+and the noise prediction copied back every step.
 Weights are seeded N(0, 0.02) bf16 with the TI2V-5B shapes, the text context is seeded, so
 `data` is synthetic.  `--impl reference` times the CPU oracle (the reference's fp32 block math,
 ref_fp32.block_fwd restated in oracle/dit_ref.py) on this host's cores instead.
@@ -228,9 +231,7 @@ def run_ours(args):
         fast(latent_dev, T_STEP)
     barrier()
 
-    # ---- device-timed steps (inputs resident), per-kernel events inside the timed region
-    timer = ops.KernelTimer()
-    ops.set_timer(timer)
+    # ---- device-timed steps (inputs resident), no per-launch events in this region
     clocks = ClockSampler(local)
     clocks.start()
     launches0 = ops.launch_count
@@ -242,9 +243,18 @@ def run_ours(args):
     t1.record(stream)
     barrier()
     launches = ops.launch_count - launches0
-    ops.set_timer(None)
     step_s = max_over_ranks(t0.elapsed_time(t1) / 1e3 / args.steps, world, device)
     clk = clocks.stop()
+
+    # ---- the same steps again with a CUDA-event pair around every launch (on its stream): the
+    # per-kernel times of the roofline and the breakdown
+    timer = ops.KernelTimer()
+    ops.set_timer(timer)
+    barrier()
+    for _ in range(args.steps):
+        out = fast(latent_dev, T_STEP)
+    barrier()
+    ops.set_timer(None)
     kern = timer.summary()
 
     # ---- end to end through the public call: pinned H2D of the latent, D2H of the prediction
@@ -295,7 +305,7 @@ def run_ours(args):
     roof["launches"] = n
     roof["ms_per_launch"] = ms / n
     roof["work_per_launch"] = work / n
-    tr = NCU_TRAFFIC_PER_LAUNCH.get(dom)
+    tr = NCU_TRAFFIC_PER_LAUNCH.get(dom) if world == 1 else None  # captured on the 1-GPU launch shapes
     roof["traffic"] = tr[0] if tr else None
     if tr:
         roof["traffic_note"] = tr[1]
@@ -351,7 +361,7 @@ def main():
                     help="N>1: tp = TP over all N ranks (batched CFG); cfg = CFG-parallel groups of N/2 "
                          "(token-sharded TP inside each); sp = Q-local sequence parallelism over all N ranks "
                          "(batched CFG, K/V all-gather); cfgsp = CFG-parallel groups of N/2 with Q-local SP "
-                         "inside; cfgsptp = CFG-parallel groups of SP2 x TP(N/4); auto = cfg for even N")
+                         "inside; cfgsptp = CFG-parallel groups of SP2 x TP(N/4); auto = cfgsp for even N, else sp")
     ap.add_argument("--layers", type=int, default=30, help="blocks per step (30 for the bench line)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

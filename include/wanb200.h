@@ -103,6 +103,14 @@ typedef struct wanb200_attn_params {
    * (workspace, wanb200_attn_workspace_bytes() bytes) that a merge kernel combines.  0 or 1 =
    * no split; wanb200_attn_kv_splits() gives the split count the library would pick. */
   int kv_splits; void* workspace; int64_t workspace_bytes;
+  /* partial slots, for one attention over a key set given in pieces (e.g. the keys of this rank
+   * while the other ranks' keys are still in flight, then those): with part_nslots > 0 this
+   * launch's kv_splits splits write unnormalised partials into slots part_slot0 .. part_slot0 +
+   * kv_splits - 1 of a workspace of wanb200_attn_workspace_bytes(batch, heads, q_len,
+   * part_nslots) bytes, and unless defer_combine != 0 the merge of slots 0 .. part_nslots - 1
+   * into o follows.  Every slot must have been written (by this or an earlier launch on the
+   * stream over the same q) before the merging launch.  0, 0, 0 = the whole key set here. */
+  int part_slot0, part_nslots, defer_combine;
 } wanb200_attn_params;
 
 int wanb200_attn_fwd(const wanb200_attn_params* p, void* stream);
@@ -198,18 +206,19 @@ int wanb200_peer_barrier(int* const* flags, int rank, int world, int epoch, void
  * The K/V all-gather of sequence-parallel self-attention: `WanSelfAttentionSP.forward`
  * (models/dit_attention_sp.py:88-99) all-gathers the normed, rotated k and v of every rank's
  * query shard over the attn-sp group (`ps.all_gather_into_tensor`, parallel_state.py) so each
- * rank attends its own queries to all keys.  Here the owner of a shard stores it into every
- * rank's gathered buffer over NVLink: row i < valid_rows of batch element b of the shard,
- * src + (b * shard_rows + i) * src_ld (width bf16), goes to
- * dst[p] + b * dst_batch_stride + (dst_row0 + i) * dst_ld for every p < ndst (peer-mapped
- * buffers, this rank's own included; rows >= valid_rows are the padding of the last shard and
- * are not sent).  Every rank calls wanb200_peer_barrier before it reads the gathered rows.
+ * rank attends its own queries to all keys.  Here the owner of a shard stores it into the
+ * gathered buffers of the other ranks over NVLink: row i < valid_rows of batch element b of
+ * the shard, src + (b * shard_rows + i) * src_ld (width bf16), goes to
+ * dst[p] + b * dst_batch_stride + (dst_row0[p] + i) * dst_ld for every p < ndst (peer-mapped
+ * buffers; each destination places the shard at its own row; rows >= valid_rows are the padding
+ * of the last shard and are not sent).  Every rank calls wanb200_peer_barrier before it reads
+ * the gathered rows.
  * Limits: width % 8 == 0, src_ld, dst_ld, dst_batch_stride % 8 == 0, 16-byte aligned pointers. */
 typedef struct wanb200_shard_gather_params {
   const void* src; int64_t src_ld;
   int64_t batch, shard_rows, valid_rows, width;
   void* dst[WANB200_MAX_PEERS]; int ndst;
-  int64_t dst_ld, dst_batch_stride, dst_row0;
+  int64_t dst_ld, dst_batch_stride, dst_row0[WANB200_MAX_PEERS];
 } wanb200_shard_gather_params;
 
 int wanb200_shard_gather(const wanb200_shard_gather_params* p, void* stream);

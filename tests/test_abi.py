@@ -147,7 +147,7 @@ def test_frame_index_and_shard_gather_reject_bad_args_on_host():
     assert rc == -1 and "rows_per_seq" in msg
     g = L.ShardGatherParams()
     g.src, g.src_ld, g.batch, g.shard_rows, g.valid_rows, g.width = 64, 256, 2, 10, 10, 256
-    g.dst[0], g.ndst, g.dst_ld, g.dst_batch_stride, g.dst_row0 = 128, 1, 256, 256 * 40, 0
+    g.dst[0], g.ndst, g.dst_ld, g.dst_batch_stride = 128, 1, 256, 256 * 40
     g.valid_rows = 11  # more valid rows than the shard holds
     rc, msg = _rc_msg(lib.wanb200_shard_gather, g)
     assert rc == -1 and "valid_rows" in msg

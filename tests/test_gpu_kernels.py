@@ -166,6 +166,19 @@ def test_attention_split_choice():
     assert lib.wanb200_attn_kv_splits(1, 6, 7854, 7854) > 1      # TP 4, batch 1
 
 
+@pytest.mark.parametrize("cut,s1,s2", [(600, 1, 2), (1, 1, 1), (1499, 2, 1)])
+def test_attention_key_set_in_pieces(cut, s1, s2):
+    """Partial slots: the keys [0, cut) and [cut, Lk) in two launches that share a workspace,
+    the second merging all slots, equal one attention over all keys."""
+    B, H, Lq, Lk = 2, 3, 700, 1500
+    q, k, v = randn(B, Lq, H, 128, seed=61), randn(B, Lk, H, 128, seed=62), randn(B, Lk, H, 128, seed=63)
+    o = torch.empty_like(q)
+    n = s1 + s2
+    ops.attention(q, k[:, :cut], v[:, :cut], out=o, kv_splits=s1, parts=(0, n, True))
+    ops.attention(q, k[:, cut:], v[:, cut:], out=o, kv_splits=s2, parts=(s1, n, False))
+    assert rel(o, sdpa_ref(q, k, v)) < 1e-2
+
+
 def test_attention_split_kv_rejects_empty_split():
     q = randn(1, 128, 1, 128, seed=44)
     k = randn(1, 300, 1, 128, seed=45)  # 3 key tiles

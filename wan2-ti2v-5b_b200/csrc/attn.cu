@@ -53,8 +53,11 @@ struct AttnArgs {
   // [split * kv_tiles_per_split, ...); with kv_splits > 1 it writes its unnormalised O and
   // (running max, row sum) to o_part / ml_part and attn_combine_kernel merges the splits.
   int kv_splits, kv_tiles_per_split;
-  float* o_part;   // [kv_splits, B*H*Lq, 128]
-  float* ml_part;  // [kv_splits, B*H*Lq, 2]
+  // partial slots: with part_nslots > 1 split s writes slot part_slot0 + s and the merge reads
+  // slots 0 .. part_nslots-1 (several launches over different key sets may fill one workspace)
+  int part_slot0, part_nslots;
+  float* o_part;   // [part_nslots, B*H*Lq, 128]
+  float* ml_part;  // [part_nslots, B*H*Lq, 2]
   int64_t part_rows;  // B*H*Lq
   int* err;
 };
@@ -288,11 +291,12 @@ __global__ void __launch_bounds__(A_THREADS, 1)
       if (lane == 0) mbar_arrive(p_full + 8 * t);
     }
     if (ok) ok = mbar_wait_warp(o_done + 8 * t, 0, abort_flag, err, kErrTimeoutAttnSoftmax);
-    if (ok && args.kv_splits > 1) {
+    if (ok && args.part_nslots > 1) {
       // partial result of this key range: unnormalised O, running max (log2 units), row sum
       tc_fence_after();
       const int qrow = q0 + t * ABM + r;
-      const int64_t prow = (int64_t)split * args.part_rows + ((int64_t)b * args.heads + h) * args.Lq + qrow;
+      const int64_t prow =
+          (int64_t)(args.part_slot0 + split) * args.part_rows + ((int64_t)b * args.heads + h) * args.Lq + qrow;
       float4* dst = reinterpret_cast<float4*>(args.o_part + prow * AD);
 #pragma unroll
       for (int c = 0; c < AD / 32; ++c) {
@@ -345,10 +349,10 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const AttnArgs a) {
   const int64_t bh = w / a.Lq;
   const int h = (int)(bh % a.heads), b = (int)(bh / a.heads);
   float m = -INFINITY;
-  for (int s = 0; s < a.kv_splits; ++s) m = fmaxf(m, a.ml_part[(s * a.part_rows + w) * 2]);
+  for (int s = 0; s < a.part_nslots; ++s) m = fmaxf(m, a.ml_part[(s * a.part_rows + w) * 2]);
   float l = 0.f;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int s = 0; s < a.kv_splits; ++s) {
+  for (int s = 0; s < a.part_nslots; ++s) {
     const float2 ml = *reinterpret_cast<const float2*>(a.ml_part + (s * a.part_rows + w) * 2);
     const float wgt = ex2_approx(ml.x - m);
     l = fmaf(wgt, ml.y, l);
@@ -399,9 +403,18 @@ int attn_fwd(const wanb200_attn_params* p, cudaStream_t st) {
   const int per = (nkv + p->kv_splits - 1) / p->kv_splits;
   if ((int64_t)(p->kv_splits - 1) * per >= nkv)
     return set_error(WANB200_EINVAL, "attn: kv_splits leaves a split without key tiles (use attn_kv_splits)");
-  const int64_t need = attn_workspace_bytes(p->batch, p->heads, p->q_len, p->kv_splits);
+  if (pp.part_nslots == 0) {
+    if (pp.part_slot0 != 0 || pp.defer_combine != 0)
+      return set_error(WANB200_EINVAL, "attn: part_slot0 / defer_combine need part_nslots > 0");
+    pp.part_nslots = pp.kv_splits;
+  } else if (pp.part_nslots < 1 || pp.part_nslots > 64 || pp.part_slot0 < 0 ||
+             pp.part_slot0 + pp.kv_splits > pp.part_nslots) {
+    return set_error(WANB200_EINVAL, "attn: need 0 <= part_slot0 and part_slot0 + kv_splits <= part_nslots <= 64");
+  }
+  const int64_t need = attn_workspace_bytes(p->batch, p->heads, p->q_len, pp.part_nslots);
   if (need > 0 && (!p->workspace || !aligned16(p->workspace) || p->workspace_bytes < need))
-    return set_error(WANB200_EINVAL, "attn: kv_splits > 1 needs a 16-byte aligned workspace of wanb200_attn_workspace_bytes()");
+    return set_error(WANB200_EINVAL, "attn: partial slots (kv_splits or part_nslots > 1) need a 16-byte aligned "
+                                     "workspace of wanb200_attn_workspace_bytes(.., part_nslots)");
   int* err = device_error_word();
   if (!err) return WANB200_ECUDA;
   return attn_launch(p, err, st);
@@ -435,9 +448,11 @@ int attn_launch(const wanb200_attn_params* p, int* err, cudaStream_t st) {
   aa.scale_log2 = p->softmax_scale * 1.4426950408889634f;
   aa.kv_splits = p->kv_splits;
   aa.kv_tiles_per_split = (int)(((p->kv_len + ABN - 1) / ABN + p->kv_splits - 1) / p->kv_splits);
+  aa.part_slot0 = p->part_slot0;
+  aa.part_nslots = p->part_nslots > 0 ? p->part_nslots : p->kv_splits;
   aa.part_rows = p->batch * p->heads * p->q_len;
   aa.o_part = reinterpret_cast<float*>(p->workspace);
-  aa.ml_part = aa.o_part ? aa.o_part + (int64_t)p->kv_splits * aa.part_rows * AD : nullptr;
+  aa.ml_part = aa.o_part ? aa.o_part + (int64_t)aa.part_nslots * aa.part_rows * AD : nullptr;
   aa.err = err;
 
   static bool attr_set[kMaxDevices] = {};
@@ -454,7 +469,7 @@ int attn_launch(const wanb200_attn_params* p, int* err, cudaStream_t st) {
   attn_fwd_kernel<<<grid, A_THREADS, A_SMEM_BYTES, st>>>(tq, tk, tv, aa);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error("attn_fwd_kernel launch", e);
-  if (p->kv_splits > 1) {
+  if (aa.part_nslots > 1 && !p->defer_combine) {
     attn_combine_kernel<<<(unsigned)((aa.part_rows + 7) / 8), 256, 0, st>>>(aa);
     e = cudaGetLastError();
     if (e != cudaSuccess) return set_cuda_error("attn_combine_kernel launch", e);
@@ -560,6 +575,9 @@ int attn_fwd_noalloc(const wanb200_attn_params* p, cudaStream_t st) {
     return set_error(WANB200_EINVAL, "attn_noalloc: q/k/v/o must be 16-byte aligned");
   if (!(p->softmax_scale > 0.f)) return set_error(WANB200_EINVAL, "attn_noalloc: softmax_scale must be positive");
   wanb200_attn_params pp = *p;
+  if (pp.part_slot0 || pp.part_nslots || pp.defer_combine)
+    return set_error(WANB200_EINVAL, "attn_noalloc: partial slots (part_slot0, part_nslots, defer_combine) need "
+                                     "wanb200_attn_fwd and a caller workspace");
   if (pp.kv_splits == 0) pp.kv_splits = 1;
   if (pp.kv_splits < 1 || pp.kv_splits > 64) return set_error(WANB200_EINVAL, "attn_noalloc: kv_splits must be 0..64");
   const int nkv = (int)((pp.kv_len + ABN - 1) / ABN);

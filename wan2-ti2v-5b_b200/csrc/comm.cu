@@ -79,7 +79,8 @@ struct GatherArgs {
   int64_t src_ld, shard_rows, valid_rows, rows;  // rows = batch * valid_rows
   int vecs;                                     // 16-byte vectors per row (width / 8)
   __nv_bfloat16* dst[WANB200_MAX_PEERS];
-  int64_t dst_ld, dst_batch_stride, dst_row0;
+  int64_t dst_row0[WANB200_MAX_PEERS];
+  int64_t dst_ld, dst_batch_stride;
 };
 
 // One warp per (row, destination): blockIdx.y picks the destination, the warp's row is one of
@@ -91,11 +92,15 @@ __global__ void __launch_bounds__(256) shard_gather_kernel(const GatherArgs a) {
   const int lane = threadIdx.x & 31;
   const int64_t b = r / a.valid_rows, i = r - b * a.valid_rows;
   __nv_bfloat16* dst = a.dst[0];
+  int64_t row0 = a.dst_row0[0];
 #pragma unroll
   for (int k = 1; k < WANB200_MAX_PEERS; ++k)
-    if ((int)blockIdx.y == k) dst = a.dst[k];
+    if ((int)blockIdx.y == k) {
+      dst = a.dst[k];
+      row0 = a.dst_row0[k];
+    }
   const uint4* s = reinterpret_cast<const uint4*>(a.src + (b * a.shard_rows + i) * a.src_ld);
-  uint4* d = reinterpret_cast<uint4*>(dst + b * a.dst_batch_stride + (a.dst_row0 + i) * a.dst_ld);
+  uint4* d = reinterpret_cast<uint4*>(dst + b * a.dst_batch_stride + (row0 + i) * a.dst_ld);
   int v = lane;
   for (; v + 96 < a.vecs; v += 128) {
     const uint4 x0 = s[v], x1 = s[v + 32], x2 = s[v + 64], x3 = s[v + 96];
@@ -110,16 +115,20 @@ __global__ void __launch_bounds__(256) shard_gather_kernel(const GatherArgs a) {
 int shard_gather(const wanb200_shard_gather_params* p, cudaStream_t st) {
   if (!p || !p->src || p->batch <= 0 || p->shard_rows <= 0 || p->valid_rows < 0 || p->valid_rows > p->shard_rows ||
       p->width <= 0 || p->width % 8 || p->src_ld < p->width || p->src_ld % 8 || p->dst_ld < p->width || p->dst_ld % 8 ||
-      p->dst_batch_stride % 8 || p->dst_row0 < 0 || p->ndst < 1 || p->ndst > WANB200_MAX_PEERS)
+      p->dst_batch_stride % 8 || p->ndst < 1 || p->ndst > WANB200_MAX_PEERS)
     return set_error(WANB200_EINVAL, "shard_gather: need src, batch > 0, 0 <= valid_rows <= shard_rows, width % 8 == 0, "
                                      "src_ld/dst_ld >= width and % 8 == 0, dst_batch_stride % 8 == 0, "
-                                     "dst_row0 >= 0, 1 <= ndst <= 8");
-  if (p->batch > 1 && p->dst_batch_stride < (p->dst_row0 + p->valid_rows) * p->dst_ld)
-    return set_error(WANB200_EINVAL, "shard_gather: dst_batch_stride smaller than the rows of one batch element");
+                                     "1 <= ndst <= 8");
+  for (int k = 0; k < p->ndst; ++k) {
+    if (p->dst_row0[k] < 0) return set_error(WANB200_EINVAL, "shard_gather: dst_row0 must be >= 0");
+    if (p->batch > 1 && p->dst_batch_stride < (p->dst_row0[k] + p->valid_rows) * p->dst_ld)
+      return set_error(WANB200_EINVAL, "shard_gather: dst_batch_stride smaller than the rows of one batch element");
+  }
   if (!aligned16(p->src)) return set_error(WANB200_EINVAL, "shard_gather: src must be 16-byte aligned");
   GatherArgs a;
   for (int k = 0; k < WANB200_MAX_PEERS; ++k) {
     a.dst[k] = reinterpret_cast<__nv_bfloat16*>(k < p->ndst ? p->dst[k] : p->dst[0]);
+    a.dst_row0[k] = k < p->ndst ? p->dst_row0[k] : p->dst_row0[0];
     if (k < p->ndst && (!p->dst[k] || !aligned16(p->dst[k])))
       return set_error(WANB200_EINVAL, "shard_gather: destinations must be non-null and 16-byte aligned");
   }
@@ -132,7 +141,6 @@ int shard_gather(const wanb200_shard_gather_params* p, cudaStream_t st) {
   a.vecs = (int)(p->width / 8);
   a.dst_ld = p->dst_ld;
   a.dst_batch_stride = p->dst_batch_stride;
-  a.dst_row0 = p->dst_row0;
   const int64_t blocks = (a.rows + 7) / 8;
   if (blocks > INT32_MAX || p->width / 8 > INT32_MAX) return set_error(WANB200_EINVAL, "shard_gather: too large");
   shard_gather_kernel<<<dim3((unsigned)blocks, (unsigned)p->ndst), 256, 0, st>>>(a);

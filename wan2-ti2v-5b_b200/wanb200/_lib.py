@@ -38,7 +38,7 @@ class AttnParams(ctypes.Structure):
                 ("o", c_void_p), ("o_tok_stride", c_int64), ("o_batch_stride", c_int64),
                 ("batch", c_int64), ("heads", c_int64), ("q_len", c_int64), ("kv_len", c_int64),
                 ("head_dim", c_int64), ("softmax_scale", c_float), ("kv_splits", c_int), ("workspace", c_void_p),
-                ("workspace_bytes", c_int64)]
+                ("workspace_bytes", c_int64), ("part_slot0", c_int), ("part_nslots", c_int), ("defer_combine", c_int)]
 
 
 class LnParams(ctypes.Structure):
@@ -68,7 +68,7 @@ class ResidualParams(ctypes.Structure):
 class ShardGatherParams(ctypes.Structure):
     _fields_ = [("src", c_void_p), ("src_ld", c_int64), ("batch", c_int64), ("shard_rows", c_int64),
                 ("valid_rows", c_int64), ("width", c_int64), ("dst", c_void_p * 8), ("ndst", c_int),
-                ("dst_ld", c_int64), ("dst_batch_stride", c_int64), ("dst_row0", c_int64)]
+                ("dst_ld", c_int64), ("dst_batch_stride", c_int64), ("dst_row0", c_int64 * 8)]
 
 
 EXPORTS = ("wanb200_gemm_bf16", "wanb200_attn_fwd", "wanb200_layernorm", "wanb200_qk_norm_rope",

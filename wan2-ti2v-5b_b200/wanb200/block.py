@@ -128,14 +128,33 @@ class FastBlock:
         ops.qk_norm_rope(ws.qkv, [(0, ws.ss[0], w.g_q), (Cl, ws.ss[1], w.g_k)], Cl, C, eps=self.eps,
                          cos=cos2, sin=sin2, seq_len=Lx)
         q = ws.qkv[:, :Cl].view(B, Lx, nl, 128)
+        y = ws.y.view(B, Lx, nl, 128)
         if sp is None:
             k = ws.qkv[:, Cl:2 * Cl].view(B, Lx, nl, 128)
             v = ws.qkv[:, 2 * Cl:].view(B, Lx, nl, 128)
-        else:  # Q-local: this shard's queries against the whole sequence's keys
+            ops.attention(q, k, v, out=y, kind="attn_self")
+        elif sp.overlapped:
+            # Q-local: the other ranks' K/V cross NVLink while this shard's queries attend the
+            # shard's own keys; the remote keys follow and the partials of both are merged
+            sp.start(ws.qkv[:, Cl:])
+            n_loc, n_rem = sp.valid, sp.remote_len
+            s_loc = ops.kv_splits(B, nl, Lx, n_loc) if n_loc else 0
+            s_rem = ops.kv_splits(B, nl, Lx, n_rem) if n_rem else 0
+            n = s_loc + s_rem
+            if n_loc:
+                k = ws.qkv[:, Cl:2 * Cl].view(B, Lx, nl, 128)[:, :n_loc]
+                v = ws.qkv[:, 2 * Cl:].view(B, Lx, nl, 128)[:, :n_loc]
+                ops.attention(q, k, v, out=y, kind="attn_self", kv_splits=s_loc, parts=(0, n, n_rem > 0))
+            kv = sp.finish()
+            if n_rem:
+                k = kv[:, :, :Cl].unflatten(2, (nl, 128))
+                v = kv[:, :, Cl:].unflatten(2, (nl, 128))
+                ops.attention(q, k, v, out=y, kind="attn_self", kv_splits=s_rem, parts=(s_loc, n, False))
+        else:  # Q-local over NCCL: gather the whole sequence's keys, then one attention
             kv = sp.gather(ws.qkv[:, Cl:])[:, :L_seq]
             k = kv[:, :, :Cl].unflatten(2, (nl, 128))
             v = kv[:, :, Cl:].unflatten(2, (nl, 128))
-        ops.attention(q, k, v, out=ws.y.view(B, Lx, nl, 128), kind="attn_self")
+            ops.attention(q, k, v, out=y, kind="attn_self")
         x1 = torch.empty_like(xf)
         gate2 = (mod[2], e0[:, 2, :])
         if self.tp:
@@ -179,8 +198,8 @@ class FastBlock:
     @property
     def launches(self) -> int:
         n = 13 if not self.tp else 16
-        if self.sp is not None and self.sp.comm == "peer":
-            n += 2  # shard gather + peer barrier
+        if self.sp is not None and self.sp.overlapped:
+            n += 3  # shard gather + peer barrier + the second attention piece
         return n
 
 

@@ -161,9 +161,17 @@ def _workspace(device, nbytes):
     return ws
 
 
-def attention(q, k, v, out=None, softmax_scale=None, kind="attn", kv_splits=None):
+def kv_splits(batch, heads, q_len, kv_len) -> int:
+    """The library's split-KV count for an attention of this shape (wanb200_attn_kv_splits)."""
+    return L.load().wanb200_attn_kv_splits(batch, heads, q_len, kv_len)
+
+
+def attention(q, k, v, out=None, softmax_scale=None, kind="attn", kv_splits=None, parts=None):
     """o = softmax(q k^T * scale) v on [B, L, H, 128] tensors (head stride 128, unit d stride).
-    kv_splits: None = the library's choice for the grid size, 1 = no split."""
+    kv_splits: None = the library's choice for the grid size, 1 = no split.
+    parts: (slot0, nslots, defer_combine) when the key set comes in pieces: this launch writes
+    partial slots slot0.. of a workspace of nslots slots, and merges all of them into `out`
+    unless defer_combine (wanb200_attn_params)."""
     _cuda(q, k, v, out)
     for name, t in (("q", q), ("k", k), ("v", v)):
         _need(t.dtype == BF16 and t.dim() == 4 and t.shape[-1] == 128 and t.stride(3) == 1 and t.stride(2) == 128,
@@ -183,8 +191,12 @@ def attention(q, k, v, out=None, softmax_scale=None, kind="attn", kv_splits=None
     lib = L.load()
     splits = kv_splits if kv_splits is not None else lib.wanb200_attn_kv_splits(B, H, Lq, k.shape[1])
     p.kv_splits = splits
-    if splits > 1:
-        nbytes = lib.wanb200_attn_workspace_bytes(B, H, Lq, splits)
+    slots = splits
+    if parts is not None:
+        p.part_slot0, p.part_nslots, p.defer_combine = parts[0], parts[1], int(bool(parts[2]))
+        slots = parts[1]
+    if slots > 1:
+        nbytes = lib.wanb200_attn_workspace_bytes(B, H, Lq, slots)
         p.workspace, p.workspace_bytes = _workspace(q.device, nbytes).data_ptr(), nbytes
     flops = 4.0 * B * H * Lq * k.shape[1] * D
     L.check(_launch(q, kind, flops, lambda: lib.wanb200_attn_fwd(ctypes.byref(p), _stream(q))), "wanb200_attn_fwd")
@@ -304,11 +316,12 @@ def peer_barrier(flag_ptrs, rank, epoch, device):
                     lambda: lib.wanb200_peer_barrier(arr, rank, len(flag_ptrs), epoch, st)), "wanb200_peer_barrier")
 
 
-def shard_gather(src, batch, shard_rows, valid_rows, dst_ptrs, dst_ld, dst_batch_stride, dst_row0, device):
-    """Push this rank's shard rows into every gathered buffer (include/wanb200.h,
+def shard_gather(src, batch, shard_rows, valid_rows, dst_ptrs, dst_ld, dst_batch_stride, dst_rows, device):
+    """Push this rank's shard rows into gathered buffers (include/wanb200.h,
     wanb200_shard_gather).  src: [batch * shard_rows, width] bf16 view with unit column stride
     (e.g. the k|v columns of the QKV buffer); dst_ptrs: device addresses of the gathered buffers
-    (peer-mapped), all with row stride dst_ld and batch stride dst_batch_stride elements."""
+    (peer-mapped), all with row stride dst_ld and batch stride dst_batch_stride elements;
+    dst_rows[i]: the row of dst_ptrs[i] that receives shard row 0."""
     _cuda(src)
     _need(src.dtype == BF16, "shard_gather: src must be bf16")
     _need(src.shape[0] >= batch * shard_rows, "shard_gather: src has fewer than batch * shard_rows rows")
@@ -318,7 +331,9 @@ def shard_gather(src, batch, shard_rows, valid_rows, dst_ptrs, dst_ld, dst_batch
     for i, ptr in enumerate(dst_ptrs):
         p.dst[i] = ptr
     p.ndst = len(dst_ptrs)
-    p.dst_ld, p.dst_batch_stride, p.dst_row0 = dst_ld, dst_batch_stride, dst_row0
+    p.dst_ld, p.dst_batch_stride = dst_ld, dst_batch_stride
+    for i, r in enumerate(dst_rows):
+        p.dst_row0[i] = r
     lib = L.load()
     nbytes = 2.0 * batch * valid_rows * src.shape[1] * (1 + len(dst_ptrs))  # local read + one write per rank
     L.check(_launch(src, "kv_gather", nbytes, lambda: lib.wanb200_shard_gather(ctypes.byref(p), _stream(src))),

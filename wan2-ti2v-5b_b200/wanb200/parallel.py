@@ -61,15 +61,15 @@ def _cfg_split(world: int):
 
 
 def make_layout(kind: str = "auto") -> Layout:
-    """Build the groups for `kind` (one of KINDS; "auto": "cfg" when the world size is even,
-    else "tp")."""
+    """Build the groups for `kind` (one of KINDS; "auto": "cfgsp" when the world size is even --
+    the fastest measured layout at 2, 4 and 8 B200s -- else "sp")."""
     if kind not in KINDS:
         raise ValueError(f"layout must be one of {KINDS}")
     if not dist.is_initialized() or dist.get_world_size() == 1:
         return Layout("single")
     world, rank = dist.get_world_size(), dist.get_rank()
     if kind == "auto":
-        kind = "cfg" if world % 2 == 0 else "tp"
+        kind = "cfgsp" if world % 2 == 0 else "sp"
     if kind == "tp":
         return Layout("tp", tp_group=dist.group.WORLD, tp_size=world)
     if kind == "sp":
