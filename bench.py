@@ -349,6 +349,91 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+GRID4, LATENT4, STEPS4, SHIFT4 = (31, 22, 40), (48, 31, 44, 80), 10, 1.0
+
+
+def run_config4(args):
+    """the 10-step UniPC denoise loop at 1280x704, 121 frames (27280 tokens),
+    CFG, image frame pinned to a seeded image latent, timesteps linear from 999 (shift 1), on N
+    GPUs in --layout.  One JSON line: seconds per loop (device time, max over ranks), e2e with
+    the latent copied in and the result copied out."""
+    world, rank, local = init_dist(args.gpus)
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    torch.set_grad_enabled(False)
+    from wanb200 import FastWanDiT, TI2V_5B, random_model_state
+    from wanb200 import ops
+    from wanb200.parallel import make_layout
+    from wanb200.unipc import denoise
+    from wanb200.dit import block_flops
+
+    spec = TI2V_5B
+    sd = random_model_state(spec, seed=0, device=device, num_layers=args.layers)
+    lay = make_layout(args.layout)
+    fast = FastWanDiT((spec, sd), GRID4, GUIDE, device, cfg_group=lay.cfg_group, pair_group=lay.pair_group,
+                      tp_group=lay.tp_group, num_layers=args.layers, comm=args.comm, sp_group=lay.sp_group)
+    del sd
+    g = torch.Generator(device=device).manual_seed(123)
+    fast.set_context(torch.randn(CTX_LEN, TEXT_DIM, generator=g, device=device),
+                     torch.randn(CTX_LEN, TEXT_DIM, generator=g, device=device))
+    gh = torch.Generator().manual_seed(0)
+    latent_host = torch.randn(LATENT4, generator=gh).pin_memory()
+    image_host = torch.randn((LATENT4[0], 1) + LATENT4[2:], generator=gh).pin_memory()
+    latent_dev, image_dev = latent_host.to(device), image_host.to(device)
+    out_host = torch.empty(LATENT4, dtype=torch.float32).pin_memory()
+    stream = torch.cuda.current_stream(device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(device)
+
+    for _ in range(args.warmup):
+        fast(latent_dev, 999.0)
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    launches0 = ops.launch_count
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.loops):
+        out = denoise(fast, latent_dev, STEPS4, SHIFT4, image_dev)
+    t1.record(stream)
+    barrier()
+    launches = ops.launch_count - launches0
+    loop_s = max_over_ranks(t0.elapsed_time(t1) / 1e3 / args.loops, world, device)
+    clk = clocks.stop()
+    assert torch.isfinite(out).all()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    lat = latent_host.to(device, non_blocking=True)
+    img = image_host.to(device, non_blocking=True)
+    out = denoise(fast, lat, STEPS4, SHIFT4, img)
+    out_host.copy_(out, non_blocking=True)
+    e1.record(stream)
+    barrier()
+    e2e_s = max_over_ranks(e0.elapsed_time(e1) / 1e3, world, device)
+    if rank == 0:
+        L4 = GRID4[0] * GRID4[1] * GRID4[2]
+        fl = block_flops(CFG_BATCH * L4, L4)
+        loop_flops = STEPS4 * args.layers * sum(fl.values())
+        print(json.dumps({
+            "metric": "s per 10-step UniPC denoise loop @27280 tok CFG=2 (BASELINE config 4)", "value": loop_s,
+            "unit": "s/loop", "s_per_step": loop_s / STEPS4, "n_gpus": world, "loops": args.loops,
+            "warmup": args.warmup, "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) bf16 weights, seeded latent / image latent / context)",
+            "config": {"workload": f"config4: {args.layers}-layer Wan2.2-TI2V-5B DiT, 27280 tokens (31x22x40), CFG, "
+                                   f"{STEPS4}-step UniPC (shift {SHIFT4}), image frame pinned",
+                       "parallelism": lay.describe(world), "seq_len": L4, "layers": args.layers},
+            "e2e": {"value": e2e_s, "unit": "s/loop", "h2d_bytes_per_loop": (latent_host.numel() + image_host.numel()) * 4,
+                    "d2h_bytes_per_loop": out_host.numel() * 4},
+            "gpu_launches": launches, "loop_tflops": loop_flops / loop_s / 1e12, "clocks": clk}), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -364,11 +449,17 @@ def main():
                          "inside; cfgsptp = CFG-parallel groups of SP2 x TP(N/4); auto = cfgsp for even N, else sp")
     ap.add_argument("--layers", type=int, default=30, help="blocks per step (30 for the bench line)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="config2", choices=["config2", "config4"],
+                    help="config2: the bench line (s/step at 7854 tokens); config4: one line for BASELINE "
+                         "config 4, the 10-step UniPC loop at 27280 tokens (--loops loops timed)")
+    ap.add_argument("--loops", type=int, default=1, help="config4: denoise loops in the timed region")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "config4":
+        run_config4(args)
     else:
         run_ours(args)
 

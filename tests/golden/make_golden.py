@@ -17,7 +17,11 @@ and records:
     plus the reference's bf16 `WanAttentionBlock.forward` and bf16 `_FastBlock.forward`
     outputs on the same inputs (calibration of the reference's own bf16 error);
   * rope_small.pt -- `fast_dit._rope_tables` for small grids and strided rows of the three
-    BASELINE grids, and `fast_dit._rope` on a random tensor.
+    BASELINE grids, and `fast_dit._rope` on a random tensor;
+  * unipc_small.pt -- the reference's sampler, `FlowUniPCMultistepScheduler`
+    (wan/utils/fm_solvers_unipc.py) constructed and stepped as inference_neuron_ti2v.py:497-532
+    does, on seeded latents and model outputs (fp32 and bf16; shift 5 and 1; 10 and 3 steps).
+    `--unipc-only` regenerates just this file.
 
 The GPU box never runs this script (the reference is not there); the fixtures travel.
 """
@@ -31,7 +35,8 @@ import torch
 import torch.nn as nn
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("WAN_REF_ROOT", "/root/reference")
+_ARGS = [a for a in sys.argv[1:] if not a.startswith("--")]
+REF = _ARGS[0] if _ARGS else os.environ.get("WAN_REF_ROOT", "/root/reference")
 
 DIM, FFN, HEADS, LAYERS, TEXT_DIM, FREQ_DIM, IN_DIM, LC = 256, 512, 2, 2, 64, 256, 48, 16
 GRID_LATENT = (2, 6, 8)  # latent [48, F, H, W] -> token grid (2, 3, 4), L = 24
@@ -172,5 +177,83 @@ def main():
         print(f, os.path.getsize(os.path.join(HERE, f)))
 
 
+def import_reference_scheduler():
+    """FlowUniPCMultistepScheduler with a `diffusers` stub for its base classes: the config
+    decorator records the constructor arguments as `self.config`, as diffusers' does."""
+    import functools
+    import inspect
+    cu = types.ModuleType("diffusers.configuration_utils")
+
+    class ConfigMixin:
+        def register_to_config(self, **kw):
+            for k, v in kw.items():
+                setattr(self.config, k, v)
+
+    def register_to_config(init):
+        sig = inspect.signature(init)
+
+        @functools.wraps(init)
+        def wrapper(self, *args, **kwargs):
+            bound = sig.bind(self, *args, **kwargs)
+            bound.apply_defaults()
+            cfg = dict(bound.arguments)
+            cfg.pop("self")
+            self.config = types.SimpleNamespace(**cfg)
+            init(self, *args, **kwargs)
+        return wrapper
+
+    cu.ConfigMixin, cu.register_to_config = ConfigMixin, register_to_config
+    su = types.ModuleType("diffusers.schedulers.scheduling_utils")
+    su.KarrasDiffusionSchedulers = []
+    su.SchedulerMixin = type("SchedulerMixin", (), {})
+    su.SchedulerOutput = lambda prev_sample: types.SimpleNamespace(prev_sample=prev_sample)
+    du = types.ModuleType("diffusers.utils")
+    du.deprecate = lambda *a, **k: None
+    du.is_scipy_available = lambda: False
+    saved = {k: sys.modules.get(k) for k in ("diffusers", "diffusers.configuration_utils", "diffusers.schedulers",
+                                              "diffusers.schedulers.scheduling_utils", "diffusers.utils")}
+    sys.modules.update({"diffusers": types.ModuleType("diffusers"), "diffusers.configuration_utils": cu,
+                        "diffusers.schedulers": types.ModuleType("diffusers.schedulers"),
+                        "diffusers.schedulers.scheduling_utils": su, "diffusers.utils": du})
+    try:
+        spec = importlib.util.spec_from_file_location("ref_fm_solvers_unipc",
+                                                      os.path.join(REF, "wan/utils/fm_solvers_unipc.py"))
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+    finally:
+        for k, v in saved.items():
+            if v is None:
+                sys.modules.pop(k, None)
+            else:
+                sys.modules[k] = v
+    return mod.FlowUniPCMultistepScheduler
+
+
+def unipc_golden():
+    Sched = import_reference_scheduler()
+    cases = []
+    for dtype, shift, steps in ((torch.float32, 5.0, 10), (torch.float32, 1.0, 10), (torch.bfloat16, 5.0, 10),
+                                (torch.float32, 5.0, 3)):
+        s = Sched(num_train_timesteps=1000, shift=1, use_dynamic_shifting=False)
+        s.set_timesteps(steps, device=torch.device("cpu"), shift=shift)
+        g = torch.Generator().manual_seed(len(cases))
+        shape = (1, 48, 2, 4, 6)
+        x = torch.randn(shape, generator=g).to(dtype)
+        x_init, outs, mos = x.clone(), [], []
+        for i, t in enumerate(s.timesteps):
+            mo = (torch.randn(shape, generator=g) * 0.7 + 0.1 * i).to(dtype)
+            x = s.step(mo, t, x, return_dict=False)[0]
+            mos.append(mo)
+            outs.append(x.clone())
+        cases.append({"dtype": str(dtype), "shift": shift, "steps": steps, "timesteps": s.timesteps.clone(),
+                      "sigmas": s.sigmas.clone(), "x_init": x_init, "model_outputs": mos, "outputs": outs})
+    torch.save({"cases": cases}, os.path.join(HERE, "unipc_small.pt"))
+    print("unipc_small.pt", os.path.getsize(os.path.join(HERE, "unipc_small.pt")))
+
+
 if __name__ == "__main__":
-    main()
+    if "--unipc-only" in sys.argv:
+        unipc_golden()
+    else:
+        main()
+        unipc_golden()
