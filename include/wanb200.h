@@ -129,6 +129,21 @@ int wanb200_attn_fwd(const wanb200_attn_params* p, void* stream);
  * wanb200_device_error() when another entry point has already created it on this device. */
 int wanb200_attn_fwd_noalloc(const wanb200_attn_params* p, void* stream);
 int64_t wanb200_attn_workspace_bytes(int64_t batch, int64_t heads, int64_t q_len, int kv_splits);
+
+/* FP8 (e4m3) variant of the attention (no counterpart in the reference, whose trn2 runs never
+ * used FP8).  Takes the same bf16 q, k, v, o and options; inside, q and k are quantised with one
+ * scale per (batch, head, 128-token block) and v with one per (batch, head) (scale = amax / 448,
+ * round to nearest, saturating), the scores and P @ V run as kind::f8f6f4 tcgen05 MMAs with
+ * P in e4m3, and the scales are folded into the exponent and the output.  Results differ from
+ * the bf16 path by the e4m3 rounding (about 2-3% relative RMS).  fp8_workspace holds the e4m3
+ * operands and scales: wanb200_attn_fp8_workspace_bytes() bytes, 256-byte aligned. */
+typedef struct wanb200_attn_fp8_params {
+  wanb200_attn_params attn;
+  void* fp8_workspace; int64_t fp8_workspace_bytes;
+} wanb200_attn_fp8_params;
+
+int wanb200_attn_fwd_fp8(const wanb200_attn_fp8_params* p, void* stream);
+int64_t wanb200_attn_fp8_workspace_bytes(int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len);
 int wanb200_attn_kv_splits(int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len);
 
 /* ---------------------------------------------------------------- LayerNorm (+ modulation)
@@ -230,7 +245,7 @@ const char* wanb200_last_error(void);
 int wanb200_device_error(int reset);
 /* Library version, e.g. 100 for 0.1.0. */
 int wanb200_version(void);
-/* sizeof of the parameter structs in declaration order (gemm, attn, ln, qknorm, residual, shard_gather)
+/* sizeof of the parameter structs (gemm, attn, ln, qknorm, residual, shard_gather, attn_fp8)
  * written to out[0..n); returns the number of structs.  Lets a binding detect a library built
  * from a different header. */
 int wanb200_struct_sizes(int64_t* out, int n);

@@ -36,6 +36,7 @@ STRUCTS = {
     "wanb200_qknorm_params": L.QkNormParams,
     "wanb200_residual_params": L.ResidualParams,
     "wanb200_shard_gather_params": L.ShardGatherParams,
+    "wanb200_attn_fp8_params": L.AttnFp8Params,
 }
 
 

@@ -109,3 +109,41 @@ def test_block_is_deterministic_and_functional():
     assert torch.equal(xd, x0), "the block must not modify its input"
     # Σx² uses fp32 atomics, so runs may differ in the last bits of the norm scale
     assert R.rel_rms(y1.float(), y2.float()) < 1e-3
+
+
+def test_block_with_fp8_attention_config0():
+    """BASELINE config 3's optional FP8 variant at the block level: self-attention in e4m3
+    (per-block scales) against the fp32 oracle and against the bf16 device block.  The output
+    stays within the block tolerance; the attention's e4m3 rounding shows in the update."""
+    grid = (6, 12, 15)
+    spec, sd, x, e0, context = _config0_inputs(L_grid=grid)
+    cos, sin = R.rope_tables(R.model_freqs(128), grid, 128)
+    p32 = fp32(sd)
+    ck, cv = R.cross_kv(p32, context, spec.num_heads)
+    y_ref = R.block_fwd(p32, x, e0, cos, sin, ck, cv, grid[0], spec.num_heads)
+    w = BlockWeights(sd, spec.num_heads, DEV)
+    ckd, cvd = FastCrossKV(w)(context.to(DEV, torch.bfloat16))
+    cosd, sind = rope_tables(grid, 128, DEV)
+    xd = x.to(DEV, torch.bfloat16)
+    y8 = FastBlock(w, grid[0], attn_fp8=True)(xd, e0.to(DEV), cosd, sind, ckd, cvd).float().cpu()
+    y16 = FastBlock(w, grid[0])(xd, e0.to(DEV), cosd, sind, ckd, cvd).float().cpu()
+    err, upd = R.rel_rms(y8, y_ref), R.rel_rms(y8 - x, y_ref - x)
+    upd16 = R.rel_rms(y16 - x, y_ref - x)
+    print(f"config0 block, fp8 self-attention: output {err:.2e}, update {upd:.2e} (bf16 update {upd16:.2e})")
+    assert err < BLOCK_TOL
+    assert upd < 1e-1
+
+
+def test_step_with_fp8_attention_matches_reference_golden():
+    mg = torch.load(os.path.join(GOLD, "model_small.pt"), weights_only=False)
+    cfg = mg["cfg"]
+    spec = WanSpec(dim=cfg["dim"], ffn_dim=cfg["ffn_dim"], num_heads=cfg["num_heads"], num_layers=cfg["num_layers"],
+                   freq_dim=cfg["freq_dim"], text_dim=cfg["text_dim"], in_dim=cfg["in_dim"], out_dim=cfg["out_dim"],
+                   text_len=cfg["text_len"])
+    lat = mg["latent"]
+    grid = (lat.shape[1], lat.shape[2] // 2, lat.shape[3] // 2)
+    fast = FastWanDiT((spec, mg["state_dict"]), grid, mg["guide"], DEV, attn_fp8=True)
+    fast.set_context(mg["ctx"].to(DEV), mg["ctx_null"].to(DEV))
+    err = R.rel_rms(fast(lat.to(DEV), mg["t"]).float().cpu(), mg["noise_pred"])
+    print(f"golden step with fp8 self-attention: rel-RMS {err:.3e}")
+    assert err < STEP_TOL

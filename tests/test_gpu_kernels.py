@@ -179,6 +179,41 @@ def test_attention_key_set_in_pieces(cut, s1, s2):
     assert rel(o, sdpa_ref(q, k, v)) < 1e-2
 
 
+@pytest.mark.parametrize("B,H,Lq,Lk,splits", [(1, 2, 128, 128, 1), (2, 3, 300, 1080, None), (1, 2, 127, 129, 1),
+                                              (2, 2, 1000, 512, 1), (1, 6, 1000, 2100, 3), (1, 1, 129, 4100, 2)])
+def test_attention_fp8_vs_sdpa_and_bf16(B, H, Lq, Lk, splits):
+    """The e4m3 variant (q, k per 128-token-block scales, v per head, P in e4m3) against fp32
+    SDPA: within the e4m3 rounding (3 mantissa bits), far above the bf16 path's error but
+    averaged over the keys; ragged q / k tails and split-KV included."""
+    q, k, v = randn(B, Lq, H, 128, seed=71), randn(B, Lk, H, 128, seed=72), randn(B, Lk, H, 128, seed=73)
+    ref = sdpa_ref(q, k, v)
+    o8 = ops.attention(q, k, v, kv_splits=splits, fp8=True)
+    o16 = ops.attention(q, k, v, kv_splits=splits)
+    e8, e16 = rel(o8, ref), rel(o16, ref)
+    print(f"fp8 rel-RMS {e8:.4f} (bf16 {e16:.4f})")
+    assert e8 < 6e-2
+    assert e16 < 1e-2
+
+
+def test_attention_fp8_scaled_inputs():
+    """Per-block scales: q blocks of magnitude 1..64 and k blocks of 1..1/8 (softmax kept as flat
+    as in the other cases) give the same accuracy as unscaled inputs; and scaling q by 64 and k
+    by 1/32 with the softmax scale compensated gives the same e4m3 codes, so the same result."""
+    B, H, L = 1, 2, 512
+    q, k, v = randn(B, L, H, 128, seed=74), randn(B, L, H, 128, seed=75), randn(B, L, H, 128, seed=76)
+    mag = torch.tensor([1.0, 4.0, 16.0, 64.0], device=DEV).repeat_interleave(128)[None, :, None, None]
+    qs = (q.float() * mag).to(torch.bfloat16)
+    ks = (k.float() / mag.flip(1).sqrt()).to(torch.bfloat16)
+    sc = 1.0 / (64.0 * math.sqrt(128.0))
+    err = rel(ops.attention(qs, ks, v, softmax_scale=sc, fp8=True), sdpa_ref(qs, ks, v, scale=sc))
+    print(f"fp8 rel-RMS with block magnitudes 1..64: {err:.4f}")
+    assert err < 6e-2
+    o = ops.attention(q, k, v, softmax_scale=0.1, fp8=True)
+    o2 = ops.attention((q.float() * 64).to(torch.bfloat16), (k.float() / 32).to(torch.bfloat16), v,
+                       softmax_scale=0.1 / 2, fp8=True)
+    assert rel(o2, o.float()) < 1e-3
+
+
 def test_attention_split_kv_rejects_empty_split():
     q = randn(1, 128, 1, 128, seed=44)
     k = randn(1, 300, 1, 128, seed=45)  # 3 key tiles

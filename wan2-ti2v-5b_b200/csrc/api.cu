@@ -90,11 +90,11 @@ static EncodeTiledFn encode_fn() {
 }
 
 static int encode(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides_bytes,
-                  const cuuint32_t* box) {
+                  const cuuint32_t* box, CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return set_error(WANB200_ECUDA, "cuTensorMapEncodeTiled entry point unavailable");
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, const_cast<void*>(base), dims, strides_bytes,
+  CUresult r = fn(m, dtype, (cuuint32_t)rank, const_cast<void*>(base), dims, strides_bytes,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
@@ -119,6 +119,14 @@ int make_tmap_4d(CUtensorMap* m, const void* base, const int64_t dims[4], const 
   return encode(m, base, 4, d, s, b);
 }
 
+int make_tmap_4d_u8(CUtensorMap* m, const void* base, const int64_t dims[4], const int64_t strides[4],
+                    const int box[4]) {
+  const cuuint64_t d[4] = {(cuuint64_t)dims[0], (cuuint64_t)dims[1], (cuuint64_t)dims[2], (cuuint64_t)dims[3]};
+  const cuuint64_t s[3] = {(cuuint64_t)strides[1], (cuuint64_t)strides[2], (cuuint64_t)strides[3]};
+  const cuuint32_t b[4] = {(cuuint32_t)box[0], (cuuint32_t)box[1], (cuuint32_t)box[2], (cuuint32_t)box[3]};
+  return encode(m, base, 4, d, s, b, CU_TENSOR_MAP_DATA_TYPE_UINT8);
+}
+
 }  // namespace wanb200
 
 using namespace wanb200;
@@ -135,6 +143,14 @@ int wanb200_attn_fwd(const wanb200_attn_params* p, void* stream) {
 
 int wanb200_attn_fwd_noalloc(const wanb200_attn_params* p, void* stream) {
   return attn_fwd_noalloc(p, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int wanb200_attn_fwd_fp8(const wanb200_attn_fp8_params* p, void* stream) {
+  return attn_fwd_fp8(p, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int64_t wanb200_attn_fp8_workspace_bytes(int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len) {
+  return attn_fp8_workspace_bytes(batch, heads, q_len, kv_len);
 }
 
 int64_t wanb200_attn_workspace_bytes(int64_t batch, int64_t heads, int64_t q_len, int kv_splits) {
@@ -185,11 +201,12 @@ int wanb200_device_error(int reset) {
 int wanb200_version(void) { return 100; }
 
 int wanb200_struct_sizes(int64_t* out, int n) {
-  const int64_t sizes[6] = {(int64_t)sizeof(wanb200_gemm_params), (int64_t)sizeof(wanb200_attn_params),
+  const int64_t sizes[7] = {(int64_t)sizeof(wanb200_gemm_params), (int64_t)sizeof(wanb200_attn_params),
                             (int64_t)sizeof(wanb200_ln_params), (int64_t)sizeof(wanb200_qknorm_params),
-                            (int64_t)sizeof(wanb200_residual_params), (int64_t)sizeof(wanb200_shard_gather_params)};
-  for (int i = 0; i < n && i < 6; ++i) out[i] = sizes[i];
-  return 6;
+                            (int64_t)sizeof(wanb200_residual_params), (int64_t)sizeof(wanb200_shard_gather_params),
+                            (int64_t)sizeof(wanb200_attn_fp8_params)};
+  for (int i = 0; i < n && i < 7; ++i) out[i] = sizes[i];
+  return 7;
 }
 
 }  // extern "C"

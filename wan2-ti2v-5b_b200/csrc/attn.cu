@@ -40,6 +40,10 @@ constexpr int A_OFF_P = A_OFF_Q + 2 * A_TILE;   // P_0, P_1
 constexpr int A_OFF_R = A_OFF_P + 2 * A_TILE;   // ring
 constexpr int A_TILES_END = A_OFF_R + A_RING * A_TILE;  // 229376
 constexpr int A_SMEM_BYTES = A_TILES_END + 256 + 1024;
+// e4m3 variant: every tile is one 16 KB swizzle block (128 rows x 128 one-byte elements)
+constexpr int A_TILES_END8 = (2 + 2 + A_RING) * A_BLK;  // 114688
+constexpr int A_SMEM_BYTES8 = A_TILES_END8 + 256 + 1024;
+constexpr float A_E4M3_MAX = 448.f;
 constexpr uint32_t A_TMEM_COLS = 512;
 constexpr int A_THREADS = 320;
 constexpr float A_RESCALE_THRESHOLD = 8.0f;  // log2 units
@@ -59,17 +63,29 @@ struct AttnArgs {
   float* o_part;   // [part_nslots, B*H*Lq, 128]
   float* ml_part;  // [part_nslots, B*H*Lq, 2]
   int64_t part_rows;  // B*H*Lq
+  // e4m3 variant: q / k dequantisation scales per (batch, head, 128-token block), v per
+  // (batch, head); nqb / nkb = blocks per (batch, head)
+  const float* q_scale;
+  const float* k_scale;
+  const float* v_scale;
+  int nqb, nkb;
   int* err;
 };
 
+// FP8: Q, K e4m3 [B, L, H, 128] and V transposed e4m3 [B, H, 128, L] (keys contiguous, so both
+// MMAs take K-major operands), P packed to e4m3; S is dequantised by the q and k block scales
+// inside the exponent's multiplier, O by the v scale at the end.
+template <bool FP8>
 __global__ void __launch_bounds__(A_THREADS, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const AttnArgs args) {
+  constexpr int TILE = FP8 ? A_BLK : A_TILE;
+  constexpr int OFF_Q = 0, OFF_P = 2 * TILE, OFF_R = 4 * TILE, TILES_END = OFF_R + A_RING * TILE;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   const uint32_t sbase = smem_u32(smem);
-  uint8_t* meta = smem + A_TILES_END;
+  uint8_t* meta = smem + TILES_END;
   const uint32_t m0 = smem_u32(meta);
   const uint32_t q_full = m0;                 // 1
   const uint32_t kv_full = m0 + 8;            // 3
@@ -122,10 +138,10 @@ __global__ void __launch_bounds__(A_THREADS, 1)
     if (lane == 0) {
       uint32_t issued = 0, last_ph = 0;
       bool ok = true;
-      mbar_expect_tx(q_full, 2 * A_TILE);
+      mbar_expect_tx(q_full, 2 * TILE);
       for (int t = 0; t < 2; ++t) {
-        tma_load_4d(sbase + A_OFF_Q + t * A_TILE, &tmQ, q_full, 0, h, q0 + t * ABM, b);
-        tma_load_4d(sbase + A_OFF_Q + t * A_TILE + A_BLK, &tmQ, q_full, 64, h, q0 + t * ABM, b);
+        tma_load_4d(sbase + OFF_Q + t * TILE, &tmQ, q_full, 0, h, q0 + t * ABM, b);
+        if constexpr (!FP8) tma_load_4d(sbase + OFF_Q + t * TILE + A_BLK, &tmQ, q_full, 64, h, q0 + t * ABM, b);
       }
       for (int i = 0; i < 2 * nkv; ++i) {
         const int slot = i % A_RING;
@@ -135,10 +151,18 @@ __global__ void __launch_bounds__(A_THREADS, 1)
           break;
         }
         const void* map = (i & 1) ? static_cast<const void*>(&tmV) : static_cast<const void*>(&tmK);
-        const uint32_t dst = sbase + A_OFF_R + slot * A_TILE;
-        mbar_expect_tx(kv_full + 8 * slot, A_TILE);
-        tma_load_4d(dst, map, kv_full + 8 * slot, 0, h, (kv0 + (i >> 1)) * ABN, b);
-        tma_load_4d(dst + A_BLK, map, kv_full + 8 * slot, 64, h, (kv0 + (i >> 1)) * ABN, b);
+        const uint32_t dst = sbase + OFF_R + slot * TILE;
+        const int key0 = (kv0 + (i >> 1)) * ABN;
+        mbar_expect_tx(kv_full + 8 * slot, TILE);
+        if constexpr (FP8) {
+          if (i & 1)
+            tma_load_4d(dst, map, kv_full + 8 * slot, key0, 0, h, b);  // V^T: (key, d, head, batch)
+          else
+            tma_load_4d(dst, map, kv_full + 8 * slot, 0, h, key0, b);
+        } else {
+          tma_load_4d(dst, map, kv_full + 8 * slot, 0, h, key0, b);
+          tma_load_4d(dst + A_BLK, map, kv_full + 8 * slot, 64, h, key0, b);
+        }
         issued |= 1u << slot;
         last_ph = (last_ph & ~(1u << slot)) | (ph << slot);
       }
@@ -151,8 +175,9 @@ __global__ void __launch_bounds__(A_THREADS, 1)
   } else if (warp == 9) {
     // ------------------------------------------------------------ UMMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc_s = idesc_bf16_f32(ABM, ABN, false, false);  // Q, K both K(=d)-major
-      constexpr uint32_t idesc_o = idesc_bf16_f32(ABM, AD, false, true);    // P K-major, V MN(=d)-major
+      // bf16: Q, K both K(=d)-major; P K-major, V MN(=d)-major.  e4m3: every operand K-major.
+      constexpr uint32_t idesc_s = FP8 ? idesc_e4m3_f32(ABM, ABN, false, false) : idesc_bf16_f32(ABM, ABN, false, false);
+      constexpr uint32_t idesc_o = FP8 ? idesc_e4m3_f32(ABM, AD, false, false) : idesc_bf16_f32(ABM, AD, false, true);
       auto kv_wait = [&](int i) -> bool {
         return mbar_wait(kv_full + 8 * (i % A_RING), (i / A_RING) & 1, abort_flag, err, kErrTimeoutAttnMma);
       };
@@ -160,12 +185,18 @@ __global__ void __launch_bounds__(A_THREADS, 1)
         const int slot = (2 * j) % A_RING;
         tc_fence_after();
         const uint32_t d = tmem_base + t * ABN;
-        const uint32_t qb = sbase + A_OFF_Q + t * A_TILE;
-        const uint32_t kb = sbase + A_OFF_R + slot * A_TILE;
+        const uint32_t qb = sbase + OFF_Q + t * TILE;
+        const uint32_t kb = sbase + OFF_R + slot * TILE;
+        if constexpr (FP8) {
 #pragma unroll
-        for (int kk = 0; kk < AD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * A_BLK + (kk & 3) * 32;
-          umma_bf16(d, sw128_desc(qb + off, 16, 1024), sw128_desc(kb + off, 16, 1024), idesc_s, kk != 0);
+          for (int kk = 0; kk < AD / 32; ++kk)  // 32 one-byte elements = 32 B per instruction
+            umma_e4m3(d, sw128_desc(qb + kk * 32, 16, 1024), sw128_desc(kb + kk * 32, 16, 1024), idesc_s, kk != 0);
+        } else {
+#pragma unroll
+          for (int kk = 0; kk < AD / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * A_BLK + (kk & 3) * 32;
+            umma_bf16(d, sw128_desc(qb + off, 16, 1024), sw128_desc(kb + off, 16, 1024), idesc_s, kk != 0);
+          }
         }
         umma_commit(s_full + 8 * t);
         if (t == 1) umma_commit(kv_empty + 8 * slot);
@@ -175,14 +206,21 @@ __global__ void __launch_bounds__(A_THREADS, 1)
         const int slot = (2 * j + 1) % A_RING;
         tc_fence_after();
         const uint32_t d = tmem_base + 2 * ABN + t * AD;
-        const uint32_t pb = sbase + A_OFF_P + t * A_TILE;
-        const uint32_t vb = sbase + A_OFF_R + slot * A_TILE;
+        const uint32_t pb = sbase + OFF_P + t * TILE;
+        const uint32_t vb = sbase + OFF_R + slot * TILE;
+        if constexpr (FP8) {
 #pragma unroll
-        for (int kk = 0; kk < ABN / 16; ++kk) {
-          const uint32_t poff = (kk >> 2) * A_BLK + (kk & 3) * 32;
-          // V tile: key row k at k*128 B inside each 64-wide d block; d blocks 16 KB apart.
-          umma_bf16(d, sw128_desc(pb + poff, 16, 1024), sw128_desc(vb + kk * 2048, A_BLK, 1024), idesc_o,
-                    (j | kk) != 0);
+          for (int kk = 0; kk < ABN / 32; ++kk)  // P (query x key) and V^T (d x key), both key-major
+            umma_e4m3(d, sw128_desc(pb + kk * 32, 16, 1024), sw128_desc(vb + kk * 32, 16, 1024), idesc_o,
+                      (j | kk) != 0);
+        } else {
+#pragma unroll
+          for (int kk = 0; kk < ABN / 16; ++kk) {
+            const uint32_t poff = (kk >> 2) * A_BLK + (kk & 3) * 32;
+            // V tile: key row k at k*128 B inside each 64-wide d block; d blocks 16 KB apart.
+            umma_bf16(d, sw128_desc(pb + poff, 16, 1024), sw128_desc(vb + kk * 2048, A_BLK, 1024), idesc_o,
+                      (j | kk) != 0);
+          }
         }
         if (t == 1) umma_commit(kv_empty + 8 * slot);
         if (j == nkv - 1) umma_commit(o_done + 8 * t);
@@ -212,8 +250,15 @@ __global__ void __launch_bounds__(A_THREADS, 1)
     const uint32_t lane_off = uint32_t((warp & 3) * 32) << 16;
     const uint32_t t_s = tmem_base + lane_off + t * ABN;
     const uint32_t t_o = tmem_base + lane_off + 2 * ABN + t * AD;
-    uint8_t* pbuf = smem + A_OFF_P + t * A_TILE;
-    const float sl2 = args.scale_log2;
+    uint8_t* pbuf = smem + OFF_P + t * TILE;
+    const float sl2_base = args.scale_log2;
+    const float* ksc = nullptr;
+    float qsc = 1.f;
+    if constexpr (FP8) {
+      // the second tile of the last pair may lie past q_len (its rows are never stored)
+      qsc = __ldg(args.q_scale + ((int64_t)b * args.heads + h) * args.nqb + min(q0 / ABM + t, args.nqb - 1));
+      ksc = args.k_scale + ((int64_t)b * args.heads + h) * args.nkb + kv0;
+    }
     float m_used = -INFINITY, l_run = 0.f;
     bool ok = true;
 
@@ -228,6 +273,8 @@ __global__ void __launch_bounds__(A_THREADS, 1)
       for (int c = 0; c < ABN / 32; ++c) tmem_ld32_nowait(t_s + c * 32, sr + c * 32);
       tmem_wait_ld();
       float* s = reinterpret_cast<float*>(sr);
+      float sl2 = sl2_base;  // e4m3: scores carry the q and k block scales
+      if constexpr (FP8) sl2 = sl2_base * qsc * __ldg(ksc + j);
       const int kbase = (kv0 + j) * ABN;
       if (kbase + ABN > args.Lk) {  // CTA-uniform: mask the key tail
 #pragma unroll
@@ -254,22 +301,46 @@ __global__ void __launch_bounds__(A_THREADS, 1)
       }
       const float neg = -m_used;
       float r8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // 8 partial row sums (short dependency chains)
+      if constexpr (FP8) {
+        // P in e4m3 (at most 2^8 under the lazy max, inside the 448 range): 32 keys = 32 bytes
+        uint8_t* rowp = pbuf + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
-      for (int c = 0; c < ABN / 32; ++c) {
-        uint32_t pk[16];
+        for (int c = 0; c < ABN / 32; ++c) {
+          uint32_t pk[8];
 #pragma unroll
-        for (int k = 0; k < 32; k += 2) {
-          const float p0 = ex2_approx(fmaf(s[c * 32 + k], sl2, neg));
-          const float p1 = ex2_approx(fmaf(s[c * 32 + k + 1], sl2, neg));
-          r8[(k >> 1) & 7] += p0 + p1;
-          pk[k >> 1] = pack_bf16x2(p0, p1);
+          for (int k = 0; k < 32; k += 4) {
+            const float p0 = ex2_approx(fmaf(s[c * 32 + k], sl2, neg));
+            const float p1 = ex2_approx(fmaf(s[c * 32 + k + 1], sl2, neg));
+            const float p2 = ex2_approx(fmaf(s[c * 32 + k + 2], sl2, neg));
+            const float p3 = ex2_approx(fmaf(s[c * 32 + k + 3], sl2, neg));
+            r8[(k >> 2) & 7] += (p0 + p1) + (p2 + p3);
+            pk[k >> 2] = pack_e4m3x2(p0, p1) | (pack_e4m3x2(p2, p3) << 16);
+          }
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const int ch = c * 2 + q;
+            *reinterpret_cast<uint4*>(rowp + ((ch ^ (r & 7)) << 4)) =
+                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          }
         }
-        uint8_t* rowp = pbuf + (c >> 1) * A_BLK + (r >> 3) * 1024 + (r & 7) * 128;
+      } else {
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int ch = (c & 1) * 4 + q;
-          *reinterpret_cast<uint4*>(rowp + ((ch ^ (r & 7)) << 4)) =
-              make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+        for (int c = 0; c < ABN / 32; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int k = 0; k < 32; k += 2) {
+            const float p0 = ex2_approx(fmaf(s[c * 32 + k], sl2, neg));
+            const float p1 = ex2_approx(fmaf(s[c * 32 + k + 1], sl2, neg));
+            r8[(k >> 1) & 7] += p0 + p1;
+            pk[k >> 1] = pack_bf16x2(p0, p1);
+          }
+          uint8_t* rowp = pbuf + (c >> 1) * A_BLK + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int ch = (c & 1) * 4 + q;
+            *reinterpret_cast<uint4*>(rowp + ((ch ^ (r & 7)) << 4)) =
+                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          }
         }
       }
       l_run += ((r8[0] + r8[1]) + (r8[2] + r8[3])) + ((r8[4] + r8[5]) + (r8[6] + r8[7]));
@@ -291,6 +362,8 @@ __global__ void __launch_bounds__(A_THREADS, 1)
       if (lane == 0) mbar_arrive(p_full + 8 * t);
     }
     if (ok) ok = mbar_wait_warp(o_done + 8 * t, 0, abort_flag, err, kErrTimeoutAttnSoftmax);
+    float vsc = 1.f;  // e4m3: O carries the v scale
+    if constexpr (FP8) vsc = __ldg(args.v_scale + (int64_t)b * args.heads + h);
     if (ok && args.part_nslots > 1) {
       // partial result of this key range: unnormalised O, running max (log2 units), row sum
       tc_fence_after();
@@ -304,14 +377,15 @@ __global__ void __launch_bounds__(A_THREADS, 1)
         tmem_ld32(t_o + c * 32, o);
         if (qrow < args.Lq) {
 #pragma unroll
-          for (int q = 0; q < 8; ++q) dst[c * 8 + q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+          for (int q = 0; q < 8; ++q)
+            dst[c * 8 + q] = make_float4(o[4 * q] * vsc, o[4 * q + 1] * vsc, o[4 * q + 2] * vsc, o[4 * q + 3] * vsc);
         }
       }
       if (qrow < args.Lq) *reinterpret_cast<float2*>(args.ml_part + prow * 2) = make_float2(m_used, l_run);
     } else if (ok) {
       tc_fence_after();
       const int qrow = q0 + t * ABM + r;
-      const float inv_l = 1.f / l_run;
+      const float inv_l = vsc / l_run;
       uint4* dst = reinterpret_cast<uint4*>(args.o + (int64_t)b * args.o_batch_stride +
                                             (int64_t)qrow * args.o_tok_stride + (int64_t)h * AD);
 #pragma unroll
@@ -375,7 +449,9 @@ int64_t attn_workspace_bytes(int64_t batch, int64_t heads, int64_t q_len, int kv
   return kv_splits > 1 ? (int64_t)kv_splits * batch * heads * q_len * (AD + 2) * 4 : 0;
 }
 
-int attn_fwd(const wanb200_attn_params* p, cudaStream_t st) {
+// Host validation shared by the bf16 and e4m3 entry points; *out = the params with the
+// defaults filled in (kv_splits 0 -> 1, part_nslots 0 -> kv_splits).
+static int attn_validate(const wanb200_attn_params* p, wanb200_attn_params* out) {
   if (!p) return set_error(WANB200_EINVAL, "attn: null params");
   if (!p->q || !p->k || !p->v || !p->o) return set_error(WANB200_EINVAL, "attn: null q/k/v/o");
   if (p->head_dim != AD) return set_error(WANB200_EINVAL, "attn: head_dim must be 128");
@@ -415,24 +491,45 @@ int attn_fwd(const wanb200_attn_params* p, cudaStream_t st) {
   if (need > 0 && (!p->workspace || !aligned16(p->workspace) || p->workspace_bytes < need))
     return set_error(WANB200_EINVAL, "attn: partial slots (kv_splits or part_nslots > 1) need a 16-byte aligned "
                                      "workspace of wanb200_attn_workspace_bytes(.., part_nslots)");
-  int* err = device_error_word();
-  if (!err) return WANB200_ECUDA;
-  return attn_launch(p, err, st);
+  *out = pp;
+  return WANB200_OK;
 }
 
-int attn_launch(const wanb200_attn_params* p, int* err, cudaStream_t st) {
+int attn_fwd(const wanb200_attn_params* p, cudaStream_t st) {
+  wanb200_attn_params pp;
+  const int rc = attn_validate(p, &pp);
+  if (rc) return rc;
+  int* err = device_error_word();
+  if (!err) return WANB200_ECUDA;
+  return attn_launch(&pp, err, st);
+}
+
+int attn_launch(const wanb200_attn_params* p, int* err, cudaStream_t st, const AttnFp8Operands* f8) {
   CUtensorMap tq, tk, tv;
   const int box[4] = {64, 1, ABM, 1};
-  {
-    const int64_t dims[4] = {AD, p->heads, p->q_len, p->batch};
-    const int64_t str[4] = {1, AD, p->q_tok_stride, p->q_batch_stride};
-    int rc = make_tmap_4d(&tq, p->q, dims, str, box);
+  if (f8) {  // e4m3 operands: one 128 x 128-byte box per tile
+    const int box8[4] = {128, 1, ABM, 1};
+    const int64_t dq[4] = {AD, p->heads, p->q_len, p->batch};
+    const int64_t sq[4] = {1, AD, p->heads * AD, p->q_len * p->heads * AD};
+    int rc = make_tmap_4d_u8(&tq, f8->q8, dq, sq, box8);
     if (rc) return rc;
-  }
-  {
+    const int64_t dk[4] = {AD, p->heads, p->kv_len, p->batch};
+    const int64_t sk[4] = {1, AD, p->heads * AD, p->kv_len * p->heads * AD};
+    rc = make_tmap_4d_u8(&tk, f8->k8, dk, sk, box8);
+    if (rc) return rc;
+    const int boxv[4] = {ABN, AD, 1, 1};
+    const int64_t dv[4] = {p->kv_len, AD, p->heads, p->batch};
+    const int64_t sv[4] = {1, f8->kv_len16, AD * f8->kv_len16, p->heads * AD * f8->kv_len16};
+    rc = make_tmap_4d_u8(&tv, f8->v8t, dv, sv, boxv);
+    if (rc) return rc;
+  } else {
+    const int64_t dq[4] = {AD, p->heads, p->q_len, p->batch};
+    const int64_t sq[4] = {1, AD, p->q_tok_stride, p->q_batch_stride};
+    int rc = make_tmap_4d(&tq, p->q, dq, sq, box);
+    if (rc) return rc;
     const int64_t dims[4] = {AD, p->heads, p->kv_len, p->batch};
     const int64_t sk[4] = {1, AD, p->k_tok_stride, p->k_batch_stride};
-    int rc = make_tmap_4d(&tk, p->k, dims, sk, box);
+    rc = make_tmap_4d(&tk, p->k, dims, sk, box);
     if (rc) return rc;
     const int64_t sv[4] = {1, AD, p->v_tok_stride, p->v_batch_stride};
     rc = make_tmap_4d(&tv, p->v, dims, sv, box);
@@ -453,20 +550,31 @@ int attn_launch(const wanb200_attn_params* p, int* err, cudaStream_t st) {
   aa.part_rows = p->batch * p->heads * p->q_len;
   aa.o_part = reinterpret_cast<float*>(p->workspace);
   aa.ml_part = aa.o_part ? aa.o_part + (int64_t)aa.part_nslots * aa.part_rows * AD : nullptr;
+  aa.q_scale = f8 ? f8->q_scale : nullptr;
+  aa.k_scale = f8 ? f8->k_scale : nullptr;
+  aa.v_scale = f8 ? f8->v_scale : nullptr;
+  aa.nqb = (int)((p->q_len + ABM - 1) / ABM);
+  aa.nkb = (int)((p->kv_len + ABN - 1) / ABN);
   aa.err = err;
 
-  static bool attr_set[kMaxDevices] = {};
+  static bool attr_set[kMaxDevices][2] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, A_SMEM_BYTES);
+  if (!attr_set[dev][f8 ? 1 : 0]) {
+    cudaError_t e = f8 ? cudaFuncSetAttribute(attn_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              A_SMEM_BYTES8)
+                       : cudaFuncSetAttribute(attn_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              A_SMEM_BYTES);
     if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(attn)", e);
-    attr_set[dev] = true;
+    attr_set[dev][f8 ? 1 : 0] = true;
   }
   const int64_t gx = ((p->q_len + 2 * ABM - 1) / (2 * ABM)) * p->kv_splits;
   if (gx > INT32_MAX) return set_error(WANB200_EINVAL, "attn: grid too large");
   dim3 grid((unsigned)gx, (unsigned)p->heads, (unsigned)p->batch);
-  attn_fwd_kernel<<<grid, A_THREADS, A_SMEM_BYTES, st>>>(tq, tk, tv, aa);
+  if (f8)
+    attn_fwd_kernel<true><<<grid, A_THREADS, A_SMEM_BYTES8, st>>>(tq, tk, tv, aa);
+  else
+    attn_fwd_kernel<false><<<grid, A_THREADS, A_SMEM_BYTES, st>>>(tq, tk, tv, aa);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error("attn_fwd_kernel launch", e);
   if (aa.part_nslots > 1 && !p->defer_combine) {
@@ -475,6 +583,222 @@ int attn_launch(const wanb200_attn_params* p, int* err, cudaStream_t st) {
     if (e != cudaSuccess) return set_cuda_error("attn_combine_kernel launch", e);
   }
   return WANB200_OK;
+}
+
+// ------------------------------------------------------------------ e4m3 operands
+// Q and K: a scale per (batch, head, 128-token block) = amax / 448 and e4m3(x / scale) in
+// [B, L, H, 128]; V: e4m3(v / scale) transposed to [B, H, 128, kv_len16] with one scale per
+// (batch, head) = amax over the head / 448 (a per-block V scale would have to be folded into
+// P, whose small entries would then underflow e4m3).
+struct QuantArgs {
+  const __nv_bfloat16* src[3];
+  int64_t tok_stride[3], batch_stride[3];
+  int len[3], nb[3];
+  uint8_t* dst[2];  // q8, k8
+  float* scale[3];  // q_scale, k_scale, v block amax
+  int heads;
+};
+
+// One CTA per (batch, head, 128-token block) of q (z % 3 == 0), k (1) or v (2, amax only);
+// thread t: token t / 2 of the block, head dims 64 * (t % 2) .. + 63.
+__global__ void __launch_bounds__(256) attn_quant_blocks_kernel(const QuantArgs a) {
+  __shared__ float red[8];
+  const int which = blockIdx.z % 3, b = blockIdx.z / 3, h = blockIdx.y, blk = blockIdx.x;
+  if (blk >= a.nb[which]) return;  // CTA-uniform
+  const int row = threadIdx.x >> 1, half = threadIdx.x & 1;
+  const int tok = blk * ABM + row;
+  const bool live = tok < a.len[which];
+  uint4 x[8];
+  float amax = 0.f;
+  if (live) {
+    const uint4* src = reinterpret_cast<const uint4*>(a.src[which] + (int64_t)b * a.batch_stride[which] +
+                                                      (int64_t)tok * a.tok_stride[which] + h * AD + half * 64);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      x[i] = src[i];
+      float f[8];
+      unpack_bf16x8(x[i], f);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) amax = fmaxf(amax, fabsf(f[k]));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  amax = red[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) amax = fmaxf(amax, red[i]);
+  if (threadIdx.x == 0)
+    a.scale[which][((int64_t)b * a.heads + h) * a.nb[which] + blk] = which == 2 ? amax : amax / A_E4M3_MAX;
+  if (which == 2 || !live) return;
+  const float inv = amax > 0.f ? A_E4M3_MAX / amax : 0.f;
+  uint32_t w[16];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float f[8];
+    unpack_bf16x8(x[i], f);
+    w[2 * i] = pack_e4m3x2(f[0] * inv, f[1] * inv) | (pack_e4m3x2(f[2] * inv, f[3] * inv) << 16);
+    w[2 * i + 1] = pack_e4m3x2(f[4] * inv, f[5] * inv) | (pack_e4m3x2(f[6] * inv, f[7] * inv) << 16);
+  }
+  uint4* dst = reinterpret_cast<uint4*>(a.dst[which] + (((int64_t)b * a.len[which] + tok) * a.heads + h) * AD +
+                                        half * 64);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+}
+
+struct VtArgs {
+  const __nv_bfloat16* v;
+  int64_t tok_stride, batch_stride, len16;
+  int len, heads, nkb;
+  const float* v_amax;
+  float* v_scale;
+  uint8_t* v8t;
+};
+
+// One CTA per (batch, head, 128-key block): e4m3 of the block with the head's scale, transposed
+// through shared memory so that each d row of V^T gets 128 consecutive keys.
+__global__ void __launch_bounds__(256) attn_quant_vt_kernel(const VtArgs a) {
+  __shared__ __align__(16) uint8_t tile[AD][ABN + 16];  // [d][key], rows padded against bank conflicts
+  __shared__ float red[8];
+  const int blk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const float* am = a.v_amax + ((int64_t)b * a.heads + h) * a.nkb;
+  float m = 0.f;
+  for (int i = threadIdx.x; i < a.nkb; i += blockDim.x) m = fmaxf(m, am[i]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  m = red[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) m = fmaxf(m, red[i]);
+  if (blk == 0 && threadIdx.x == 0) a.v_scale[(int64_t)b * a.heads + h] = m / A_E4M3_MAX;
+  const float inv = m > 0.f ? A_E4M3_MAX / m : 0.f;
+  const int key = threadIdx.x >> 1, half = threadIdx.x & 1;
+  const int tok = blk * ABN + key;
+  float f[64];
+  if (tok < a.len) {
+    const uint4* src =
+        reinterpret_cast<const uint4*>(a.v + (int64_t)b * a.batch_stride + (int64_t)tok * a.tok_stride + h * AD + half * 64);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) unpack_bf16x8(src[i], f + 8 * i);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 64; ++i) f[i] = 0.f;
+  }
+#pragma unroll
+  for (int i = 0; i < 64; i += 2) {
+    const uint32_t pr = pack_e4m3x2(f[i] * inv, f[i + 1] * inv);
+    tile[half * 64 + i][key] = (uint8_t)(pr & 0xff);
+    tile[half * 64 + i + 1][key] = (uint8_t)(pr >> 8);
+  }
+  __syncthreads();
+  // thread t: d row t / 2, keys 64 * (t % 2) .. + 63 as four 16-byte stores
+  const int d = threadIdx.x >> 1, k0 = (threadIdx.x & 1) * 64;
+  uint8_t* dst = a.v8t + (((int64_t)b * a.heads + h) * AD + d) * a.len16 + (int64_t)blk * ABN + k0;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    if ((int64_t)blk * ABN + k0 + c * 16 < a.len16)
+      *reinterpret_cast<uint4*>(dst + c * 16) = *reinterpret_cast<const uint4*>(&tile[d][k0 + c * 16]);
+  }
+}
+
+// Workspace carve-up of the e4m3 entry point (each region 256-byte aligned).
+struct Fp8Layout {
+  int64_t q8, k8, v8t, qs, ks, vam, vs, total, len16;
+  int nqb, nkb;
+};
+
+static Fp8Layout fp8_layout(int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len) {
+  auto up = [](int64_t x) { return (x + 255) / 256 * 256; };
+  Fp8Layout l;
+  l.nqb = (int)((q_len + ABM - 1) / ABM);
+  l.nkb = (int)((kv_len + ABN - 1) / ABN);
+  l.len16 = (kv_len + 15) / 16 * 16;
+  int64_t off = 0;
+  l.q8 = off;
+  off += up(batch * q_len * heads * AD);
+  l.k8 = off;
+  off += up(batch * kv_len * heads * AD);
+  l.v8t = off;
+  off += up(batch * heads * AD * l.len16);
+  l.qs = off;
+  off += up(batch * heads * l.nqb * 4);
+  l.ks = off;
+  off += up(batch * heads * l.nkb * 4);
+  l.vam = off;
+  off += up(batch * heads * l.nkb * 4);
+  l.vs = off;
+  off += up(batch * heads * 4);
+  l.total = off;
+  return l;
+}
+
+int64_t attn_fp8_workspace_bytes(int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len) {
+  if (batch <= 0 || heads <= 0 || q_len <= 0 || kv_len <= 0) return 0;
+  return fp8_layout(batch, heads, q_len, kv_len).total;
+}
+
+int attn_fwd_fp8(const wanb200_attn_fp8_params* p, cudaStream_t st) {
+  if (!p) return set_error(WANB200_EINVAL, "attn_fp8: null params");
+  wanb200_attn_params pp;
+  int rc = attn_validate(&p->attn, &pp);
+  if (rc) return rc;
+  const Fp8Layout l = fp8_layout(pp.batch, pp.heads, pp.q_len, pp.kv_len);
+  if (!p->fp8_workspace || (reinterpret_cast<uintptr_t>(p->fp8_workspace) & 255) || p->fp8_workspace_bytes < l.total)
+    return set_error(WANB200_EINVAL, "attn_fp8: needs a 256-byte aligned fp8_workspace of "
+                                     "wanb200_attn_fp8_workspace_bytes() bytes");
+  int* err = device_error_word();
+  if (!err) return WANB200_ECUDA;
+  uint8_t* ws = reinterpret_cast<uint8_t*>(p->fp8_workspace);
+  QuantArgs qa;
+  qa.src[0] = reinterpret_cast<const __nv_bfloat16*>(pp.q);
+  qa.src[1] = reinterpret_cast<const __nv_bfloat16*>(pp.k);
+  qa.src[2] = reinterpret_cast<const __nv_bfloat16*>(pp.v);
+  qa.tok_stride[0] = pp.q_tok_stride;
+  qa.tok_stride[1] = pp.k_tok_stride;
+  qa.tok_stride[2] = pp.v_tok_stride;
+  qa.batch_stride[0] = pp.q_batch_stride;
+  qa.batch_stride[1] = pp.k_batch_stride;
+  qa.batch_stride[2] = pp.v_batch_stride;
+  qa.len[0] = (int)pp.q_len;
+  qa.len[1] = qa.len[2] = (int)pp.kv_len;
+  qa.nb[0] = l.nqb;
+  qa.nb[1] = qa.nb[2] = l.nkb;
+  qa.dst[0] = ws + l.q8;
+  qa.dst[1] = ws + l.k8;
+  qa.scale[0] = reinterpret_cast<float*>(ws + l.qs);
+  qa.scale[1] = reinterpret_cast<float*>(ws + l.ks);
+  qa.scale[2] = reinterpret_cast<float*>(ws + l.vam);
+  qa.heads = (int)pp.heads;
+  if ((int64_t)pp.batch * 3 > 65535) return set_error(WANB200_EINVAL, "attn_fp8: batch too large");
+  attn_quant_blocks_kernel<<<dim3((unsigned)std::max(l.nqb, l.nkb), (unsigned)pp.heads, (unsigned)(3 * pp.batch)),
+                             256, 0, st>>>(qa);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error("attn_quant_blocks_kernel launch", e);
+  VtArgs va;
+  va.v = qa.src[2];
+  va.tok_stride = pp.v_tok_stride;
+  va.batch_stride = pp.v_batch_stride;
+  va.len16 = l.len16;
+  va.len = (int)pp.kv_len;
+  va.heads = (int)pp.heads;
+  va.nkb = l.nkb;
+  va.v_amax = qa.scale[2];
+  va.v_scale = reinterpret_cast<float*>(ws + l.vs);
+  va.v8t = ws + l.v8t;
+  attn_quant_vt_kernel<<<dim3((unsigned)l.nkb, (unsigned)pp.heads, (unsigned)pp.batch), 256, 0, st>>>(va);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error("attn_quant_vt_kernel launch", e);
+  AttnFp8Operands f8;
+  f8.q8 = ws + l.q8;
+  f8.k8 = ws + l.k8;
+  f8.v8t = ws + l.v8t;
+  f8.q_scale = qa.scale[0];
+  f8.k_scale = qa.scale[1];
+  f8.v_scale = va.v_scale;
+  f8.kv_len16 = l.len16;
+  return attn_launch(&pp, err, st, &f8);
 }
 
 int attn_kv_splits(int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len) {

@@ -164,6 +164,18 @@ __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint6
       : "memory");
 }
 
+// D(tmem) (+)= A(smem desc) * B(smem desc), fp8 e4m3 inputs (kind::f8f6f4, K = 32 per
+// instruction), fp32 accumulate; one thread issues.
+__device__ __forceinline__ void umma_e4m3(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive (once) on an mbarrier when every tcgen05 op issued so far by this thread completes.
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
@@ -229,6 +241,20 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, bool a_mn_major, bool b_mn_major) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(a_mn_major) << 15) | (uint32_t(b_mn_major) << 16) |
          (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
+}
+
+// Instruction descriptor for kind::f8f6f4 with e4m3 A and B (format code 0) and an fp32 D.
+__host__ __device__ constexpr uint32_t idesc_e4m3_f32(int M, int N, bool a_mn_major, bool b_mn_major) {
+  return (1u << 4) | (uint32_t(a_mn_major) << 15) | (uint32_t(b_mn_major) << 16) | (uint32_t(N >> 3) << 17) |
+         (uint32_t(M >> 4) << 24);
+}
+
+// Two fp32 values to two e4m3 bytes (round to nearest even, saturating at +-448): `lo` lands
+// in the low byte (the lower address), `hi` in the high byte.
+__device__ __forceinline__ uint32_t pack_e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
 }
 
 // UMMA shared-memory descriptor for a 128-byte-swizzled operand tile.

@@ -28,23 +28,38 @@ struct LnArgs {
   int64_t push_row0;
 };
 
-// One warp per row: lane l holds the 16-byte vectors at columns (i*32 + l)*8, i < dim/256.
+// RW warps per row (RW = 2 when dim % 512 == 0, else 1): thread t < 32*RW of the row holds the
+// 16-byte vectors at columns (i*32*RW + t)*8, i < NVEC = dim / (256*RW); the row statistics are
+// reduced over the row's warps through shared memory.  Two warps per row halve the registers a
+// thread holds, so twice as many rows are in flight per SM (the kernel is latency-bound).
 //   MODE 0 (modulate): WanLayerNorm without affine (wan/modules/model.py:89-99), then
 //     `_modulate` (models/fast_dit.py:172-176): y * (1 + scale[f]) + shift[f] with
 //     shift/scale[f, c] = modulation[idx, c] + e0[f, idx, c] (fast_dit.py:276-277).
 //   MODE 1 (affine): norm3 = WanLayerNorm(elementwise_affine=True) (model.py:207-209).
-template <int MODE, int NVEC, bool PUSH>
-__global__ void __launch_bounds__(256, 2) layernorm_kernel(const LnArgs a) {
+template <int MODE, int NVEC, bool PUSH, int RW>
+__global__ void __launch_bounds__(256, RW == 2 ? 3 : 2) layernorm_kernel(const LnArgs a) {
+  __shared__ float red[8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < a.zero_count;
        i += (int64_t)gridDim.x * blockDim.x)
     a.zero_buf[i] = 0.f;
-  const int64_t row = (int64_t)blockIdx.x * 8 + warp;
-  if (row >= a.rows) return;
-  const uint4* xr = reinterpret_cast<const uint4*>(a.x + row * a.dim);
+  const int64_t row = (int64_t)blockIdx.x * (8 / RW) + warp / RW;
+  const int t = (warp % RW) * 32 + lane;
+  const bool live = row < a.rows;  // dead rows still join the block's barriers
+  const uint4* xr = reinterpret_cast<const uint4*>(a.x + (live ? row : 0) * a.dim);
   uint4 xv[NVEC];  // the row stays packed (bf16) in registers: half the footprint of fp32
 #pragma unroll
-  for (int i = 0; i < NVEC; ++i) xv[i] = __ldg(xr + i * 32 + lane);
+  for (int i = 0; i < NVEC; ++i) xv[i] = live ? __ldg(xr + i * 32 * RW + t) : make_uint4(0, 0, 0, 0);
+  auto row_sum = [&](float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if constexpr (RW == 1) return v;
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    const float tot = red[warp & ~1] + red[warp | 1];
+    __syncthreads();  // red is reused by the next reduction
+    return tot;
+  };
   float sum = 0.f;
 #pragma unroll
   for (int i = 0; i < NVEC; ++i) {
@@ -53,9 +68,7 @@ __global__ void __launch_bounds__(256, 2) layernorm_kernel(const LnArgs a) {
 #pragma unroll
     for (int k = 0; k < 8; ++k) sum += x[k];
   }
-#pragma unroll
-  for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-  const float mean = sum / a.dim;
+  const float mean = row_sum(sum) / a.dim;
   float var = 0.f;
 #pragma unroll
   for (int i = 0; i < NVEC; ++i) {
@@ -67,9 +80,8 @@ __global__ void __launch_bounds__(256, 2) layernorm_kernel(const LnArgs a) {
       var = fmaf(d, d, var);
     }
   }
-#pragma unroll
-  for (int o = 16; o; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
-  const float rstd = rsqrtf(var / a.dim + a.eps);
+  const float rstd = rsqrtf(row_sum(var) / a.dim + a.eps);
+  if (!live) return;
 
   const float* shp = nullptr;
   const float* scp = nullptr;
@@ -81,52 +93,62 @@ __global__ void __launch_bounds__(256, 2) layernorm_kernel(const LnArgs a) {
   uint4* outr = a.out ? reinterpret_cast<uint4*>(a.out + row * a.dim) : nullptr;
 #pragma unroll
   for (int i = 0; i < NVEC; ++i) {
-    {
-      const int col = (i * 32 + lane) * 8;
-      float x[8], y[8];
-      unpack_bf16x8(xv[i], x);
-      if constexpr (MODE == 0) {
-        float ms[8], mc[8];
-        unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.modulation + (int64_t)a.shift_idx * a.dim + col)), ms);
-        unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.modulation + (int64_t)a.scale_idx * a.dim + col)), mc);
-        const float4 s0 = __ldg(reinterpret_cast<const float4*>(shp + col));
-        const float4 s1 = __ldg(reinterpret_cast<const float4*>(shp + col + 4));
-        const float4 c0 = __ldg(reinterpret_cast<const float4*>(scp + col));
-        const float4 c1 = __ldg(reinterpret_cast<const float4*>(scp + col + 4));
-        const float sh[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-        const float sc[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    const int v = i * 32 * RW + t;
+    const int col = v * 8;
+    float x[8], y[8];
+    unpack_bf16x8(xv[i], x);
+    if constexpr (MODE == 0) {
+      float ms[8], mc[8];
+      unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.modulation + (int64_t)a.shift_idx * a.dim + col)), ms);
+      unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.modulation + (int64_t)a.scale_idx * a.dim + col)), mc);
+      const float4 s0 = __ldg(reinterpret_cast<const float4*>(shp + col));
+      const float4 s1 = __ldg(reinterpret_cast<const float4*>(shp + col + 4));
+      const float4 c0 = __ldg(reinterpret_cast<const float4*>(scp + col));
+      const float4 c1 = __ldg(reinterpret_cast<const float4*>(scp + col + 4));
+      const float sh[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+      const float sc[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
 #pragma unroll
-        for (int k = 0; k < 8; ++k) y[k] = fmaf((x[k] - mean) * rstd, 1.f + (mc[k] + sc[k]), ms[k] + sh[k]);
-      } else {
-        float w[8], bb[8];
-        unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.weight + col)), w);
-        unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.bias + col)), bb);
+      for (int k = 0; k < 8; ++k) y[k] = fmaf((x[k] - mean) * rstd, 1.f + (mc[k] + sc[k]), ms[k] + sh[k]);
+    } else {
+      float w[8], bb[8];
+      unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.weight + col)), w);
+      unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.bias + col)), bb);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) y[k] = fmaf((x[k] - mean) * rstd, w[k], bb[k]);
-      }
-      uint4 u;
-      u.x = pack_bf16x2(y[0], y[1]);
-      u.y = pack_bf16x2(y[2], y[3]);
-      u.z = pack_bf16x2(y[4], y[5]);
-      u.w = pack_bf16x2(y[6], y[7]);
-      if (!PUSH || outr) outr[i * 32 + lane] = u;
-#pragma unroll
-      for (int p = 0; p < (PUSH ? WANB200_MAX_PEERS : 0); ++p)  // all-gather fused into the norm: push the row to every rank
-        if (p < a.npush)
-        reinterpret_cast<uint4*>(a.push_out[p] + (a.push_row0 + row) * a.dim)[i * 32 + lane] = u;
+      for (int k = 0; k < 8; ++k) y[k] = fmaf((x[k] - mean) * rstd, w[k], bb[k]);
     }
+    uint4 u;
+    u.x = pack_bf16x2(y[0], y[1]);
+    u.y = pack_bf16x2(y[2], y[3]);
+    u.z = pack_bf16x2(y[4], y[5]);
+    u.w = pack_bf16x2(y[6], y[7]);
+    if (!PUSH || outr) outr[v] = u;
+#pragma unroll
+    for (int p = 0; p < (PUSH ? WANB200_MAX_PEERS : 0); ++p)  // all-gather fused into the norm: push the row to every rank
+      if (p < a.npush) reinterpret_cast<uint4*>(a.push_out[p] + (a.push_row0 + row) * a.dim)[v] = u;
   }
 }
 
 template <int MODE, bool PUSH>
-static void launch_ln(int nvec, const LnArgs& a, unsigned blocks, cudaStream_t st) {
-  switch (nvec) {
+static void launch_ln(int dim, const LnArgs& a, int64_t rows, cudaStream_t st) {
+  if (dim % 512 == 0) {  // two warps per row, 4 rows per block
+    const unsigned blocks = (unsigned)((rows + 3) / 4);
+    switch (dim / 512) {
+#define WANB200_LN_CASE2(n) \
+  case n: layernorm_kernel<MODE, n, PUSH, 2><<<blocks, 256, 0, st>>>(a); break;
+      WANB200_LN_CASE2(1) WANB200_LN_CASE2(2) WANB200_LN_CASE2(3) WANB200_LN_CASE2(4) WANB200_LN_CASE2(5)
+      WANB200_LN_CASE2(6) WANB200_LN_CASE2(7)
+      default: layernorm_kernel<MODE, 8, PUSH, 2><<<blocks, 256, 0, st>>>(a); break;
+#undef WANB200_LN_CASE2
+    }
+    return;
+  }
+  const unsigned blocks = (unsigned)((rows + 7) / 8);
+  switch (dim / 256) {
 #define WANB200_LN_CASE(n) \
-  case n: layernorm_kernel<MODE, n, PUSH><<<blocks, 256, 0, st>>>(a); break;
-    WANB200_LN_CASE(1) WANB200_LN_CASE(2) WANB200_LN_CASE(3) WANB200_LN_CASE(4) WANB200_LN_CASE(5)
-    WANB200_LN_CASE(6) WANB200_LN_CASE(7) WANB200_LN_CASE(8) WANB200_LN_CASE(9) WANB200_LN_CASE(10)
-    WANB200_LN_CASE(11) WANB200_LN_CASE(12) WANB200_LN_CASE(13) WANB200_LN_CASE(14) WANB200_LN_CASE(15)
-    default: layernorm_kernel<MODE, 16, PUSH><<<blocks, 256, 0, st>>>(a); break;
+  case n: layernorm_kernel<MODE, n, PUSH, 1><<<blocks, 256, 0, st>>>(a); break;
+    WANB200_LN_CASE(1) WANB200_LN_CASE(3) WANB200_LN_CASE(5) WANB200_LN_CASE(7) WANB200_LN_CASE(9)
+    WANB200_LN_CASE(11) WANB200_LN_CASE(13)
+    default: layernorm_kernel<MODE, 15, PUSH, 1><<<blocks, 256, 0, st>>>(a); break;
 #undef WANB200_LN_CASE
   }
 }
@@ -179,14 +201,12 @@ int layernorm(const wanb200_ln_params* p, cudaStream_t st) {
     a.push_out[i] = reinterpret_cast<__nv_bfloat16*>(i < p->npush ? p->push_out[i] : nullptr);
   a.npush = p->npush;
   a.push_row0 = p->push_row0;
-  const int64_t blocks = (p->rows + 7) / 8;
-  if (blocks > INT32_MAX) return set_error(WANB200_EINVAL, "layernorm: too many rows");
-  const int nvec = a.dim / 256;
+  if ((p->rows + 3) / 4 > INT32_MAX) return set_error(WANB200_EINVAL, "layernorm: too many rows");
   const bool push = a.npush > 0;
   if (p->mode == WANB200_LN_MODULATE)
-    push ? launch_ln<0, true>(nvec, a, (unsigned)blocks, st) : launch_ln<0, false>(nvec, a, (unsigned)blocks, st);
+    push ? launch_ln<0, true>(a.dim, a, p->rows, st) : launch_ln<0, false>(a.dim, a, p->rows, st);
   else
-    push ? launch_ln<1, true>(nvec, a, (unsigned)blocks, st) : launch_ln<1, false>(nvec, a, (unsigned)blocks, st);
+    push ? launch_ln<1, true>(a.dim, a, p->rows, st) : launch_ln<1, false>(a.dim, a, p->rows, st);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error("layernorm_kernel launch", e);
   return WANB200_OK;

@@ -88,9 +88,23 @@ __device__ __forceinline__ void tile_origin(int tile, int num_m, int num_n, int 
   n0 = (r / gm) * bn;
 }
 
+constexpr bool epi_has_residual(int epi) {
+  return epi == WANB200_EPI_BIAS_GATE_RES || epi == WANB200_EPI_BIAS_RES;
+}
+
+// The residual chunk (32 bf16 = 4 x 16 B) of `row` at col0, loaded one chunk ahead of its use so
+// the HBM latency of the residual overlaps the previous chunk's TMEM load and arithmetic.
+__device__ __forceinline__ void load_residual_chunk(const GemmArgs& a, int row, int col0, uint4 (&r)[4]) {
+  if (row < a.M && col0 < a.N) {
+    const uint4* rp = reinterpret_cast<const uint4*>(a.residual + (int64_t)row * a.ldr + col0);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) r[q] = rp[q];
+  }
+}
+
 template <int EPI>
 __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v, int row, int col0, float& ss_acc,
-                                                    int& ss_sec) {
+                                                    int& ss_sec, const uint4 (&res)[4]) {
   if constexpr (EPI != WANB200_EPI_NONE && EPI != WANB200_EPI_SCATTER) {
     const uint4* bp = reinterpret_cast<const uint4*>(a.bias + col0);
 #pragma unroll
@@ -107,7 +121,7 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v,
   }
   if constexpr (EPI == WANB200_EPI_BIAS_GATE_RES || EPI == WANB200_EPI_BIAS_RES) {
     if (row < a.M) {
-      const uint4* rp = reinterpret_cast<const uint4*>(a.residual + (int64_t)row * a.ldr + col0);
+      const uint4* rp = res;
       if constexpr (EPI == WANB200_EPI_BIAS_GATE_RES) {
         const int f = (int)frame_of_row(row, a.rows_per_seq, a.row_offset, a.seq_len, a.tokens_per_frame);
         const float4* ep = reinterpret_cast<const float4*>(a.gate_e0 + (int64_t)f * a.gate_frame_stride + col0);
@@ -322,13 +336,20 @@ __global__ void __launch_bounds__(192, 1)
         }
         __syncwarp();
       } else {
+        uint4 res_next[4] = {}, res_cur[4];
+        if constexpr (epi_has_residual(EPI)) load_residual_chunk(args, row, n0, res_next);
 #pragma unroll 1
         for (int c = 0; c < bn / 32; ++c) {
           const int col0 = n0 + c * 32;
           if (col0 >= args.N) break;  // warp-uniform
+#pragma unroll
+          for (int q = 0; q < 4; ++q) res_cur[q] = res_next[q];
+          if constexpr (epi_has_residual(EPI)) {
+            if (c + 1 < bn / 32) load_residual_chunk(args, row, col0 + 32, res_next);
+          }
           float v[32];
           tmem_ld32(t_row + c * 32, v);
-          gemm_epilogue_chunk<EPI>(args, v, row, col0, ss_acc, ss_sec);
+          gemm_epilogue_chunk<EPI>(args, v, row, col0, ss_acc, ss_sec, res_cur);
         }
       }
       if constexpr (EPI == WANB200_EPI_BIAS_SUMSQ) {

@@ -34,11 +34,27 @@ int make_tmap_2d(CUtensorMap* m, const void* base, int64_t inner, int64_t outer,
                  int box_outer);
 int make_tmap_4d(CUtensorMap* m, const void* base, const int64_t dims[4], const int64_t strides[4],
                  const int box[4]);
+// The same for 8-bit elements (fp8 e4m3 tiles): strides in bytes.
+int make_tmap_4d_u8(CUtensorMap* m, const void* base, const int64_t dims[4], const int64_t strides[4],
+                    const int box[4]);
 
 // Launchers (one per public entry point).
 int gemm_bf16(const wanb200_gemm_params* p, cudaStream_t st);
 int attn_fwd(const wanb200_attn_params* p, cudaStream_t st);
-int attn_launch(const wanb200_attn_params* p, int* err, cudaStream_t st);  // validated params
+// e4m3 operands of the attention (quantised by attn_fwd_fp8)
+struct AttnFp8Operands {
+  const void* q8;   // [B, q_len, H, 128]
+  const void* k8;   // [B, kv_len, H, 128]
+  const void* v8t;  // [B, H, 128, kv_len16]
+  const float* q_scale;  // [B, H, ceil(q_len / 128)]
+  const float* k_scale;  // [B, H, ceil(kv_len / 128)]
+  const float* v_scale;  // [B, H]
+  int64_t kv_len16;
+};
+int attn_launch(const wanb200_attn_params* p, int* err, cudaStream_t st,
+                const AttnFp8Operands* f8 = nullptr);  // validated params
+int attn_fwd_fp8(const wanb200_attn_fp8_params* p, cudaStream_t st);
+int64_t attn_fp8_workspace_bytes(int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len);
 int attn_fwd_noalloc(const wanb200_attn_params* p, cudaStream_t st);
 int64_t attn_workspace_bytes(int64_t batch, int64_t heads, int64_t q_len, int kv_splits);
 int attn_kv_splits(int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len);

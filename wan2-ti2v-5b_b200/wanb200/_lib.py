@@ -71,10 +71,15 @@ class ShardGatherParams(ctypes.Structure):
                 ("dst_ld", c_int64), ("dst_batch_stride", c_int64), ("dst_row0", c_int64 * 8)]
 
 
+class AttnFp8Params(ctypes.Structure):
+    _fields_ = [("attn", AttnParams), ("fp8_workspace", c_void_p), ("fp8_workspace_bytes", c_int64)]
+
+
 EXPORTS = ("wanb200_gemm_bf16", "wanb200_attn_fwd", "wanb200_layernorm", "wanb200_qk_norm_rope",
            "wanb200_bias_gate_residual", "wanb200_last_error", "wanb200_device_error", "wanb200_version",
            "wanb200_struct_sizes", "wanb200_peer_barrier", "wanb200_attn_workspace_bytes",
-           "wanb200_attn_kv_splits", "wanb200_attn_fwd_noalloc", "wanb200_shard_gather")
+           "wanb200_attn_kv_splits", "wanb200_attn_fwd_noalloc", "wanb200_shard_gather", "wanb200_attn_fwd_fp8",
+           "wanb200_attn_fp8_workspace_bytes")
 
 _lock = threading.Lock()
 _lib = None
@@ -119,7 +124,12 @@ def load():
             lib.wanb200_attn_kv_splits.restype = c_int
             lib.wanb200_attn_fwd_noalloc.argtypes = [ctypes.POINTER(AttnParams), c_void_p]
             lib.wanb200_attn_fwd_noalloc.restype = c_int
-            structs = (GemmParams, AttnParams, LnParams, QkNormParams, ResidualParams, ShardGatherParams)
+            lib.wanb200_attn_fwd_fp8.argtypes = [ctypes.POINTER(AttnFp8Params), c_void_p]
+            lib.wanb200_attn_fwd_fp8.restype = c_int
+            lib.wanb200_attn_fp8_workspace_bytes.argtypes = [c_int64, c_int64, c_int64, c_int64]
+            lib.wanb200_attn_fp8_workspace_bytes.restype = c_int64
+            structs = (GemmParams, AttnParams, LnParams, QkNormParams, ResidualParams, ShardGatherParams,
+                       AttnFp8Params)
             sizes = (c_int64 * len(structs))()
             n = lib.wanb200_struct_sizes(sizes, len(structs))
             want = [ctypes.sizeof(c) for c in structs]

@@ -71,17 +71,20 @@ class FastBlock:
     size 1 = single GPU).
     """
 
-    def __init__(self, weights: BlockWeights, num_frames: int, tp_group=None, eps: float = 1e-6, sp=None):
+    def __init__(self, weights: BlockWeights, num_frames: int, tp_group=None, eps: float = 1e-6, sp=None,
+                 attn_fp8: bool = False):
         """sp: a wanb200.comm.KVGather of the sequence-parallel group for Q-local self-attention
         (`WanSelfAttentionSP`, models/dit_attention_sp.py:25-152): x then holds the tokens
         sp.rank*S .. sp.rank*S + S - 1 of every batch element, every op runs on those rows, and
-        only K/V are gathered from the group.  None = x holds whole sequences."""
+        only K/V are gathered from the group.  None = x holds whole sequences.
+        attn_fp8: self-attention through the e4m3 variant (wanb200_attn_fwd_fp8)."""
         self.w = weights
         self.num_frames = num_frames
         self.tp_group = tp_group
         self.tp = weights.tp_size > 1
         self.eps = eps
         self.sp = sp
+        self.attn_fp8 = attn_fp8
 
     def _all_reduce(self, t):
         if self.tp:
@@ -132,7 +135,7 @@ class FastBlock:
         if sp is None:
             k = ws.qkv[:, Cl:2 * Cl].view(B, Lx, nl, 128)
             v = ws.qkv[:, 2 * Cl:].view(B, Lx, nl, 128)
-            ops.attention(q, k, v, out=y, kind="attn_self")
+            ops.attention(q, k, v, out=y, kind="attn_self", fp8=self.attn_fp8)
         elif sp.overlapped:
             # Q-local: the other ranks' K/V cross NVLink while this shard's queries attend the
             # shard's own keys; the remote keys follow and the partials of both are merged
@@ -144,17 +147,19 @@ class FastBlock:
             if n_loc:
                 k = ws.qkv[:, Cl:2 * Cl].view(B, Lx, nl, 128)[:, :n_loc]
                 v = ws.qkv[:, 2 * Cl:].view(B, Lx, nl, 128)[:, :n_loc]
-                ops.attention(q, k, v, out=y, kind="attn_self", kv_splits=s_loc, parts=(0, n, n_rem > 0))
+                ops.attention(q, k, v, out=y, kind="attn_self", kv_splits=s_loc, parts=(0, n, n_rem > 0),
+                              fp8=self.attn_fp8)
             kv = sp.finish()
             if n_rem:
                 k = kv[:, :, :Cl].unflatten(2, (nl, 128))
                 v = kv[:, :, Cl:].unflatten(2, (nl, 128))
-                ops.attention(q, k, v, out=y, kind="attn_self", kv_splits=s_rem, parts=(s_loc, n, False))
+                ops.attention(q, k, v, out=y, kind="attn_self", kv_splits=s_rem, parts=(s_loc, n, False),
+                              fp8=self.attn_fp8)
         else:  # Q-local over NCCL: gather the whole sequence's keys, then one attention
             kv = sp.gather(ws.qkv[:, Cl:])[:, :L_seq]
             k = kv[:, :, :Cl].unflatten(2, (nl, 128))
             v = kv[:, :, Cl:].unflatten(2, (nl, 128))
-            ops.attention(q, k, v, out=y, kind="attn_self")
+            ops.attention(q, k, v, out=y, kind="attn_self", fp8=self.attn_fp8)
         x1 = torch.empty_like(xf)
         gate2 = (mod[2], e0[:, 2, :])
         if self.tp:

@@ -74,7 +74,7 @@ def _spec_and_state(model):
 
 class FastWanDiT:
     def __init__(self, model, grid, guide_scale, device, cfg_group=None, pair_group=None, tp_group=None,
-                 num_layers=None, seq_parallel=None, comm="peer", sp_group=None):
+                 num_layers=None, seq_parallel=None, comm="peer", sp_group=None, attn_fp8=False):
         """seq_parallel: token-sharded residual inside the TP group with local all-head
         cross-attention (`_FastBlockSP`, fast_dit.py:314-389); default on for CFG-parallel with
         TP > 1 (batch 1) and no sp_group, the reference's best layout.
@@ -83,7 +83,9 @@ class FastWanDiT:
         and gathers only the normed, rotated K/V of the group (TP inside, by tp_group, as usual);
         the head runs on the token shard and its 4*48-wide output is gathered.
         comm: how the sequence-parallel collectives run: "peer" = fused into the kernels /
-        pushed over NVLink peer memory (wanb200.comm), "nccl" = torch.distributed collectives."""
+        pushed over NVLink peer memory (wanb200.comm), "nccl" = torch.distributed collectives.
+        attn_fp8: self-attention in e4m3 (BASELINE config 3's optional variant; not with
+        seq_parallel)."""
         spec, sd = _spec_and_state(model)
         self.spec = spec
         self.grid = tuple(int(g) for g in grid)
@@ -115,6 +117,8 @@ class FastWanDiT:
             seq_parallel = cfg_group is not None and tp > 1 and spn == 1
         if seq_parallel and (self.batch != 1 or tp == 1 or spn > 1):
             raise ValueError("seq_parallel needs CFG-parallel (batch 1), a TP group of size > 1 and no sp_group")
+        if seq_parallel and attn_fp8:
+            raise ValueError("attn_fp8 is available with the tp / sp layouts, not with seq_parallel")
         self.sp = seq_parallel
         self.kv_gather = None
         if spn > 1:
@@ -138,7 +142,7 @@ class FastWanDiT:
             self.blocks = [FastBlockSP(w, self.seq_len, self.num_frames, tp_group, spec.eps, comm=self.comm)
                            for w in self.block_weights]
         else:
-            self.blocks = [FastBlock(w, self.num_frames, tp_group, spec.eps, sp=self.kv_gather)
+            self.blocks = [FastBlock(w, self.num_frames, tp_group, spec.eps, sp=self.kv_gather, attn_fp8=attn_fp8)
                            for w in self.block_weights]
         self.cross_kv = [FastCrossKV(w, tp_group, spec.eps) for w in self.block_weights]
         self.context = None

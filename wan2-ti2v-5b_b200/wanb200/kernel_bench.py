@@ -64,8 +64,8 @@ def bench_attn(a):
     k = torch.randn(a.B, a.Lk, a.H, 128, generator=g, device=dev).to(torch.bfloat16)
     v = torch.randn(a.B, a.Lk, a.H, 128, generator=g, device=dev).to(torch.bfloat16)
     o = torch.empty_like(q)
-    ms = _time(lambda: ops.attention(q, k, v, out=o), a.iters)
-    return {"kernel": "attn", "B": a.B, "H": a.H, "Lq": a.Lq, "Lk": a.Lk, "ms": ms,
+    ms = _time(lambda: ops.attention(q, k, v, out=o, fp8=a.fp8), a.iters)
+    return {"kernel": "attn_fp8" if a.fp8 else "attn", "B": a.B, "H": a.H, "Lq": a.Lq, "Lk": a.Lk, "ms": ms,
             "tflops": 4 * a.B * a.H * a.Lq * a.Lk * 128 / ms / 1e9}
 
 
@@ -93,6 +93,7 @@ def main():
     ap.add_argument("--Lk", type=int, default=7854)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--tile-n", type=int, default=0, help="gemm tile width along N (0 = the library's choice)")
+    ap.add_argument("--fp8", action="store_true", help="attn: the e4m3 variant (quantisation included in the time)")
     a = ap.parse_args()
     torch.cuda.set_device(0)
     r = {"gemm": bench_gemm, "attn": bench_attn, "ln": bench_ln}[a.kind](a)

@@ -166,12 +166,17 @@ def kv_splits(batch, heads, q_len, kv_len) -> int:
     return L.load().wanb200_attn_kv_splits(batch, heads, q_len, kv_len)
 
 
-def attention(q, k, v, out=None, softmax_scale=None, kind="attn", kv_splits=None, parts=None):
+_FP8_WORKSPACES = {}
+
+
+def attention(q, k, v, out=None, softmax_scale=None, kind="attn", kv_splits=None, parts=None, fp8=False):
     """o = softmax(q k^T * scale) v on [B, L, H, 128] tensors (head stride 128, unit d stride).
     kv_splits: None = the library's choice for the grid size, 1 = no split.
     parts: (slot0, nslots, defer_combine) when the key set comes in pieces: this launch writes
     partial slots slot0.. of a workspace of nslots slots, and merges all of them into `out`
-    unless defer_combine (wanb200_attn_params)."""
+    unless defer_combine (wanb200_attn_params).
+    fp8: the e4m3 variant (wanb200_attn_fwd_fp8): q, k, v are quantised with per-block scales
+    inside the call; the result differs from the bf16 path by the e4m3 rounding."""
     _cuda(q, k, v, out)
     for name, t in (("q", q), ("k", k), ("v", v)):
         _need(t.dtype == BF16 and t.dim() == 4 and t.shape[-1] == 128 and t.stride(3) == 1 and t.stride(2) == 128,
@@ -199,6 +204,18 @@ def attention(q, k, v, out=None, softmax_scale=None, kind="attn", kv_splits=None
         nbytes = lib.wanb200_attn_workspace_bytes(B, H, Lq, slots)
         p.workspace, p.workspace_bytes = _workspace(q.device, nbytes).data_ptr(), nbytes
     flops = 4.0 * B * H * Lq * k.shape[1] * D
+    if fp8:
+        f = L.AttnFp8Params()
+        f.attn = p
+        nb = lib.wanb200_attn_fp8_workspace_bytes(B, H, Lq, k.shape[1])
+        key = str(q.device)
+        ws = _FP8_WORKSPACES.get(key)
+        if ws is None or ws.numel() < nb:
+            ws = _FP8_WORKSPACES[key] = torch.empty(nb, dtype=torch.uint8, device=q.device)
+        f.fp8_workspace, f.fp8_workspace_bytes = ws.data_ptr(), nb
+        L.check(_launch(q, kind, flops, lambda: lib.wanb200_attn_fwd_fp8(ctypes.byref(f), _stream(q))),
+                "wanb200_attn_fwd_fp8")
+        return out
     L.check(_launch(q, kind, flops, lambda: lib.wanb200_attn_fwd(ctypes.byref(p), _stream(q))), "wanb200_attn_fwd")
     return out
 
