@@ -147,3 +147,31 @@ def test_step_with_fp8_attention_matches_reference_golden():
     err = R.rel_rms(fast(lat.to(DEV), mg["t"]).float().cpu(), mg["noise_pred"])
     print(f"golden step with fp8 self-attention: rel-RMS {err:.3e}")
     assert err < STEP_TOL
+
+
+def test_denoise_loop_matches_oracle_loop():
+    """The denoise loop (BASELINE config 4's structure) on the golden 2-layer model: three UniPC
+    steps with the image frame pinned, the DiT on the device vs the fp32 oracle step on the CPU
+    driving the same sampler (itself bit-identical to the reference's scheduler on the CPU)."""
+    from wanb200.unipc import FlowUniPC, denoise
+    mg = torch.load(os.path.join(GOLD, "model_small.pt"), weights_only=False)
+    cfg = mg["cfg"]
+    spec = WanSpec(dim=cfg["dim"], ffn_dim=cfg["ffn_dim"], num_heads=cfg["num_heads"], num_layers=cfg["num_layers"],
+                   freq_dim=cfg["freq_dim"], text_dim=cfg["text_dim"], in_dim=cfg["in_dim"], out_dim=cfg["out_dim"],
+                   text_len=cfg["text_len"])
+    lat = mg["latent"].float()
+    img = torch.randn(lat.shape[0], 1, lat.shape[2], lat.shape[3], generator=torch.Generator().manual_seed(9))
+    grid = (lat.shape[1], lat.shape[2] // 2, lat.shape[3] // 2)
+    fast = FastWanDiT((spec, mg["state_dict"]), grid, mg["guide"], DEV)
+    fast.set_context(mg["ctx"].to(DEV), mg["ctx_null"].to(DEV))
+    out = denoise(fast, lat.to(DEV), 3, 5.0, img.to(DEV)).float().cpu()
+
+    mp = fp32(mg["state_dict"])
+    ocfg = {"num_heads": cfg["num_heads"], "num_layers": cfg["num_layers"], "freq_dim": cfg["freq_dim"],
+            "patch": cfg["patch"], "out_dim": cfg["out_dim"]}
+    ref = denoise(lambda x, t: R.step(mp, ocfg, x, t, mg["ctx"].float(), mg["ctx_null"].float(), mg["guide"]),
+                  lat.clone(), 3, 5.0, img, sampler=FlowUniPC())
+    err = R.rel_rms(out, ref)
+    print(f"3-step denoise loop vs oracle loop: rel-RMS {err:.3e}")
+    assert torch.equal(out[:, :1], img)
+    assert err < STEP_TOL
