@@ -62,3 +62,23 @@ def test_layout_kinds_and_names():
     assert Layout("sp", sp_size=8).describe(8) == "sp8"
     assert Layout("cfgsp", cfg_group=1, sp_size=4).describe(8) == "cfg2xsp4"
     assert Layout("cfgsptp", cfg_group=0, tp_size=2, sp_size=2).describe(8) == "cfg2xsp2xtp2"
+
+
+def test_kv_gather_packs_the_other_ranks_rows_contiguously():
+    """The Q-local K/V push (wanb200.comm.KVGather): on rank p the shards of the other ranks are
+    packed in the order p+1, p+2, ... so they tile rows [0, L - valid_p) exactly (the attention
+    over the remote keys is one contiguous key range), padded last shards included."""
+    from wanb200.comm import KVGather
+    for T, L in ((2, 30), (4, 30), (4, 24), (8, 27280), (8, 7854), (3, 10)):
+        g = KVGather.__new__(KVGather)  # the row arithmetic only (no process group)
+        g.T = T
+        S = -(-L // T)
+        g.valid_all = [max(0, min(S, L - r * S)) for r in range(T)]
+        assert sum(g.valid_all) == L
+        for p in range(T):
+            spans = sorted((g.chunk_row(p, r), g.chunk_row(p, r) + g.valid_all[r]) for r in range(T) if r != p)
+            cursor = 0
+            for a, b in spans:
+                assert a == cursor, (T, L, p, spans)
+                cursor = b
+            assert cursor == L - g.valid_all[p]
