@@ -5,8 +5,8 @@
 // cross-q, FFN up (3072 -> 14336, GELU-tanh) and FFN down (14336 -> 3072, gate + residual).
 //
 // Tile 128 x BN x 64 with BN <= 256 chosen per launch (a multiple of 32; 256 unless a narrower
-// tile fills the last wave of the persistent grid better), 4-stage TMA ring (up to 48 KB per
-// stage), fp32 accumulators in TMEM, two accumulator buffers (2 x 256 columns) so the epilogue
+// tile fills the last wave of the persistent grid better), a TMA ring of 4-6 stages (as many as
+// fit: 16 KB of A + BN*128 B of W each), fp32 accumulators in TMEM, two accumulator buffers (2 x 256 columns) so the epilogue
 // of tile t overlaps the main loop of tile t+1.  One CTA per SM, tiles strided over the
 // persistent grid in grouped order so the CTAs running together share A rows and W.
 //
@@ -22,22 +22,21 @@ namespace wanb200 {
 
 constexpr int GBM = 128, GBN = 256, GBK = 64;
 constexpr int G_A_BYTES = GBM * GBK * 2;  // 16 KB
-constexpr int G_B_BYTES = GBN * GBK * 2;  // 32 KB
-constexpr int G_STAGE_BYTES = G_A_BYTES + G_B_BYTES;
 constexpr uint32_t G_TMEM_COLS = 512;
 
 // Shared-memory plan per epilogue.  The scatter epilogue (reduce-scatter fused into the GEMM)
 // stages each warp's 32 x 256 output rows in shared memory so that every remote store is one
 // coalesced 512-byte row segment (16-byte stores per thread scattered over rows run at a
 // fraction of the NVLink bandwidth); it gives up one pipeline stage for the staging buffer.
+// The TMA ring has as many stages as fit (at most G_MAX_STAGES): a stage holds the A tile and a
+// BN-wide W tile, so narrow tiles get a deeper ring to cover the load latency of short K loops.
+constexpr int G_MAX_STAGES = 6;
+constexpr int G_SMEM_LIMIT = 232448;  // 227 KB of dynamic shared memory per CTA
 template <int EPI>
 struct GemmCfg {
-  static constexpr int STAGES = EPI == WANB200_EPI_SCATTER ? 3 : 4;
   static constexpr int STAGING_ROW = GBN * 2 + 16;  // padded: the 16-byte row writes of a warp hit distinct banks
   static constexpr int STAGING = EPI == WANB200_EPI_SCATTER ? 4 * 32 * STAGING_ROW : 0;
-  static constexpr int TILES = STAGES * G_STAGE_BYTES;
-  static constexpr int META = TILES + STAGING;
-  static constexpr int SMEM = META + 256 + 1024;  // barriers + alignment slack
+  static constexpr int FIXED = STAGING + 256 + 1024;  // staging + barriers + alignment slack
 };
 
 struct GemmArgs {
@@ -58,6 +57,9 @@ struct GemmArgs {
   int npeers, src_rank;
   int64_t shard_rows;
   int bn;  // tile width along N: multiple of 32, <= GBN
+  int stages;             // TMA ring depth
+  uint32_t stage_bytes;   // A tile + BN-wide W tile
+  uint32_t tiles_bytes;   // stages * stage_bytes
   int* err;
 };
 
@@ -185,14 +187,15 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   const uint32_t tiles = smem_u32(smem);
-  constexpr int GSTAGES = GemmCfg<EPI>::STAGES;
-  uint8_t* meta = smem + GemmCfg<EPI>::META;
-  const uint32_t full0 = smem_u32(meta);           // GSTAGES x 8
-  const uint32_t empty0 = full0 + 8 * GSTAGES;     // GSTAGES x 8
-  const uint32_t tfull0 = empty0 + 8 * GSTAGES;    // 2 x 8
+  const int GSTAGES = args.stages;
+  const uint32_t SB = args.stage_bytes;
+  uint8_t* meta = smem + args.tiles_bytes + GemmCfg<EPI>::STAGING;
+  const uint32_t full0 = smem_u32(meta);             // G_MAX_STAGES x 8
+  const uint32_t empty0 = full0 + 8 * G_MAX_STAGES;  // G_MAX_STAGES x 8
+  const uint32_t tfull0 = empty0 + 8 * G_MAX_STAGES;  // 2 x 8
   const uint32_t tempty0 = tfull0 + 16;            // 2 x 8
   const uint32_t done_bar = tempty0 + 16;          // 8
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(meta + 8 * (2 * GSTAGES + 5));
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(meta + 8 * (2 * G_MAX_STAGES + 5));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* err = args.err;
 
@@ -242,7 +245,7 @@ __global__ void __launch_bounds__(192, 1)
             ok = false;
             break;
           }
-          const uint32_t a_dst = tiles + stage * G_STAGE_BYTES;
+          const uint32_t a_dst = tiles + stage * SB;
           mbar_expect_tx(full0 + 8 * stage, G_A_BYTES + bn * GBK * 2);
           tma_load_2d(a_dst, &tmA, full0 + 8 * stage, kb * GBK, m0);
           tma_load_2d(a_dst + G_A_BYTES, &tmB, full0 + 8 * stage, kb * GBK, n0);
@@ -275,7 +278,7 @@ __global__ void __launch_bounds__(192, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = tiles + stage * G_STAGE_BYTES;
+          const uint32_t a_addr = tiles + stage * SB;
           const uint32_t b_addr = a_addr + G_A_BYTES;
 #pragma unroll
           for (int kk = 0; kk < GBK / 16; ++kk) {
@@ -314,7 +317,7 @@ __global__ void __launch_bounds__(192, 1)
       if constexpr (EPI == WANB200_EPI_SCATTER) {
         // stage this warp's 32 rows (lane = row), then write each row as one 512-byte segment
         constexpr int SR = GemmCfg<EPI>::STAGING_ROW;
-        uint8_t* stg = smem + GemmCfg<EPI>::TILES + quad * 32 * SR;
+        uint8_t* stg = smem + args.tiles_bytes + quad * 32 * SR;
         const int ncols = min(bn, args.N - n0);  // multiple of 32
 #pragma unroll 1
         for (int c = 0; c < ncols / 32; ++c) {
@@ -377,11 +380,12 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmA
   cudaGetDevice(&dev);
   if (!attr_set[dev]) {
     cudaError_t e =
-        cudaFuncSetAttribute(gemm_bf16_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<EPI>::SMEM);
+        cudaFuncSetAttribute(gemm_bf16_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM_LIMIT);
     if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(gemm)", e);
     attr_set[dev] = true;
   }
-  gemm_bf16_kernel<EPI><<<grid, 192, GemmCfg<EPI>::SMEM, st>>>(ta, tb, ga);
+  const int smem = (int)ga.tiles_bytes + GemmCfg<EPI>::FIXED;
+  gemm_bf16_kernel<EPI><<<grid, 192, smem, st>>>(ta, tb, ga);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error("gemm_bf16_kernel launch", e);
   return WANB200_OK;
@@ -484,6 +488,12 @@ int gemm_bf16(const wanb200_gemm_params* p, cudaStream_t st) {
   ga.src_rank = p->src_rank;
   ga.shard_rows = p->shard_rows > 0 ? p->shard_rows : 1;
   ga.bn = bn;
+  ga.stage_bytes = (uint32_t)(G_A_BYTES + bn * GBK * 2);
+  {
+    const int fixed = scatter ? GemmCfg<WANB200_EPI_SCATTER>::FIXED : GemmCfg<WANB200_EPI_NONE>::FIXED;
+    ga.stages = std::min<int>(G_MAX_STAGES, (G_SMEM_LIMIT - fixed) / (int)ga.stage_bytes);
+  }
+  ga.tiles_bytes = (uint32_t)ga.stages * ga.stage_bytes;
   ga.err = err;
 
   const int64_t tiles = ((p->M + GBM - 1) / GBM) * ((p->N + bn - 1) / bn);
