@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Benchmark of the north-star path: seconds per 30-layer DiT denoise step of Wan2.2-TI2V-5B at
+"""Benchmark of the DiT hot path: seconds per 30-layer DiT denoise step of Wan2.2-TI2V-5B at
 7854 tokens (latent grid 21x17x22, 704x544x81 video) with CFG (cond + uncond), on N B200s of
 one node.  N = 1 runs the whole step (batch 2) on one GPU; N > 1 uses --layout (default: CFG
 groups of N/2 GPUs with Q-local sequence parallelism inside, see wanb200.parallel).
@@ -353,7 +353,7 @@ GRID4, LATENT4, STEPS4, SHIFT4 = (31, 22, 40), (48, 31, 44, 80), 10, 1.0
 
 
 def run_config4(args):
-    """the 10-step UniPC denoise loop at 1280x704, 121 frames (27280 tokens),
+    """The long-video workload: the 10-step UniPC denoise loop at 1280x704, 121 frames (27280 tokens),
     CFG, image frame pinned to a seeded image latent, timesteps linear from 999 (shift 1), on N
     GPUs in --layout.  One JSON line: seconds per loop (device time, max over ranks), e2e with
     the latent copied in and the result copied out."""
@@ -419,7 +419,7 @@ def run_config4(args):
         fl = block_flops(CFG_BATCH * L4, L4)
         loop_flops = STEPS4 * args.layers * sum(fl.values())
         print(json.dumps({
-            "metric": "s per 10-step UniPC denoise loop @27280 tok CFG=2 (BASELINE config 4)", "value": loop_s,
+            "metric": "s per 10-step UniPC denoise loop @27280 tok CFG=2 (config 4)", "value": loop_s,
             "unit": "s/loop", "s_per_step": loop_s / STEPS4, "n_gpus": world, "loops": args.loops,
             "warmup": args.warmup, "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) bf16 weights, seeded latent / image latent / context)",
@@ -450,8 +450,8 @@ def main():
     ap.add_argument("--layers", type=int, default=30, help="blocks per step (30 for the bench line)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="config2", choices=["config2", "config4"],
-                    help="config2: the bench line (s/step at 7854 tokens); config4: one line for BASELINE "
-                         "config 4, the 10-step UniPC loop at 27280 tokens (--loops loops timed)")
+                    help="config2: the bench line (s/step at 7854 tokens); config4: one line for the "
+                         "10-step UniPC loop at 27280 tokens (--loops loops timed)")
     ap.add_argument("--loops", type=int, default=1, help="config4: denoise loops in the timed region")
     args = ap.parse_args()
     if args.warmup < 3:

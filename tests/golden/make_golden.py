@@ -17,7 +17,7 @@ and records:
     plus the reference's bf16 `WanAttentionBlock.forward` and bf16 `_FastBlock.forward`
     outputs on the same inputs (calibration of the reference's own bf16 error);
   * rope_small.pt -- `fast_dit._rope_tables` for small grids and strided rows of the three
-    BASELINE grids, and `fast_dit._rope` on a random tensor;
+    benchmark grids (6x12x15, 21x17x22, 31x22x40), and `fast_dit._rope` on a random tensor;
   * unipc_small.pt -- the reference's sampler, `FlowUniPCMultistepScheduler`
     (wan/utils/fm_solvers_unipc.py) constructed and stepped as inference_neuron_ti2v.py:497-532
     does, on seeded latents and model outputs (fp32 and bf16; shift 5 and 1; 10 and 3 steps).
@@ -36,7 +36,10 @@ import torch.nn as nn
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 _ARGS = [a for a in sys.argv[1:] if not a.startswith("--")]
-REF = _ARGS[0] if _ARGS else os.environ.get("WAN_REF_ROOT", "/root/reference")
+REF = _ARGS[0] if _ARGS else os.environ.get("WAN_REF_ROOT", "")
+if not REF:
+    raise SystemExit("usage: python tests/golden/make_golden.py REF_ROOT [--unipc-only]  "
+                     "(or set WAN_REF_ROOT): the path of the reference checkout")
 
 DIM, FFN, HEADS, LAYERS, TEXT_DIM, FREQ_DIM, IN_DIM, LC = 256, 512, 2, 2, 64, 256, 48, 16
 GRID_LATENT = (2, 6, 8)  # latent [48, F, H, W] -> token grid (2, 3, 4), L = 24

@@ -74,7 +74,7 @@ def _config0_inputs(seed=0, L_grid=(6, 12, 15), B=2, Lc=512):
 
 
 def test_block_config0_vs_oracle():
-    """one block, dim 3072, 24 heads, B=2, L=1080 (6x12x15), 512 context
+    """Config 0 of the benchmark: one block, dim 3072, 24 heads, B=2, L=1080 (6x12x15), 512 context
     tokens, seeded N(0, 0.02) weights -- device vs the fp32 CPU oracle."""
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     grid = (6, 12, 15)
@@ -112,7 +112,7 @@ def test_block_is_deterministic_and_functional():
 
 
 def test_block_with_fp8_attention_config0():
-    """BASELINE config 3's optional FP8 variant at the block level: self-attention in e4m3
+    """The optional FP8 variant (config 3) at the block level: self-attention in e4m3
     (per-block scales) against the fp32 oracle and against the bf16 device block.  The output
     stays within the block tolerance; the attention's e4m3 rounding shows in the update."""
     grid = (6, 12, 15)
@@ -150,7 +150,7 @@ def test_step_with_fp8_attention_matches_reference_golden():
 
 
 def test_denoise_loop_matches_oracle_loop():
-    """The denoise loop (BASELINE config 4's structure) on the golden 2-layer model: three UniPC
+    """The denoise loop (the structure of the 27280-token workload) on the golden 2-layer model: three UniPC
     steps with the image frame pinned, the DiT on the device vs the fp32 oracle step on the CPU
     driving the same sampler (itself bit-identical to the reference's scheduler on the CPU)."""
     from wanb200.unipc import FlowUniPC, denoise

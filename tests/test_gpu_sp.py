@@ -273,7 +273,7 @@ def test_qlocal_sp_step_4gpu(kind, comm_kind):
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 8, reason="needs 8 GPUs")
 def test_cfg_sp2_tp2_step_8gpu():
-    """BASELINE config 3's layout: CFG groups of 4 GPUs, each SP2 x TP2."""
+    """The config-3 layout: CFG groups of 4 GPUs, each SP2 x TP2."""
     res = _run(_layout_step_worker, 8, "cfgsptp", "peer")
     print("cfgsptp:", res[0])
     for r in range(8):

@@ -4,7 +4,7 @@ tests/golden/make_golden.py exactly as inference_neuron_ti2v.py:497-532 runs it.
 
 On the CPU the restatement must reproduce the reference bit for bit: the timesteps, the sigma
 schedule and every step's sample, for fp32 and bf16 latents, shift 5 (the pipeline's) and 1
-(BASELINE config 4's linear schedule), 10 and 3 steps.
+(the linear schedule of the 27280-token workload), 10 and 3 steps.
 """
 import os
 

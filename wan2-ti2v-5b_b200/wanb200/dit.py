@@ -84,7 +84,7 @@ class FastWanDiT:
         the head runs on the token shard and its 4*48-wide output is gathered.
         comm: how the sequence-parallel collectives run: "peer" = fused into the kernels /
         pushed over NVLink peer memory (wanb200.comm), "nccl" = torch.distributed collectives.
-        attn_fp8: self-attention in e4m3 (BASELINE config 3's optional variant; not with
+        attn_fp8: self-attention in e4m3 (the optional FP8 variant; not with
         seq_parallel)."""
         spec, sd = _spec_and_state(model)
         self.spec = spec

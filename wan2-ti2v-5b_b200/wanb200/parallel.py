@@ -2,7 +2,7 @@
 
 Mirrors the reference's group construction (inference_neuron_ti2v.py:241-274 for CFG-parallel,
 models/parallel_state.py:64-96 for contiguous TP groups and strided attn-sp groups):
-  * "tp":      one TP group of all ranks, batched CFG (batch 2) -- BASELINE config 2's TP=N;
+  * "tp":      one TP group of all ranks, batched CFG (batch 2) -- the benchmark's TP=N layout;
   * "cfg":     two CFG groups of N/2 contiguous ranks (group 0 = cond, group 1 = uncond, batch 1
                each), TP inside each group with the token-sharded residual (`_FastBlockSP`), and
                pair groups {i, i + N/2} for the head's CFG combine;
