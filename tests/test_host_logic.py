@@ -82,3 +82,15 @@ def test_kv_gather_packs_the_other_ranks_rows_contiguously():
                 assert a == cursor, (T, L, p, spans)
                 cursor = b
             assert cursor == L - g.valid_all[p]
+
+
+def test_attention_custom_op_traces_without_a_device():
+    """`torch.ops.wanb200.attn` (the reference's attention seam fn(q, k, v) -> o) has a fake kernel,
+    so torch.compile / tracing can propagate shapes through it without running the kernel."""
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    from wanb200 import ops  # noqa: F401  (registers the op)
+    with FakeTensorMode():
+        q = torch.empty(2, 100, 3, 128, dtype=torch.bfloat16, device="meta")
+        k = torch.empty(2, 77, 3, 128, dtype=torch.bfloat16, device="meta")
+        o = torch.ops.wanb200.attn(q, k, k, 0.1)
+    assert tuple(o.shape) == (2, 100, 3, 128) and o.dtype == torch.bfloat16
