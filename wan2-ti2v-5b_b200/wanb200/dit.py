@@ -147,6 +147,15 @@ class FastWanDiT:
         self.cross_kv = [FastCrossKV(w, tp_group, spec.eps) for w in self.block_weights]
         self.context = None
 
+    @classmethod
+    def from_checkpoint(cls, path, grid, guide_scale, device, **kwargs):
+        """Build from a Wan2.2 checkpoint directory (config.json + diffusion_pytorch_model
+        safetensors, as `WanModel.from_pretrained` reads it; wanb200.checkpoint).  kwargs as for
+        the constructor; num_layers also limits which blocks are read."""
+        from .checkpoint import load_wan_checkpoint
+        return cls(load_wan_checkpoint(path, num_layers=kwargs.get("num_layers")), grid, guide_scale, device,
+                   **kwargs)
+
     # ------------------------------------------------------------------ embeddings (torch, fp32)
     def set_context(self, ctx_cond, ctx_null):
         """Text embedding + every block's cross K/V, once per prompt (fast_dit.py:658-664)."""

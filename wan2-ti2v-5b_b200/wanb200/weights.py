@@ -73,10 +73,9 @@ def random_block_state(spec: WanSpec, seed: int, device="cpu") -> dict:
     return {k: _fill(k, s, gen, device, spec.dim) for k, s in sorted(_block_shapes(spec).items())}
 
 
-def random_model_state(spec: WanSpec, seed: int, device="cpu", num_layers=None) -> dict:
-    """Whole-model seeded state dict (bf16) with the checkpoint's key names."""
+def model_shapes(spec: WanSpec, num_layers=None) -> dict:
+    """Every DiT parameter the fast path reads, by checkpoint key, with its shape."""
     C = spec.dim
-    gen = torch.Generator(device=device).manual_seed(seed)
     p = spec.patch_size
     shapes = {
         "patch_embedding.weight": (C, spec.in_dim) + tuple(p), "patch_embedding.bias": (C,),
@@ -88,11 +87,16 @@ def random_model_state(spec: WanSpec, seed: int, device="cpu", num_layers=None) 
         "head.modulation": (1, 2, C), "head.head.weight": (p[0] * p[1] * p[2] * spec.out_dim, C),
         "head.head.bias": (p[0] * p[1] * p[2] * spec.out_dim,),
     }
-    sd = {k: _fill(k, s, gen, device, C) for k, s in shapes.items()}
     for i in range(spec.num_layers if num_layers is None else num_layers):
-        for k, s in sorted(_block_shapes(spec).items()):
-            sd[f"blocks.{i}.{k}"] = _fill(k, s, gen, device, C)
-    return sd
+        for k, sh in sorted(_block_shapes(spec).items()):
+            shapes[f"blocks.{i}.{k}"] = sh
+    return shapes
+
+
+def random_model_state(spec: WanSpec, seed: int, device="cpu", num_layers=None) -> dict:
+    """Whole-model seeded state dict (bf16) with the checkpoint's key names."""
+    gen = torch.Generator(device=device).manual_seed(seed)
+    return {k: _fill(k, s, gen, device, spec.dim) for k, s in model_shapes(spec, num_layers).items()}
 
 
 def block_state(sd: dict, i: int) -> dict:
