@@ -13,8 +13,12 @@ second pass over the same steps with a CUDA-event pair around every launch; `e2e
 step through the public `FastWanDiT.__call__` with the latent copied from pinned host memory
 and the noise prediction copied back every step.
 Weights are seeded N(0, 0.02) bf16 with the TI2V-5B shapes, the text context is seeded, so
-`data` is synthetic.  `--impl reference` times the CPU oracle (the reference's fp32 block math,
-ref_fp32.block_fwd restated in oracle/dit_ref.py) on this host's cores instead.
+`data` is synthetic.  `device_error` is the kernels' error word after all the timed steps (max
+over ranks); `parity` is the rel-RMS of the step-0 prediction against the fp32 CPU oracle over
+all the layers (N = 1; that oracle run is also the `cpu_baseline`) or against a single-GPU run of
+the same model (N > 1).  A non-zero error word or a parity miss ends the run with a non-zero
+status after the line is printed.  `--impl reference` times the CPU oracle (the reference's fp32
+block math, ref_fp32.main restated in oracle/dit_ref.py): one whole step on this host's cores.
 """
 import argparse
 import json
@@ -138,24 +142,30 @@ def max_over_ranks(x, world, device):
     return float(t.item())
 
 
-def cpu_block_sample(threads=None):
-    """One block of config 2 (B=2, L=7854, dim 3072) through the fp32 CPU oracle; returns seconds."""
+STEP_TOL = 5e-2  # north star: rel-RMS of the step-0 noise prediction
+
+
+def rel_rms(a, b) -> float:
+    """||a - b|| / ||b|| (the reference's error score, ref_fp32.py:108)."""
+    a, b = a.double().cpu(), b.double().cpu()
+    return float((a - b).norm() / b.norm().clamp_min(1e-30))
+
+
+ORACLE_CFG = {"num_heads": 24, "num_layers": 30, "freq_dim": 256, "patch": (1, 2, 2), "out_dim": 48}
+
+
+def oracle_step(sd, ctx, ctx_null, latent, layers, threads=None):
+    """Step-0 CFG noise prediction of config 2 through the fp32 CPU oracle (the reference's
+    scripts/validate/ref_fp32.py:62-99, restated in oracle/dit_ref.py) on this host's cores.
+    sd may live on the GPU in bf16: the oracle copies one block at a time to fp32 host tensors.
+    Returns (prediction [48, F, H, W] fp32, seconds)."""
     from oracle import dit_ref as R
-    from wanb200.weights import TI2V_5B, random_block_state
     torch.set_num_threads(threads or os.cpu_count() or 1)
-    spec = TI2V_5B
-    sd = {k: v.float() for k, v in random_block_state(spec, 0).items()}
-    g = torch.Generator().manual_seed(1)
-    Lx = GRID[0] * GRID[1] * GRID[2]
-    x = torch.randn(CFG_BATCH, Lx, spec.dim, generator=g)
-    e0 = torch.randn(1, GRID[0], 6, spec.dim, generator=g) * 0.1
-    ctx = torch.randn(CFG_BATCH, CTX_LEN, spec.dim, generator=g)
-    cos, sin = R.rope_tables(R.model_freqs(spec.head_dim), GRID, spec.head_dim)
-    ck, cv = R.cross_kv(sd, ctx, spec.num_heads)
+    cfg = dict(ORACLE_CFG, num_layers=layers)
     with torch.no_grad():
         t0 = time.perf_counter()
-        R.block_fwd(sd, x, e0, cos, sin, ck, cv, GRID[0], spec.num_heads)
-        return time.perf_counter() - t0
+        pred = R.step(sd, cfg, latent, T_STEP, ctx, ctx_null, GUIDE)
+        return pred, time.perf_counter() - t0
 
 
 def cpu_info():
@@ -169,29 +179,43 @@ def cpu_info():
 
 
 def run_reference(args):
-    """Reference arm: the reference's block math (fp32, CPU) on the host cores, rank 0 only."""
+    """Reference arm: the reference's own CPU implementation of the path (its fp32 block math,
+    ref_fp32.block_fwd / main, restated in oracle/dit_ref.py) on all host cores, rank 0 only: one
+    whole 30-layer config-2 step (B=2, L=7854, dim 3072) timed end to end, nothing extrapolated.
+    The 30 layers share one seeded block's fp32 weights (CPU time does not depend on the values;
+    generating 30 distinct blocks on the host would take longer than the step)."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     torch.set_grad_enabled(False)
+    from wanb200.weights import TI2V_5B, random_block_state, random_model_state
     threads = os.cpu_count() or 1
-    layers = 30
-    for _ in range(args.warmup):
-        cpu_block_sample(threads)
-    times = [cpu_block_sample(threads) for _ in range(args.steps)]
-    per_step = statistics.mean(times) * layers
+    torch.set_num_threads(threads)
+    spec = TI2V_5B
+    emb = {k: v.float() for k, v in random_model_state(spec, seed=0, num_layers=0).items()}
+    blk = {k: v.float() for k, v in random_block_state(spec, 0).items()}
+    sd = dict(emb)
+    for i in range(args.layers):
+        sd.update({f"blocks.{i}.{k}": v for k, v in blk.items()})
+    g = torch.Generator().manual_seed(123)
+    ctx, ctx_null = torch.randn(CTX_LEN, TEXT_DIM, generator=g), torch.randn(CTX_LEN, TEXT_DIM, generator=g)
+    latent = torch.randn(LATENT, generator=torch.Generator().manual_seed(7))
+    pred, secs = oracle_step(sd, ctx, ctx_null, latent, args.layers, threads)
+    assert torch.isfinite(pred).all()
+    sample = (f"one whole {args.layers}-layer config-2 step-0 (B=2, L=7854, dim 3072, CFG) through the fp32 oracle "
+              f"(ref_fp32.main restated), timed once; --steps/--warmup not used (one step is ~{secs:.0f} s); "
+              f"host: {cpu_info()}")
     line = {
-        "impl": "reference", "metric": METRIC, "value": per_step, "unit": "s/step", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": False,
+        "impl": "reference", "metric": METRIC, "value": secs, "unit": "s/step", "n_gpus": world,
+        "steps": 1, "warmup": 0, "requested_steps": args.steps, "requested_warmup": args.warmup,
+        "layers_timed": args.layers, "extrapolated": False, "ms_per_step": secs * 1e3, "higher_is_better": False,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config2: 30-layer Wan2.2-TI2V-5B DiT step, 7854 tokens (21x17x22), CFG batch 2",
-                   "global_batch": CFG_BATCH, "seq_len": GRID[0] * GRID[1] * GRID[2],
+        "config": {"workload": f"config2: {args.layers}-layer Wan2.2-TI2V-5B DiT step, 7854 tokens (21x17x22), "
+                               "CFG batch 2", "global_batch": CFG_BATCH, "seq_len": GRID[0] * GRID[1] * GRID[2],
                    "parallelism": "cpu", "inputs_larger_than_l2": True},
-        "cpu_baseline": {"value": per_step, "unit": "s/step", "cores": threads, "kind": "port",
-                         "sample": f"1 of 30 blocks per step (B=2, L=7854, dim 3072), fp32 oracle "
-                                   f"(ref_fp32.block_fwd restated), x30; host: {cpu_info()}"},
-        "e2e": {"value": per_step, "unit": "s/step", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "cpu_baseline": {"value": secs, "unit": "s/step", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": secs, "unit": "s/step", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
@@ -212,14 +236,15 @@ def run_ours(args):
     lay = make_layout(args.layout)
     fast = FastWanDiT((spec, sd), GRID, GUIDE, device, cfg_group=lay.cfg_group, pair_group=lay.pair_group,
                       tp_group=lay.tp_group, num_layers=layers, comm=args.comm, sp_group=lay.sp_group)
-    del sd
+    # sd stays: the parity check below runs the same seeded weights through the oracle (N = 1) or
+    # through a single-GPU model on rank 0 (N > 1)
     g = torch.Generator(device=device).manual_seed(123)
     ctx = torch.randn(CTX_LEN, TEXT_DIM, generator=g, device=device)
     ctx_null = torch.randn(CTX_LEN, TEXT_DIM, generator=g, device=device)
     fast.set_context(ctx, ctx_null)
     latent_host = torch.randn(LATENT, generator=torch.Generator().manual_seed(7)).pin_memory()
     latent_dev = latent_host.to(device)
-    out_host = torch.empty(LATENT, dtype=torch.float32).pin_memory()
+    out_host = torch.empty(LATENT, dtype=torch.bfloat16).pin_memory()  # the prediction is bf16, as the reference's
     stream = torch.cuda.current_stream(device)
 
     def barrier():
@@ -269,6 +294,33 @@ def run_ours(args):
     barrier()
     e2e_s = max_over_ranks(e0.elapsed_time(e1) / 1e3 / args.steps, world, device)
     assert torch.isfinite(out_host).all()
+
+    # ---- device error word: every bounded wait inside the kernels of all the steps above
+    derr = int(max_over_ranks(float(fast.check_device_errors(raise_error=False)), world, device))
+
+    # ---- parity of the step-0 prediction: N = 1 against the fp32 CPU oracle over all the
+    # layers (the reference's own score, ref_fp32.py:62-109; its time is the cpu_baseline); N > 1
+    # against a single-GPU run of the same seeded model on rank 0
+    pred = fast(latent_dev, T_STEP).float()
+    parity, oracle_s = None, None
+    if world == 1:
+        if not args.no_cpu_baseline:
+            ref, oracle_s = oracle_step(sd, ctx, ctx_null, latent_host, layers)
+            parity = {"rel_rms": rel_rms(pred, ref), "tol": STEP_TOL,
+                      "against": f"fp32 CPU oracle, whole {layers}-layer step-0 (ref_fp32.main restated)"}
+    else:
+        if rank == 0:
+            single = FastWanDiT((spec, sd), GRID, GUIDE, device, num_layers=layers)
+            single.set_context(ctx, ctx_null)
+            ref = single(latent_dev, T_STEP).float()
+            parity = {"rel_rms": rel_rms(pred, ref), "tol": STEP_TOL,
+                      "against": "single-GPU step-0 of the same seeded model (rank 0; itself checked against the "
+                                 "CPU oracle at N = 1)"}
+            del single, ref
+        barrier()
+    if parity is not None:
+        parity["ok"] = parity["rel_rms"] <= parity["tol"]
+    del sd
 
     if rank != 0:
         if world > 1:
@@ -336,17 +388,21 @@ def run_ours(args):
         "step_tflops": step_flops / step_s / 1e12,
         "kernels": per_kernel,
         "clocks": clk,
+        "device_error": derr,
+        "parity": parity,
     }
-    if world == 1 and not args.no_cpu_baseline:
-        t_blk = cpu_block_sample()
-        line["cpu_baseline"] = {"value": t_blk * 30, "unit": "s/step", "cores": torch.get_num_threads(),
+    if oracle_s is not None:
+        line["cpu_baseline"] = {"value": oracle_s, "unit": "s/step", "cores": torch.get_num_threads(),
                                 "kind": "port",
-                                "sample": f"1 of 30 blocks (B=2, L=7854, dim 3072) through the fp32 oracle, x30; "
+                                "sample": f"one whole {layers}-layer step-0 (B=2, L=7854, dim 3072, CFG) through the "
+                                          f"fp32 oracle, timed once (the run the parity key compares with); "
                                           f"host: {cpu_info()}"}
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
+    if derr or (parity is not None and not parity["ok"]):
+        raise SystemExit(f"invalid run: device error word {derr}, parity {parity}")
 
 
 GRID4, LATENT4, STEPS4, SHIFT4 = (31, 22, 40), (48, 31, 44, 80), 10, 1.0
@@ -448,7 +504,8 @@ def main():
                          "(batched CFG, K/V all-gather); cfgsp = CFG-parallel groups of N/2 with Q-local SP "
                          "inside; cfgsptp = CFG-parallel groups of SP2 x TP(N/4); auto = cfgsp for even N, else sp")
     ap.add_argument("--layers", type=int, default=30, help="blocks per step (30 for the bench line)")
-    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true",
+                    help="skip the CPU oracle step (the N = 1 cpu_baseline and parity keys)")
     ap.add_argument("--workload", default="config2", choices=["config2", "config4"],
                     help="config2: the bench line (s/step at 7854 tokens); config4: one line for the "
                          "10-step UniPC loop at 27280 tokens (--loops loops timed)")

@@ -14,8 +14,9 @@
  * float.  Strides are in elements.  `stream` is a cudaStream_t passed as void*.  Every entry
  * point validates its arguments on the host, launches asynchronously on `stream`, and returns
  * 0 or a negative WANB200_E* code; wanb200_last_error() gives a message for the calling
- * thread's last failure.  Nothing here allocates per call except a one-time per-device error
- * word (see wanb200_device_error).
+ * thread's last failure.  No entry point allocates device memory: scratch comes from the caller
+ * (workspace pointers) or, for wanb200_attn_fwd_noalloc, from an array inside the library, and
+ * the device error word is a variable of the library image (see wanb200_device_error).
  */
 #ifndef WANB200_H_
 #define WANB200_H_
@@ -118,15 +119,16 @@ int wanb200_attn_fwd(const wanb200_attn_params* p, void* stream);
  * boundary).  For callers that cannot have a library allocate device memory: applications that
  * give all GPU memory to their own pool or allocator (an allocation behind their back fails or
  * escapes their accounting) and latency-critical loops that avoid cudaMalloc / cudaFree because
- * those can block on the device.  It takes the same parameters (workspace ignored) and calls no
- * allocating routine: the split-KV partials live in a fixed 16 MiB array inside the library,
- * which every GPU that loads the library holds until the process exits.  Shapes whose partials
- * need more (kv_splits * batch * heads * q_len * 520 bytes > 16 MiB) are rejected with
- * WANB200_EINVAL; kv_splits 0 or 1 needs none.  The first call on a device resolves the array's
- * device address (cudaGetSymbolAddress) with that device current; make that first call before
- * any stream capture.  All calls on a device share the array: calls that overlap on the GPU
- * (unordered streams) race.  Deadline expiries inside its kernels go to the error word read by
- * wanb200_device_error() when another entry point has already created it on this device. */
+ * those can block on the device.  It takes the same parameters (workspace ignored; partial slots
+ * refused) with the same checks and calls no allocating routine: the split-KV partials live in a
+ * fixed 16 MiB array inside the library, which every GPU that loads the library holds until the
+ * process exits.  Shapes whose partials need more (kv_splits * batch * heads * q_len * 520 bytes
+ * > 16 MiB) are rejected with WANB200_EINVAL; kv_splits 0 or 1 needs none.  The first call on a
+ * device resolves the array's device address (cudaGetSymbolAddress) with that device current;
+ * make that first call before any stream capture.  All calls on a device share the array: calls
+ * that overlap on the GPU (unordered streams) race.  Deadline expiries inside its kernels are
+ * reported through wanb200_device_error / wanb200_device_error_async like every other entry
+ * point's. */
 int wanb200_attn_fwd_noalloc(const wanb200_attn_params* p, void* stream);
 int64_t wanb200_attn_workspace_bytes(int64_t batch, int64_t heads, int64_t q_len, int kv_splits);
 
@@ -241,9 +243,17 @@ int wanb200_shard_gather(const wanb200_shard_gather_params* p, void* stream);
 /* ---------------------------------------------------------------- status */
 const char* wanb200_last_error(void);
 /* Device-side error word of the current device: 0 or a code (a bounded wait expired inside a
- * kernel).  Synchronizes the device.  reset != 0 clears it. */
+ * kernel; the first code wins and stays until reset).  Synchronizes the device.  reset != 0
+ * clears it.  The word is a __device__ variable of the library (one per device), so neither
+ * this call nor any kernel launch allocates for it. */
 int wanb200_device_error(int reset);
-/* Library version, e.g. 100 for 0.1.0. */
+/* The same word without synchronizing: queues a 4-byte device-to-host copy of it into *host_out
+ * on `stream`, behind the work already queued there.  The value is valid once the stream has
+ * passed this point (record an event after the call and wait for or query it); host_out should
+ * be page-locked for the copy to be asynchronous.  Lets a step driver check every step at no
+ * cost to the pipeline (the word is sticky, so a later read also reports an earlier expiry). */
+int wanb200_device_error_async(int* host_out, void* stream);
+/* Library version, e.g. 200 for 0.2.0. */
 int wanb200_version(void);
 /* sizeof of the parameter structs (gemm, attn, ln, qknorm, residual, shard_gather, attn_fp8)
  * written to out[0..n); returns the number of structs.  Lets a binding detect a library built

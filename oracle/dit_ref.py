@@ -192,23 +192,32 @@ def step(mp: dict, cfg: dict, latent, t, ctx, ctx_null, guide: float = 5.0, laye
 
     cfg: {"num_heads", "num_layers", "freq_dim", "patch", "out_dim"}.  latent [C_in, F, H, W];
     ctx / ctx_null [Lc, text_dim].  `layers` limits the block loop (for bounded CPU samples).
+    mp may hold its tensors on any device and in any float dtype: the embedding / head params
+    are copied to fp32 CPU tensors once and each block's params just before the block runs, so
+    a full-size model needs one block's fp32 params on the host at a time.
     """
     C_in, nf, H, W = latent.shape
     p = tuple(cfg.get("patch", (1, 2, 2)))
     grid = (nf // p[0], H // p[1], W // p[2])
     n = cfg["num_heads"]
-    dim = mp["patch_embedding.weight"].shape[0]
+
+    def f32(d):
+        return {k: v.detach().to("cpu", torch.float32) for k, v in d.items()}
+
+    emb = f32({k: v for k, v in mp.items() if not k.startswith("blocks.")})
+    dim = emb["patch_embedding.weight"].shape[0]
     d = dim // n
     cos, sin = rope_tables(model_freqs(d), grid, d)
-    e, e0 = time_embed(mp, t, grid[0], cfg["freq_dim"])
-    context = text_embed(mp, torch.stack([ctx, ctx_null], 0).float())
-    x = patch_embed(mp, latent.float(), p).expand(2, -1, -1).contiguous()
+    e, e0 = time_embed(emb, t, grid[0], cfg["freq_dim"])
+    context = text_embed(emb, torch.stack([ctx, ctx_null], 0).float().cpu())
+    x = patch_embed(emb, latent.float().cpu(), p).expand(2, -1, -1).contiguous()
     nl = cfg["num_layers"] if layers is None else layers
     for i in range(nl):
-        bp = block_params(mp, i)
+        bp = f32(block_params(mp, i))
         ck, cv = cross_kv(bp, context, n)
         x = block_fwd(bp, x, e0, cos, sin, ck, cv, grid[0], n)
-    y = head(mp, x, e, grid, p, cfg.get("out_dim", 48))
+        del bp
+    y = head(emb, x, e, grid, p, cfg.get("out_dim", 48))
     return y[1] + guide * (y[0] - y[1])
 
 

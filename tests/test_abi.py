@@ -26,7 +26,7 @@ def test_library_exports_every_declared_function():
     for n in names:
         assert hasattr(lib, n), n
     assert set(names) == set(L.EXPORTS)
-    assert lib.wanb200_version() == 100
+    assert lib.wanb200_version() == 200
 
 
 STRUCTS = {

@@ -92,6 +92,27 @@ def test_missing_or_misshapen_tensors_are_refused(golden, tmp_path):
         spec_from_config({"dim": 256})
 
 
+def test_configs_of_other_model_variants_are_refused(golden, tmp_path):
+    """A checkpoint whose config asks for math the fast path does not implement must not load
+    (WanModel.__init__ arguments, wan/modules/model.py:304-317): local-window attention, the
+    i2v / other model types, a model without the QK or cross-attention norms."""
+    path = str(tmp_path / "ck")
+    _reference_layout(path, golden)
+    cfg_path = os.path.join(path, "config.json")
+    base = json.load(open(cfg_path))
+    spec_from_config(base)  # the TI2V-5B config loads
+    spec_from_config(dict(base, model_type="t2v"))
+    for change, match in (({"window_size": [256, 256]}, "window_size"), ({"model_type": "i2v"}, "model_type"),
+                          ({"model_type": "s2v"}, "model_type"), ({"qk_norm": False}, "qk_norm"),
+                          ({"cross_attn_norm": False}, "cross_attn_norm")):
+        with pytest.raises(ValueError, match=match):
+            spec_from_config(dict(base, **change))
+        with open(cfg_path, "w") as f:
+            json.dump(dict(base, **change), f)
+        with pytest.raises(ValueError, match=match):
+            load_wan_checkpoint(path)
+
+
 def test_fast_dit_from_checkpoint_builds_the_fused_weights(golden, tmp_path):
     """FastWanDiT.from_checkpoint: the blocks' fused Q/K/V weight is the checkpoint's q, k, v
     stacked (construction only; the step itself runs in the GPU tests)."""

@@ -175,3 +175,118 @@ def test_denoise_loop_matches_oracle_loop():
     print(f"3-step denoise loop vs oracle loop: rel-RMS {err:.3e}")
     assert torch.equal(out[:, :1], img)
     assert err < STEP_TOL
+
+
+def test_block_config2_full_size_vs_oracle():
+    """One block at the benchmark's full size (config 2: dim 3072, 24 heads, B=2, L=7854 on the
+    21x17x22 grid, 512 context tokens) against the fp32 CPU oracle (ref_fp32.block_fwd)."""
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    grid = (21, 17, 22)
+    spec, sd, x, e0, context = _config0_inputs(seed=4, L_grid=grid)
+    cos, sin = R.rope_tables(R.model_freqs(128), grid, 128)
+    p32 = fp32(sd)
+    ck, cv = R.cross_kv(p32, context, spec.num_heads)
+    y_ref = R.block_fwd(p32, x, e0, cos, sin, ck, cv, grid[0], spec.num_heads)
+    w = BlockWeights(sd, spec.num_heads, DEV)
+    ckd, cvd = FastCrossKV(w)(context.to(DEV, torch.bfloat16))
+    cosd, sind = rope_tables(grid, 128, DEV)
+    y = FastBlock(w, grid[0])(x.to(DEV, torch.bfloat16), e0.to(DEV), cosd, sind, ckd, cvd).float().cpu()
+    err, upd = R.rel_rms(y, y_ref), R.rel_rms(y - x, y_ref - x)
+    print(f"config2 block (L=7854) rel-RMS output {err:.2e}, update {upd:.2e}")
+    assert err < BLOCK_TOL
+    assert upd < 5e-2
+
+
+def test_step_30_layers_full_width_vs_oracle():
+    """A whole step-0 noise prediction of the TI2V-5B architecture (30 layers, dim 3072, 24 heads,
+    ffn 14336, text dim 4096, seeded weights) at 1080 tokens (6x12x15 grid, latent [48, 6, 24, 30])
+    against the fp32 CPU oracle chained over all 30 blocks (ref_fp32.main restated): the
+    north-star's step-0 tolerance over the whole depth of the model."""
+    from wanb200 import TI2V_5B, random_model_state
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    spec = TI2V_5B
+    sd = random_model_state(spec, seed=11, device=DEV)
+    g = torch.Generator().manual_seed(12)
+    lat = torch.randn(48, 6, 24, 30, generator=g)
+    ctx, ctx_null = torch.randn(512, 4096, generator=g), torch.randn(512, 4096, generator=g)
+    fast = FastWanDiT((spec, sd), (6, 12, 15), 5.0, DEV)
+    fast.set_context(ctx.to(DEV), ctx_null.to(DEV))
+    pred = fast(lat.to(DEV), 999.0)
+    assert pred.dtype == torch.bfloat16 and tuple(pred.shape) == (48, 6, 24, 30)
+    assert fast.check_device_errors() == 0
+    cfg = {"num_heads": 24, "num_layers": 30, "freq_dim": 256, "patch": (1, 2, 2), "out_dim": 48}
+    with torch.no_grad():
+        ref = R.step(sd, cfg, lat, 999.0, ctx, ctx_null, 5.0)
+    err = R.rel_rms(pred.float().cpu(), ref)
+    print(f"30-layer dim-3072 step-0 (L=1080) rel-RMS vs oracle {err:.3e}")
+    assert err < STEP_TOL
+
+
+def test_block_op_traces_under_torch_compile_fullgraph():
+    """torch.ops.wanb200.block / cross_attn are custom ops with fake kernels: a step built from
+    them compiles with fullgraph=True (no graph break) and gives the eager result."""
+    mg = torch.load(os.path.join(GOLD, "model_small.pt"), weights_only=False)
+    cfg = mg["cfg"]
+    spec = WanSpec(dim=cfg["dim"], ffn_dim=cfg["ffn_dim"], num_heads=cfg["num_heads"], num_layers=cfg["num_layers"],
+                   freq_dim=cfg["freq_dim"], text_dim=cfg["text_dim"], in_dim=cfg["in_dim"], out_dim=cfg["out_dim"],
+                   text_len=cfg["text_len"])
+    lat = mg["latent"]
+    grid = (lat.shape[1], lat.shape[2] // 2, lat.shape[3] // 2)
+    fast = FastWanDiT((spec, mg["state_dict"]), grid, mg["guide"], DEV)
+    fast.set_context(mg["ctx"].to(DEV), mg["ctx_null"].to(DEV))
+    _, e0 = fast.time_embed(mg["t"])
+    x = fast.patch(lat.to(DEV))
+    eager = fast.forward_blocks(x, e0)
+    torch._dynamo.reset()
+    compiled = torch.compile(fast.forward_blocks_op, backend="eager", fullgraph=True)
+    got = compiled(x, e0)
+    assert torch.equal(got, eager)
+    ck, cv = fast.context[0]
+    q = torch.randn(2, 40, ck.shape[2], 128, device=DEV).to(torch.bfloat16)
+    o = torch.compile(lambda a: torch.ops.wanb200.cross_attn(a, ck, cv, 128 ** -0.5), backend="eager",
+                      fullgraph=True)(q)
+    ref = R.attn(q.float(), ck.float(), cv.float())
+    assert R.rel_rms(o.float(), ref) < 1e-2
+
+
+def test_bounded_wait_expiry_reaches_the_step_driver():
+    """A bounded wait that expires inside a kernel surfaces as WanB200Error from the product path.
+    The expiry is made the safe way: a two-rank peer barrier run by one rank on this GPU alone
+    waits for a flag that nothing sets, gives up after its 2 s deadline, records the code in the
+    device error word and returns (no fault, no hang).  FastWanDiT then refuses to go on."""
+    from wanb200 import ops
+    mg = torch.load(os.path.join(GOLD, "model_small.pt"), weights_only=False)
+    cfg = mg["cfg"]
+    spec = WanSpec(dim=cfg["dim"], ffn_dim=cfg["ffn_dim"], num_heads=cfg["num_heads"], num_layers=cfg["num_layers"],
+                   freq_dim=cfg["freq_dim"], text_dim=cfg["text_dim"], in_dim=cfg["in_dim"], out_dim=cfg["out_dim"],
+                   text_len=cfg["text_len"])
+    lat = mg["latent"].to(DEV)
+    grid = (lat.shape[1], lat.shape[2] // 2, lat.shape[3] // 2)
+    fast = FastWanDiT((spec, mg["state_dict"]), grid, mg["guide"], DEV)
+    fast.set_context(mg["ctx"].to(DEV), mg["ctx_null"].to(DEV))
+    fast(lat, mg["t"])
+    assert fast.check_device_errors() == 0
+    dev = torch.device(DEV)
+
+    def expire():  # rank 1 of the two never arrives: the wait gives up after 2 s
+        flags = [torch.zeros(2, dtype=torch.int32, device=DEV) for _ in range(2)]
+        ops.peer_barrier([f.data_ptr() for f in flags], 0, 1, dev)
+        return flags
+
+    keep = expire()
+    with pytest.raises(L.WanB200Error, match="device error word 401"):
+        fast.check_device_errors()
+    with pytest.raises(L.WanB200Error, match="device error word 401"):
+        fast(lat, mg["t"])  # a step refuses to run on top of a reported expiry
+    assert L.device_error(reset=True) == 401
+    assert fast.check_device_errors() == 0
+    # without any synchronous check: a step queued behind the expiry posts the word, and the
+    # next step reports it
+    keep = expire()
+    fast(lat, mg["t"])
+    torch.cuda.synchronize()
+    with pytest.raises(L.WanB200Error, match="device error word 401"):
+        fast(lat, mg["t"])
+    del keep
+    assert L.device_error(reset=True) == 401
+    assert fast.check_device_errors() == 0

@@ -44,13 +44,18 @@ def test_sharded_head_matches_oracle_head():
     e = torch.randn(1, fd.num_frames, C, generator=g) * 0.1
     y_ref = R.head(fd.emb, x, e, fd.grid)
     want = y_ref[1] + fd.guide_scale * (y_ref[0] - y_ref[1])
-    assert R.rel_rms(fd.head(x, e), want) < 1e-6
+    whole = fd.head(x, e)
+    # bf16 out, as _FastHead returns (fast_dit.py:503-505); fp32 math rounded once
+    assert whole.dtype == torch.bfloat16
+    assert R.rel_rms(whole, want) < 4e-3
     for sp in (2, 5):  # 24 tokens: 5 shards of 5 leave the last one with 4 tokens + 1 pad row
         S = -(-L // sp)
         xp = torch.cat([x, x.new_zeros(2, sp * S - L, C)], dim=1)
         parts = [fd.head_tokens(xp[:, r * S:(r + 1) * S], e, r * S) for r in range(sp)]
-        got = fd.combine(torch.cat(parts, dim=1)[:, :L])
-        assert R.rel_rms(got, want) < 1e-6, sp
+        tok = torch.cat(parts, dim=1)[:, :L]
+        assert R.rel_rms(tok, fd.head_tokens(x, e)) < 1e-6, sp
+        got = fd.combine(tok)
+        assert got.dtype == torch.bfloat16 and R.rel_rms(got, want) < 4e-3, sp
 
 
 def test_layout_kinds_and_names():

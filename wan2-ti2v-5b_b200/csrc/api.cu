@@ -21,6 +21,11 @@ int set_cuda_error(const char* what, cudaError_t e) {
 }
 
 static std::mutex g_mu;
+// The error word lives in the library image: a file-scope __device__ int of which every device
+// that loads the library holds its own zero-initialised copy, so no entry point allocates for it.
+// Host code cannot use the symbol's name as an address; the device address is resolved once per
+// device (cudaGetSymbolAddress, with that device current) and cached here.
+static __device__ int g_err_dev_word;
 static int* g_err_word[kMaxDevices] = {};
 static int g_num_sms[kMaxDevices] = {};
 
@@ -37,26 +42,14 @@ int* device_error_word() {
   }
   std::lock_guard<std::mutex> lk(g_mu);
   if (!g_err_word[dev]) {
-    int* p = nullptr;
-    e = cudaMalloc(&p, sizeof(int));
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_err_dev_word);
     if (e != cudaSuccess) {
-      set_cuda_error("cudaMalloc(error word)", e);
+      set_cuda_error("cudaGetSymbolAddress(error word)", e);
       return nullptr;
     }
-    e = cudaMemset(p, 0, sizeof(int));
-    if (e != cudaSuccess) {
-      set_cuda_error("cudaMemset(error word)", e);
-      return nullptr;
-    }
-    g_err_word[dev] = p;
+    g_err_word[dev] = static_cast<int*>(p);
   }
-  return g_err_word[dev];
-}
-
-int* device_error_word_if_present() {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
-  std::lock_guard<std::mutex> lk(g_mu);
   return g_err_word[dev];
 }
 
@@ -198,7 +191,16 @@ int wanb200_device_error(int reset) {
   return v;
 }
 
-int wanb200_version(void) { return 100; }
+int wanb200_device_error_async(int* host_out, void* stream) {
+  if (!host_out) return set_error(WANB200_EINVAL, "device_error_async: null host_out");
+  int* w = device_error_word();
+  if (!w) return WANB200_ECUDA;
+  cudaError_t e = cudaMemcpyAsync(host_out, w, sizeof(int), cudaMemcpyDeviceToHost, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return set_cuda_error("cudaMemcpyAsync(error word)", e);
+  return WANB200_OK;
+}
+
+int wanb200_version(void) { return 200; }
 
 int wanb200_struct_sizes(int64_t* out, int n) {
   const int64_t sizes[7] = {(int64_t)sizeof(wanb200_gemm_params), (int64_t)sizeof(wanb200_attn_params),

@@ -24,6 +24,7 @@
 // Warp roles (320 threads): warps 0-3 softmax of tile 0, warps 4-7 softmax of tile 1 (thread
 // row = TMEM lane), warp 8 TMA producer, warp 9 TMEM allocator + UMMA issuer.  K and V tiles
 // stream through one 3-slot ring (K_0, V_0, K_1, V_1, ...).
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -449,9 +450,10 @@ int64_t attn_workspace_bytes(int64_t batch, int64_t heads, int64_t q_len, int kv
   return kv_splits > 1 ? (int64_t)kv_splits * batch * heads * q_len * (AD + 2) * 4 : 0;
 }
 
-// Host validation shared by the bf16 and e4m3 entry points; *out = the params with the
-// defaults filled in (kv_splits 0 -> 1, part_nslots 0 -> kv_splits).
-static int attn_validate(const wanb200_attn_params* p, wanb200_attn_params* out) {
+// Host validation of everything but the workspace, shared by every attention entry point (bf16,
+// e4m3 and the allocation-free variant); *out = the params with the defaults filled in
+// (kv_splits 0 -> 1, part_nslots 0 -> kv_splits).
+static int attn_validate_shape(const wanb200_attn_params* p, wanb200_attn_params* out) {
   if (!p) return set_error(WANB200_EINVAL, "attn: null params");
   if (!p->q || !p->k || !p->v || !p->o) return set_error(WANB200_EINVAL, "attn: null q/k/v/o");
   if (p->head_dim != AD) return set_error(WANB200_EINVAL, "attn: head_dim must be 128");
@@ -473,11 +475,10 @@ static int attn_validate(const wanb200_attn_params* p, wanb200_attn_params* out)
 
   wanb200_attn_params pp = *p;  // kv_splits 0 means 1 (no split)
   if (pp.kv_splits == 0) pp.kv_splits = 1;
-  p = &pp;
-  if (p->kv_splits < 1 || p->kv_splits > 64) return set_error(WANB200_EINVAL, "attn: kv_splits must be 0..64");
-  const int nkv = (int)((p->kv_len + ABN - 1) / ABN);
-  const int per = (nkv + p->kv_splits - 1) / p->kv_splits;
-  if ((int64_t)(p->kv_splits - 1) * per >= nkv)
+  if (pp.kv_splits < 1 || pp.kv_splits > 64) return set_error(WANB200_EINVAL, "attn: kv_splits must be 0..64");
+  const int nkv = (int)((pp.kv_len + ABN - 1) / ABN);
+  const int per = (nkv + pp.kv_splits - 1) / pp.kv_splits;
+  if ((int64_t)(pp.kv_splits - 1) * per >= nkv)
     return set_error(WANB200_EINVAL, "attn: kv_splits leaves a split without key tiles (use attn_kv_splits)");
   if (pp.part_nslots == 0) {
     if (pp.part_slot0 != 0 || pp.defer_combine != 0)
@@ -487,8 +488,17 @@ static int attn_validate(const wanb200_attn_params* p, wanb200_attn_params* out)
              pp.part_slot0 + pp.kv_splits > pp.part_nslots) {
     return set_error(WANB200_EINVAL, "attn: need 0 <= part_slot0 and part_slot0 + kv_splits <= part_nslots <= 64");
   }
-  const int64_t need = attn_workspace_bytes(p->batch, p->heads, p->q_len, pp.part_nslots);
-  if (need > 0 && (!p->workspace || !aligned16(p->workspace) || p->workspace_bytes < need))
+  *out = pp;
+  return WANB200_OK;
+}
+
+// Shape validation plus the caller's workspace (bf16 and e4m3 entry points).
+static int attn_validate(const wanb200_attn_params* p, wanb200_attn_params* out) {
+  wanb200_attn_params pp;
+  const int rc = attn_validate_shape(p, &pp);
+  if (rc) return rc;
+  const int64_t need = attn_workspace_bytes(pp.batch, pp.heads, pp.q_len, pp.part_nslots);
+  if (need > 0 && (!pp.workspace || !aligned16(pp.workspace) || pp.workspace_bytes < need))
     return set_error(WANB200_EINVAL, "attn: partial slots (kv_splits or part_nslots > 1) need a 16-byte aligned "
                                      "workspace of wanb200_attn_workspace_bytes(.., part_nslots)");
   *out = pp;
@@ -557,16 +567,19 @@ int attn_launch(const wanb200_attn_params* p, int* err, cudaStream_t st, const A
   aa.nkb = (int)((p->kv_len + ABN - 1) / ABN);
   aa.err = err;
 
-  static bool attr_set[kMaxDevices][2] = {};
+  // the shared-memory opt-in, once per device and variant (any host thread may get here first;
+  // setting the attribute twice is harmless, the flag only saves the call)
+  static std::atomic<bool> attr_set[kMaxDevices][2] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!attr_set[dev][f8 ? 1 : 0]) {
+  if (dev < 0 || dev >= kMaxDevices) return set_error(WANB200_EINVAL, "device index out of range");
+  if (!attr_set[dev][f8 ? 1 : 0].load(std::memory_order_acquire)) {
     cudaError_t e = f8 ? cudaFuncSetAttribute(attn_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               A_SMEM_BYTES8)
                        : cudaFuncSetAttribute(attn_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               A_SMEM_BYTES);
     if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(attn)", e);
-    attr_set[dev][f8 ? 1 : 0] = true;
+    attr_set[dev][f8 ? 1 : 0].store(true, std::memory_order_release);
   }
   const int64_t gx = ((p->q_len + 2 * ABM - 1) / (2 * ABM)) * p->kv_splits;
   if (gx > INT32_MAX) return set_error(WANB200_EINVAL, "attn: grid too large");
@@ -824,11 +837,6 @@ int attn_kv_splits(int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len) 
   return best;
 }
 
-
-}  // namespace wanb200
-
-namespace wanb200 {
-
 // ------------------------------------------------------------------ allocation-free variant
 // Some callers cannot let a library allocate device memory: applications that hand all GPU memory
 // to their own pool or allocator at start-up (an allocation behind their back either fails for
@@ -843,83 +851,48 @@ namespace wanb200 {
 // the GPU (different streams, no ordering between them) race on the array.
 constexpr int64_t kNoAllocScratchBytes = int64_t(16) << 20;  // 16 MiB
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
-// Deadline word for the kernels of this variant when the library's per-device error word (which
-// the other entry points allocate on first use) does not exist yet.
-static __device__ int g_noalloc_status;
 
-struct NoAllocDevice {
-  void* scratch = nullptr;
-  int* status = nullptr;
-};
-static NoAllocDevice g_noalloc_dev[kMaxDevices];
+static void* g_noalloc_dev[kMaxDevices] = {};
 static std::mutex g_noalloc_mu;
 
-// Device addresses of the file-scope arrays for the current device.  In host code the array names
-// only stand in for the symbols; the address a kernel may use comes from cudaGetSymbolAddress,
-// resolved once per device, with that device current, on the first call.
-static int noalloc_setup(NoAllocDevice* out) {
+// Device address of the array for the current device.  In host code the array's name only stands
+// in for the symbol; the address a kernel may use comes from cudaGetSymbolAddress, resolved once
+// per device, with that device current, on the first call.
+static int noalloc_scratch(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return set_cuda_error("cudaGetDevice", e);
   if (dev < 0 || dev >= kMaxDevices) return set_error(WANB200_EINVAL, "device index out of range");
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  NoAllocDevice& d = g_noalloc_dev[dev];
-  if (!d.scratch) {
+  if (!g_noalloc_dev[dev]) {
     void* scratch = nullptr;
-    void* status = nullptr;
     e = cudaGetSymbolAddress(&scratch, g_noalloc_scratch);
     if (e != cudaSuccess) return set_cuda_error("cudaGetSymbolAddress(static attention workspace)", e);
-    e = cudaGetSymbolAddress(&status, g_noalloc_status);
-    if (e != cudaSuccess) return set_cuda_error("cudaGetSymbolAddress(static status word)", e);
-    d.status = static_cast<int*>(status);
-    d.scratch = scratch;
+    g_noalloc_dev[dev] = scratch;
   }
-  *out = d;
+  *out = g_noalloc_dev[dev];
   return WANB200_OK;
 }
 
 int attn_fwd_noalloc(const wanb200_attn_params* p, cudaStream_t st) {
   if (!p) return set_error(WANB200_EINVAL, "attn_noalloc: null params");
-  if (!p->q || !p->k || !p->v || !p->o) return set_error(WANB200_EINVAL, "attn_noalloc: null q/k/v/o");
-  if (p->head_dim != AD) return set_error(WANB200_EINVAL, "attn_noalloc: head_dim must be 128");
-  if (p->batch <= 0 || p->heads <= 0 || p->q_len <= 0 || p->kv_len <= 0)
-    return set_error(WANB200_EINVAL, "attn_noalloc: batch, heads, q_len, kv_len must be positive");
-  if (p->batch > 65535 || p->heads > 65535 || p->q_len > (int64_t)INT32_MAX - 2 * ABM ||
-      p->kv_len > (int64_t)INT32_MAX - ABN)
-    return set_error(WANB200_EINVAL, "attn_noalloc: batch/heads/lengths too large");
-  const int64_t strides[8] = {p->q_tok_stride, p->q_batch_stride, p->k_tok_stride, p->k_batch_stride,
-                              p->v_tok_stride, p->v_batch_stride, p->o_tok_stride, p->o_batch_stride};
-  for (int i = 0; i < 8; ++i)
-    if (strides[i] <= 0 || strides[i] % 8)
-      return set_error(WANB200_EINVAL, "attn_noalloc: strides must be positive multiples of 8");
-  if (p->q_tok_stride < p->heads * AD || p->k_tok_stride < p->heads * AD || p->v_tok_stride < p->heads * AD ||
-      p->o_tok_stride < p->heads * AD)
-    return set_error(WANB200_EINVAL, "attn_noalloc: token stride smaller than heads*128");
-  if (!aligned16(p->q) || !aligned16(p->k) || !aligned16(p->v) || !aligned16(p->o))
-    return set_error(WANB200_EINVAL, "attn_noalloc: q/k/v/o must be 16-byte aligned");
-  if (!(p->softmax_scale > 0.f)) return set_error(WANB200_EINVAL, "attn_noalloc: softmax_scale must be positive");
-  wanb200_attn_params pp = *p;
-  if (pp.part_slot0 || pp.part_nslots || pp.defer_combine)
+  if (p->part_slot0 || p->part_nslots || p->defer_combine)
     return set_error(WANB200_EINVAL, "attn_noalloc: partial slots (part_slot0, part_nslots, defer_combine) need "
                                      "wanb200_attn_fwd and a caller workspace");
-  if (pp.kv_splits == 0) pp.kv_splits = 1;
-  if (pp.kv_splits < 1 || pp.kv_splits > 64) return set_error(WANB200_EINVAL, "attn_noalloc: kv_splits must be 0..64");
-  const int nkv = (int)((pp.kv_len + ABN - 1) / ABN);
-  const int per = (nkv + pp.kv_splits - 1) / pp.kv_splits;
-  if ((int64_t)(pp.kv_splits - 1) * per >= nkv)
-    return set_error(WANB200_EINVAL, "attn_noalloc: kv_splits leaves a split without key tiles");
-  const int64_t need = attn_workspace_bytes(pp.batch, pp.heads, pp.q_len, pp.kv_splits);
-  if (need > kNoAllocScratchBytes)
+  wanb200_attn_params pp;
+  int rc = attn_validate_shape(p, &pp);  // the same checks as every other attention entry point
+  if (rc) return rc;
+  if (attn_workspace_bytes(pp.batch, pp.heads, pp.q_len, pp.kv_splits) > kNoAllocScratchBytes)
     return set_error(WANB200_EINVAL,
                      "attn_noalloc: the split-KV partials need more than the fixed 16 MiB static workspace "
                      "(kv_splits * batch * heads * q_len * 520 bytes); use fewer splits or wanb200_attn_fwd");
-  NoAllocDevice d;
-  const int rc = noalloc_setup(&d);
+  rc = noalloc_scratch(&pp.workspace);
   if (rc) return rc;
-  pp.workspace = d.scratch;
   pp.workspace_bytes = kNoAllocScratchBytes;
-  int* err = device_error_word_if_present();
-  return attn_launch(&pp, err ? err : d.status, st);
+  // the library's error word is a __device__ variable too: resolving it allocates nothing
+  int* err = device_error_word();
+  if (!err) return WANB200_ECUDA;
+  return attn_launch(&pp, err, st);
 }
 
 }  // namespace wanb200

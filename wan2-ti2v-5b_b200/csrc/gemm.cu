@@ -15,6 +15,8 @@
 //   warp 1      TMEM allocator + UMMA issuer (one lane)
 //   warps 2..5  epilogue: warp w drains TMEM lanes 32*(w%4)..+31 (= tile rows), 32 columns
 //               per tcgen05.ld, applies the epilogue in fp32 and stores bf16.
+#include <atomic>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -375,14 +377,16 @@ __global__ void __launch_bounds__(192, 1)
 // ------------------------------------------------------------------ host launcher
 template <int EPI>
 static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& ga, int grid, cudaStream_t st) {
-  static bool attr_set[kMaxDevices] = {};
+  // the shared-memory opt-in, once per device (setting it twice from racing threads is harmless)
+  static std::atomic<bool> attr_set[kMaxDevices] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!attr_set[dev]) {
+  if (dev < 0 || dev >= kMaxDevices) return set_error(WANB200_EINVAL, "device index out of range");
+  if (!attr_set[dev].load(std::memory_order_acquire)) {
     cudaError_t e =
         cudaFuncSetAttribute(gemm_bf16_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM_LIMIT);
     if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(gemm)", e);
-    attr_set[dev] = true;
+    attr_set[dev].store(true, std::memory_order_release);
   }
   const int smem = (int)ga.tiles_bytes + GemmCfg<EPI>::FIXED;
   gemm_bf16_kernel<EPI><<<grid, 192, smem, st>>>(ta, tb, ga);

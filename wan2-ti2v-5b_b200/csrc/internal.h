@@ -19,12 +19,10 @@ int set_cuda_error(const char* what, cudaError_t e);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Per-device int in global memory that kernels write error codes into (allocated once per
-// device on first use; nullptr + last error set on failure).
+// Device address of the current device's error word, the int that kernels write error codes
+// into (a __device__ variable of the library, resolved once per device; allocates nothing;
+// nullptr + last error set on failure).
 int* device_error_word();
-// The error word of the current device if some entry point already created it, else nullptr
-// (never allocates).
-int* device_error_word_if_present();
 int num_sms();
 
 // 2-D / 4-D bf16 TMA descriptors with 128-byte swizzle and zero fill out of bounds.

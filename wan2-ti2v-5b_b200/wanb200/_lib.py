@@ -79,7 +79,7 @@ EXPORTS = ("wanb200_gemm_bf16", "wanb200_attn_fwd", "wanb200_layernorm", "wanb20
            "wanb200_bias_gate_residual", "wanb200_last_error", "wanb200_device_error", "wanb200_version",
            "wanb200_struct_sizes", "wanb200_peer_barrier", "wanb200_attn_workspace_bytes",
            "wanb200_attn_kv_splits", "wanb200_attn_fwd_noalloc", "wanb200_shard_gather", "wanb200_attn_fwd_fp8",
-           "wanb200_attn_fp8_workspace_bytes")
+           "wanb200_attn_fp8_workspace_bytes", "wanb200_device_error_async")
 
 _lock = threading.Lock()
 _lib = None
@@ -113,6 +113,8 @@ def load():
             lib.wanb200_last_error.argtypes = []
             lib.wanb200_device_error.argtypes = [c_int]
             lib.wanb200_device_error.restype = c_int
+            lib.wanb200_device_error_async.argtypes = [c_void_p, c_void_p]
+            lib.wanb200_device_error_async.restype = c_int
             lib.wanb200_version.restype = c_int
             lib.wanb200_struct_sizes.argtypes = [ctypes.POINTER(c_int64), c_int]
             lib.wanb200_struct_sizes.restype = c_int
@@ -148,4 +150,63 @@ def check(rc: int, what: str):
 
 def device_error(reset: bool = False) -> int:
     """Device-side error word of the current device (synchronizes)."""
-    return load().wanb200_device_error(1 if reset else 0)
+    v = load().wanb200_device_error(1 if reset else 0)
+    if v < 0:
+        check(v, "wanb200_device_error")
+    return v
+
+
+class DeviceErrorProbe:
+    """Reads a device's error word behind the work queued on a stream, without synchronizing.
+
+    `post(stream)` queues a copy of the word into page-locked host memory
+    (wanb200_device_error_async) and records an event after it; `poll()` returns the value of
+    the last copy that has landed (0 while none has); `wait(stream)` queues a fresh copy and
+    blocks for it.  The word is sticky (the first expiry stays until reset), so a copy taken at
+    any later point reports an earlier expiry: a step driver that posts once per step and polls
+    at the start of the next one sees every expiry at most a step or two late, at no cost to the
+    pipeline.  While a copy is still in flight, `post` leaves it be and queues nothing.
+    """
+
+    def __init__(self, device):
+        import torch
+        self._torch = torch
+        self.device = torch.device(device)
+        self._buf = None  # page-locked int32, made on the first post (construction needs no GPU)
+        self._event = None
+        self._seen = 0
+
+    def post(self, stream=None):
+        t = self._torch
+        if self._event is not None and not self._event.query():
+            return
+        if self._event is not None:
+            self._seen = int(self._buf[0])
+        if self._buf is None:
+            self._buf = t.zeros(1, dtype=t.int32).pin_memory()
+        st = stream if stream is not None else t.cuda.current_stream(self.device)
+        check(load().wanb200_device_error_async(self._buf.data_ptr(), st.cuda_stream), "wanb200_device_error_async")
+        self._event = t.cuda.Event()
+        self._event.record(st)
+
+    def poll(self) -> int:
+        if self._event is not None and self._event.query():
+            self._seen = int(self._buf[0])
+        return self._seen
+
+    def wait(self, stream=None) -> int:
+        if self._event is not None:
+            self._event.synchronize()
+        self._event = None
+        self.post(stream)
+        self._event.synchronize()
+        self._seen = int(self._buf[0])
+        return self._seen
+
+
+def raise_on_device_error(code: int, where: str):
+    """Raise WanB200Error for a non-zero device error word (a bounded wait inside a kernel gave up,
+    so the outputs of that launch are incomplete)."""
+    if code:
+        raise WanB200Error(f"{where}: device error word {code} (a bounded wait expired inside a kernel; the "
+                           "results since the last check are not valid; wanb200.device_error(reset=True) clears it)")

@@ -24,6 +24,9 @@ Op sequence of one block (N = B*L tokens, C = 3072, C_l = C / TP, F_l = 14336 / 
 """
 from __future__ import annotations
 
+import itertools
+import weakref
+
 import torch
 import torch.distributed as dist
 
@@ -362,3 +365,35 @@ class FastBlockSP:
     def launches(self) -> int:
         return 15
 
+
+
+# ---------------------------------------------------------------------------- torch.library op
+# The per-block compiled unit of the reference (`_FastBlock.forward` / `_FastBlockSP.forward`,
+# models/fast_dit.py:270, 349, compiled whole at 586 / 646-649) as one custom op, so a step built
+# from these blocks traces under torch.compile(fullgraph=True) / make_fx as one opaque node per
+# block.  The block's weights and collectives are not tensors of the op: a block object is
+# registered once and named by an integer handle (held weakly; it lives as long as its owner).
+_BLOCKS = weakref.WeakValueDictionary()
+_NEXT_HANDLE = itertools.count(1)
+
+
+def register_block(block) -> int:
+    """Handle of a FastBlock / FastBlockSP for torch.ops.wanb200.block."""
+    h = next(_NEXT_HANDLE)
+    _BLOCKS[h] = block
+    return h
+
+
+@torch.library.custom_op("wanb200::block", mutates_args=())
+def block_op(x: torch.Tensor, e: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, ck: torch.Tensor,
+             cv: torch.Tensor, handle: int) -> torch.Tensor:
+    """x -> the block's new residual stream (a new tensor of x's shape; no input is modified)."""
+    blk = _BLOCKS.get(handle)
+    if blk is None:
+        raise KeyError(f"wanb200::block: no live block with handle {handle}")
+    return blk.forward(x, e, cos, sin, ck, cv)
+
+
+@block_op.register_fake
+def _(x, e, cos, sin, ck, cv, handle):
+    return torch.empty_like(x)

@@ -33,6 +33,19 @@ def spec_from_config(cfg: dict) -> WanSpec:
     missing = [k for k in need if k not in cfg]
     if missing:
         raise ValueError(f"config.json lacks {missing}")
+    # the fast path implements the TI2V / T2V forward with full (global) attention; a config that
+    # asks for something else must not load and silently run another model's math
+    # (WanModel.__init__, wan/modules/model.py:304-317)
+    window = tuple(int(x) for x in cfg.get("window_size", (-1, -1)))
+    if window != (-1, -1):
+        raise ValueError(f"window_size {window}: local-window attention is not implemented (only (-1, -1))")
+    model_type = cfg.get("model_type", "t2v")
+    if model_type not in ("t2v", "ti2v"):
+        raise ValueError(f"model_type {model_type!r} is not implemented (only 't2v' / 'ti2v', the TI2V-5B DiT; "
+                         "i2v adds image-embedding cross-attention)")
+    for flag in ("qk_norm", "cross_attn_norm"):
+        if not cfg.get(flag, True):
+            raise ValueError(f"{flag}=False is not implemented (the TI2V-5B DiT has both norms)")
     return WanSpec(dim=int(cfg["dim"]), ffn_dim=int(cfg["ffn_dim"]), num_heads=int(cfg["num_heads"]),
                    num_layers=int(cfg["num_layers"]), freq_dim=int(cfg["freq_dim"]), text_dim=int(cfg["text_dim"]),
                    in_dim=int(cfg["in_dim"]), out_dim=int(cfg["out_dim"]),

@@ -25,7 +25,8 @@ import torch
 import torch.distributed as dist
 import torch.nn.functional as F
 
-from .block import FastBlock, FastBlockSP, FastCrossKV
+from . import _lib as L
+from .block import FastBlock, FastBlockSP, FastCrossKV, register_block
 from .weights import BlockWeights, WanSpec, block_state
 
 BF16 = torch.bfloat16
@@ -146,6 +147,8 @@ class FastWanDiT:
                            for w in self.block_weights]
         self.cross_kv = [FastCrossKV(w, tp_group, spec.eps) for w in self.block_weights]
         self.context = None
+        self._err_probe = L.DeviceErrorProbe(self.device)
+        self._handles = None
 
     @classmethod
     def from_checkpoint(cls, path, grid, guide_scale, device, **kwargs):
@@ -212,24 +215,35 @@ class FastWanDiT:
         return self.combine(self.head_tokens(x, e))
 
     def combine(self, y):
-        """Unpatchify [B, L, 4*48] and combine the CFG branches."""
+        """Unpatchify [B, L, 4*48] and combine the CFG branches -> [48, F, H, W] bf16, the dtype
+        `_FastHead` / `_FastHeadCfgPar` return (fast_dit.py:503-505, 522-524).  The combine runs
+        in fp32 and rounds once (the reference rounds the branches to bf16 first)."""
         f, h, w = self.grid
         p, q, r = self.spec.patch_size
         c = self.spec.out_dim
         B = y.shape[0]
         y = y.view(B, f, h, w, p, q, r, c).permute(0, 7, 1, 4, 2, 5, 3, 6).reshape(B, c, f * p, h * q, w * r)
         if self.cfg_group is None:
-            return y[1] + self.guide_scale * (y[0] - y[1])
+            return (y[1] + self.guide_scale * (y[0] - y[1])).to(BF16)
         # CFG-parallel: uncond + g (cond - uncond) = g * cond + (1 - g) * uncond, summed over the pair
         out = (y[0] * self.cfg_w).contiguous()
         if self.pair_group is not None:
             dist.all_reduce(out, group=self.pair_group)
-        return out
+        return out.to(BF16)
 
     # ------------------------------------------------------------------ step
     def forward_blocks(self, x, e0):
         for blk, (ck, cv) in zip(self.blocks, self.context):
             x = blk(x, e0, self.cos, self.sin, ck, cv)
+        return x
+
+    def forward_blocks_op(self, x, e0):
+        """forward_blocks through the torch.ops.wanb200.block custom op (one opaque node per block,
+        with a fake kernel), for callers that trace the step with torch.compile / make_fx."""
+        if self._handles is None:
+            self._handles = [register_block(b) for b in self.blocks]
+        for h, (ck, cv) in zip(self._handles, self.context):
+            x = torch.ops.wanb200.block(x, e0, self.cos, self.sin, ck, cv, h)
         return x
 
     def shard(self, x):
@@ -267,18 +281,34 @@ class FastWanDiT:
         return full.permute(1, 0, 2, 3).reshape(B, self.sp_size * S, D)[:, :self.seq_len]
 
     def __call__(self, latent, t):
+        """One CFG noise prediction: latent [C, F, H, W], timestep t -> [C, F, H, W] bf16.
+
+        Every call queues a read of the device error word behind its launches and checks the
+        last read that has landed (a step or two late, without synchronizing), raising
+        WanB200Error if a kernel's bounded wait expired; `check_device_errors()` checks now."""
         if self.context is None:
             raise RuntimeError("call set_context() first")
+        L.raise_on_device_error(self._err_probe.poll(), "FastWanDiT")
         e, e0 = self.time_embed(t)
         x = self.patch(latent)
         if self.kv_gather is not None:
             xs = self.forward_blocks(self.shard_q(x), e0)
-            return self.combine(self.gather_q(self.head_tokens(xs, e, self.sp_rank * self.kv_gather.S)))
-        if self.sp:
+            out = self.combine(self.gather_q(self.head_tokens(xs, e, self.sp_rank * self.kv_gather.S)))
+        elif self.sp:
             x = self.unshard(self.forward_blocks(self.shard(x), e0))
+            out = self.head(x, e)
         else:
-            x = self.forward_blocks(x, e0)
-        return self.head(x, e)
+            out = self.head(self.forward_blocks(x, e0), e)
+        self._err_probe.post()
+        return out
+
+    def check_device_errors(self, raise_error: bool = True) -> int:
+        """Wait for the work queued so far and read the device error word: 0, or (raise_error)
+        WanB200Error for a bounded wait that expired inside a kernel."""
+        code = self._err_probe.wait()
+        if raise_error:
+            L.raise_on_device_error(code, "FastWanDiT")
+        return code
 
     @property
     def launches_per_step(self) -> int:

@@ -368,3 +368,15 @@ def attn_op(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, softmax_scale: fl
 @attn_op.register_fake
 def _(q, k, v, softmax_scale):
     return torch.empty(q.shape[0], q.shape[1], q.shape[2], q.shape[3], dtype=q.dtype, device=q.device)
+
+
+# The cross-attention seam (`_nki_cross` / `_cte` over the cached text K/V, fast_dit.py:244-255):
+# q [B, L, H, 128] against ck / cv [B, Lc, H, 128].
+@torch.library.custom_op("wanb200::cross_attn", mutates_args=())
+def cross_attn_op(q: torch.Tensor, ck: torch.Tensor, cv: torch.Tensor, softmax_scale: float) -> torch.Tensor:
+    return attention(q, ck, cv, softmax_scale=softmax_scale, kind="attn_cross")
+
+
+@cross_attn_op.register_fake
+def _(q, ck, cv, softmax_scale):
+    return torch.empty(q.shape[0], q.shape[1], q.shape[2], q.shape[3], dtype=q.dtype, device=q.device)

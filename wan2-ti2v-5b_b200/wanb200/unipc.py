@@ -146,7 +146,9 @@ class FlowUniPC:
 def denoise(dit, latent: torch.Tensor, steps: int, shift: float = 5.0, image_latent: torch.Tensor = None,
             sampler: FlowUniPC = None) -> torch.Tensor:
     """The reference's denoise loop (inference_neuron_ti2v.py:505-532, device scheduler) with
-    `dit(latent, t)` the CFG noise prediction (`FastWanDiT.__call__`).
+    `dit(latent, t)` the CFG noise prediction (`FastWanDiT.__call__`).  When `dit` has
+    `check_device_errors` (FastWanDiT does), the loop ends with it: a bounded wait that expired
+    inside a kernel raises WanB200Error instead of returning a silently wrong latent.
 
     latent [C, F, H, W] on the device; image_latent [C, 1, H, W] (optional): frame 0 is pinned to
     it after every step.  Returns the final latent."""
@@ -160,4 +162,7 @@ def denoise(dit, latent: torch.Tensor, steps: int, shift: float = 5.0, image_lat
         latent = s.step(noise.reshape(latent.shape).to(latent.dtype), latent)
         if image_latent is not None:
             latent[:, :1] = image_latent.to(latent.dtype)
+    check = getattr(dit, "check_device_errors", None)
+    if check is not None:  # the loop's result is only valid if no kernel's bounded wait expired
+        check()
     return latent
