@@ -79,6 +79,11 @@ typedef struct wanb200_gemm_params {
   void* peer_out[WANB200_MAX_PEERS]; int npeers; int src_rank; int64_t shard_rows; /* SCATTER */
   int tile_n;  /* tile width along N: 0 = the library's choice (fills the SMs' last wave), else a
                 * multiple of 32 in 64..256 (for tuning; results do not depend on it) */
+  /* fp32 residual stream (GATE_RES / RES only): residual_f32 != 0 reads residual as fp32
+   * [M, ldr], out_f32 != 0 writes d as fp32 [M, ldd] (strides still in elements).  The sums
+   * x + y stay in fp32 across a step instead of being rounded to bf16 after every block's three
+   * updates, the dominant error of a 30-layer bf16 step. */
+  int residual_f32, out_f32;
 } wanb200_gemm_params;
 
 int wanb200_gemm_bf16(const wanb200_gemm_params* p, void* stream);
@@ -171,6 +176,7 @@ typedef struct wanb200_ln_params {
   /* all-gather fused into the norm: when npush > 0 every output row is also stored at
    * push_out[p] + (push_row0 + row) * dim for p < npush (peer-mapped buffers; out may be NULL) */
   void* push_out[WANB200_MAX_PEERS]; int npush; int64_t push_row0;
+  int x_f32;  /* x is fp32 (the fp32 residual stream); out stays bf16 */
 } wanb200_ln_params;
 
 int wanb200_layernorm(const wanb200_ln_params* p, void* stream);
@@ -206,6 +212,7 @@ typedef struct wanb200_residual_params {
   const void* gate_mod; const float* gate_e0; int64_t gate_frame_stride;
   int64_t seq_len, tokens_per_frame, row_offset, rows_per_seq; /* frame(row) as for the GEMM */
   int nsum; int64_t y_slice_stride; /* y = sum of nsum slices y + s * y_slice_stride (0/1: y alone) */
+  int residual_f32, out_f32;        /* residual / out are fp32 (the fp32 residual stream); y stays bf16 */
 } wanb200_residual_params;
 
 int wanb200_bias_gate_residual(const wanb200_residual_params* p, void* stream);

@@ -91,6 +91,9 @@ def test_gemm_rejects_bad_shapes_on_host():
     p.epilogue = 9
     rc, msg = _rc_msg(lib.wanb200_gemm_bf16, p)
     assert rc == -1 and "epilogue" in msg
+    p.epilogue, p.bias, p.out_f32 = L.EPI_BIAS, 48, 1  # fp32 output is for the residual epilogues only
+    rc, msg = _rc_msg(lib.wanb200_gemm_bf16, p)
+    assert rc == -1 and "residual_f32 / out_f32" in msg
 
 
 def test_attn_rejects_bad_args_on_host():

@@ -298,3 +298,73 @@ def test_bias_gate_residual():
     assert rel(out, res.float() + (y.float() + b.float()) * g) < 4e-3
     out2 = ops.bias_gate_residual(res, y, b)
     assert rel(out2, res.float() + y.float() + b.float()) < 4e-3
+
+
+# ---------------------------------------------------------------------------- fp32 residual stream
+F32 = torch.float32
+
+
+@pytest.mark.parametrize("res_dt,out_dt,inplace", [(F32, F32, False), (F32, F32, True), (torch.bfloat16, F32, False),
+                                                   (F32, torch.bfloat16, False)])
+def test_gemm_gate_residual_fp32_stream(res_dt, out_dt, inplace):
+    """GATE_RES with an fp32 residual and / or an fp32 output: the sum is formed in fp32 and stored
+    without rounding (fp32 out: error of the bf16 GEMM operands only, far below bf16 output rounding)."""
+    Lx, nf, B = 360, 6, 2
+    M, N, K = B * Lx, 512, 384
+    a, w, b = randn(M, K, seed=61), randn(N, K, scale=0.05, seed=62), randn(N, scale=0.1, seed=63)
+    res = (torch.randn(M, N, generator=torch.Generator(device=DEV).manual_seed(64), device=DEV) * 3).to(res_dt)
+    mod = randn(6, N, scale=0.1, seed=65)
+    e0 = torch.randn(nf, 6, N, device=DEV) * 0.1
+    res0 = res.clone()
+    out = res if inplace else torch.empty(M, N, device=DEV, dtype=out_dt)
+    ops.linear(a, w, b, epilogue=L.EPI_BIAS_GATE_RES, residual=res, gate=(mod[2], e0[:, 2, :]),
+               frames=(Lx, Lx // nf), out=out)
+    g = (mod[2].float() + e0[:, 2, :]).repeat_interleave(Lx // nf, 0).repeat(B, 1)
+    y = (a.float() @ w.float().t() + b.float()) * g
+    ref = res0.float() + y
+    assert out.dtype == out_dt
+    if out_dt == F32:  # the residual part is exact: only the GEMM's fp32 accumulation differs
+        assert rel(out - res0.float(), y) < 1e-5
+    assert rel(out, ref) < (1e-6 if out_dt == F32 else 4e-3)
+
+
+def test_gemm_residual_fp32_stream():
+    M, N, K = 333, 256, 128
+    a, w, b = randn(M, K, seed=66), randn(N, K, scale=0.05, seed=67), randn(N, seed=68)
+    res = torch.randn(M, N, device=DEV) * 5
+    res0 = res.clone()
+    out = ops.linear(a, w, b, epilogue=L.EPI_BIAS_RES, residual=res, out=res)  # in place, fp32
+    assert out is res and out.dtype == F32
+    assert rel(out, res0 + a.float() @ w.float().t() + b.float()) < 1e-6
+
+
+def test_layernorm_reads_the_fp32_stream():
+    B, Lx, nf, C = 2, 540, 6, 3072
+    x = torch.randn(B * Lx, C, device=DEV) * 4 + 1
+    mod = randn(6, C, scale=0.1, seed=69)
+    e0 = torch.randn(nf, 6, C, device=DEV) * 0.1
+    h = ops.layernorm_modulate(x, mod, e0, 3, 4, (Lx, Lx // nf))
+    ln = torch.nn.functional.layer_norm(x, (C,), eps=1e-6)
+    sh = (mod[3].float() + e0[:, 3]).repeat_interleave(Lx // nf, 0).repeat(B, 1)
+    sc = (mod[4].float() + e0[:, 4]).repeat_interleave(Lx // nf, 0).repeat(B, 1)
+    assert h.dtype == torch.bfloat16 and rel(h, ln * (1 + sc) + sh) < 4e-3
+    wgt, bia = randn(C, seed=70), randn(C, seed=71)
+    h2 = ops.layernorm_affine(x, wgt, bia)
+    assert rel(h2, torch.nn.functional.layer_norm(x, (C,), wgt.float(), bia.float(), eps=1e-6)) < 4e-3
+    x3 = torch.randn(37, 768, device=DEV)  # one warp per row (dim % 512 != 0)
+    h3 = ops.layernorm_affine(x3, wgt[:768], bia[:768])
+    assert rel(h3, torch.nn.functional.layer_norm(x3, (768,), wgt[:768].float(), bia[:768].float(), eps=1e-6)) < 4e-3
+
+
+def test_bias_gate_residual_fp32_stream():
+    B, Lx, nf, C = 2, 120, 4, 768
+    res, y, b = torch.randn(B * Lx, C, device=DEV) * 3, randn(B * Lx, C, seed=72), randn(C, seed=73)
+    mod = randn(6, C, scale=0.1, seed=74)
+    e0 = torch.randn(nf, 6, C, device=DEV) * 0.1
+    g = (mod[5].float() + e0[:, 5]).repeat_interleave(Lx // nf, 0).repeat(B, 1)
+    ref = res + (y.float() + b.float()) * g
+    out = ops.bias_gate_residual(res, y, b, gate=(mod[5], e0[:, 5, :]), frames=(Lx, Lx // nf))
+    assert out.dtype == F32 and rel(out, ref) < 1e-6
+    out16 = torch.empty(B * Lx, C, device=DEV, dtype=torch.bfloat16)
+    ops.bias_gate_residual(res, y, b, gate=(mod[5], e0[:, 5, :]), frames=(Lx, Lx // nf), out=out16)
+    assert rel(out16, ref) < 4e-3

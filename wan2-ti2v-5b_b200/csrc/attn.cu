@@ -8,8 +8,10 @@
 //
 // One CTA = one (batch, head) and TWO 128-query tiles (t = 0, 1).  Per 128-key tile j:
 //   S_t = Q_t K_j^T          UMMA 128x128x128 into TMEM (S_0 cols 0..127, S_1 cols 128..255)
-//   P_t = exp2(S_t*c - m_t)  softmax warpgroup t, bf16, into swizzled shared memory
-//   O_t += P_t V_j           UMMA into TMEM (O_0 cols 256..383, O_1 cols 384..511)
+//   P_t = exp2(S_t*c - m_t)  softmax warpgroup t, bf16 pairs written back into TMEM over the
+//                            first 64 columns of S_t (e4m3 variant: swizzled shared memory)
+//   O_t += P_t V_j           UMMA with A = P_t read from TMEM, into TMEM (O_0 cols 256..383,
+//                            O_1 cols 384..511)
 // The tensor core alternates between the tiles, so the MMAs of one tile run while the other
 // tile's warpgroup exponentiates.  O stays in TMEM for the whole key loop; the running max used
 // for the exponent is only raised when a tile's max exceeds it by more than 8 (a factor 256 in
@@ -23,7 +25,8 @@
 //
 // Warp roles (320 threads): warps 0-3 softmax of tile 0, warps 4-7 softmax of tile 1 (thread
 // row = TMEM lane), warp 8 TMA producer, warp 9 TMEM allocator + UMMA issuer.  K and V tiles
-// stream through one 3-slot ring (K_0, V_0, K_1, V_1, ...).
+// stream through one ring (K_0, V_0, K_1, V_1, ...): 5 slots of 32 KB in the bf16 kernel, whose
+// P needs no shared memory, 3 slots of 16 KB in the e4m3 one.
 #include <atomic>
 #include <mutex>
 
@@ -35,11 +38,9 @@ namespace wanb200 {
 constexpr int ABM = 128, ABN = 128, AD = 128;
 constexpr int A_TILE = ABM * AD * 2;  // 32 KB: two 64-column swizzle blocks of 16 KB
 constexpr int A_BLK = 16384;
-constexpr int A_RING = 3;
-constexpr int A_OFF_Q = 0;                      // Q_0, Q_1
-constexpr int A_OFF_P = A_OFF_Q + 2 * A_TILE;   // P_0, P_1
-constexpr int A_OFF_R = A_OFF_P + 2 * A_TILE;   // ring
-constexpr int A_TILES_END = A_OFF_R + A_RING * A_TILE;  // 229376
+constexpr int A_RING = 3;    // e4m3 variant: K/V ring slots (Q_0, Q_1, P_0, P_1 and the ring in shared memory)
+constexpr int A_RING16 = 5;  // bf16: P lives in tensor memory, so the ring takes P's 64 KB: Q_0, Q_1, 5 slots
+constexpr int A_TILES_END = (2 + A_RING16) * A_TILE;  // 229376
 constexpr int A_SMEM_BYTES = A_TILES_END + 256 + 1024;
 // e4m3 variant: every tile is one 16 KB swizzle block (128 rows x 128 one-byte elements)
 constexpr int A_TILES_END8 = (2 + 2 + A_RING) * A_BLK;  // 114688
@@ -81,7 +82,9 @@ __global__ void __launch_bounds__(A_THREADS, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const AttnArgs args) {
   constexpr int TILE = FP8 ? A_BLK : A_TILE;
-  constexpr int OFF_Q = 0, OFF_P = 2 * TILE, OFF_R = 4 * TILE, TILES_END = OFF_R + A_RING * TILE;
+  constexpr int RING = FP8 ? A_RING : A_RING16;
+  // bf16: [Q_0 Q_1 | ring]; e4m3: [Q_0 Q_1 | P_0 P_1 | ring] (the bf16 P goes to tensor memory)
+  constexpr int OFF_Q = 0, OFF_P = 2 * TILE, OFF_R = (FP8 ? 4 : 2) * TILE, TILES_END = OFF_R + RING * TILE;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
@@ -89,14 +92,14 @@ __global__ void __launch_bounds__(A_THREADS, 1)
   uint8_t* meta = smem + TILES_END;
   const uint32_t m0 = smem_u32(meta);
   const uint32_t q_full = m0;                 // 1
-  const uint32_t kv_full = m0 + 8;            // 3
-  const uint32_t kv_empty = m0 + 32;          // 3
-  const uint32_t s_full = m0 + 56;            // 2
-  const uint32_t p_full = m0 + 72;            // 2
-  const uint32_t o_done = m0 + 88;            // 2
-  const uint32_t done_bar = m0 + 104;         // 1
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(meta + 112);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(meta + 116);
+  const uint32_t kv_full = m0 + 8;            // RING (<= 5)
+  const uint32_t kv_empty = m0 + 48;          // RING
+  const uint32_t s_full = m0 + 88;            // 2
+  const uint32_t p_full = m0 + 104;           // 2
+  const uint32_t o_done = m0 + 120;           // 2
+  const uint32_t done_bar = m0 + 136;         // 1
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(meta + 144);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(meta + 148);
   int* err = args.err;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -107,7 +110,7 @@ __global__ void __launch_bounds__(A_THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < A_RING; ++s) {
+    for (int s = 0; s < RING; ++s) {
       mbar_init(kv_full + 8 * s, 1);
       mbar_init(kv_empty + 8 * s, 1);
     }
@@ -145,8 +148,8 @@ __global__ void __launch_bounds__(A_THREADS, 1)
         if constexpr (!FP8) tma_load_4d(sbase + OFF_Q + t * TILE + A_BLK, &tmQ, q_full, 64, h, q0 + t * ABM, b);
       }
       for (int i = 0; i < 2 * nkv; ++i) {
-        const int slot = i % A_RING;
-        const uint32_t ph = (i / A_RING) & 1;
+        const int slot = i % RING;
+        const uint32_t ph = (i / RING) & 1;
         if (!mbar_wait(kv_empty + 8 * slot, ph ^ 1, abort_flag, err, kErrTimeoutAttnProducer)) {
           ok = false;
           break;
@@ -169,7 +172,7 @@ __global__ void __launch_bounds__(A_THREADS, 1)
       }
       if (!ok) {
         mbar_drain(q_full, 0, err);
-        for (int s = 0; s < A_RING; ++s)
+        for (int s = 0; s < RING; ++s)
           if ((issued >> s) & 1) mbar_drain(kv_full + 8 * s, (last_ph >> s) & 1, err);
       }
     }
@@ -180,10 +183,10 @@ __global__ void __launch_bounds__(A_THREADS, 1)
       constexpr uint32_t idesc_s = FP8 ? idesc_e4m3_f32(ABM, ABN, false, false) : idesc_bf16_f32(ABM, ABN, false, false);
       constexpr uint32_t idesc_o = FP8 ? idesc_e4m3_f32(ABM, AD, false, false) : idesc_bf16_f32(ABM, AD, false, true);
       auto kv_wait = [&](int i) -> bool {
-        return mbar_wait(kv_full + 8 * (i % A_RING), (i / A_RING) & 1, abort_flag, err, kErrTimeoutAttnMma);
+        return mbar_wait(kv_full + 8 * (i % RING), (i / RING) & 1, abort_flag, err, kErrTimeoutAttnMma);
       };
       auto qk = [&](int t, int j) {
-        const int slot = (2 * j) % A_RING;
+        const int slot = (2 * j) % RING;
         tc_fence_after();
         const uint32_t d = tmem_base + t * ABN;
         const uint32_t qb = sbase + OFF_Q + t * TILE;
@@ -204,24 +207,24 @@ __global__ void __launch_bounds__(A_THREADS, 1)
       };
       auto pv = [&](int t, int j) -> bool {
         if (!mbar_wait(p_full + 8 * t, j & 1, abort_flag, err, kErrTimeoutAttnMma)) return false;
-        const int slot = (2 * j + 1) % A_RING;
+        const int slot = (2 * j + 1) % RING;
         tc_fence_after();
         const uint32_t d = tmem_base + 2 * ABN + t * AD;
-        const uint32_t pb = sbase + OFF_P + t * TILE;
         const uint32_t vb = sbase + OFF_R + slot * TILE;
         if constexpr (FP8) {
+          const uint32_t pb = sbase + OFF_P + t * TILE;
 #pragma unroll
           for (int kk = 0; kk < ABN / 32; ++kk)  // P (query x key) and V^T (d x key), both key-major
             umma_e4m3(d, sw128_desc(pb + kk * 32, 16, 1024), sw128_desc(vb + kk * 32, 16, 1024), idesc_o,
                       (j | kk) != 0);
         } else {
+          // P_t in tensor memory, in the columns of S_t (64 columns of bf16 pairs); the next
+          // S_t = Q_t K^T is issued after this MMA and UMMAs of one thread execute in order.
+          const uint32_t pa = tmem_base + t * ABN;
 #pragma unroll
-          for (int kk = 0; kk < ABN / 16; ++kk) {
-            const uint32_t poff = (kk >> 2) * A_BLK + (kk & 3) * 32;
+          for (int kk = 0; kk < ABN / 16; ++kk)
             // V tile: key row k at k*128 B inside each 64-wide d block; d blocks 16 KB apart.
-            umma_bf16(d, sw128_desc(pb + poff, 16, 1024), sw128_desc(vb + kk * 2048, A_BLK, 1024), idesc_o,
-                      (j | kk) != 0);
-          }
+            umma_bf16_tmem_a(d, pa + kk * 8, sw128_desc(vb + kk * 2048, A_BLK, 1024), idesc_o, (j | kk) != 0);
         }
         if (t == 1) umma_commit(kv_empty + 8 * slot);
         if (j == nkv - 1) umma_commit(o_done + 8 * t);
@@ -282,14 +285,16 @@ __global__ void __launch_bounds__(A_THREADS, 1)
         for (int k = 0; k < ABN; ++k)
           if (kbase + k >= args.Lk) s[k] = -INFINITY;
       }
-      // row max with 8 independent partial maxima (a single chain of 127 dependent FMNMX would
-      // dominate the warp's latency; two softmax warps per sub-partition cannot hide it)
+      // row max with 8 independent partial maxima of three-input FMNMX (a single chain of 127
+      // dependent FMNMX would dominate the warp's latency; two values per instruction)
       float m8[8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) m8[k] = s[k];
+      for (int c = 0; c < 8; ++c) m8[c] = fmaxf(s[2 * c], s[2 * c + 1]);
 #pragma unroll
-      for (int k = 8; k < ABN; ++k) m8[k & 7] = fmaxf(m8[k & 7], s[k]);
-      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+      for (int i = 1; i < ABN / 16; ++i)
+#pragma unroll
+        for (int c = 0; c < 8; ++c) m8[c] = fmax3(m8[c], s[16 * i + 2 * c], s[16 * i + 2 * c + 1]);
+      const float mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
       const float m_cand = mx * sl2;
       const bool need = m_cand > m_used + A_RESCALE_THRESHOLD;
       const bool any_need = __any_sync(0xffffffffu, need);
@@ -325,24 +330,27 @@ __global__ void __launch_bounds__(A_THREADS, 1)
           }
         }
       } else {
+        // P in bf16 pairs straight into tensor memory over S_t's first 64 columns (S is already
+        // in registers); packed fp32x2 FMA / add halve the instructions of the scale and the sums
+        const float2 sl2v = make_float2(sl2, sl2), negv = make_float2(neg, neg);
+        float2 acc2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};  // 4 partial sums (4 pairs spill)
 #pragma unroll
         for (int c = 0; c < ABN / 32; ++c) {
           uint32_t pk[16];
 #pragma unroll
           for (int k = 0; k < 32; k += 2) {
-            const float p0 = ex2_approx(fmaf(s[c * 32 + k], sl2, neg));
-            const float p1 = ex2_approx(fmaf(s[c * 32 + k + 1], sl2, neg));
-            r8[(k >> 1) & 7] += p0 + p1;
+            const float2 x = __ffma2_rn(make_float2(s[c * 32 + k], s[c * 32 + k + 1]), sl2v, negv);
+            const float p0 = ex2_approx(x.x), p1 = ex2_approx(x.y);
+            acc2[(k >> 1) & 1] = __fadd2_rn(acc2[(k >> 1) & 1], make_float2(p0, p1));
             pk[k >> 1] = pack_bf16x2(p0, p1);
           }
-          uint8_t* rowp = pbuf + (c >> 1) * A_BLK + (r >> 3) * 1024 + (r & 7) * 128;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int ch = (c & 1) * 4 + q;
-            *reinterpret_cast<uint4*>(rowp + ((ch ^ (r & 7)) << 4)) =
-                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-          }
+          tmem_st16_nowait(t_s + c * 16, pk);
         }
+        tmem_wait_st();
+        r8[0] = acc2[0].x;
+        r8[1] = acc2[0].y;
+        r8[2] = acc2[1].x;
+        r8[3] = acc2[1].y;
       }
       l_run += ((r8[0] + r8[1]) + (r8[2] + r8[3])) + ((r8[4] + r8[5]) + (r8[6] + r8[7]));
       // Rescale O_t (rare).  PV_t(j-1) has completed (see the ordering note above) and PV_t(j)
@@ -358,7 +366,7 @@ __global__ void __launch_bounds__(A_THREADS, 1)
         }
       }
       tc_fence_before();
-      fence_proxy_async_smem();
+      if constexpr (FP8) fence_proxy_async_smem();  // e4m3 P in shared memory, read by the async proxy
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full + 8 * t);
     }

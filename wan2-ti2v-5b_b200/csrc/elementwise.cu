@@ -9,7 +9,7 @@ namespace wanb200 {
 constexpr int LN_MAX_VEC = 16;  // dim <= 16 * 256 = 4096
 
 struct LnArgs {
-  const __nv_bfloat16* x;
+  const void* x;  // bf16, or fp32 (XF32: the fp32 residual stream)
   __nv_bfloat16* out;
   int64_t rows;
   int dim;
@@ -36,7 +36,8 @@ struct LnArgs {
 //     `_modulate` (models/fast_dit.py:172-176): y * (1 + scale[f]) + shift[f] with
 //     shift/scale[f, c] = modulation[idx, c] + e0[f, idx, c] (fast_dit.py:276-277).
 //   MODE 1 (affine): norm3 = WanLayerNorm(elementwise_affine=True) (model.py:207-209).
-template <int MODE, int NVEC, bool PUSH, int RW>
+//   XF32: x is fp32 (the residual stream kept in fp32 across the step); the output stays bf16.
+template <int MODE, int NVEC, bool PUSH, int RW, bool XF32>
 __global__ void __launch_bounds__(256, RW == 2 ? 3 : 2) layernorm_kernel(const LnArgs a) {
   __shared__ float red[8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -46,10 +47,24 @@ __global__ void __launch_bounds__(256, RW == 2 ? 3 : 2) layernorm_kernel(const L
   const int64_t row = (int64_t)blockIdx.x * (8 / RW) + warp / RW;
   const int t = (warp % RW) * 32 + lane;
   const bool live = row < a.rows;  // dead rows still join the block's barriers
-  const uint4* xr = reinterpret_cast<const uint4*>(a.x + (live ? row : 0) * a.dim);
-  uint4 xv[NVEC];  // the row stays packed (bf16) in registers: half the footprint of fp32
+  // the row stays in registers as loaded: 8 values per 16 bytes of bf16, per 32 bytes of fp32
+  constexpr int W = XF32 ? 2 : 1;
+  const uint4* xr = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.x) +
+                                                   (live ? row : 0) * a.dim * (XF32 ? 4 : 2));
+  uint4 xv[NVEC * W];
 #pragma unroll
-  for (int i = 0; i < NVEC; ++i) xv[i] = live ? __ldg(xr + i * 32 * RW + t) : make_uint4(0, 0, 0, 0);
+  for (int i = 0; i < NVEC; ++i)
+#pragma unroll
+    for (int w = 0; w < W; ++w) xv[i * W + w] = live ? __ldg(xr + (i * 32 * RW + t) * W + w) : make_uint4(0, 0, 0, 0);
+  auto values = [&](int i, float* x) {  // the 8 values of vector i as fp32
+    if constexpr (XF32) {
+      const uint4 lo = xv[2 * i], hi = xv[2 * i + 1];
+      x[0] = __uint_as_float(lo.x); x[1] = __uint_as_float(lo.y); x[2] = __uint_as_float(lo.z); x[3] = __uint_as_float(lo.w);
+      x[4] = __uint_as_float(hi.x); x[5] = __uint_as_float(hi.y); x[6] = __uint_as_float(hi.z); x[7] = __uint_as_float(hi.w);
+    } else {
+      unpack_bf16x8(xv[i], x);
+    }
+  };
   auto row_sum = [&](float v) {
 #pragma unroll
     for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -64,7 +79,7 @@ __global__ void __launch_bounds__(256, RW == 2 ? 3 : 2) layernorm_kernel(const L
 #pragma unroll
   for (int i = 0; i < NVEC; ++i) {
     float x[8];
-    unpack_bf16x8(xv[i], x);
+    values(i, x);
 #pragma unroll
     for (int k = 0; k < 8; ++k) sum += x[k];
   }
@@ -73,7 +88,7 @@ __global__ void __launch_bounds__(256, RW == 2 ? 3 : 2) layernorm_kernel(const L
 #pragma unroll
   for (int i = 0; i < NVEC; ++i) {
     float x[8];
-    unpack_bf16x8(xv[i], x);
+    values(i, x);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const float d = x[k] - mean;
@@ -96,7 +111,7 @@ __global__ void __launch_bounds__(256, RW == 2 ? 3 : 2) layernorm_kernel(const L
     const int v = i * 32 * RW + t;
     const int col = v * 8;
     float x[8], y[8];
-    unpack_bf16x8(xv[i], x);
+    values(i, x);
     if constexpr (MODE == 0) {
       float ms[8], mc[8];
       unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.modulation + (int64_t)a.shift_idx * a.dim + col)), ms);
@@ -128,16 +143,16 @@ __global__ void __launch_bounds__(256, RW == 2 ? 3 : 2) layernorm_kernel(const L
   }
 }
 
-template <int MODE, bool PUSH>
+template <int MODE, bool PUSH, bool XF32>
 static void launch_ln(int dim, const LnArgs& a, int64_t rows, cudaStream_t st) {
   if (dim % 512 == 0) {  // two warps per row, 4 rows per block
     const unsigned blocks = (unsigned)((rows + 3) / 4);
     switch (dim / 512) {
 #define WANB200_LN_CASE2(n) \
-  case n: layernorm_kernel<MODE, n, PUSH, 2><<<blocks, 256, 0, st>>>(a); break;
+  case n: layernorm_kernel<MODE, n, PUSH, 2, XF32><<<blocks, 256, 0, st>>>(a); break;
       WANB200_LN_CASE2(1) WANB200_LN_CASE2(2) WANB200_LN_CASE2(3) WANB200_LN_CASE2(4) WANB200_LN_CASE2(5)
       WANB200_LN_CASE2(6) WANB200_LN_CASE2(7)
-      default: layernorm_kernel<MODE, 8, PUSH, 2><<<blocks, 256, 0, st>>>(a); break;
+      default: layernorm_kernel<MODE, 8, PUSH, 2, XF32><<<blocks, 256, 0, st>>>(a); break;
 #undef WANB200_LN_CASE2
     }
     return;
@@ -145,12 +160,20 @@ static void launch_ln(int dim, const LnArgs& a, int64_t rows, cudaStream_t st) {
   const unsigned blocks = (unsigned)((rows + 7) / 8);
   switch (dim / 256) {
 #define WANB200_LN_CASE(n) \
-  case n: layernorm_kernel<MODE, n, PUSH, 1><<<blocks, 256, 0, st>>>(a); break;
+  case n: layernorm_kernel<MODE, n, PUSH, 1, XF32><<<blocks, 256, 0, st>>>(a); break;
     WANB200_LN_CASE(1) WANB200_LN_CASE(3) WANB200_LN_CASE(5) WANB200_LN_CASE(7) WANB200_LN_CASE(9)
     WANB200_LN_CASE(11) WANB200_LN_CASE(13)
-    default: layernorm_kernel<MODE, 15, PUSH, 1><<<blocks, 256, 0, st>>>(a); break;
+    default: layernorm_kernel<MODE, 15, PUSH, 1, XF32><<<blocks, 256, 0, st>>>(a); break;
 #undef WANB200_LN_CASE
   }
+}
+
+template <int MODE, bool PUSH>
+static void launch_ln(int dim, const LnArgs& a, int64_t rows, bool xf32, cudaStream_t st) {
+  if (xf32)
+    launch_ln<MODE, PUSH, true>(dim, a, rows, st);
+  else
+    launch_ln<MODE, PUSH, false>(dim, a, rows, st);
 }
 
 int layernorm(const wanb200_ln_params* p, cudaStream_t st) {
@@ -179,7 +202,7 @@ int layernorm(const wanb200_ln_params* p, cudaStream_t st) {
   if (p->zero_count < 0 || (p->zero_count > 0 && !p->zero_buf))
     return set_error(WANB200_EINVAL, "layernorm: zero_count > 0 needs zero_buf");
   LnArgs a;
-  a.x = reinterpret_cast<const __nv_bfloat16*>(p->x);
+  a.x = p->x;
   a.out = reinterpret_cast<__nv_bfloat16*>(p->out);
   a.rows = p->rows;
   a.dim = (int)p->dim;
@@ -202,11 +225,11 @@ int layernorm(const wanb200_ln_params* p, cudaStream_t st) {
   a.npush = p->npush;
   a.push_row0 = p->push_row0;
   if ((p->rows + 3) / 4 > INT32_MAX) return set_error(WANB200_EINVAL, "layernorm: too many rows");
-  const bool push = a.npush > 0;
+  const bool push = a.npush > 0, xf32 = p->x_f32 != 0;
   if (p->mode == WANB200_LN_MODULATE)
-    push ? launch_ln<0, true>(a.dim, a, p->rows, st) : launch_ln<0, false>(a.dim, a, p->rows, st);
+    push ? launch_ln<0, true>(a.dim, a, p->rows, xf32, st) : launch_ln<0, false>(a.dim, a, p->rows, xf32, st);
   else
-    push ? launch_ln<1, true>(a.dim, a, p->rows, st) : launch_ln<1, false>(a.dim, a, p->rows, st);
+    push ? launch_ln<1, true>(a.dim, a, p->rows, xf32, st) : launch_ln<1, false>(a.dim, a, p->rows, xf32, st);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error("layernorm_kernel launch", e);
   return WANB200_OK;
@@ -307,8 +330,9 @@ int qk_norm_rope(const wanb200_qknorm_params* p, cudaStream_t st) {
 
 // ------------------------------------------------------------------ bias + gate + residual
 struct ResArgs {
-  __nv_bfloat16* out;
-  const __nv_bfloat16* residual;
+  void* out;             // bf16, or fp32 (out_f32)
+  const void* residual;  // bf16, or fp32 (res_f32)
+  int res_f32, out_f32;
   const __nv_bfloat16* y;
   int64_t rows;
   int dim;
@@ -330,7 +354,13 @@ __global__ void __launch_bounds__(256) bias_gate_residual_kernel(const ResArgs a
   const int64_t row = idx / vpr;
   const int col = (int)(idx - row * vpr) * 8;
   float r[8], y[8], b[8];
-  unpack_bf16x8(*reinterpret_cast<const uint4*>(a.residual + row * a.dim + col), r);
+  if (a.res_f32) {
+    const float4* rp = reinterpret_cast<const float4*>(static_cast<const float*>(a.residual) + row * a.dim + col);
+    const float4 lo = rp[0], hi = rp[1];
+    r[0] = lo.x; r[1] = lo.y; r[2] = lo.z; r[3] = lo.w; r[4] = hi.x; r[5] = hi.y; r[6] = hi.z; r[7] = hi.w;
+  } else {
+    unpack_bf16x8(*reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.residual) + row * a.dim + col), r);
+  }
   unpack_bf16x8(*reinterpret_cast<const uint4*>(a.y + row * a.dim + col), y);
   for (int s = 1; s < a.nsum; ++s) {  // the inbox slices of a fused reduce-scatter
     float t[8];
@@ -353,12 +383,18 @@ __global__ void __launch_bounds__(256) bias_gate_residual_kernel(const ResArgs a
 #pragma unroll
     for (int k = 0; k < 8; ++k) r[k] += y[k] + b[k];
   }
+  if (a.out_f32) {
+    float4* op = reinterpret_cast<float4*>(static_cast<float*>(a.out) + row * a.dim + col);
+    op[0] = make_float4(r[0], r[1], r[2], r[3]);
+    op[1] = make_float4(r[4], r[5], r[6], r[7]);
+    return;
+  }
   uint4 u;
   u.x = pack_bf16x2(r[0], r[1]);
   u.y = pack_bf16x2(r[2], r[3]);
   u.z = pack_bf16x2(r[4], r[5]);
   u.w = pack_bf16x2(r[6], r[7]);
-  *reinterpret_cast<uint4*>(a.out + row * a.dim + col) = u;
+  *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + row * a.dim + col) = u;
 }
 
 int bias_gate_residual(const wanb200_residual_params* p, cudaStream_t st) {
@@ -374,8 +410,10 @@ int bias_gate_residual(const wanb200_residual_params* p, cudaStream_t st) {
     return set_error(WANB200_EINVAL, "bias_gate_residual: gate needs gate_e0, seq_len, tokens_per_frame "
                                      "(row_offset, rows_per_seq >= 0)");
   ResArgs a;
-  a.out = reinterpret_cast<__nv_bfloat16*>(p->out);
-  a.residual = reinterpret_cast<const __nv_bfloat16*>(p->residual);
+  a.out = p->out;
+  a.residual = p->residual;
+  a.res_f32 = p->residual_f32 != 0;
+  a.out_f32 = p->out_f32 != 0;
   a.y = reinterpret_cast<const __nv_bfloat16*>(p->y);
   a.rows = p->rows;
   a.dim = (int)p->dim;

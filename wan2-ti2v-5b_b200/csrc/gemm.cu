@@ -42,12 +42,13 @@ struct GemmCfg {
 };
 
 struct GemmArgs {
-  __nv_bfloat16* d;
+  void* d;  // bf16, or fp32 when out_f32
   int64_t ldd;
   int M, N, K;
   const __nv_bfloat16* bias;
-  const __nv_bfloat16* residual;
+  const void* residual;  // bf16, or fp32 when res_f32
   int64_t ldr;
+  int res_f32, out_f32;  // the fp32 residual stream (GATE_RES / RES epilogues)
   const __nv_bfloat16* gate_mod;
   const float* gate_e0;
   int64_t gate_frame_stride;
@@ -96,19 +97,44 @@ constexpr bool epi_has_residual(int epi) {
   return epi == WANB200_EPI_BIAS_GATE_RES || epi == WANB200_EPI_BIAS_RES;
 }
 
-// The residual chunk (32 bf16 = 4 x 16 B) of `row` at col0, loaded one chunk ahead of its use so
-// the HBM latency of the residual overlaps the previous chunk's TMEM load and arithmetic.
-__device__ __forceinline__ void load_residual_chunk(const GemmArgs& a, int row, int col0, uint4 (&r)[4]) {
+// The residual chunk of `row` at col0 (32 values: 4 x 16 B of bf16, or 8 x 16 B of fp32), loaded
+// one chunk ahead of its use so the HBM latency of the residual overlaps the previous chunk's TMEM
+// load and arithmetic.
+__device__ __forceinline__ void load_residual_chunk(const GemmArgs& a, int row, int col0, uint4 (&r)[8]) {
   if (row < a.M && col0 < a.N) {
-    const uint4* rp = reinterpret_cast<const uint4*>(a.residual + (int64_t)row * a.ldr + col0);
+    if (a.res_f32) {
+      const uint4* rp =
+          reinterpret_cast<const uint4*>(static_cast<const float*>(a.residual) + (int64_t)row * a.ldr + col0);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) r[q] = rp[q];
+      for (int q = 0; q < 8; ++q) r[q] = rp[q];
+    } else {
+      const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.residual) +
+                                                       (int64_t)row * a.ldr + col0);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) r[q] = rp[q];
+    }
+  }
+}
+
+// The 32 residual values of a chunk as fp32.
+__device__ __forceinline__ void residual_values(const GemmArgs& a, const uint4 (&res)[8], float* r) {
+  if (a.res_f32) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      r[4 * q] = __uint_as_float(res[q].x);
+      r[4 * q + 1] = __uint_as_float(res[q].y);
+      r[4 * q + 2] = __uint_as_float(res[q].z);
+      r[4 * q + 3] = __uint_as_float(res[q].w);
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) unpack_bf16x8(res[q], r + 8 * q);
   }
 }
 
 template <int EPI>
 __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v, int row, int col0, float& ss_acc,
-                                                    int& ss_sec, const uint4 (&res)[4]) {
+                                                    int& ss_sec, const uint4 (&res)[8]) {
   if constexpr (EPI != WANB200_EPI_NONE && EPI != WANB200_EPI_SCATTER) {
     const uint4* bp = reinterpret_cast<const uint4*>(a.bias + col0);
 #pragma unroll
@@ -125,30 +151,25 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v,
   }
   if constexpr (EPI == WANB200_EPI_BIAS_GATE_RES || EPI == WANB200_EPI_BIAS_RES) {
     if (row < a.M) {
-      const uint4* rp = res;
+      float r[32];
+      residual_values(a, res, r);
       if constexpr (EPI == WANB200_EPI_BIAS_GATE_RES) {
         const int f = (int)frame_of_row(row, a.rows_per_seq, a.row_offset, a.seq_len, a.tokens_per_frame);
         const float4* ep = reinterpret_cast<const float4*>(a.gate_e0 + (int64_t)f * a.gate_frame_stride + col0);
         const uint4* mp = reinterpret_cast<const uint4*>(a.gate_mod + col0);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          float r[8], g[8];
-          unpack_bf16x8(rp[q], r);
+          float g[8];
           unpack_bf16x8(__ldg(mp + q), g);
           const float4 e_lo = __ldg(ep + 2 * q), e_hi = __ldg(ep + 2 * q + 1);
           g[0] += e_lo.x; g[1] += e_lo.y; g[2] += e_lo.z; g[3] += e_lo.w;
           g[4] += e_hi.x; g[5] += e_hi.y; g[6] += e_hi.z; g[7] += e_hi.w;
 #pragma unroll
-          for (int i = 0; i < 8; ++i) v[q * 8 + i] = r[i] + v[q * 8 + i] * g[i];
+          for (int i = 0; i < 8; ++i) v[q * 8 + i] = r[q * 8 + i] + v[q * 8 + i] * g[i];
         }
       } else {
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float r[8];
-          unpack_bf16x8(rp[q], r);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) v[q * 8 + i] += r[i];
-        }
+        for (int i = 0; i < 32; ++i) v[i] += r[i];
       }
     }
   }
@@ -162,12 +183,18 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v,
 #pragma unroll
     for (int i = 0; i < 32; ++i) ss_acc = fmaf(v[i], v[i], ss_acc);
   }
-  if (row < a.M) {
+  if (epi_has_residual(EPI) && a.out_f32) {
+    if (row < a.M) {
+      float4* dp = reinterpret_cast<float4*>(static_cast<float*>(a.d) + (int64_t)row * a.ldd + col0);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) dp[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    }
+  } else if (row < a.M) {
     __nv_bfloat16* drow;
     if constexpr (EPI == WANB200_EPI_SCATTER)
       drow = scatter_row_ptr(a, row);
     else
-      drow = a.d + (int64_t)row * a.ldd;
+      drow = static_cast<__nv_bfloat16*>(a.d) + (int64_t)row * a.ldd;
     uint4* dp = reinterpret_cast<uint4*>(drow + col0);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
@@ -341,14 +368,14 @@ __global__ void __launch_bounds__(192, 1)
         }
         __syncwarp();
       } else {
-        uint4 res_next[4] = {}, res_cur[4];
+        uint4 res_next[8] = {}, res_cur[8];
         if constexpr (epi_has_residual(EPI)) load_residual_chunk(args, row, n0, res_next);
 #pragma unroll 1
         for (int c = 0; c < bn / 32; ++c) {
           const int col0 = n0 + c * 32;
           if (col0 >= args.N) break;  // warp-uniform
 #pragma unroll
-          for (int q = 0; q < 4; ++q) res_cur[q] = res_next[q];
+          for (int q = 0; q < 8; ++q) res_cur[q] = res_next[q];
           if constexpr (epi_has_residual(EPI)) {
             if (c + 1 < bn / 32) load_residual_chunk(args, row, col0 + 32, res_next);
           }
@@ -442,6 +469,8 @@ int gemm_bf16(const wanb200_gemm_params* p, cudaStream_t st) {
   if (epi == WANB200_EPI_BIAS_GATE_RES || epi == WANB200_EPI_BIAS_RES) {
     if (!p->residual || !aligned16(p->residual) || p->ldr < p->N || (p->ldr % 8))
       return set_error(WANB200_EINVAL, "gemm: residual epilogue needs an aligned residual with ldr >= N, ldr % 8 == 0");
+  } else if (p->residual_f32 || p->out_f32) {
+    return set_error(WANB200_EINVAL, "gemm: residual_f32 / out_f32 apply to the GATE_RES and RES epilogues only");
   }
   if (epi == WANB200_EPI_BIAS_GATE_RES) {
     if (!p->gate_mod || !p->gate_e0 || !aligned16(p->gate_mod) || !aligned16(p->gate_e0) ||
@@ -468,13 +497,15 @@ int gemm_bf16(const wanb200_gemm_params* p, cudaStream_t st) {
   if (rc) return rc;
 
   GemmArgs ga;
-  ga.d = reinterpret_cast<__nv_bfloat16*>(p->d);
+  ga.d = p->d;
   ga.ldd = p->ldd;
+  ga.res_f32 = p->residual_f32 != 0;
+  ga.out_f32 = p->out_f32 != 0;
   ga.M = (int)p->M;
   ga.N = (int)p->N;
   ga.K = (int)p->K;
   ga.bias = reinterpret_cast<const __nv_bfloat16*>(p->bias);
-  ga.residual = reinterpret_cast<const __nv_bfloat16*>(p->residual);
+  ga.residual = p->residual;
   ga.ldr = p->ldr;
   ga.gate_mod = reinterpret_cast<const __nv_bfloat16*>(p->gate_mod);
   ga.gate_e0 = p->gate_e0;

@@ -28,7 +28,7 @@ class GemmParams(ctypes.Structure):
                 ("tokens_per_frame", c_int64), ("row_offset", c_int64), ("rows_per_seq", c_int64), ("rowss", c_void_p),
                 ("ss_section", c_int64),
                 ("ss_nsections", c_int), ("peer_out", c_void_p * 8), ("npeers", c_int), ("src_rank", c_int),
-                ("shard_rows", c_int64), ("tile_n", c_int)]
+                ("shard_rows", c_int64), ("tile_n", c_int), ("residual_f32", c_int), ("out_f32", c_int)]
 
 
 class AttnParams(ctypes.Structure):
@@ -47,7 +47,7 @@ class LnParams(ctypes.Structure):
                 ("shift_idx", c_int), ("scale_idx", c_int), ("seq_len", c_int64), ("tokens_per_frame", c_int64),
                 ("row_offset", c_int64), ("rows_per_seq", c_int64),
                 ("weight", c_void_p), ("bias", c_void_p), ("zero_buf", c_void_p), ("zero_count", c_int64),
-                ("push_out", c_void_p * 8), ("npush", c_int), ("push_row0", c_int64)]
+                ("push_out", c_void_p * 8), ("npush", c_int), ("push_row0", c_int64), ("x_f32", c_int)]
 
 
 class QkNormParams(ctypes.Structure):
@@ -62,7 +62,7 @@ class ResidualParams(ctypes.Structure):
                 ("bias", c_void_p), ("gate_mod", c_void_p), ("gate_e0", c_void_p), ("gate_frame_stride", c_int64),
                 ("seq_len", c_int64), ("tokens_per_frame", c_int64), ("row_offset", c_int64), ("rows_per_seq", c_int64),
                 ("nsum", c_int),
-                ("y_slice_stride", c_int64)]
+                ("y_slice_stride", c_int64), ("residual_f32", c_int), ("out_f32", c_int)]
 
 
 class ShardGatherParams(ctypes.Structure):

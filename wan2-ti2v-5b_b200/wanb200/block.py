@@ -11,7 +11,7 @@ Op sequence of one block (N = B*L tokens, C = 3072, C_l = C / TP, F_l = 14336 / 
       [TP: all-reduce Σq², Σk²]
    3  q,k = RoPE(x * rsqrt(Σ/C + eps) * γ)                   qk_norm_rope (in place)
    4  y   = softmax(q k^T / sqrt(d)) v                       flash attention
-   5  x1  = x + (y W_o^T + b_o) * gate2                      GEMM, GATE_RES epilogue
+   5  x1  = x + (y W_o^T + b_o) * gate2                      GEMM, GATE_RES epilogue (x1 fp32)
       [TP: GEMM partial -> all-reduce -> bias_gate_residual]
    6  h   = LN3_affine(x1)
    7  qc  = h W_cq^T + b, Σqc²                              GEMM, SUMSQ  [TP: all-reduce Σ]
@@ -21,6 +21,13 @@ Op sequence of one block (N = B*L tokens, C = 3072, C_l = C / TP, F_l = 14336 / 
   11  h   = LN2(x1) * (1 + scale) + shift
   12  f   = gelu_tanh(h W_1^T + b_1)                         GEMM, GELU epilogue
   13  x1 += (f W_2^T + b_2) * gate5                          GEMM, GATE_RES  [TP: AR path]
+
+The residual stream x1 is fp32 inside the block (the GEMM epilogues and norms read and write it in
+fp32); x may come in as bf16 (the reference's dtype, rounded once at the block's output) or fp32
+(FastWanDiT keeps it fp32 across all the blocks of a step).  Rounding the stream to bf16 after each
+of a block's three updates is the dominant error of a bf16 step: over the 30 layers of config 2
+it alone takes the step-0 prediction to ~5e-2 of the fp32 result; keeping it in fp32 leaves the
+bf16 roundings of the GEMM and attention operands, ~1e-2.
 """
 from __future__ import annotations
 
@@ -94,8 +101,9 @@ class FastBlock:
             dist.all_reduce(t, group=self.tp_group)
 
     def forward(self, x, e, cos, sin, ck, cv):
-        """x [B, L, C] bf16; e [1, F, 6, C] per-frame time projection (any float dtype);
-        cos/sin [1, L, 1, 64] fp32; ck/cv [B, Lc, H_local, 128] bf16 -> new x [B, L, C] bf16."""
+        """x [B, L, C] bf16 or fp32 (the residual stream); e [1, F, 6, C] per-frame time projection
+        (any float dtype); cos/sin [1, L, 1, 64] fp32; ck/cv [B, Lc, H_local, 128] bf16 -> new x
+        [B, L, C] in x's dtype (fp32 inside the block either way)."""
         w, sp = self.w, self.sp
         B, Lx, C = x.shape  # Lx: rows per batch element held here (the shard length under sp)
         nf = self.num_frames
@@ -163,7 +171,10 @@ class FastBlock:
             k = kv[:, :, :Cl].unflatten(2, (nl, 128))
             v = kv[:, :, Cl:].unflatten(2, (nl, 128))
             ops.attention(q, k, v, out=y, kind="attn_self", fp8=self.attn_fp8)
-        x1 = torch.empty_like(xf)
+        if xf.dtype not in (BF16, torch.float32):
+            raise ValueError(f"x must be bf16 or fp32, not {xf.dtype}")
+        x1 = torch.empty(N, C, device=x.device, dtype=torch.float32)  # the fp32 residual stream
+        x_out = x1 if xf.dtype == torch.float32 else torch.empty(N, C, device=x.device, dtype=BF16)
         gate2 = (mod[2], e0[:, 2, :])
         if self.tp:
             ops.linear(ws.y, w.w_o, None, epilogue=L.EPI_NONE, out=ws.part, kind="gemm_o")
@@ -194,11 +205,11 @@ class FastBlock:
         if self.tp:
             ops.linear(ws.f, w.w2, None, epilogue=L.EPI_NONE, out=ws.part, kind="gemm_ffn_down")
             self._all_reduce(ws.part)
-            ops.bias_gate_residual(x1, ws.part, w.b2, gate=gate5, frames=frames, out=x1)
+            ops.bias_gate_residual(x1, ws.part, w.b2, gate=gate5, frames=frames, out=x_out)
         else:
-            ops.linear(ws.f, w.w2, w.b2, epilogue=L.EPI_BIAS_GATE_RES, out=x1, residual=x1, gate=gate5,
+            ops.linear(ws.f, w.w2, w.b2, epilogue=L.EPI_BIAS_GATE_RES, out=x_out, residual=x1, gate=gate5,
                        frames=frames, kind="gemm_ffn_down")
-        return x1.view(B, Lx, C)
+        return x_out.view(B, Lx, C)
 
     __call__ = forward
 
@@ -315,7 +326,8 @@ class FastBlockSP:
         return ws
 
     def forward(self, xs, e, cos, sin, ck, cv):
-        """xs [S, C] bf16 shard; e [1, F, 6, C]; cos/sin [1, L, 1, 64] fp32; ck/cv [1, Lc, 24, 128]."""
+        """xs [S, C] shard, bf16 or fp32 (the residual stream, fp32 inside the block); e [1, F, 6, C];
+        cos/sin [1, L, 1, 64] fp32; ck/cv [1, Lc, 24, 128] -> new xs in xs's dtype."""
         w, Lx, nf, g = self.w, self.L, self.num_frames, self.tp_group
         S, C = xs.shape
         N, Cl, nl = Lx, w.local_dim, w.local_heads  # batch 1
@@ -341,7 +353,10 @@ class FastBlockSP:
         k = ws.qkv[:N, Cl:2 * Cl].view(1, Lx, nl, 128)
         v = ws.qkv[:N, 2 * Cl:].view(1, Lx, nl, 128)
         ops.attention(q, k, v, out=ws.y[:N].view(1, Lx, nl, 128), kind="attn_self")
-        x1 = torch.empty_like(xs)
+        if xs.dtype not in (BF16, torch.float32):
+            raise ValueError(f"xs must be bf16 or fp32, not {xs.dtype}")
+        x1 = torch.empty(S, C, device=xs.device, dtype=torch.float32)  # the fp32 residual stream
+        x_out = x1 if xs.dtype == torch.float32 else torch.empty(S, C, device=xs.device, dtype=BF16)
         self._rowpar_residual(ws.y, w.w_o, w.b_o, xs, (mod[2], e0[:, 2, :]), frames_s, x1, ws, "gemm_o")
 
         # -- cross-attention on the shard, all heads, no collective
@@ -356,8 +371,8 @@ class FastBlockSP:
         # -- FFN: LN on the shard, all-gather, column/row-parallel GEMMs, reduce-scatter
         hf = self._ln_gather(x1, mod, e0, 3, 4, frames_s, ws)
         ops.linear(hf, w.w1, w.b1, epilogue=L.EPI_BIAS_GELU, out=ws.f, kind="gemm_ffn_up")
-        self._rowpar_residual(ws.f, w.w2, w.b2, x1, (mod[5], e0[:, 5, :]), frames_s, x1, ws, "gemm_ffn_down")
-        return x1
+        self._rowpar_residual(ws.f, w.w2, w.b2, x1, (mod[5], e0[:, 5, :]), frames_s, x_out, ws, "gemm_ffn_down")
+        return x_out
 
     __call__ = forward
 

@@ -148,7 +148,7 @@ class FastWanDiT:
         self.cross_kv = [FastCrossKV(w, tp_group, spec.eps) for w in self.block_weights]
         self.context = None
         self._err_probe = L.DeviceErrorProbe(self.device)
-        self._handles = None
+        self._handles = [register_block(b) for b in self.blocks]  # names for torch.ops.wanb200.block
 
     @classmethod
     def from_checkpoint(cls, path, grid, guide_scale, device, **kwargs):
@@ -187,7 +187,8 @@ class FastWanDiT:
         return e, e0.reshape(self.num_frames, 6, self.spec.dim).contiguous()
 
     def patch(self, latent):
-        """Conv3d patchify (stride = kernel) as one fp32 matmul -> x [2, L, C] bf16."""
+        """Conv3d patchify (stride = kernel) as one fp32 matmul -> x [B, L, C] fp32, the residual
+        stream the blocks carry in fp32 through the step."""
         m = self.emb
         C_in, Fr, H, W = latent.shape
         p, q, r = self.spec.patch_size
@@ -196,7 +197,7 @@ class FastWanDiT:
         x = x.reshape(-1, C_in * p * q * r)
         wt = m["patch_embedding.weight"].reshape(self.spec.dim, -1)
         x = torch.addmm(m["patch_embedding.bias"], x, wt.t())
-        return x.to(BF16).unsqueeze(0).expand(self.batch, -1, -1).contiguous()
+        return x.unsqueeze(0).expand(self.batch, -1, -1).contiguous()
 
     def head_tokens(self, x, e, row0=0):
         """LN + 2-way modulation + Linear of `_FastHead` (fast_dit.py:480-505) per token:
@@ -240,8 +241,6 @@ class FastWanDiT:
     def forward_blocks_op(self, x, e0):
         """forward_blocks through the torch.ops.wanb200.block custom op (one opaque node per block,
         with a fake kernel), for callers that trace the step with torch.compile / make_fx."""
-        if self._handles is None:
-            self._handles = [register_block(b) for b in self.blocks]
         for h, (ck, cv) in zip(self._handles, self.context):
             x = torch.ops.wanb200.block(x, e0, self.cos, self.sin, ck, cv, h)
         return x

@@ -109,6 +109,7 @@ def linear(a, w, bias=None, *, epilogue=L.EPI_BIAS, out=None, residual=None, gat
     gate: (gate_mod [N] bf16, gate_e0 [F, N] fp32 view with unit column stride) for EPI_BIAS_GATE_RES.
     frames: (seq_len, tokens_per_frame) mapping a row to its latent frame.
     rowss: fp32 [ss_nsections, M] accumulators for EPI_BIAS_SUMSQ (must be zeroed first).
+    residual / out may be fp32 for the residual epilogues (the fp32 residual stream).
     """
     _cuda(a, w, bias, out, residual, rowss)
     _need(a.dtype == BF16 and w.dtype == BF16, "linear: a and w must be bf16")
@@ -119,7 +120,11 @@ def linear(a, w, bias=None, *, epilogue=L.EPI_BIAS, out=None, residual=None, gat
     if out is None and scatter is None:
         out = torch.empty(M, N, dtype=BF16, device=a.device)
     ldd = _rows(out, "out") if out is not None else N  # scatter: rows land in the peers' inboxes
+    for name, t in (("out", out), ("residual", residual)):
+        _need(t is None or t.dtype in (BF16, torch.float32), f"linear: {name} must be bf16 or fp32")
     p = L.GemmParams()
+    p.out_f32 = int(out is not None and out.dtype == torch.float32)
+    p.residual_f32 = int(residual is not None and residual.dtype == torch.float32)
     p.a, p.lda, p.w, p.ldw, p.d, p.ldd = _p(a), lda, _p(w), ldw, _p(out), ldd
     p.M, p.N, p.K, p.epilogue = M, N, K, epilogue
     p.tile_n = tile_n
@@ -232,15 +237,22 @@ def _set_push(p, push):
         p.npush, p.push_row0 = len(ptrs), row0
 
 
+def _ln_input(x):
+    _need(x.dtype in (BF16, torch.float32) and x.is_contiguous() and x.dim() == 2,
+          "layernorm: x must be contiguous bf16 or fp32 [M, C]")
+
+
 def layernorm_modulate(x, modulation, e0, shift_idx, scale_idx, frames, out=None, eps=1e-6, zero=None, push=None):
-    """LN(x) * (1 + scale[f]) + shift[f]; modulation [6, C] bf16, e0 [F, 6, C] fp32."""
+    """LN(x) * (1 + scale[f]) + shift[f] -> bf16; x [M, C] bf16 or fp32 (the fp32 residual
+    stream), modulation [6, C] bf16, e0 [F, 6, C] fp32."""
     _cuda(x, modulation, e0, out, zero)
-    _need(x.dtype == BF16 and x.is_contiguous() and x.dim() == 2, "layernorm: x must be contiguous bf16 [M, C]")
+    _ln_input(x)
     _need(e0.dtype == torch.float32 and e0.is_contiguous() and modulation.dtype == BF16, "layernorm: bad mod tensors")
     M, C = x.shape
     if out is None and push is None:
-        out = torch.empty_like(x)
+        out = torch.empty(M, C, dtype=BF16, device=x.device)
     p = L.LnParams()
+    p.x_f32 = int(x.dtype == torch.float32)
     _set_push(p, push)
     p.x, p.out, p.rows, p.dim, p.eps, p.mode = _p(x), _p(out), M, C, eps, L.LN_MODULATE
     p.modulation, p.e0, p.e0_frame_stride = _p(modulation), _p(e0), 6 * C
@@ -249,25 +261,27 @@ def layernorm_modulate(x, modulation, e0, shift_idx, scale_idx, frames, out=None
     if zero is not None:
         p.zero_buf, p.zero_count = _p(zero), zero.numel()
     lib = L.load()
-    L.check(_launch(x, "layernorm", 4.0 * M * C, lambda: lib.wanb200_layernorm(ctypes.byref(p), _stream(x))),
-            "wanb200_layernorm")
+    L.check(_launch(x, "layernorm", (x.element_size() + 2.0) * M * C,
+                    lambda: lib.wanb200_layernorm(ctypes.byref(p), _stream(x))), "wanb200_layernorm")
     return out
 
 
 def layernorm_affine(x, weight, bias, out=None, eps=1e-6, zero=None):
+    """LN(x) * weight + bias -> bf16; x [M, C] bf16 or fp32."""
     _cuda(x, weight, bias, out, zero)
-    _need(x.dtype == BF16 and x.is_contiguous() and x.dim() == 2, "layernorm: x must be contiguous bf16 [M, C]")
+    _ln_input(x)
     M, C = x.shape
     if out is None:
-        out = torch.empty_like(x)
+        out = torch.empty(M, C, dtype=BF16, device=x.device)
     p = L.LnParams()
+    p.x_f32 = int(x.dtype == torch.float32)
     p.x, p.out, p.rows, p.dim, p.eps, p.mode = _p(x), _p(out), M, C, eps, L.LN_AFFINE
     p.weight, p.bias = _p(weight), _p(bias)
     if zero is not None:
         p.zero_buf, p.zero_count = _p(zero), zero.numel()
     lib = L.load()
-    L.check(_launch(x, "layernorm", 4.0 * M * C, lambda: lib.wanb200_layernorm(ctypes.byref(p), _stream(x))),
-            "wanb200_layernorm")
+    L.check(_launch(x, "layernorm", (x.element_size() + 2.0) * M * C,
+                    lambda: lib.wanb200_layernorm(ctypes.byref(p), _stream(x))), "wanb200_layernorm")
     return out
 
 
@@ -296,14 +310,18 @@ def qk_norm_rope(x, sections, width, global_dim, eps=1e-6, cos=None, sin=None, s
 def bias_gate_residual(residual, y, bias, gate=None, frames=None, out=None, nsum=1):
     """out = residual + (y + bias) * gate[f]  (or residual + y + bias without gate).
     nsum > 1: y is [nsum * M, C] (the inbox of a fused reduce-scatter) and its nsum slices of M
-    rows are summed first."""
+    rows are summed first.  residual / out: bf16 or fp32 (the fp32 residual stream); y bf16."""
     _cuda(residual, y, bias, out)
     M, C = residual.shape
     _need(residual.is_contiguous() and y.is_contiguous() and tuple(y.shape) == (nsum * M, C),
           "bias_gate_residual: layout")
     if out is None:
         out = torch.empty_like(residual)
+    _need(out.is_contiguous() and tuple(out.shape) == (M, C), "bias_gate_residual: out layout")
+    for name, t in (("out", out), ("residual", residual)):
+        _need(t.dtype in (BF16, torch.float32), f"bias_gate_residual: {name} must be bf16 or fp32")
     p = L.ResidualParams()
+    p.residual_f32, p.out_f32 = int(residual.dtype == torch.float32), int(out.dtype == torch.float32)
     p.out, p.residual, p.y, p.rows, p.dim, p.bias = _p(out), _p(residual), _p(y), M, C, _p(bias)
     p.nsum, p.y_slice_stride = nsum, M * C
     if gate is not None:
@@ -311,7 +329,7 @@ def bias_gate_residual(residual, y, bias, gate=None, frames=None, out=None, nsum
         p.gate_mod, p.gate_e0, p.gate_frame_stride = _p(gm), _p(ge), ge.stride(0)
         _set_frames(p, frames)
     lib = L.load()
-    L.check(_launch(residual, "bias_gate_residual", 6.0 * M * C,
+    L.check(_launch(residual, "bias_gate_residual", (residual.element_size() + 2.0 * nsum + out.element_size()) * M * C,
                     lambda: lib.wanb200_bias_gate_residual(ctypes.byref(p), _stream(residual))),
             "wanb200_bias_gate_residual")
     return out
