@@ -82,12 +82,14 @@ class FastBlock:
     """
 
     def __init__(self, weights: BlockWeights, num_frames: int, tp_group=None, eps: float = 1e-6, sp=None,
-                 attn_fp8: bool = False):
+                 attn_fp8: bool = False, tp_chunks: int = 4):
         """sp: a wanb200.comm.KVGather of the sequence-parallel group for Q-local self-attention
         (`WanSelfAttentionSP`, models/dit_attention_sp.py:25-152): x then holds the tokens
         sp.rank*S .. sp.rank*S + S - 1 of every batch element, every op runs on those rows, and
         only K/V are gathered from the group.  None = x holds whole sequences.
-        attn_fp8: self-attention through the e4m3 variant (wanb200_attn_fwd_fp8)."""
+        attn_fp8: self-attention through the e4m3 variant (wanb200_attn_fwd_fp8).
+        tp_chunks: row blocks of a row-parallel projection whose all-reduces overlap the next
+        block's GEMM (TP only)."""
         self.w = weights
         self.num_frames = num_frames
         self.tp_group = tp_group
@@ -95,10 +97,30 @@ class FastBlock:
         self.eps = eps
         self.sp = sp
         self.attn_fp8 = attn_fp8
+        self.tp_chunks = max(1, int(tp_chunks))
 
     def _all_reduce(self, t):
         if self.tp:
             dist.all_reduce(t, group=self.tp_group)
+
+    def _row_parallel(self, a, wmat, part, kind):
+        """part = all_reduce(a @ wmat^T) over the TP group: the partial sums of a row-parallel
+        projection (`_row_linear`, models/fast_dit.py:126-131).  The rows go in tp_chunks blocks
+        of whole 128-row GEMM tiles; block c's all-reduce runs on NCCL's stream while block c+1's
+        GEMM runs on this one (the reference also chunks this all-reduce, fast_dit.py:88-99), and
+        this stream waits for all of them before the bias / gate / residual pass reads part."""
+        M = a.shape[0]
+        n = max(1, min(self.tp_chunks, M // 1024))
+        bounds = [0] + [min(M, (M * i // n + 127) // 128 * 128) for i in range(1, n)] + [M]
+        works = []
+        for r0, r1 in zip(bounds[:-1], bounds[1:]):
+            if r1 > r0:
+                ops.linear(a[r0:r1], wmat, None, epilogue=L.EPI_NONE, out=part[r0:r1], kind=kind)
+                works.append(dist.all_reduce(part[r0:r1], group=self.tp_group, async_op=True))
+        t0 = ops.region_begin(part)
+        for wk in works:
+            wk.wait()
+        ops.region_end(part, t0, "tp_allreduce_exposed", 2.0 * part.numel())
 
     def forward(self, x, e, cos, sin, ck, cv):
         """x [B, L, C] bf16 or fp32 (the residual stream); e [1, F, 6, C] per-frame time projection
@@ -177,8 +199,7 @@ class FastBlock:
         x_out = x1 if xf.dtype == torch.float32 else torch.empty(N, C, device=x.device, dtype=BF16)
         gate2 = (mod[2], e0[:, 2, :])
         if self.tp:
-            ops.linear(ws.y, w.w_o, None, epilogue=L.EPI_NONE, out=ws.part, kind="gemm_o")
-            self._all_reduce(ws.part)
+            self._row_parallel(ws.y, w.w_o, ws.part, "gemm_o")
             ops.bias_gate_residual(xf, ws.part, w.b_o, gate=gate2, frames=frames, out=x1)
         else:
             ops.linear(ws.y, w.w_o, w.b_o, epilogue=L.EPI_BIAS_GATE_RES, out=x1, residual=xf, gate=gate2,
@@ -192,8 +213,7 @@ class FastBlock:
         ops.qk_norm_rope(ws.cq, [(0, ws.ss[2], w.g_cq)], Cl, C, eps=self.eps)
         ops.attention(ws.cq.view(B, Lx, nl, 128), ck, cv, out=ws.y.view(B, Lx, nl, 128), kind="attn_cross")
         if self.tp:
-            ops.linear(ws.y, w.w_co, None, epilogue=L.EPI_NONE, out=ws.part, kind="gemm_cross_o")
-            self._all_reduce(ws.part)
+            self._row_parallel(ws.y, w.w_co, ws.part, "gemm_cross_o")
             ops.bias_gate_residual(x1, ws.part, w.b_co, out=x1)
         else:
             ops.linear(ws.y, w.w_co, w.b_co, epilogue=L.EPI_BIAS_RES, out=x1, residual=x1, kind="gemm_cross_o")
@@ -203,8 +223,7 @@ class FastBlock:
         ops.linear(ws.h, w.w1, w.b1, epilogue=L.EPI_BIAS_GELU, out=ws.f, kind="gemm_ffn_up")
         gate5 = (mod[5], e0[:, 5, :])
         if self.tp:
-            ops.linear(ws.f, w.w2, None, epilogue=L.EPI_NONE, out=ws.part, kind="gemm_ffn_down")
-            self._all_reduce(ws.part)
+            self._row_parallel(ws.f, w.w2, ws.part, "gemm_ffn_down")
             ops.bias_gate_residual(x1, ws.part, w.b2, gate=gate5, frames=frames, out=x_out)
         else:
             ops.linear(ws.f, w.w2, w.b2, epilogue=L.EPI_BIAS_GATE_RES, out=x_out, residual=x1, gate=gate5,
@@ -213,10 +232,11 @@ class FastBlock:
 
     __call__ = forward
 
-    # kernel launches per forward (for the bench's gpu_launches count)
+    # kernel launches per forward at the config-2 shapes (an estimate; the bench counts the
+    # launches it makes)
     @property
     def launches(self) -> int:
-        n = 13 if not self.tp else 16
+        n = 13 if not self.tp else 16 + 3 * (self.tp_chunks - 1)
         if self.sp is not None and self.sp.overlapped:
             n += 3  # shard gather + peer barrier + the second attention piece
         return n

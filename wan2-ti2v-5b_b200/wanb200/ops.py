@@ -66,6 +66,17 @@ def _launch(t, kind, work, fn):
     return rc
 
 
+def region_begin(t):
+    """Start of a timed region on t's current stream (None when no KernelTimer is installed)."""
+    return _timer.begin(t) if _timer is not None else None
+
+
+def region_end(t, start, kind, work):
+    """End of a region started by region_begin: recorded under `kind` with `work` (bytes)."""
+    if _timer is not None and start is not None:
+        _timer.end(t, start, kind, work)
+
+
 def _stream(t: torch.Tensor) -> int:
     return torch.cuda.current_stream(t.device).cuda_stream
 
