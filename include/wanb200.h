@@ -247,6 +247,56 @@ typedef struct wanb200_shard_gather_params {
 
 int wanb200_shard_gather(const wanb200_shard_gather_params* p, void* stream);
 
+/* ---------------------------------------------------------------- whole block
+ * One WanAttentionBlock forward in one call: `_FastBlock.forward(x, e, cos, sin, ck, cv)`
+ * (models/fast_dit.py:260-311; the unit the reference compiles whole, fast_dit.py:586, 646-649)
+ * with batched CFG, per-frame modulation and TP by heads.  Queues the block's launches on
+ * `stream` (LN1 + modulation, QKV GEMM with the Σq², Σk² epilogue, QK-norm + RoPE,
+ * self-attention, out-projection with gate + residual, LN3, cross-q GEMM with Σ, cross-q norm,
+ * cross-attention over ck / cv, cross out-projection with residual, LN2 + modulation, FFN up with
+ * GELU, FFN down with gate + residual).  The residual stream is fp32 in the workspace; x and
+ * x_out are bf16 or fp32 (x_f32, out_f32).  Weights as `shard_model_tp` slices them for this
+ * TP rank (tp_utils.py:378-458): w_qkv = [q; k; v] rows of this rank's heads [3*C_l, C], g_q /
+ * g_k / g_cq the RMSNorm gains of those heads, w_o / w_co the matching input columns [C, C_l],
+ * w1 rows [F_l, C], w2 columns [C, F_l], full biases of the row-parallel projections.
+ * The library issues no collective.  With tp_size > 1 the caller's all_reduce callback is called
+ * (on the calling thread, in stream order) to queue an in-place sum over the TP group on `stream`
+ * at the reference's points (fast_dit.py:141, 159, 293, 305, 310): buf, count elements, dtype
+ * 0 = fp32 (the Σx² rows), 1 = bf16 (the projection partial sums); it returns 0 on success.
+ * Limits: dim % 512 == 0, dim <= 4096, local_heads * 128 * tp_size == dim, ffn_local % 64 == 0,
+ * seq_len a multiple of num_frames; ck / cv [B, ctx_len, local_heads, 128] with the given token
+ * and batch strides (e.g. the two halves of the cross K/V buffer). */
+typedef int (*wanb200_allreduce_fn)(void* buf, int64_t count, int dtype, void* ctx, void* stream);
+
+typedef struct wanb200_block_weights {
+  const void* modulation;                              /* [6, C] */
+  const void* w_qkv; const void* b_qkv;                /* [3*C_l, C], [3*C_l] */
+  const void* g_q; const void* g_k;                    /* [C_l] */
+  const void* w_o; const void* b_o;                    /* [C, C_l], [C] */
+  const void* ln3_w; const void* ln3_b;                /* [C] */
+  const void* w_cq; const void* b_cq; const void* g_cq; /* [C_l, C], [C_l], [C_l] */
+  const void* w_co; const void* b_co;                  /* [C, C_l], [C] */
+  const void* w1; const void* b1;                      /* [F_l, C], [F_l] */
+  const void* w2; const void* b2;                      /* [C, F_l], [C] */
+} wanb200_block_weights;
+
+typedef struct wanb200_block_params {
+  const void* x; int x_f32;          /* [B*L, C] residual stream in (bf16, or fp32) */
+  void* x_out; int out_f32;          /* [B*L, C] out, distinct from x */
+  int64_t batch, seq_len, dim, local_heads, ffn_local, num_frames;
+  float eps;                         /* 1e-6 */
+  const float* e0;                   /* [F, 6, C] per-frame time projection */
+  const float* cos; const float* sin; /* [seq_len, 64] RoPE tables */
+  const void* ck; const void* cv; int64_t ctx_len, ckv_tok_stride, ckv_batch_stride;
+  wanb200_block_weights w;
+  void* workspace; int64_t workspace_bytes; /* 256-byte aligned, wanb200_block_workspace_bytes() */
+  int tp_size; wanb200_allreduce_fn all_reduce; void* all_reduce_ctx;
+} wanb200_block_params;
+
+int64_t wanb200_block_workspace_bytes(int64_t batch, int64_t seq_len, int64_t dim, int64_t local_heads,
+                                      int64_t ffn_local, int64_t ctx_len, int tp_size);
+int wanb200_block_forward(const wanb200_block_params* p, void* stream);
+
 /* ---------------------------------------------------------------- status */
 const char* wanb200_last_error(void);
 /* Device-side error word of the current device: 0 or a code (a bounded wait expired inside a
@@ -262,7 +312,7 @@ int wanb200_device_error(int reset);
 int wanb200_device_error_async(int* host_out, void* stream);
 /* Library version, e.g. 200 for 0.2.0. */
 int wanb200_version(void);
-/* sizeof of the parameter structs (gemm, attn, ln, qknorm, residual, shard_gather, attn_fp8)
+/* sizeof of the parameter structs (gemm, attn, ln, qknorm, residual, shard_gather, attn_fp8, block)
  * written to out[0..n); returns the number of structs.  Lets a binding detect a library built
  * from a different header. */
 int wanb200_struct_sizes(int64_t* out, int n);

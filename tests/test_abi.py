@@ -37,6 +37,8 @@ STRUCTS = {
     "wanb200_residual_params": L.ResidualParams,
     "wanb200_shard_gather_params": L.ShardGatherParams,
     "wanb200_attn_fp8_params": L.AttnFp8Params,
+    "wanb200_block_params": L.BlockParams,
+    "wanb200_block_weights": L.BlockWeightsC,
 }
 
 
@@ -175,3 +177,32 @@ def test_ops_refuse_cpu_tensors():
     a = torch.zeros(128, 128, dtype=torch.bfloat16)
     with pytest.raises(L.WanB200Error):
         ops.linear(a, a, None, epilogue=L.EPI_NONE)
+
+
+def test_block_forward_rejects_bad_args_on_host():
+    lib = L.load()
+    p = L.BlockParams()
+    rc, msg = _rc_msg(lib.wanb200_block_forward, p)
+    assert rc == -1 and "dim % 512" in msg
+    p.batch, p.seq_len, p.dim, p.local_heads, p.ffn_local, p.num_frames = 2, 1080, 3072, 24, 14336, 6
+    p.ctx_len, p.ckv_tok_stride, p.ckv_batch_stride, p.tp_size = 512, 3072, 512 * 3072, 1
+    rc, msg = _rc_msg(lib.wanb200_block_forward, p)
+    assert rc == -1 and "distinct" in msg
+    p.x, p.x_out = 256, 256
+    rc, msg = _rc_msg(lib.wanb200_block_forward, p)
+    assert rc == -1 and "distinct" in msg
+    p.x_out, p.e0, p.cos, p.sin, p.ck, p.cv = 512, 1024, 1024, 1024, 1024, 1024
+    rc, msg = _rc_msg(lib.wanb200_block_forward, p)
+    assert rc == -1 and "weight pointer" in msg
+    for f, _ in L.BlockWeightsC._fields_:
+        setattr(p.w, f, 4096)
+    rc, msg = _rc_msg(lib.wanb200_block_forward, p)
+    assert rc == -1 and "workspace" in msg
+    p.local_heads, p.tp_size = 12, 2  # TP without the all-reduce callback
+    rc, msg = _rc_msg(lib.wanb200_block_forward, p)
+    assert rc == -1 and "all_reduce callback" in msg
+    p.local_heads = 10  # heads * 128 * tp != dim
+    rc, msg = _rc_msg(lib.wanb200_block_forward, p)
+    assert rc == -1 and "local_heads" in msg
+    assert lib.wanb200_block_workspace_bytes(2, 1080, 3072, 24, 14336, 512, 1) > 2 * 1080 * 3072 * 4
+    assert lib.wanb200_block_workspace_bytes(0, 1080, 3072, 24, 14336, 512, 1) == 0

@@ -290,3 +290,30 @@ def test_bounded_wait_expiry_reaches_the_step_driver():
     del keep
     assert L.device_error(reset=True) == 401
     assert fast.check_device_errors() == 0
+
+
+def test_block_forward_c_entry_matches_the_python_block_op():
+    """wanb200_block_forward (the whole block as one C call) against FastBlock.forward on the
+    config-0 block: the same kernels in the same order, so they agree up to the run-to-run drift
+    of the Σx² atomics; and against the fp32 oracle, with bf16 and fp32 residual streams."""
+    from wanb200.block import block_forward_c
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    grid = (6, 12, 15)
+    spec, sd, x, e0, context = _config0_inputs(seed=5, L_grid=grid)
+    cos, sin = R.rope_tables(R.model_freqs(128), grid, 128)
+    p32 = fp32(sd)
+    ck, cv = R.cross_kv(p32, context, spec.num_heads)
+    y_ref = R.block_fwd(p32, x, e0, cos, sin, ck, cv, grid[0], spec.num_heads)
+    w = BlockWeights(sd, spec.num_heads, DEV)
+    ckd, cvd = FastCrossKV(w)(context.to(DEV, torch.bfloat16))
+    cosd, sind = rope_tables(grid, 128, DEV)
+    blk = FastBlock(w, grid[0])
+    xd = x.to(DEV, torch.bfloat16)
+    y_py = blk(xd, e0.to(DEV), cosd, sind, ckd, cvd)
+    y_c = block_forward_c(blk, xd, e0.to(DEV), cosd, sind, ckd, cvd)
+    assert y_c.dtype == torch.bfloat16
+    assert R.rel_rms(y_c.float(), y_py.float()) < 1e-3
+    assert R.rel_rms(y_c.float().cpu(), y_ref) < BLOCK_TOL
+    y32 = block_forward_c(blk, x.to(DEV), e0.to(DEV), cosd, sind, ckd, cvd, out_dtype=torch.float32)
+    assert y32.dtype == torch.float32
+    assert R.rel_rms(y32.cpu(), y_ref) < R.rel_rms(y_c.float().cpu(), y_ref)  # no output rounding

@@ -174,6 +174,15 @@ int wanb200_shard_gather(const wanb200_shard_gather_params* p, void* stream) {
   return shard_gather(p, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int wanb200_block_forward(const wanb200_block_params* p, void* stream) {
+  return block_forward(p, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int64_t wanb200_block_workspace_bytes(int64_t batch, int64_t seq_len, int64_t dim, int64_t local_heads,
+                                      int64_t ffn_local, int64_t ctx_len, int tp_size) {
+  return block_workspace_bytes(batch, seq_len, dim, local_heads, ffn_local, ctx_len, tp_size);
+}
+
 const char* wanb200_last_error(void) { return t_last_error.c_str(); }
 
 int wanb200_device_error(int reset) {
@@ -203,12 +212,12 @@ int wanb200_device_error_async(int* host_out, void* stream) {
 int wanb200_version(void) { return 200; }
 
 int wanb200_struct_sizes(int64_t* out, int n) {
-  const int64_t sizes[7] = {(int64_t)sizeof(wanb200_gemm_params), (int64_t)sizeof(wanb200_attn_params),
+  const int64_t sizes[8] = {(int64_t)sizeof(wanb200_gemm_params), (int64_t)sizeof(wanb200_attn_params),
                             (int64_t)sizeof(wanb200_ln_params), (int64_t)sizeof(wanb200_qknorm_params),
                             (int64_t)sizeof(wanb200_residual_params), (int64_t)sizeof(wanb200_shard_gather_params),
-                            (int64_t)sizeof(wanb200_attn_fp8_params)};
-  for (int i = 0; i < n && i < 7; ++i) out[i] = sizes[i];
-  return 7;
+                            (int64_t)sizeof(wanb200_attn_fp8_params), (int64_t)sizeof(wanb200_block_params)};
+  for (int i = 0; i < n && i < 8; ++i) out[i] = sizes[i];
+  return 8;
 }
 
 }  // extern "C"

@@ -75,11 +75,30 @@ class AttnFp8Params(ctypes.Structure):
     _fields_ = [("attn", AttnParams), ("fp8_workspace", c_void_p), ("fp8_workspace_bytes", c_int64)]
 
 
+class BlockWeightsC(ctypes.Structure):
+    _fields_ = [(n, c_void_p) for n in ("modulation", "w_qkv", "b_qkv", "g_q", "g_k", "w_o", "b_o", "ln3_w",
+                                        "ln3_b", "w_cq", "b_cq", "g_cq", "w_co", "b_co", "w1", "b1", "w2", "b2")]
+
+
+ALLREDUCE_FN = ctypes.CFUNCTYPE(c_int, c_void_p, c_int64, c_int, c_void_p, c_void_p)
+
+
+class BlockParams(ctypes.Structure):
+    _fields_ = [("x", c_void_p), ("x_f32", c_int), ("x_out", c_void_p), ("out_f32", c_int), ("batch", c_int64),
+                ("seq_len", c_int64), ("dim", c_int64), ("local_heads", c_int64), ("ffn_local", c_int64),
+                ("num_frames", c_int64), ("eps", c_float), ("e0", c_void_p), ("cos", c_void_p), ("sin", c_void_p),
+                ("ck", c_void_p), ("cv", c_void_p), ("ctx_len", c_int64), ("ckv_tok_stride", c_int64),
+                ("ckv_batch_stride", c_int64), ("w", BlockWeightsC), ("workspace", c_void_p),
+                ("workspace_bytes", c_int64), ("tp_size", c_int), ("all_reduce", ALLREDUCE_FN),
+                ("all_reduce_ctx", c_void_p)]
+
+
 EXPORTS = ("wanb200_gemm_bf16", "wanb200_attn_fwd", "wanb200_layernorm", "wanb200_qk_norm_rope",
            "wanb200_bias_gate_residual", "wanb200_last_error", "wanb200_device_error", "wanb200_version",
            "wanb200_struct_sizes", "wanb200_peer_barrier", "wanb200_attn_workspace_bytes",
            "wanb200_attn_kv_splits", "wanb200_attn_fwd_noalloc", "wanb200_shard_gather", "wanb200_attn_fwd_fp8",
-           "wanb200_attn_fp8_workspace_bytes", "wanb200_device_error_async")
+           "wanb200_attn_fp8_workspace_bytes", "wanb200_device_error_async", "wanb200_block_forward",
+           "wanb200_block_workspace_bytes")
 
 _lock = threading.Lock()
 _lib = None
@@ -130,8 +149,12 @@ def load():
             lib.wanb200_attn_fwd_fp8.restype = c_int
             lib.wanb200_attn_fp8_workspace_bytes.argtypes = [c_int64, c_int64, c_int64, c_int64]
             lib.wanb200_attn_fp8_workspace_bytes.restype = c_int64
+            lib.wanb200_block_forward.argtypes = [ctypes.POINTER(BlockParams), c_void_p]
+            lib.wanb200_block_forward.restype = c_int
+            lib.wanb200_block_workspace_bytes.argtypes = [c_int64] * 6 + [c_int]
+            lib.wanb200_block_workspace_bytes.restype = c_int64
             structs = (GemmParams, AttnParams, LnParams, QkNormParams, ResidualParams, ShardGatherParams,
-                       AttnFp8Params)
+                       AttnFp8Params, BlockParams)
             sizes = (c_int64 * len(structs))()
             n = lib.wanb200_struct_sizes(sizes, len(structs))
             want = [ctypes.sizeof(c) for c in structs]

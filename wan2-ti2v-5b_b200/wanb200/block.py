@@ -31,6 +31,7 @@ bf16 roundings of the GEMM and attention operands, ~1e-2.
 """
 from __future__ import annotations
 
+import ctypes
 import itertools
 import weakref
 
@@ -400,6 +401,66 @@ class FastBlockSP:
     def launches(self) -> int:
         return 15
 
+
+
+# ---------------------------------------------------------------------------- C entry
+_C_WORKSPACES = {}
+
+
+def block_forward_c(block: FastBlock, x, e, cos, sin, ck, cv, out_dtype=None):
+    """The same block through the library's one-call entry point (wanb200_block_forward): every
+    launch of the block queued by C on the current stream.  x [B, L, C] bf16 or fp32; returns
+    [B, L, C] in out_dtype (default x's dtype).  With TP the C side calls back into
+    torch.distributed.all_reduce on the group's buffers (views of the workspace)."""
+    if block.sp is not None:
+        raise ValueError("block_forward_c covers the whole-sequence block (sp=None)")
+    w = block.w
+    B, Lx, C = x.shape
+    N = B * Lx
+    lib = L.load()
+    xf = x.reshape(N, C).contiguous()
+    out_dtype = out_dtype or x.dtype
+    out = torch.empty(N, C, device=x.device, dtype=out_dtype)
+    e0 = e.reshape(-1, 6, C).float().contiguous()
+    cos2 = cos.reshape(-1, cos.shape[-1])[:Lx].float().contiguous()
+    sin2 = sin.reshape(-1, sin.shape[-1])[:Lx].float().contiguous()
+    tp = w.tp_size
+    nbytes = lib.wanb200_block_workspace_bytes(B, Lx, C, w.local_heads, w.ffn_local, ck.shape[1], tp)
+    key = (str(x.device), nbytes)
+    ws = _C_WORKSPACES.get(key)
+    if ws is None:
+        _C_WORKSPACES.clear()
+        ws = _C_WORKSPACES[key] = torch.empty(nbytes + 256, dtype=torch.uint8, device=x.device)
+    base = (ws.data_ptr() + 255) // 256 * 256
+    p = L.BlockParams()
+    p.x, p.x_f32, p.x_out, p.out_f32 = xf.data_ptr(), int(xf.dtype == torch.float32), out.data_ptr(), \
+        int(out_dtype == torch.float32)
+    p.batch, p.seq_len, p.dim, p.local_heads, p.ffn_local = B, Lx, C, w.local_heads, w.ffn_local
+    p.num_frames, p.eps = block.num_frames, block.eps
+    p.e0, p.cos, p.sin = e0.data_ptr(), cos2.data_ptr(), sin2.data_ptr()
+    p.ck, p.cv, p.ctx_len = ck.data_ptr(), cv.data_ptr(), ck.shape[1]
+    p.ckv_tok_stride, p.ckv_batch_stride = ck.stride(1), ck.stride(0)
+    for f in ("modulation", "w_qkv", "b_qkv", "g_q", "g_k", "w_o", "b_o", "ln3_w", "ln3_b", "w_cq", "b_cq", "g_cq",
+              "w_co", "b_co", "w1", "b1", "w2", "b2"):
+        setattr(p.w, f, getattr(w, f).data_ptr())
+    p.workspace, p.workspace_bytes, p.tp_size = base, nbytes, tp
+    if tp > 1:
+        u8 = ws
+
+        def all_reduce(buf, count, dtype, ctx, stream):
+            try:
+                off = buf - ws.data_ptr()
+                el = 4 if dtype == 0 else 2
+                t = u8[off:off + count * el].view(torch.float32 if dtype == 0 else BF16)
+                dist.all_reduce(t, group=block.tp_group)
+                return 0
+            except Exception:  # reported to the C side as a failed callback
+                return 1
+
+        p.all_reduce = L.ALLREDUCE_FN(all_reduce)
+    L.check(ops._launch(x, "block", 0.0, lambda: lib.wanb200_block_forward(ctypes.byref(p), ops._stream(x))),
+            "wanb200_block_forward")
+    return out.view(B, Lx, C)
 
 
 # ---------------------------------------------------------------------------- torch.library op

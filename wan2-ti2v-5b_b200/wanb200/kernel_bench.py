@@ -2,7 +2,8 @@
 
     python -m wanb200.kernel_bench gemm --M 15708 --N 14336 --K 3072 --epi gelu [--iters 20]
     python -m wanb200.kernel_bench attn --B 2 --H 24 --Lq 7854 --Lk 7854 [--iters 20]
-    python -m wanb200.kernel_bench ln --M 15708 --C 3072
+    python -m wanb200.kernel_bench ln --M 15708 --C 3072 [--f32]
+    python -m wanb200.kernel_bench gemm --M 15708 --N 3072 --K 3072 --epi gate_res --f32
 
 (run from wan2-ti2v-5b_b200/ or with it on sys.path).  Prints one JSON line with the mean
 time per launch and the algorithmic TFLOP/s or GB/s.  Used for sweeps and as the small-case
@@ -45,7 +46,9 @@ def bench_gemm(a):
     epi = EPIS[a.epi]
     kw = {}
     if epi in (L.EPI_BIAS_GATE_RES, L.EPI_BIAS_RES):
-        kw["residual"] = torch.zeros_like(out)
+        kw["residual"] = torch.zeros(a.M, a.N, device=dev, dtype=torch.float32 if a.f32 else torch.bfloat16)
+        if a.f32:  # the fp32 residual stream, updated in place as in the block
+            out = kw["residual"]
     if epi == L.EPI_BIAS_GATE_RES:
         kw["gate"] = (torch.zeros(a.N, device=dev, dtype=torch.bfloat16), torch.ones(21, 6 * a.N, device=dev)[:, :a.N])
         kw["frames"] = (a.M, max(1, a.M // 21))
@@ -53,7 +56,8 @@ def bench_gemm(a):
         kw["rowss"] = torch.zeros(2, a.M, device=dev)
         kw["ss_section"], kw["ss_nsections"] = a.N // 3, 2
     ms = _time(lambda: ops.linear(x, w, b if epi else None, epilogue=epi, out=out, tile_n=a.tile_n, **kw), a.iters)
-    return {"kernel": "gemm", "M": a.M, "N": a.N, "K": a.K, "epi": a.epi, "tile_n": a.tile_n, "ms": ms,
+    return {"kernel": "gemm", "M": a.M, "N": a.N, "K": a.K, "epi": a.epi, "f32_residual": a.f32,
+            "tile_n": a.tile_n, "ms": ms,
             "tflops": 2 * a.M * a.N * a.K / ms / 1e9}
 
 
@@ -71,12 +75,15 @@ def bench_attn(a):
 
 def bench_ln(a):
     dev = "cuda"
-    x = torch.randn(a.M, a.C, device=dev).to(torch.bfloat16)
+    x = torch.randn(a.M, a.C, device=dev)
+    if not a.f32:
+        x = x.to(torch.bfloat16)
     mod = torch.zeros(6, a.C, device=dev, dtype=torch.bfloat16)
     e0 = torch.zeros(21, 6, a.C, device=dev)
-    out = torch.empty_like(x)
+    out = torch.empty(a.M, a.C, device=dev, dtype=torch.bfloat16)
     ms = _time(lambda: ops.layernorm_modulate(x, mod, e0, 0, 1, (a.M, max(1, a.M // 21)), out=out), a.iters)
-    return {"kernel": "layernorm_modulate", "M": a.M, "C": a.C, "ms": ms, "gbs": 4 * a.M * a.C / ms / 1e6}
+    return {"kernel": "layernorm_modulate", "M": a.M, "C": a.C, "x_f32": a.f32, "ms": ms,
+            "gbs": (x.element_size() + 2) * a.M * a.C / ms / 1e6}
 
 
 def main():
@@ -94,6 +101,7 @@ def main():
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--tile-n", type=int, default=0, help="gemm tile width along N (0 = the library's choice)")
     ap.add_argument("--fp8", action="store_true", help="attn: the e4m3 variant (quantisation included in the time)")
+    ap.add_argument("--f32", action="store_true", help="gemm residual epilogues / ln: the fp32 residual stream")
     a = ap.parse_args()
     torch.cuda.set_device(0)
     r = {"gemm": bench_gemm, "attn": bench_attn, "ln": bench_ln}[a.kind](a)
