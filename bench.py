@@ -330,7 +330,7 @@ def run_ours(args):
 
     peaks = measured_peaks()
     hbm_kinds = {"layernorm", "qk_norm_rope", "bias_gate_residual", "kv_gather", "peer_barrier",
-                 "tp_allreduce_exposed"}
+                 "tp_allreduce_exposed", "patchify", "unpatchify"}
     total_ms = sum(x[1] for x in kern.values())
     per_kernel = {k: {"launches": v[0], "ms": v[1], "share": v[1] / total_ms,
                       ("tflops" if k not in hbm_kinds else "gbs"):
@@ -381,8 +381,11 @@ def run_ours(args):
                                                           if (fast.sp or fast.kv_gather is not None) else ""),
                    "layers": layers, "inputs_larger_than_l2": True,
                    "l2_note": "each step streams ~9.8 GB of weights, far above the 126 MB L2"},
-        "e2e": {"value": e2e_s, "unit": "s/step", "h2d_bytes_per_step": latent_host.numel() * 4,
-                "d2h_bytes_per_step": out_host.numel() * 4},
+        "e2e": {"value": e2e_s, "unit": "s/step",
+                # the latent, and the timestep's per-frame sinusoid (computed on the host, as the
+                # reference's _time_embed does)
+                "h2d_bytes_per_step": latent_host.numel() * 4 + GRID[0] * 256 * 2,
+                "d2h_bytes_per_step": out_host.numel() * out_host.element_size()},
         "gpu_launches": launches,
         "roofline": roof,
         "self_attn": self_attn,

@@ -36,7 +36,9 @@ extern "C" {
  * d[M, N] = epilogue(a[M, K] . w[N, K]^T)  -- nn.Linear with the weight as stored.
  * Replaces `_lin` / `_mm` (fast_dit.py:103-109) and the elementwise ops that follow them:
  *   WANB200_EPI_BIAS          d = acc + bias                                  (_lin)
- *   WANB200_EPI_BIAS_GELU     d = gelu_tanh(acc + bias)                       (ffn[0], ffn[1])
+ *   WANB200_EPI_BIAS_GELU     d = gelu_tanh(acc + bias)                       (ffn[0], ffn[1]; text_embedding)
+ *   WANB200_EPI_BIAS_SILU     d = silu(acc + bias)                            (time_embedding[0..1], the
+ *                             SiLU in front of time_projection, wan/modules/model.py:381-386)
  *   WANB200_EPI_BIAS_GATE_RES d = residual + (acc + bias) * gate[frame(row)]  (_gate + residual, 294/311)
  *   WANB200_EPI_BIAS_RES      d = residual + acc + bias                       (cross-attn residual, 305)
  *   WANB200_EPI_BIAS_SUMSQ    d = acc + bias; rowss[s*M + row] += sum over section s of d^2
@@ -62,6 +64,7 @@ extern "C" {
 #define WANB200_EPI_BIAS_RES 4
 #define WANB200_EPI_BIAS_SUMSQ 5
 #define WANB200_EPI_SCATTER 6
+#define WANB200_EPI_BIAS_SILU 7
 #define WANB200_MAX_PEERS 8
 
 typedef struct wanb200_gemm_params {
@@ -79,10 +82,12 @@ typedef struct wanb200_gemm_params {
   void* peer_out[WANB200_MAX_PEERS]; int npeers; int src_rank; int64_t shard_rows; /* SCATTER */
   int tile_n;  /* tile width along N: 0 = the library's choice (fills the SMs' last wave), else a
                 * multiple of 32 in 64..256 (for tuning; results do not depend on it) */
-  /* fp32 residual stream (GATE_RES / RES only): residual_f32 != 0 reads residual as fp32
-   * [M, ldr], out_f32 != 0 writes d as fp32 [M, ldd] (strides still in elements).  The sums
-   * x + y stay in fp32 across a step instead of being rounded to bf16 after every block's three
-   * updates, the dominant error of a 30-layer bf16 step. */
+  /* fp32 residual stream: residual_f32 != 0 (GATE_RES / RES only) reads residual as fp32
+   * [M, ldr]; out_f32 != 0 (every epilogue but SUMSQ and SCATTER) writes d as fp32 [M, ldd]
+   * (strides still in elements).  The sums x + y stay in fp32 across a step instead of being
+   * rounded to bf16 after every block's three updates, the dominant error of a 30-layer bf16
+   * step; the patch embedding writes the stream's first value and the time embedding its
+   * fp32 modulation rows the same way. */
   int residual_f32, out_f32;
 } wanb200_gemm_params;
 
@@ -177,6 +182,10 @@ typedef struct wanb200_ln_params {
    * push_out[p] + (push_row0 + row) * dim for p < npush (peer-mapped buffers; out may be NULL) */
   void* push_out[WANB200_MAX_PEERS]; int npush; int64_t push_row0;
   int x_f32;  /* x is fp32 (the fp32 residual stream); out stays bf16 */
+  /* e0_one_row != 0: shift and scale both add the same row e0 + frame * e0_frame_stride (the
+   * head's modulation `head.modulation + e`, one time-embedding row per frame, fast_dit.py:496-498;
+   * modulation is then [2, dim] with shift_idx 0, scale_idx 1) */
+  int e0_one_row;
 } wanb200_ln_params;
 
 int wanb200_layernorm(const wanb200_ln_params* p, void* stream);
@@ -247,6 +256,42 @@ typedef struct wanb200_shard_gather_params {
 
 int wanb200_shard_gather(const wanb200_shard_gather_params* p, void* stream);
 
+/* ---------------------------------------------------------------- embeddings and head
+ * The gathers around the patch-embedding and head GEMMs of the step driver (`_FastPatch`,
+ * models/fast_dit.py:527-537; `_FastHead` / `_FastHeadCfgPar` 480-524).
+ *
+ * wanb200_patchify: the Conv3d patchify (stride = kernel) of a latent [C, F, H, W] (fp32 or
+ * bf16) into the patch-embedding GEMM's A operand out [batch, L, C*pf*ph*pw] bf16 (the same rows
+ * for every batch copy, the CFG branches), token l = (f*H/ph + h)*W/pw + w, entry
+ * k = ((c*pf + i)*ph + j)*pw + u as the Conv3d weight [C_out, C, pf, ph, pw] flattens. */
+typedef struct wanb200_patchify_params {
+  const void* latent; int latent_f32;
+  int64_t channels, frames, height, width;
+  int pf, ph, pw;
+  int64_t batch;
+  void* out;
+} wanb200_patchify_params;
+
+int wanb200_patchify(const wanb200_patchify_params* p, void* stream);
+
+/* wanb200_unpatchify_cfg: the head GEMM's output y [batch, L, pf*ph*pw*C] fp32 (row entry
+ * ((i*ph + j)*pw + u)*C + c) back to the latent layout out [C, F*pf, H*ph, W*pw] with the CFG
+ * combine: WANB200_CFG_COMBINE (batch 2 = cond, uncond): uncond + guide * (cond - uncond);
+ * WANB200_CFG_SCALE: guide * y[0] (a CFG-parallel rank's weighted branch, summed over the pair
+ * by the caller).  out is bf16 (the reference's output dtype) or fp32 (out_f32). */
+#define WANB200_CFG_COMBINE 0
+#define WANB200_CFG_SCALE 1
+
+typedef struct wanb200_unpatchify_params {
+  const float* y; int64_t batch;
+  int64_t frames, height, width;  /* the token grid */
+  int pf, ph, pw; int64_t channels;
+  int mode; float guide;
+  void* out; int out_f32;
+} wanb200_unpatchify_params;
+
+int wanb200_unpatchify_cfg(const wanb200_unpatchify_params* p, void* stream);
+
 /* ---------------------------------------------------------------- whole block
  * One WanAttentionBlock forward in one call: `_FastBlock.forward(x, e, cos, sin, ck, cv)`
  * (models/fast_dit.py:260-311; the unit the reference compiles whole, fast_dit.py:586, 646-649)
@@ -312,7 +357,8 @@ int wanb200_device_error(int reset);
 int wanb200_device_error_async(int* host_out, void* stream);
 /* Library version, e.g. 200 for 0.2.0. */
 int wanb200_version(void);
-/* sizeof of the parameter structs (gemm, attn, ln, qknorm, residual, shard_gather, attn_fp8, block)
+/* sizeof of the parameter structs (gemm, attn, ln, qknorm, residual, shard_gather, attn_fp8, block,
+ * patchify, unpatchify)
  * written to out[0..n); returns the number of structs.  Lets a binding detect a library built
  * from a different header. */
 int wanb200_struct_sizes(int64_t* out, int n);

@@ -39,6 +39,8 @@ STRUCTS = {
     "wanb200_attn_fp8_params": L.AttnFp8Params,
     "wanb200_block_params": L.BlockParams,
     "wanb200_block_weights": L.BlockWeightsC,
+    "wanb200_patchify_params": L.PatchifyParams,
+    "wanb200_unpatchify_params": L.UnpatchifyParams,
 }
 
 
@@ -93,9 +95,12 @@ def test_gemm_rejects_bad_shapes_on_host():
     p.epilogue = 9
     rc, msg = _rc_msg(lib.wanb200_gemm_bf16, p)
     assert rc == -1 and "epilogue" in msg
-    p.epilogue, p.bias, p.out_f32 = L.EPI_BIAS, 48, 1  # fp32 output is for the residual epilogues only
+    p.epilogue, p.bias, p.residual_f32 = L.EPI_BIAS, 48, 1  # an fp32 residual is for the residual epilogues
     rc, msg = _rc_msg(lib.wanb200_gemm_bf16, p)
-    assert rc == -1 and "residual_f32 / out_f32" in msg
+    assert rc == -1 and "residual_f32" in msg
+    p.epilogue, p.residual_f32, p.out_f32 = L.EPI_BIAS_SUMSQ, 0, 1
+    rc, msg = _rc_msg(lib.wanb200_gemm_bf16, p)
+    assert rc == -1 and "out_f32" in msg
 
 
 def test_attn_rejects_bad_args_on_host():

@@ -317,3 +317,50 @@ def test_block_forward_c_entry_matches_the_python_block_op():
     y32 = block_forward_c(blk, x.to(DEV), e0.to(DEV), cosd, sind, ckd, cvd, out_dtype=torch.float32)
     assert y32.dtype == torch.float32
     assert R.rel_rms(y32.cpu(), y_ref) < R.rel_rms(y_c.float().cpu(), y_ref)  # no output rounding
+
+
+def _golden_dit(mg, **kw):
+    cfg = mg["cfg"]
+    spec = WanSpec(dim=cfg["dim"], ffn_dim=cfg["ffn_dim"], num_heads=cfg["num_heads"], num_layers=cfg["num_layers"],
+                   freq_dim=cfg["freq_dim"], text_dim=cfg["text_dim"], in_dim=cfg["in_dim"], out_dim=cfg["out_dim"],
+                   text_len=cfg["text_len"])
+    lat = mg["latent"]
+    return FastWanDiT((spec, mg["state_dict"]), (lat.shape[1], lat.shape[2] // 2, lat.shape[3] // 2), mg["guide"],
+                      DEV, **kw)
+
+
+def test_embeddings_and_head_on_the_kernels_vs_oracle():
+    """The step driver's embeddings and head run on the library's kernels in bf16 (as the
+    reference's `_time_embed` / `_FastPatch` / `_FastText` / `_FastHead` do): each against the fp32
+    oracle (ref_fp32.py:77-98) on the golden model, and the head per token shard (the Q-local
+    layouts' head, padded last shard included) against the whole-sequence head."""
+    mg = torch.load(os.path.join(GOLD, "model_small.pt"), weights_only=False)
+    fd = _golden_dit(mg)
+    mp = fp32(mg["state_dict"])
+    nf = fd.num_frames
+    e, e0 = fd.time_embed(mg["t"])
+    e_ref, e0_ref = R.time_embed(mp, mg["t"], nf, mg["cfg"]["freq_dim"])
+    assert R.rel_rms(e.cpu(), e_ref[0]) < 1e-2 and R.rel_rms(e0.cpu(), e0_ref[0]) < 1e-2
+    x = fd.patch(mg["latent"].to(DEV))
+    x_ref = R.patch_embed(mp, mg["latent"].float())
+    assert x.dtype == torch.float32 and R.rel_rms(x[0].cpu(), x_ref[0]) < 1e-2 and torch.equal(x[0], x[1])
+    ctx = torch.stack([mg["ctx"], mg["ctx_null"]]).float()
+    fd.set_context(mg["ctx"].to(DEV), mg["ctx_null"].to(DEV))
+    ck0, _ = fd.context[0]
+    ck_ref, _ = R.cross_kv(R.block_params(mp, 0), R.text_embed(mp, ctx), mg["cfg"]["num_heads"])
+    assert R.rel_rms(ck0.float().cpu(), ck_ref) < 2e-2
+    g = torch.Generator().manual_seed(5)
+    L_, C = fd.seq_len, fd.spec.dim
+    xs = torch.randn(2, L_, C, generator=g)
+    es = torch.randn(nf, C, generator=g) * 0.1
+    y_ref = R.head(mp, xs, es.unsqueeze(0), fd.grid)
+    want = y_ref[1] + fd.guide_scale * (y_ref[0] - y_ref[1])
+    whole = fd.head(xs.to(DEV), es.to(DEV))
+    assert whole.dtype == torch.bfloat16 and R.rel_rms(whole.float().cpu(), want) < 1e-2
+    tok = fd.head_tokens(xs.to(DEV), es.to(DEV))
+    for sp in (2, 5):  # 5 shards of 5 leave the last one with 4 tokens + 1 pad row
+        S = -(-L_ // sp)
+        xp = torch.cat([xs, xs.new_zeros(2, sp * S - L_, C)], dim=1).to(DEV)
+        parts = [fd.head_tokens(xp[:, r * S:(r + 1) * S].contiguous(), es.to(DEV), r * S) for r in range(sp)]
+        got = torch.cat(parts, dim=1)[:, :L_]
+        assert R.rel_rms(got.cpu(), tok.cpu()) < 1e-6, sp

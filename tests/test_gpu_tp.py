@@ -54,8 +54,16 @@ def _worker(rank, world, port, q):
         cos, sin = rope_tables(grid, 128, dev)
         w = BlockWeights(sd, spec.num_heads, dev, rank, world)
         ck, cv = FastCrossKV(w, dist.group.WORLD)(ctx.to(dev))
-        y_tp = FastBlock(w, grid[0], dist.group.WORLD)(x.to(dev), e0.to(dev), cos, sin, ck, cv)
+        blk_tp = FastBlock(w, grid[0], dist.group.WORLD)
+        y_tp = blk_tp(x.to(dev), e0.to(dev), cos, sin, ck, cv)
+        # the whole block as one C call, its all-reduces through the callback into torch.distributed
+        from wanb200.block import block_forward_c
+        y_c = block_forward_c(blk_tp, x.to(dev), e0.to(dev), cos, sin, ck, cv)
+        # one chunk (a single blocking all-reduce per projection) against the overlapped chunks
+        y_1 = FastBlock(w, grid[0], dist.group.WORLD, tp_chunks=1)(x.to(dev), e0.to(dev), cos, sin, ck, cv)
         torch.cuda.synchronize()
+        out["c_entry_vs_op"] = R.rel_rms(y_c.float().cpu(), y_tp.float().cpu())
+        out["chunks_vs_one"] = R.rel_rms(y_1.float().cpu(), y_tp.float().cpu())
         if rank == 0:
             w1 = BlockWeights(sd, spec.num_heads, dev)
             ck1, cv1 = FastCrossKV(w1)(ctx.to(dev))
@@ -114,5 +122,8 @@ def test_tp2_block_and_step():
         assert res[r]["step_vs_reference"] < 5e-2, res[r]
         assert res[r]["cfgpar_vs_reference"] < 5e-2, res[r]
     print("tp2:", res[0])
+    for r in range(WORLD):
+        assert res[r]["c_entry_vs_op"] < 1e-3, res[r]
+        assert res[r]["chunks_vs_one"] < 1e-3, res[r]
     assert res[0]["tp_vs_tp1"] < 1e-2
     assert res[0]["tp_vs_oracle"] < 2e-2

@@ -174,6 +174,14 @@ int wanb200_shard_gather(const wanb200_shard_gather_params* p, void* stream) {
   return shard_gather(p, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int wanb200_patchify(const wanb200_patchify_params* p, void* stream) {
+  return patchify(p, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int wanb200_unpatchify_cfg(const wanb200_unpatchify_params* p, void* stream) {
+  return unpatchify_cfg(p, reinterpret_cast<cudaStream_t>(stream));
+}
+
 int wanb200_block_forward(const wanb200_block_params* p, void* stream) {
   return block_forward(p, reinterpret_cast<cudaStream_t>(stream));
 }
@@ -212,12 +220,13 @@ int wanb200_device_error_async(int* host_out, void* stream) {
 int wanb200_version(void) { return 200; }
 
 int wanb200_struct_sizes(int64_t* out, int n) {
-  const int64_t sizes[8] = {(int64_t)sizeof(wanb200_gemm_params), (int64_t)sizeof(wanb200_attn_params),
-                            (int64_t)sizeof(wanb200_ln_params), (int64_t)sizeof(wanb200_qknorm_params),
-                            (int64_t)sizeof(wanb200_residual_params), (int64_t)sizeof(wanb200_shard_gather_params),
-                            (int64_t)sizeof(wanb200_attn_fp8_params), (int64_t)sizeof(wanb200_block_params)};
-  for (int i = 0; i < n && i < 8; ++i) out[i] = sizes[i];
-  return 8;
+  const int64_t sizes[10] = {(int64_t)sizeof(wanb200_gemm_params), (int64_t)sizeof(wanb200_attn_params),
+                             (int64_t)sizeof(wanb200_ln_params), (int64_t)sizeof(wanb200_qknorm_params),
+                             (int64_t)sizeof(wanb200_residual_params), (int64_t)sizeof(wanb200_shard_gather_params),
+                             (int64_t)sizeof(wanb200_attn_fp8_params), (int64_t)sizeof(wanb200_block_params),
+                             (int64_t)sizeof(wanb200_patchify_params), (int64_t)sizeof(wanb200_unpatchify_params)};
+  for (int i = 0; i < n && i < 10; ++i) out[i] = sizes[i];
+  return 10;
 }
 
 }  // extern "C"

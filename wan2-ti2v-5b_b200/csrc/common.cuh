@@ -340,6 +340,9 @@ __device__ __forceinline__ float gelu_tanh(float x) {
   return fmaf(hx, tanh_approx(u), hx);
 }
 
+// SiLU x * sigmoid(x) = x / (1 + 2^(-x log2 e)) (time embedding MLP, wan/modules/model.py:381-386).
+__device__ __forceinline__ float silu(float x) { return x / (1.f + ex2_approx(-1.4426950408889634f * x)); }
+
 // Latent frame of buffer row `row` (the index of its per-frame modulation row):
 // token = (rows_per_seq > 0 ? row % rows_per_seq : row) + row_offset, frame = (token % seq_len) /
 // tokens_per_frame.  rows_per_seq > 0 describes a [batch, rows_per_seq] buffer holding tokens
@@ -347,6 +350,13 @@ __device__ __forceinline__ float gelu_tanh(float x) {
 __device__ __forceinline__ int64_t frame_of_row(int64_t row, int64_t rows_per_seq, int64_t row_offset,
                                                 int64_t seq_len, int64_t tokens_per_frame) {
   const int64_t tok = (rows_per_seq > 0 ? row % rows_per_seq : row) + row_offset;
+  return (tok % seq_len) / tokens_per_frame;
+}
+
+// frame_of_row in 32-bit arithmetic (all arguments < 2^31), for kernels that compute it per thread.
+__device__ __forceinline__ int frame_of_row32(int row, int rows_per_seq, int row_offset, int seq_len,
+                                              int tokens_per_frame) {
+  const int tok = (rows_per_seq > 0 ? row % rows_per_seq : row) + row_offset;
   return (tok % seq_len) / tokens_per_frame;
 }
 

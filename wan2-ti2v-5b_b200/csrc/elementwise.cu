@@ -26,6 +26,7 @@ struct LnArgs {
   __nv_bfloat16* push_out[WANB200_MAX_PEERS];
   int npush;
   int64_t push_row0;
+  int e0_one_row;
 };
 
 // RW warps per row (RW = 2 when dim % 512 == 0, else 1): thread t < 32*RW of the row holds the
@@ -102,8 +103,8 @@ __global__ void __launch_bounds__(256, RW == 2 ? 3 : 2) layernorm_kernel(const L
   const float* scp = nullptr;
   if constexpr (MODE == 0) {
     const int64_t f = frame_of_row(row, a.rows_per_seq, a.row_offset, a.seq_len, a.tokens_per_frame);
-    shp = a.e0 + f * a.e0_frame_stride + (int64_t)a.shift_idx * a.dim;
-    scp = a.e0 + f * a.e0_frame_stride + (int64_t)a.scale_idx * a.dim;
+    shp = a.e0 + f * a.e0_frame_stride + (a.e0_one_row ? 0 : (int64_t)a.shift_idx * a.dim);
+    scp = a.e0 + f * a.e0_frame_stride + (a.e0_one_row ? 0 : (int64_t)a.scale_idx * a.dim);
   }
   uint4* outr = a.out ? reinterpret_cast<uint4*>(a.out + row * a.dim) : nullptr;
 #pragma unroll
@@ -224,6 +225,7 @@ int layernorm(const wanb200_ln_params* p, cudaStream_t st) {
     a.push_out[i] = reinterpret_cast<__nv_bfloat16*>(i < p->npush ? p->push_out[i] : nullptr);
   a.npush = p->npush;
   a.push_row0 = p->push_row0;
+  a.e0_one_row = p->e0_one_row != 0;
   if ((p->rows + 3) / 4 > INT32_MAX) return set_error(WANB200_EINVAL, "layernorm: too many rows");
   const bool push = a.npush > 0, xf32 = p->x_f32 != 0;
   if (p->mode == WANB200_LN_MODULATE)
@@ -247,23 +249,24 @@ struct QkArgs {
   int rope;
   const float* cos;
   const float* sin;
-  int64_t seq_len;
+  int seq_len;
 };
 
-// Thread = 8 consecutive channels (4 rotation pairs) of one row of one section.
+// Thread (x, y) = 8 consecutive channels (4 rotation pairs) x of row blockIdx.x * blockDim.y + y,
+// section blockIdx.y: 2-D blocks so that a thread finds its row without integer division (the
+// kernel streams 16 bytes per thread; a 64-bit divide per thread would cost more than the load).
 // `_tp_rms_qk` (models/fast_dit.py:134-147): x * rsqrt(ss/3072 + eps) * gamma, then `_rope`
 // (fast_dit.py:163-169): (x0, x1) -> (x0 c - x1 s, x0 s + x1 c) with the pair's angle.
-__global__ void __launch_bounds__(256) qknorm_rope_kernel(const QkArgs a) {
+__global__ void __launch_bounds__(1024) qknorm_rope_kernel(const QkArgs a) {
   const int sec = blockIdx.y;
-  const int64_t vpr = a.width >> 3;
-  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= a.rows * vpr) return;
-  const int64_t row = idx / vpr;
-  const int cv = (int)(idx - row * vpr) * 8;
+  const int vpr = a.width >> 3;
+  const int row = blockIdx.x * blockDim.y + threadIdx.y;
+  if (threadIdx.x >= vpr || row >= a.rows) return;
+  const int cv = threadIdx.x * 8;
   const int64_t col0 = sec ? a.col0[1] : a.col0[0];
   const float* ss = sec ? a.ss[1] : a.ss[0];
   const __nv_bfloat16* gamma = sec ? a.gamma[1] : a.gamma[0];
-  uint4* p = reinterpret_cast<uint4*>(a.x + row * a.ld + col0 + cv);
+  uint4* p = reinterpret_cast<uint4*>(a.x + (int64_t)row * a.ld + col0 + cv);
   float v[8], g[8];
   unpack_bf16x8(*p, v);
   unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(gamma + cv)), g);
@@ -271,10 +274,10 @@ __global__ void __launch_bounds__(256) qknorm_rope_kernel(const QkArgs a) {
 #pragma unroll
   for (int k = 0; k < 8; ++k) v[k] *= rs * g[k];
   if (a.rope) {
-    const int64_t pos = row % a.seq_len;
+    const int pos = row % a.seq_len;
     const int pair0 = (cv & 127) >> 1;
-    const float4 c4 = __ldg(reinterpret_cast<const float4*>(a.cos + pos * 64 + pair0));
-    const float4 s4 = __ldg(reinterpret_cast<const float4*>(a.sin + pos * 64 + pair0));
+    const float4 c4 = __ldg(reinterpret_cast<const float4*>(a.cos + (int64_t)pos * 64 + pair0));
+    const float4 s4 = __ldg(reinterpret_cast<const float4*>(a.sin + (int64_t)pos * 64 + pair0));
     float x0, x1;
     x0 = v[0]; x1 = v[1]; v[0] = x0 * c4.x - x1 * s4.x; v[1] = x0 * s4.x + x1 * c4.x;
     x0 = v[2]; x1 = v[3]; v[2] = x0 * c4.y - x1 * s4.y; v[3] = x0 * s4.y + x1 * c4.y;
@@ -287,6 +290,13 @@ __global__ void __launch_bounds__(256) qknorm_rope_kernel(const QkArgs a) {
   u.z = pack_bf16x2(v[4], v[5]);
   u.w = pack_bf16x2(v[6], v[7]);
   *p = u;
+}
+
+// Block shape of the row-streaming kernels: x = the row's 16-byte vectors (rounded up to a warp,
+// at most 1024), y = rows per block (about 256 threads, at least one row).
+static dim3 row_block(int64_t vecs_per_row) {
+  const int bx = (int)std::min<int64_t>(1024, (vecs_per_row + 31) / 32 * 32);
+  return dim3(bx, std::max(1, 256 / bx));
 }
 
 int qk_norm_rope(const wanb200_qknorm_params* p, cudaStream_t st) {
@@ -318,11 +328,13 @@ int qk_norm_rope(const wanb200_qknorm_params* p, cudaStream_t st) {
   a.rope = p->rope;
   a.cos = p->cos;
   a.sin = p->sin;
-  a.seq_len = p->seq_len > 0 ? p->seq_len : 1;
-  const int64_t total = p->rows * (p->width / 8);
-  const int64_t blocks = (total + 255) / 256;
-  if (blocks > INT32_MAX) return set_error(WANB200_EINVAL, "qk_norm_rope: too large");
-  qknorm_rope_kernel<<<dim3((unsigned)blocks, (unsigned)p->nsections), 256, 0, st>>>(a);
+  if (p->seq_len > INT32_MAX) return set_error(WANB200_EINVAL, "qk_norm_rope: seq_len too large");
+  a.seq_len = p->seq_len > 0 ? (int)p->seq_len : 1;
+  if (p->rows > INT32_MAX / 2 || p->width / 8 > 1024)
+    return set_error(WANB200_EINVAL, "qk_norm_rope: rows < 2^30, width <= 8192");
+  const dim3 blk = row_block(p->width / 8);
+  const int64_t blocks = (p->rows + blk.y - 1) / blk.y;
+  qknorm_rope_kernel<<<dim3((unsigned)blocks, (unsigned)p->nsections), blk, 0, st>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error("qknorm_rope_kernel launch", e);
   return WANB200_OK;
@@ -344,15 +356,15 @@ struct ResArgs {
   int64_t y_slice_stride;
 };
 
-// Thread = 8 channels of one row.  `x + _gate(y + b, e[k])` / `x + (y + b)` after the TP
-// all-reduce of a row-parallel projection (models/fast_dit.py:126-131, 179-181).
+// Thread (x, y) = 8 channels x of row blockIdx.x * blockDim.y + y (2-D blocks: no per-thread
+// integer division).  `x + _gate(y + b, e[k])` / `x + (y + b)` after the TP all-reduce of a
+// row-parallel projection (models/fast_dit.py:126-131, 179-181).
 template <bool GATE>
-__global__ void __launch_bounds__(256) bias_gate_residual_kernel(const ResArgs a) {
-  const int64_t vpr = a.dim >> 3;
-  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= a.rows * vpr) return;
-  const int64_t row = idx / vpr;
-  const int col = (int)(idx - row * vpr) * 8;
+__global__ void __launch_bounds__(1024) bias_gate_residual_kernel(const ResArgs a) {
+  const int vpr = a.dim >> 3;
+  const int64_t row = (int64_t)blockIdx.x * blockDim.y + threadIdx.y;
+  if ((int)threadIdx.x >= vpr || row >= a.rows) return;
+  const int col = threadIdx.x * 8;
   float r[8], y[8], b[8];
   if (a.res_f32) {
     const float4* rp = reinterpret_cast<const float4*>(static_cast<const float*>(a.residual) + row * a.dim + col);
@@ -373,7 +385,8 @@ __global__ void __launch_bounds__(256) bias_gate_residual_kernel(const ResArgs a
     float g[8];
     unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.gate_mod + col)), g);
     const float* e = a.gate_e0 +
-                     frame_of_row(row, a.rows_per_seq, a.row_offset, a.seq_len, a.tokens_per_frame) * a.gate_frame_stride + col;
+                     (int64_t)frame_of_row32((int)row, (int)a.rows_per_seq, (int)a.row_offset, (int)a.seq_len,
+                                             (int)a.tokens_per_frame) * a.gate_frame_stride + col;
     const float4 e0 = __ldg(reinterpret_cast<const float4*>(e)), e1 = __ldg(reinterpret_cast<const float4*>(e + 4));
     g[0] += e0.x; g[1] += e0.y; g[2] += e0.z; g[3] += e0.w;
     g[4] += e1.x; g[5] += e1.y; g[6] += e1.z; g[7] += e1.w;
@@ -427,12 +440,17 @@ int bias_gate_residual(const wanb200_residual_params* p, cudaStream_t st) {
   a.rows_per_seq = p->rows_per_seq;
   a.nsum = p->nsum;
   a.y_slice_stride = p->y_slice_stride;
-  const int64_t blocks = (p->rows * (p->dim / 8) + 255) / 256;
+  if (p->dim / 8 > 1024) return set_error(WANB200_EINVAL, "bias_gate_residual: dim <= 8192");
+  if (p->rows > INT32_MAX / 2 || p->seq_len > INT32_MAX || p->tokens_per_frame > INT32_MAX ||
+      p->row_offset > INT32_MAX / 2 || p->rows_per_seq > INT32_MAX)
+    return set_error(WANB200_EINVAL, "bias_gate_residual: rows / frame arguments must be < 2^30");
+  const dim3 blk = row_block(p->dim / 8);
+  const int64_t blocks = (p->rows + blk.y - 1) / blk.y;
   if (blocks > INT32_MAX) return set_error(WANB200_EINVAL, "bias_gate_residual: too large");
   if (gate)
-    bias_gate_residual_kernel<true><<<(unsigned)blocks, 256, 0, st>>>(a);
+    bias_gate_residual_kernel<true><<<(unsigned)blocks, blk, 0, st>>>(a);
   else
-    bias_gate_residual_kernel<false><<<(unsigned)blocks, 256, 0, st>>>(a);
+    bias_gate_residual_kernel<false><<<(unsigned)blocks, blk, 0, st>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error("bias_gate_residual_kernel launch", e);
   return WANB200_OK;

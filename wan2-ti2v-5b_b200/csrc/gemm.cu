@@ -10,11 +10,14 @@
 // of tile t overlaps the main loop of tile t+1.  One CTA per SM, tiles strided over the
 // persistent grid in grouped order so the CTAs running together share A rows and W.
 //
-// Warp roles (192 threads):
+// Warp roles (320 threads):
 //   warp 0      TMA producer (one lane)
 //   warp 1      TMEM allocator + UMMA issuer (one lane)
-//   warps 2..5  epilogue: warp w drains TMEM lanes 32*(w%4)..+31 (= tile rows), 32 columns
-//               per tcgen05.ld, applies the epilogue in fp32 and stores bf16.
+//   warps 2..9  epilogue: warp w drains TMEM lanes 32*(w%4)..+31 (= tile rows); the two warps
+//               on a lane quarter take alternate 32-column chunks (one tcgen05.ld each), apply
+//               the epilogue in fp32 and store.  Two warps per row block double the loads of the
+//               residual / gate in flight, which the fp32 residual stream needs to stay hidden
+//               behind the next tile's main loop.
 #include <atomic>
 
 #include "common.cuh"
@@ -33,6 +36,8 @@ constexpr uint32_t G_TMEM_COLS = 512;
 // The TMA ring has as many stages as fit (at most G_MAX_STAGES): a stage holds the A tile and a
 // BN-wide W tile, so narrow tiles get a deeper ring to cover the load latency of short K loops.
 constexpr int G_MAX_STAGES = 6;
+constexpr int G_EPI_WARPS = 8;
+constexpr int G_THREADS = 64 + 32 * G_EPI_WARPS;
 constexpr int G_SMEM_LIMIT = 232448;  // 227 KB of dynamic shared memory per CTA
 template <int EPI>
 struct GemmCfg {
@@ -134,7 +139,7 @@ __device__ __forceinline__ void residual_values(const GemmArgs& a, const uint4 (
 
 template <int EPI>
 __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v, int row, int col0, float& ss_acc,
-                                                    int& ss_sec, const uint4 (&res)[8]) {
+                                                    int& ss_sec, const uint4 (&res)[8], const float* gate_row) {
   if constexpr (EPI != WANB200_EPI_NONE && EPI != WANB200_EPI_SCATTER) {
     const uint4* bp = reinterpret_cast<const uint4*>(a.bias + col0);
 #pragma unroll
@@ -149,13 +154,16 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v,
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
   }
+  if constexpr (EPI == WANB200_EPI_BIAS_SILU) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = silu(v[i]);
+  }
   if constexpr (EPI == WANB200_EPI_BIAS_GATE_RES || EPI == WANB200_EPI_BIAS_RES) {
     if (row < a.M) {
       float r[32];
       residual_values(a, res, r);
       if constexpr (EPI == WANB200_EPI_BIAS_GATE_RES) {
-        const int f = (int)frame_of_row(row, a.rows_per_seq, a.row_offset, a.seq_len, a.tokens_per_frame);
-        const float4* ep = reinterpret_cast<const float4*>(a.gate_e0 + (int64_t)f * a.gate_frame_stride + col0);
+        const float4* ep = reinterpret_cast<const float4*>(gate_row + col0);
         const uint4* mp = reinterpret_cast<const uint4*>(a.gate_mod + col0);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -183,7 +191,7 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v,
 #pragma unroll
     for (int i = 0; i < 32; ++i) ss_acc = fmaf(v[i], v[i], ss_acc);
   }
-  if (epi_has_residual(EPI) && a.out_f32) {
+  if (EPI != WANB200_EPI_SCATTER && EPI != WANB200_EPI_BIAS_SUMSQ && a.out_f32) {
     if (row < a.M) {
       float4* dp = reinterpret_cast<float4*>(static_cast<float*>(a.d) + (int64_t)row * a.ldd + col0);
 #pragma unroll
@@ -209,7 +217,7 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v,
 }
 
 template <int EPI>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(G_THREADS, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const GemmArgs args) {
   extern __shared__ uint8_t smem_raw[];
@@ -236,7 +244,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(tfull0 + 8 * b, 1);
-      mbar_init(tempty0 + 8 * b, 128);
+      mbar_init(tempty0 + 8 * b, 32 * G_EPI_WARPS);
     }
     mbar_init(done_bar, 1);
     *abort_flag = 0;
@@ -331,6 +339,7 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;  // which of the two warps on this lane quarter
     const int r = quad * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -345,9 +354,10 @@ __global__ void __launch_bounds__(192, 1)
       int ss_sec = -1;
       if constexpr (EPI == WANB200_EPI_SCATTER) {
         // stage this warp's 32 rows (lane = row), then write each row as one 512-byte segment
+        // (the first warp of each lane quarter does the whole tile; the second only arrives)
         constexpr int SR = GemmCfg<EPI>::STAGING_ROW;
         uint8_t* stg = smem + args.tiles_bytes + quad * 32 * SR;
-        const int ncols = min(bn, args.N - n0);  // multiple of 32
+        const int ncols = half ? 0 : min(bn, args.N - n0);  // multiple of 32
 #pragma unroll 1
         for (int c = 0; c < ncols / 32; ++c) {
           float v[32];
@@ -360,7 +370,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         __syncwarp();
 #pragma unroll 1
-        for (int rr = 0; rr < 32; ++rr) {
+        for (int rr = 0; rr < (half ? 0 : 32); ++rr) {
           const int orow = m0 + quad * 32 + rr;
           if (orow < args.M && lane * 8 < ncols)
             *reinterpret_cast<uint4*>(scatter_row_ptr(args, orow) + n0 + lane * 8) =
@@ -369,19 +379,27 @@ __global__ void __launch_bounds__(192, 1)
         __syncwarp();
       } else {
         uint4 res_next[8] = {}, res_cur[8];
-        if constexpr (epi_has_residual(EPI)) load_residual_chunk(args, row, n0, res_next);
+        if constexpr (epi_has_residual(EPI)) load_residual_chunk(args, row, n0 + half * 32, res_next);
+        // the gate row of this tile row's latent frame (once per tile, not per chunk)
+        const float* gate_row = nullptr;
+        if constexpr (EPI == WANB200_EPI_BIAS_GATE_RES) {
+          const int f = row < args.M ? (int)frame_of_row(row, args.rows_per_seq, args.row_offset, args.seq_len,
+                                                         args.tokens_per_frame)
+                                     : 0;
+          gate_row = args.gate_e0 + (int64_t)f * args.gate_frame_stride;
+        }
 #pragma unroll 1
-        for (int c = 0; c < bn / 32; ++c) {
+        for (int c = half; c < bn / 32; c += 2) {
           const int col0 = n0 + c * 32;
           if (col0 >= args.N) break;  // warp-uniform
 #pragma unroll
           for (int q = 0; q < 8; ++q) res_cur[q] = res_next[q];
           if constexpr (epi_has_residual(EPI)) {
-            if (c + 1 < bn / 32) load_residual_chunk(args, row, col0 + 32, res_next);
+            if (c + 2 < bn / 32) load_residual_chunk(args, row, col0 + 64, res_next);
           }
           float v[32];
           tmem_ld32(t_row + c * 32, v);
-          gemm_epilogue_chunk<EPI>(args, v, row, col0, ss_acc, ss_sec, res_cur);
+          gemm_epilogue_chunk<EPI>(args, v, row, col0, ss_acc, ss_sec, res_cur, gate_row);
         }
       }
       if constexpr (EPI == WANB200_EPI_BIAS_SUMSQ) {
@@ -416,7 +434,7 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmA
     attr_set[dev].store(true, std::memory_order_release);
   }
   const int smem = (int)ga.tiles_bytes + GemmCfg<EPI>::FIXED;
-  gemm_bf16_kernel<EPI><<<grid, 192, smem, st>>>(ta, tb, ga);
+  gemm_bf16_kernel<EPI><<<grid, G_THREADS, smem, st>>>(ta, tb, ga);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error("gemm_bf16_kernel launch", e);
   return WANB200_OK;
@@ -444,7 +462,7 @@ static int choose_tile_n(int64_t M, int64_t N, int sms) {
 int gemm_bf16(const wanb200_gemm_params* p, cudaStream_t st) {
   if (!p) return set_error(WANB200_EINVAL, "gemm: null params");
   const int epi = p->epilogue;
-  if (epi < WANB200_EPI_NONE || epi > WANB200_EPI_SCATTER) return set_error(WANB200_EINVAL, "gemm: bad epilogue");
+  if (epi < WANB200_EPI_NONE || epi > WANB200_EPI_BIAS_SILU) return set_error(WANB200_EINVAL, "gemm: bad epilogue");
   const bool scatter = epi == WANB200_EPI_SCATTER;
   if (!p->a || !p->w || (!p->d && !scatter)) return set_error(WANB200_EINVAL, "gemm: null a/w/d");
   if (p->M <= 0 || p->N <= 0 || p->K <= 0) return set_error(WANB200_EINVAL, "gemm: M, N, K must be positive");
@@ -469,9 +487,11 @@ int gemm_bf16(const wanb200_gemm_params* p, cudaStream_t st) {
   if (epi == WANB200_EPI_BIAS_GATE_RES || epi == WANB200_EPI_BIAS_RES) {
     if (!p->residual || !aligned16(p->residual) || p->ldr < p->N || (p->ldr % 8))
       return set_error(WANB200_EINVAL, "gemm: residual epilogue needs an aligned residual with ldr >= N, ldr % 8 == 0");
-  } else if (p->residual_f32 || p->out_f32) {
-    return set_error(WANB200_EINVAL, "gemm: residual_f32 / out_f32 apply to the GATE_RES and RES epilogues only");
+  } else if (p->residual_f32) {
+    return set_error(WANB200_EINVAL, "gemm: residual_f32 applies to the GATE_RES and RES epilogues only");
   }
+  if (p->out_f32 && (epi == WANB200_EPI_SCATTER || epi == WANB200_EPI_BIAS_SUMSQ))
+    return set_error(WANB200_EINVAL, "gemm: out_f32 does not apply to the SUMSQ and SCATTER epilogues");
   if (epi == WANB200_EPI_BIAS_GATE_RES) {
     if (!p->gate_mod || !p->gate_e0 || !aligned16(p->gate_mod) || !aligned16(p->gate_e0) ||
         (p->gate_frame_stride % 4) || p->seq_len <= 0 || p->tokens_per_frame <= 0 || p->seq_len > INT32_MAX ||
@@ -537,6 +557,7 @@ int gemm_bf16(const wanb200_gemm_params* p, cudaStream_t st) {
     case WANB200_EPI_NONE: return launch_gemm<WANB200_EPI_NONE>(ta, tb, ga, grid, st);
     case WANB200_EPI_BIAS: return launch_gemm<WANB200_EPI_BIAS>(ta, tb, ga, grid, st);
     case WANB200_EPI_BIAS_GELU: return launch_gemm<WANB200_EPI_BIAS_GELU>(ta, tb, ga, grid, st);
+    case WANB200_EPI_BIAS_SILU: return launch_gemm<WANB200_EPI_BIAS_SILU>(ta, tb, ga, grid, st);
     case WANB200_EPI_BIAS_GATE_RES: return launch_gemm<WANB200_EPI_BIAS_GATE_RES>(ta, tb, ga, grid, st);
     case WANB200_EPI_BIAS_RES: return launch_gemm<WANB200_EPI_BIAS_RES>(ta, tb, ga, grid, st);
     case WANB200_EPI_SCATTER: return launch_gemm<WANB200_EPI_SCATTER>(ta, tb, ga, grid, st);

@@ -62,6 +62,8 @@ int bias_gate_residual(const wanb200_residual_params* p, cudaStream_t st);
 int peer_barrier(int* const* flags, int rank, int world, int epoch, cudaStream_t st);
 int shard_gather(const wanb200_shard_gather_params* p, cudaStream_t st);
 int block_forward(const wanb200_block_params* p, cudaStream_t st);
+int patchify(const wanb200_patchify_params* p, cudaStream_t st);
+int unpatchify_cfg(const wanb200_unpatchify_params* p, cudaStream_t st);
 int64_t block_workspace_bytes(int64_t batch, int64_t seq_len, int64_t dim, int64_t local_heads, int64_t ffn_local,
                               int64_t ctx_len, int tp_size);
 

@@ -15,7 +15,7 @@ LIB_PATH = os.path.join(_HERE, "libwanb200.so")
 c_void_p, c_int64, c_int, c_float = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float
 c_float_p = ctypes.POINTER(ctypes.c_float)
 
-EPI_NONE, EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_GATE_RES, EPI_BIAS_RES, EPI_BIAS_SUMSQ, EPI_SCATTER = range(7)
+EPI_NONE, EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_GATE_RES, EPI_BIAS_RES, EPI_BIAS_SUMSQ, EPI_SCATTER, EPI_BIAS_SILU = range(8)
 MAX_PEERS = 8
 LN_MODULATE, LN_AFFINE = 0, 1
 
@@ -47,7 +47,8 @@ class LnParams(ctypes.Structure):
                 ("shift_idx", c_int), ("scale_idx", c_int), ("seq_len", c_int64), ("tokens_per_frame", c_int64),
                 ("row_offset", c_int64), ("rows_per_seq", c_int64),
                 ("weight", c_void_p), ("bias", c_void_p), ("zero_buf", c_void_p), ("zero_count", c_int64),
-                ("push_out", c_void_p * 8), ("npush", c_int), ("push_row0", c_int64), ("x_f32", c_int)]
+                ("push_out", c_void_p * 8), ("npush", c_int), ("push_row0", c_int64), ("x_f32", c_int),
+                ("e0_one_row", c_int)]
 
 
 class QkNormParams(ctypes.Structure):
@@ -75,6 +76,21 @@ class AttnFp8Params(ctypes.Structure):
     _fields_ = [("attn", AttnParams), ("fp8_workspace", c_void_p), ("fp8_workspace_bytes", c_int64)]
 
 
+class PatchifyParams(ctypes.Structure):
+    _fields_ = [("latent", c_void_p), ("latent_f32", c_int), ("channels", c_int64), ("frames", c_int64),
+                ("height", c_int64), ("width", c_int64), ("pf", c_int), ("ph", c_int), ("pw", c_int),
+                ("batch", c_int64), ("out", c_void_p)]
+
+
+CFG_COMBINE, CFG_SCALE = 0, 1
+
+
+class UnpatchifyParams(ctypes.Structure):
+    _fields_ = [("y", c_void_p), ("batch", c_int64), ("frames", c_int64), ("height", c_int64), ("width", c_int64),
+                ("pf", c_int), ("ph", c_int), ("pw", c_int), ("channels", c_int64), ("mode", c_int),
+                ("guide", c_float), ("out", c_void_p), ("out_f32", c_int)]
+
+
 class BlockWeightsC(ctypes.Structure):
     _fields_ = [(n, c_void_p) for n in ("modulation", "w_qkv", "b_qkv", "g_q", "g_k", "w_o", "b_o", "ln3_w",
                                         "ln3_b", "w_cq", "b_cq", "g_cq", "w_co", "b_co", "w1", "b1", "w2", "b2")]
@@ -98,7 +114,7 @@ EXPORTS = ("wanb200_gemm_bf16", "wanb200_attn_fwd", "wanb200_layernorm", "wanb20
            "wanb200_struct_sizes", "wanb200_peer_barrier", "wanb200_attn_workspace_bytes",
            "wanb200_attn_kv_splits", "wanb200_attn_fwd_noalloc", "wanb200_shard_gather", "wanb200_attn_fwd_fp8",
            "wanb200_attn_fp8_workspace_bytes", "wanb200_device_error_async", "wanb200_block_forward",
-           "wanb200_block_workspace_bytes")
+           "wanb200_block_workspace_bytes", "wanb200_patchify", "wanb200_unpatchify_cfg")
 
 _lock = threading.Lock()
 _lib = None
@@ -153,8 +169,12 @@ def load():
             lib.wanb200_block_forward.restype = c_int
             lib.wanb200_block_workspace_bytes.argtypes = [c_int64] * 6 + [c_int]
             lib.wanb200_block_workspace_bytes.restype = c_int64
+            lib.wanb200_patchify.argtypes = [ctypes.POINTER(PatchifyParams), c_void_p]
+            lib.wanb200_patchify.restype = c_int
+            lib.wanb200_unpatchify_cfg.argtypes = [ctypes.POINTER(UnpatchifyParams), c_void_p]
+            lib.wanb200_unpatchify_cfg.restype = c_int
             structs = (GemmParams, AttnParams, LnParams, QkNormParams, ResidualParams, ShardGatherParams,
-                       AttnFp8Params, BlockParams)
+                       AttnFp8Params, BlockParams, PatchifyParams, UnpatchifyParams)
             sizes = (c_int64 * len(structs))()
             n = lib.wanb200_struct_sizes(sizes, len(structs))
             want = [ctypes.sizeof(c) for c in structs]

@@ -16,16 +16,18 @@ Layouts (as the reference's):
   * TP inside a group (`tp_group` of size T > 1): each rank holds 24/T heads and 1/T of the
     FFN, and the block ops all-reduce over the group (`shard_model_tp`, tp_utils.py:378-458).
 
-The time / text / patch embeddings and the head are small (about 1% of the step) and run as
-fp32 torch ops on the GPU around the block kernels.
+The time / text / patch embeddings and the head (about 1% of the step) run on the library's
+kernels too (tcgen05 GEMMs, the LayerNorm, patchify / unpatchify gathers), in the reference's
+bf16 dtype flow, so a step launches nothing but the library's kernels (plus the NCCL collectives
+of the multi-GPU layouts).
 """
 from __future__ import annotations
 
 import torch
 import torch.distributed as dist
-import torch.nn.functional as F
 
 from . import _lib as L
+from . import ops
 from .block import FastBlock, FastBlockSP, FastCrossKV, register_block
 from .weights import BlockWeights, WanSpec, block_state
 
@@ -106,10 +108,7 @@ class FastWanDiT:
         self.cos, self.sin = rope_tables(self.grid, spec.head_dim, self.device)
         nl = spec.num_layers if num_layers is None else num_layers
 
-        def f32(k):
-            return sd[k].to(device=self.device, dtype=torch.float32)
-
-        self.emb = {k: f32(k) for k in sd if not k.startswith("blocks.")}
+        self.ew = self._embedding_weights(sd)
         spn = dist.get_world_size(sp_group) if (sp_group is not None and dist.is_initialized()) else 1
         self.sp_size = spn
         self.sp_rank = dist.get_rank(sp_group) if spn > 1 else 0
@@ -148,6 +147,7 @@ class FastWanDiT:
         self.cross_kv = [FastCrossKV(w, tp_group, spec.eps) for w in self.block_weights]
         self.context = None
         self._err_probe = L.DeviceErrorProbe(self.device)
+        self._sin_ring, self._sin_slot = None, 0
         self._handles = [register_block(b) for b in self.blocks]  # names for torch.ops.wanb200.block
 
     @classmethod
@@ -159,57 +159,104 @@ class FastWanDiT:
         return cls(load_wan_checkpoint(path, num_layers=kwargs.get("num_layers")), grid, guide_scale, device,
                    **kwargs)
 
-    # ------------------------------------------------------------------ embeddings (torch, fp32)
+    # ------------------------------------------------------------------ embeddings and head
+    # On the library's kernels, in the reference's bf16 dtype flow (fast_dit.py:658-687, 480-537):
+    # the text / time / patch embeddings and the head Linear are tcgen05 GEMMs (fp32 outputs for
+    # the residual stream and the modulation rows), the patchify / unpatchify + CFG combine are
+    # gather kernels and the head norm is the LayerNorm kernel with the head's modulation.
+    def _embedding_weights(self, sd):
+        """bf16 copies of the embedding and head parameters in the [out, in] layouts the GEMMs read."""
+        C = self.spec.dim
+
+        def g(k, shape=None):
+            t = sd[k].to(device=self.device, dtype=BF16)
+            return (t.reshape(shape) if shape is not None else t).contiguous()
+
+        return {"patch_w": g("patch_embedding.weight", (C, -1)), "patch_b": g("patch_embedding.bias"),
+                "text0_w": g("text_embedding.0.weight"), "text0_b": g("text_embedding.0.bias"),
+                "text2_w": g("text_embedding.2.weight"), "text2_b": g("text_embedding.2.bias"),
+                "time0_w": g("time_embedding.0.weight"), "time0_b": g("time_embedding.0.bias"),
+                "time2_w": g("time_embedding.2.weight"), "time2_b": g("time_embedding.2.bias"),
+                "proj_w": g("time_projection.1.weight"), "proj_b": g("time_projection.1.bias"),
+                "head_mod": g("head.modulation", (2, C)), "head_w": g("head.head.weight"),
+                "head_b": g("head.head.bias")}
+
     def set_context(self, ctx_cond, ctx_null):
-        """Text embedding + every block's cross K/V, once per prompt (fast_dit.py:658-664)."""
-        m = self.emb
+        """Text embedding + every block's cross K/V, once per prompt (fast_dit.py:658-664):
+        Linear -> GELU(tanh) -> Linear in bf16, as `_FastText` runs it."""
+        ew = self.ew
         cond = ctx_cond.reshape(1, -1, ctx_cond.shape[-1])
         null = ctx_null.reshape(1, -1, ctx_null.shape[-1])
         if self.cfg_group is None:
             ctx = torch.cat([cond, null])
         else:
             ctx = cond if self.cfg_group == 0 else null
-        ctx = ctx.to(self.device, torch.float32)
-        h = F.gelu(F.linear(ctx, m["text_embedding.0.weight"], m["text_embedding.0.bias"]), approximate="tanh")
-        context = F.linear(h, m["text_embedding.2.weight"], m["text_embedding.2.bias"]).to(BF16)
-        self.context = [kv(context) for kv in self.cross_kv]
+        B, Lc, Dt = ctx.shape
+        ctx = ctx.to(self.device, BF16).reshape(B * Lc, Dt).contiguous()
+        h = ops.linear(ctx, ew["text0_w"], ew["text0_b"], epilogue=L.EPI_BIAS_GELU, kind="gemm_text")
+        context = ops.linear(h, ew["text2_w"], ew["text2_b"], epilogue=L.EPI_BIAS, kind="gemm_text")
+        self.context = [kv(context.view(B, Lc, -1)) for kv in self.cross_kv]
 
-    def time_embed(self, t):
-        """Per-frame embedding, frame 0 (the image frame) at t=0 (fast_dit.py:677-687).
-        Returns e [1, F, C] fp32 and e0 [F, 6, C] fp32."""
-        m = self.emb
+    def _sinusoid(self, t):
+        """The per-frame sinusoid of timestep t (float64 on the host, frame 0 at t = 0, as
+        `_time_embed` computes it, fast_dit.py:677-684) in bf16 on the device, through a two-slot
+        page-locked ring so that the copy is asynchronous."""
         tf = torch.full((self.num_frames,), float(t), dtype=torch.float64)
         tf[0] = 0.0
-        s = sinusoidal_embedding_1d(self.spec.freq_dim, tf).float().to(self.device).unsqueeze(0)
-        e = F.linear(F.silu(F.linear(s, m["time_embedding.0.weight"], m["time_embedding.0.bias"])),
-                     m["time_embedding.2.weight"], m["time_embedding.2.bias"])
-        e0 = F.linear(F.silu(e), m["time_projection.1.weight"], m["time_projection.1.bias"])
-        return e, e0.reshape(self.num_frames, 6, self.spec.dim).contiguous()
+        s = sinusoidal_embedding_1d(self.spec.freq_dim, tf).to(BF16)
+        if self._sin_ring is None:
+            self._sin_ring = [[torch.empty_like(s).pin_memory(), torch.empty_like(s, device=self.device), None]
+                              for _ in range(2)]
+        self._sin_slot ^= 1
+        host, dev, ev = self._sin_ring[self._sin_slot]
+        if ev is not None:
+            ev.synchronize()  # the copy from this slot two steps ago has been read
+        host.copy_(s)
+        dev.copy_(host, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.device))
+        self._sin_ring[self._sin_slot][2] = ev
+        return dev
+
+    def time_embed(self, t):
+        """Per-frame embedding, frame 0 (the image frame) at t=0 (fast_dit.py:677-687):
+        time_embedding = Linear, SiLU, Linear; time_projection = SiLU, Linear.  Returns
+        e [F, C] fp32 (the head's modulation rows) and e0 [F, 6, C] fp32 (the blocks')."""
+        ew, F_, C = self.ew, self.num_frames, self.spec.dim
+        s = self._sinusoid(t)
+        a1 = ops.linear(s, ew["time0_w"], ew["time0_b"], epilogue=L.EPI_BIAS_SILU, kind="gemm_time")
+        e = torch.empty(F_, C, device=self.device, dtype=torch.float32)
+        ops.linear(a1, ew["time2_w"], ew["time2_b"], epilogue=L.EPI_BIAS, out=e, kind="gemm_time")
+        se = ops.linear(a1, ew["time2_w"], ew["time2_b"], epilogue=L.EPI_BIAS_SILU, kind="gemm_time")
+        e0 = torch.empty(F_, 6 * C, device=self.device, dtype=torch.float32)
+        ops.linear(se, ew["proj_w"], ew["proj_b"], epilogue=L.EPI_BIAS, out=e0, kind="gemm_time")
+        return e, e0.view(F_, 6, C)
 
     def patch(self, latent):
-        """Conv3d patchify (stride = kernel) as one fp32 matmul -> x [B, L, C] fp32, the residual
-        stream the blocks carry in fp32 through the step."""
-        m = self.emb
-        C_in, Fr, H, W = latent.shape
-        p, q, r = self.spec.patch_size
-        lat = latent.to(self.device, torch.float32)
-        x = lat.view(C_in, Fr // p, p, H // q, q, W // r, r).permute(1, 3, 5, 0, 2, 4, 6)
-        x = x.reshape(-1, C_in * p * q * r)
-        wt = m["patch_embedding.weight"].reshape(self.spec.dim, -1)
-        x = torch.addmm(m["patch_embedding.bias"], x, wt.t())
-        return x.unsqueeze(0).expand(self.batch, -1, -1).contiguous()
+        """Conv3d patchify (stride = kernel) + the patch-embedding GEMM -> x [B, L, C] fp32, the
+        residual stream the blocks carry in fp32 through the step (the latent is rounded to bf16
+        on the way in, as `_FastPatch` feeds it, fast_dit.py:690)."""
+        ew = self.ew
+        lat = latent.to(self.device)
+        if lat.dtype not in (torch.float32, BF16):
+            lat = lat.float()
+        pt = ops.patchify(lat.contiguous(), self.spec.patch_size, self.batch)
+        B, Lx, K = pt.shape
+        x = torch.empty(B * Lx, self.spec.dim, device=self.device, dtype=torch.float32)
+        ops.linear(pt.view(B * Lx, K), ew["patch_w"], ew["patch_b"], epilogue=L.EPI_BIAS, out=x, kind="gemm_patch")
+        return x.view(B, Lx, self.spec.dim)
 
     def head_tokens(self, x, e, row0=0):
         """LN + 2-way modulation + Linear of `_FastHead` (fast_dit.py:480-505) per token:
-        x [B, n, C] holds tokens row0 .. row0 + n - 1 -> [B, n, 4*48] fp32."""
-        m = self.emb
+        x [B, n, C] holds tokens row0 .. row0 + n - 1 of each sequence -> [B, n, 4*48] fp32."""
+        ew = self.ew
         B, n, C = x.shape
         tpf = self.seq_len // self.num_frames
-        frame = (torch.arange(row0, row0 + n, device=x.device) // tpf).clamp_(max=self.num_frames - 1)
-        mod = (m["head.modulation"].unsqueeze(0) + e.unsqueeze(2))[0, frame]  # [n, 2, C]
-        xn = F.layer_norm(x.float(), (C,), eps=self.spec.eps)
-        xn = xn * (1 + mod[:, 1]) + mod[:, 0]
-        return F.linear(xn, m["head.head.weight"], m["head.head.bias"])
+        h = ops.layernorm_modulate(x.reshape(B * n, C).contiguous(), ew["head_mod"], e.reshape(-1, C).contiguous(),
+                                   0, 1, (self.seq_len, tpf, row0, n), eps=self.spec.eps, one_row=True)
+        y = torch.empty(B * n, ew["head_w"].shape[0], device=x.device, dtype=torch.float32)
+        ops.linear(h, ew["head_w"], ew["head_b"], epilogue=L.EPI_BIAS, out=y, kind="gemm_head")
+        return y.view(B, n, -1)
 
     def head(self, x, e):
         """LN + 2-way modulation + Linear, unpatchify, CFG combine (fast_dit.py:480-505)."""
@@ -217,17 +264,15 @@ class FastWanDiT:
 
     def combine(self, y):
         """Unpatchify [B, L, 4*48] and combine the CFG branches -> [48, F, H, W] bf16, the dtype
-        `_FastHead` / `_FastHeadCfgPar` return (fast_dit.py:503-505, 522-524).  The combine runs
-        in fp32 and rounds once (the reference rounds the branches to bf16 first)."""
-        f, h, w = self.grid
-        p, q, r = self.spec.patch_size
-        c = self.spec.out_dim
-        B = y.shape[0]
-        y = y.view(B, f, h, w, p, q, r, c).permute(0, 7, 1, 4, 2, 5, 3, 6).reshape(B, c, f * p, h * q, w * r)
+        `_FastHead` / `_FastHeadCfgPar` return (fast_dit.py:503-505, 522-524); the combine runs
+        in fp32 and rounds once."""
+        y = y.contiguous()
         if self.cfg_group is None:
-            return (y[1] + self.guide_scale * (y[0] - y[1])).to(BF16)
+            return ops.unpatchify_cfg(y, self.grid, self.spec.patch_size, self.spec.out_dim, L.CFG_COMBINE,
+                                      self.guide_scale)
         # CFG-parallel: uncond + g (cond - uncond) = g * cond + (1 - g) * uncond, summed over the pair
-        out = (y[0] * self.cfg_w).contiguous()
+        out = ops.unpatchify_cfg(y, self.grid, self.spec.patch_size, self.spec.out_dim, L.CFG_SCALE, self.cfg_w,
+                                 out_dtype=torch.float32)
         if self.pair_group is not None:
             dist.all_reduce(out, group=self.pair_group)
         return out.to(BF16)

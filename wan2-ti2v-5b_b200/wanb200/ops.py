@@ -253,9 +253,11 @@ def _ln_input(x):
           "layernorm: x must be contiguous bf16 or fp32 [M, C]")
 
 
-def layernorm_modulate(x, modulation, e0, shift_idx, scale_idx, frames, out=None, eps=1e-6, zero=None, push=None):
+def layernorm_modulate(x, modulation, e0, shift_idx, scale_idx, frames, out=None, eps=1e-6, zero=None, push=None,
+                       one_row=False):
     """LN(x) * (1 + scale[f]) + shift[f] -> bf16; x [M, C] bf16 or fp32 (the fp32 residual
-    stream), modulation [6, C] bf16, e0 [F, 6, C] fp32."""
+    stream), modulation [6, C] bf16, e0 [F, 6, C] fp32.  one_row: the head's modulation
+    (modulation [2, C], e0 [F, C]: shift and scale both add the frame's time-embedding row)."""
     _cuda(x, modulation, e0, out, zero)
     _ln_input(x)
     _need(e0.dtype == torch.float32 and e0.is_contiguous() and modulation.dtype == BF16, "layernorm: bad mod tensors")
@@ -264,9 +266,10 @@ def layernorm_modulate(x, modulation, e0, shift_idx, scale_idx, frames, out=None
         out = torch.empty(M, C, dtype=BF16, device=x.device)
     p = L.LnParams()
     p.x_f32 = int(x.dtype == torch.float32)
+    p.e0_one_row = int(one_row)
     _set_push(p, push)
     p.x, p.out, p.rows, p.dim, p.eps, p.mode = _p(x), _p(out), M, C, eps, L.LN_MODULATE
-    p.modulation, p.e0, p.e0_frame_stride = _p(modulation), _p(e0), 6 * C
+    p.modulation, p.e0, p.e0_frame_stride = _p(modulation), _p(e0), (C if one_row else 6 * C)
     p.shift_idx, p.scale_idx = shift_idx, scale_idx
     _set_frames(p, frames)
     if zero is not None:
@@ -343,6 +346,46 @@ def bias_gate_residual(residual, y, bias, gate=None, frames=None, out=None, nsum
     L.check(_launch(residual, "bias_gate_residual", (residual.element_size() + 2.0 * nsum + out.element_size()) * M * C,
                     lambda: lib.wanb200_bias_gate_residual(ctypes.byref(p), _stream(residual))),
             "wanb200_bias_gate_residual")
+    return out
+
+
+# ---------------------------------------------------------------------------- embeddings / head
+def patchify(latent, patch, batch, out=None):
+    """The Conv3d patchify of latent [C, F, H, W] (fp32 or bf16) -> [batch, L, C*pf*ph*pw] bf16,
+    the same rows in every batch copy (wanb200_patchify)."""
+    _cuda(latent, out)
+    _need(latent.dim() == 4 and latent.is_contiguous() and latent.dtype in (torch.float32, BF16),
+          "patchify: latent must be contiguous fp32 / bf16 [C, F, H, W]")
+    Cc, Fr, H, W = latent.shape
+    pf, ph, pw = patch
+    L_ = (Fr // pf) * (H // ph) * (W // pw)
+    if out is None:
+        out = torch.empty(batch, L_, Cc * pf * ph * pw, dtype=BF16, device=latent.device)
+    p = L.PatchifyParams()
+    p.latent, p.latent_f32 = latent.data_ptr(), int(latent.dtype == torch.float32)
+    p.channels, p.frames, p.height, p.width = Cc, Fr, H, W
+    p.pf, p.ph, p.pw, p.batch, p.out = pf, ph, pw, batch, out.data_ptr()
+    lib = L.load()
+    L.check(_launch(latent, "patchify", float(latent.numel() * latent.element_size() + out.numel() * 2),
+                    lambda: lib.wanb200_patchify(ctypes.byref(p), _stream(latent))), "wanb200_patchify")
+    return out
+
+
+def unpatchify_cfg(y, grid, patch, channels, mode, guide, out_dtype=BF16):
+    """Head output y [B, L, pf*ph*pw*C] fp32 -> [C, F*pf, H*ph, W*pw] with the CFG combine
+    (mode L.CFG_COMBINE: B = 2, uncond + guide (cond - uncond); L.CFG_SCALE: guide * y[0])."""
+    _cuda(y)
+    _need(y.dtype == torch.float32 and y.is_contiguous(), "unpatchify: y must be contiguous fp32")
+    f, h, w = grid
+    pf, ph, pw = patch
+    out = torch.empty(channels, f * pf, h * ph, w * pw, dtype=out_dtype, device=y.device)
+    p = L.UnpatchifyParams()
+    p.y, p.batch, p.frames, p.height, p.width = y.data_ptr(), y.shape[0], f, h, w
+    p.pf, p.ph, p.pw, p.channels, p.mode, p.guide = pf, ph, pw, channels, mode, guide
+    p.out, p.out_f32 = out.data_ptr(), int(out_dtype == torch.float32)
+    lib = L.load()
+    L.check(_launch(y, "unpatchify", float(y.numel() * 4 + out.numel() * out.element_size()),
+                    lambda: lib.wanb200_unpatchify_cfg(ctypes.byref(p), _stream(y))), "wanb200_unpatchify_cfg")
     return out
 
 
