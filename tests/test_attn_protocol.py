@@ -180,3 +180,125 @@ def test_double_buffered_variant_needs_a_p_barrier_per_buffer():
     # with one P barrier per query tile the same variant deadlocks: the model is sharp enough
     fails = sum(not run(nkv, 5, False, seed * 97 + nkv) for nkv in range(4, 10) for seed in range(60))
     assert fails > 0
+
+
+def run_persistent(units_nkv, ring, seed):
+    """The shipped bf16 kernel's persistent form (attn_persistent_kernel): one CTA walks several
+    units (query-tile pairs) of nkv key tiles each.  Q has one buffer (reloaded once the unit's last
+    QK is done: q_empty); the ring, s_full and p_full run on across units; the first P V of a unit
+    waits for the softmax warps to have read the previous unit's O (o_free)."""
+    rnd = random.Random(seed)
+    kv_full = [Bar(1) for _ in range(ring)]
+    kv_empty = [Bar(1) for _ in range(ring)]
+    s_full, p_full = [Bar(1) for _ in range(2)], [Bar(1) for _ in range(2)]
+    o_done, o_free = [Bar(1) for _ in range(2)], [Bar(1) for _ in range(2)]
+    q_full, q_empty = Bar(1), Bar(1)
+    pipe = []
+
+    def producer():
+        g = 0
+        for i, nkv in enumerate(units_nkv):
+            yield ("wait", q_empty, (i & 1) ^ 1)
+            yield ("work", rnd.randint(1, 4))
+            q_full.arrive()
+            for _ in range(2 * nkv):
+                slot, ph = g % ring, (g // ring) & 1
+                yield ("wait", kv_empty[slot], ph ^ 1)
+                yield ("work", rnd.randint(1, 5))
+                kv_full[slot].arrive()
+                g += 1
+
+    def issuer():
+        g = jg = 0
+        for i, nkv in enumerate(units_nkv):
+            def kv_wait(r):
+                return ("wait", kv_full[r % ring], (r // ring) & 1)
+
+            def qk(t, j):
+                pipe.append(["mma", rnd.randint(2, 4)])
+                pipe.append(["commit", s_full[t]])
+                if t == 1:
+                    pipe.append(["commit", kv_empty[(g + 2 * j) % ring]])
+                    if j == nkv - 1:
+                        pipe.append(["commit", q_empty])
+
+            def pv(t, j):
+                pipe.append(["mma", rnd.randint(2, 4)])
+                if t == 1:
+                    pipe.append(["commit", kv_empty[(g + 2 * j + 1) % ring]])
+                if j == nkv - 1:
+                    pipe.append(["commit", o_done[t]])
+
+            yield ("wait", q_full, i & 1)
+            yield kv_wait(g)
+            qk(0, 0), qk(1, 0)
+            for j in range(nkv):
+                yield kv_wait(g + 2 * j + 1)
+                for t in (0, 1):
+                    yield ("wait", p_full[t], (jg + j) & 1)
+                    if j == 0:
+                        yield ("wait", o_free[t], (i & 1) ^ 1)
+                    pv(t, j)
+                    if j + 1 < nkv:
+                        if t == 0:
+                            yield kv_wait(g + 2 * j + 2)
+                        qk(t, j + 1)
+            g += 2 * nkv
+            jg += nkv
+
+    def softmax(t):
+        jg = 0
+        for i, nkv in enumerate(units_nkv):
+            for j in range(nkv):
+                yield ("wait", s_full[t], (jg + j) & 1)
+                yield ("work", rnd.randint(1, 12))
+                p_full[t].arrive()
+            yield ("wait", o_done[t], i & 1)
+            yield ("work", rnd.randint(1, 6))  # the epilogue reads O_t
+            o_free[t].arrive()
+            jg += nkv
+
+    return _drive({"producer": producer(), "issuer": issuer(), "softmax0": softmax(0), "softmax1": softmax(1)},
+                  pipe, rnd)
+
+
+def _drive(agents, pipe, rnd):
+    state = dict.fromkeys(agents)
+    busy = dict.fromkeys(agents, 0)
+    finished = set()
+    for _ in range(200000):
+        if pipe:
+            if pipe[0][0] == "mma":
+                pipe[0][1] -= 1
+                if pipe[0][1] <= 0:
+                    pipe.pop(0)
+            else:
+                pipe.pop(0)[1].arrive()
+                continue
+        for k in rnd.sample(list(agents), len(agents)):
+            if k in finished:
+                continue
+            if busy[k]:
+                busy[k] -= 1
+                continue
+            it = state[k]
+            if it is not None and it[0] == "wait" and not it[1].done(it[2]):
+                continue
+            try:
+                nxt = next(agents[k])
+            except StopIteration:
+                finished.add(k)
+                continue
+            state[k] = nxt
+            if nxt[0] == "work":
+                busy[k], state[k] = nxt[1], None
+        if len(finished) == len(agents) and not pipe:
+            return True
+    return False
+
+
+def test_persistent_protocol_never_deadlocks():
+    for seed in range(300):
+        rnd = random.Random(seed)
+        units = [rnd.randint(1, 6) for _ in range(rnd.randint(1, 6))]  # cross-attention units: 4 tiles
+        assert run_persistent(units, 5, seed), (units, seed)

@@ -71,6 +71,7 @@ struct AttnArgs {
   const float* k_scale;
   const float* v_scale;
   int nqb, nkb;
+  int units, nqp;  // persistent kernel: (query pair, split, head, batch) units; query-tile pairs
   int* err;
 };
 
@@ -422,6 +423,342 @@ __global__ void __launch_bounds__(A_THREADS, 1)
   if (warp == 9) tmem_dealloc(tmem_base, A_TMEM_COLS);
 }
 
+// Persistent bf16 attention.  The grid is at most one CTA per SM; CTA c walks the units
+// u = c, c + grid, ... of (query-tile pair, key split, head, batch), consecutive units sharing a
+// head's K / V in L2.  The roles and the per-tile protocol are those of attn_fwd_kernel<false>; what
+// is new is the hand-over between units, so that a unit's prologue and epilogue overlap the
+// neighbouring units' work instead of costing a CTA launch each (a cross-attention unit has only
+// four key tiles; a 1080-token self-attention unit nine):
+//   * Q has one buffer: the producer loads unit i+1's Q as soon as unit i's last QK has completed
+//     (q_empty), while the softmax warps finish unit i's last tile and epilogue;
+//   * the first QKs of unit i+1 write S while the softmax warps still read unit i's O from TMEM;
+//     unit i+1's first P V (which overwrites O) waits for their o_free arrival;
+//   * the K/V ring, s_full and p_full run on across units (their phases count tiles globally).
+__global__ void __launch_bounds__(A_THREADS, 1)
+    attn_persistent_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                           const __grid_constant__ CUtensorMap tmV, const AttnArgs args) {
+  constexpr int TILE = A_TILE, RING = A_RING16;
+  constexpr int OFF_Q = 0, OFF_R = 2 * TILE, TILES_END = OFF_R + RING * TILE;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  const uint32_t sbase = smem_u32(smem);
+  uint8_t* meta = smem + TILES_END;
+  const uint32_t m0 = smem_u32(meta);
+  const uint32_t q_full = m0;           // 1
+  const uint32_t q_empty = m0 + 8;      // 1
+  const uint32_t kv_full = m0 + 16;     // RING
+  const uint32_t kv_empty = m0 + 56;    // RING
+  const uint32_t s_full = m0 + 96;      // 2
+  const uint32_t p_full = m0 + 112;     // 2
+  const uint32_t o_done = m0 + 128;     // 2
+  const uint32_t o_free = m0 + 144;     // 2
+  const uint32_t done_bar = m0 + 160;   // 1
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(meta + 168);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(meta + 172);
+  int* err = args.err;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nkt = (args.Lk + ABN - 1) / ABN;  // key tiles of the whole key set
+  // unit u -> (query pair, split, head, batch); splits and pairs of one head are consecutive
+  auto unit = [&](int u, int& q0, int& split, int& h, int& b, int& kv0, int& nkv) {
+    split = u % args.kv_splits;
+    int r = u / args.kv_splits;
+    const int qp = r % args.nqp;
+    r /= args.nqp;
+    h = r % args.heads;
+    b = r / args.heads;
+    q0 = qp * 2 * ABM;
+    kv0 = split * args.kv_tiles_per_split;
+    nkv = min(nkt - kv0, args.kv_tiles_per_split);
+  };
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    for (int s = 0; s < RING; ++s) {
+      mbar_init(kv_full + 8 * s, 1);
+      mbar_init(kv_empty + 8 * s, 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(s_full + 8 * t, 1);
+      mbar_init(p_full + 8 * t, 4);
+      mbar_init(o_done + 8 * t, 1);
+      mbar_init(o_free + 8 * t, 4);
+    }
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 8 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 9) {
+    tmem_alloc(smem_u32(tmem_slot), A_TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t issued = 0, last_ph = 0, q_ph = 0;
+      int g = 0, i = 0;
+      bool ok = true, q_pending = false;
+      for (int u = blockIdx.x; ok && u < args.units; u += gridDim.x, ++i) {
+        int q0, split, h, b, kv0, nkv;
+        unit(u, q0, split, h, b, kv0, nkv);
+        if (!mbar_wait(q_empty, (i & 1) ^ 1, abort_flag, err, kErrTimeoutAttnProducer)) {
+          ok = false;
+          break;
+        }
+        mbar_expect_tx(q_full, 2 * TILE);
+        for (int t = 0; t < 2; ++t) {
+          tma_load_4d(sbase + OFF_Q + t * TILE, &tmQ, q_full, 0, h, q0 + t * ABM, b);
+          tma_load_4d(sbase + OFF_Q + t * TILE + A_BLK, &tmQ, q_full, 64, h, q0 + t * ABM, b);
+        }
+        q_pending = true;
+        q_ph = i & 1;  // the phase of q_full this load completes
+        for (int k = 0; k < 2 * nkv; ++k, ++g) {
+          const int slot = g % RING;
+          const uint32_t ph = (g / RING) & 1;
+          if (!mbar_wait(kv_empty + 8 * slot, ph ^ 1, abort_flag, err, kErrTimeoutAttnProducer)) {
+            ok = false;
+            break;
+          }
+          const void* map = (k & 1) ? static_cast<const void*>(&tmV) : static_cast<const void*>(&tmK);
+          const uint32_t dst = sbase + OFF_R + slot * TILE;
+          const int key0 = (kv0 + (k >> 1)) * ABN;
+          mbar_expect_tx(kv_full + 8 * slot, TILE);
+          tma_load_4d(dst, map, kv_full + 8 * slot, 0, h, key0, b);
+          tma_load_4d(dst + A_BLK, map, kv_full + 8 * slot, 64, h, key0, b);
+          issued |= 1u << slot;
+          last_ph = (last_ph & ~(1u << slot)) | (ph << slot);
+        }
+      }
+      if (!ok) {  // let every load in flight land before the CTA's shared memory goes away
+        if (q_pending) mbar_drain(q_full, q_ph, err);
+        for (int s = 0; s < RING; ++s)
+          if ((issued >> s) & 1) mbar_drain(kv_full + 8 * s, (last_ph >> s) & 1, err);
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ UMMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_bf16_f32(ABM, ABN, false, false);
+      constexpr uint32_t idesc_o = idesc_bf16_f32(ABM, AD, false, true);
+      auto kv_wait = [&](int r) -> bool {
+        return mbar_wait(kv_full + 8 * (r % RING), (r / RING) & 1, abort_flag, err, kErrTimeoutAttnMma);
+      };
+      int g = 0, jg = 0, i = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < args.units; u += gridDim.x, ++i) {
+        int q0, split, h, b, kv0, nkv;
+        unit(u, q0, split, h, b, kv0, nkv);
+        auto qk = [&](int t, int j) {
+          const int slot = (g + 2 * j) % RING;
+          tc_fence_after();
+          const uint32_t d = tmem_base + t * ABN;
+          const uint32_t qb = sbase + OFF_Q + t * TILE;
+          const uint32_t kb = sbase + OFF_R + slot * TILE;
+#pragma unroll
+          for (int kk = 0; kk < AD / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * A_BLK + (kk & 3) * 32;
+            umma_bf16(d, sw128_desc(qb + off, 16, 1024), sw128_desc(kb + off, 16, 1024), idesc_s, kk != 0);
+          }
+          umma_commit(s_full + 8 * t);
+          if (t == 1) {
+            umma_commit(kv_empty + 8 * slot);
+            if (j == nkv - 1) umma_commit(q_empty);  // the unit's last QK: Q may be overwritten
+          }
+        };
+        auto pv = [&](int t, int j) -> bool {
+          if (!mbar_wait(p_full + 8 * t, (jg + j) & 1, abort_flag, err, kErrTimeoutAttnMma)) return false;
+          // the unit's first P V overwrites O_t: the softmax warps must have read the last unit's
+          if (j == 0 && !mbar_wait(o_free + 8 * t, (i & 1) ^ 1, abort_flag, err, kErrTimeoutAttnMma)) return false;
+          const int slot = (g + 2 * j + 1) % RING;
+          tc_fence_after();
+          const uint32_t d = tmem_base + 2 * ABN + t * AD;
+          const uint32_t pa = tmem_base + t * ABN;  // P_t over the first 64 columns of S_t
+          const uint32_t vb = sbase + OFF_R + slot * TILE;
+#pragma unroll
+          for (int kk = 0; kk < ABN / 16; ++kk)
+            umma_bf16_tmem_a(d, pa + kk * 8, sw128_desc(vb + kk * 2048, A_BLK, 1024), idesc_o, (j | kk) != 0);
+          if (t == 1) umma_commit(kv_empty + 8 * slot);
+          if (j == nkv - 1) umma_commit(o_done + 8 * t);
+          return true;
+        };
+        ok = mbar_wait(q_full, i & 1, abort_flag, err, kErrTimeoutAttnMma) && kv_wait(g);
+        if (!ok) break;
+        qk(0, 0);
+        qk(1, 0);
+        for (int j = 0; j < nkv; ++j) {
+          if (!kv_wait(g + 2 * j + 1) || !pv(0, j)) {
+            ok = false;
+            break;
+          }
+          if (j + 1 < nkv) {
+            if (!kv_wait(g + 2 * j + 2)) {
+              ok = false;
+              break;
+            }
+            qk(0, j + 1);
+          }
+          if (!pv(1, j)) {
+            ok = false;
+            break;
+          }
+          if (j + 1 < nkv) qk(1, j + 1);
+        }
+        g += 2 * nkv;
+        jg += nkv;
+      }
+      umma_commit(done_bar);
+      mbar_drain(done_bar, 0, err);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax + output (warps 0..7)
+    const int t = warp >> 2;                    // query tile of this warpgroup
+    const int r = threadIdx.x & 127;            // query row within the tile == TMEM lane
+    const uint32_t lane_off = uint32_t((warp & 3) * 32) << 16;
+    const uint32_t t_s = tmem_base + lane_off + t * ABN;
+    const uint32_t t_o = tmem_base + lane_off + 2 * ABN + t * AD;
+    const float sl2 = args.scale_log2;
+    int jg = 0, i = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; ok && u < args.units; u += gridDim.x, ++i) {
+      int q0, split, h, b, kv0, nkv;
+      unit(u, q0, split, h, b, kv0, nkv);
+      float m_used = -INFINITY, l_run = 0.f;
+      for (int j = 0; j < nkv; ++j) {
+        if (!mbar_wait_warp(s_full + 8 * t, (jg + j) & 1, abort_flag, err, kErrTimeoutAttnSoftmax)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t sr[ABN];
+#pragma unroll
+        for (int c = 0; c < ABN / 32; ++c) tmem_ld32_nowait(t_s + c * 32, sr + c * 32);
+        tmem_wait_ld();
+        float* s = reinterpret_cast<float*>(sr);
+        const int kbase = (kv0 + j) * ABN;
+        if (kbase + ABN > args.Lk) {  // CTA-uniform: mask the key tail
+#pragma unroll
+          for (int k = 0; k < ABN; ++k)
+            if (kbase + k >= args.Lk) s[k] = -INFINITY;
+        }
+        float m8[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) m8[c] = fmaxf(s[2 * c], s[2 * c + 1]);
+#pragma unroll
+        for (int q = 1; q < ABN / 16; ++q)
+#pragma unroll
+          for (int c = 0; c < 8; ++c) m8[c] = fmax3(m8[c], s[16 * q + 2 * c], s[16 * q + 2 * c + 1]);
+        const float mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
+        const float m_cand = mx * sl2;
+        const bool need = m_cand > m_used + A_RESCALE_THRESHOLD;
+        const bool any_need = __any_sync(0xffffffffu, need);
+        float alpha = 1.f;
+        if (any_need) {
+          const float m_new = need ? m_cand : m_used;
+          alpha = ex2_approx(m_used - m_new);
+          l_run *= alpha;
+          m_used = m_new;
+        }
+        const float neg = -m_used;
+        const float2 sl2v = make_float2(sl2, sl2), negv = make_float2(neg, neg);
+        float2 acc2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+        for (int c = 0; c < ABN / 32; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int k = 0; k < 32; k += 2) {
+            const float2 x = __ffma2_rn(make_float2(s[c * 32 + k], s[c * 32 + k + 1]), sl2v, negv);
+            const float p0 = ex2_approx(x.x), p1 = ex2_approx(x.y);
+            acc2[(k >> 1) & 1] = __fadd2_rn(acc2[(k >> 1) & 1], make_float2(p0, p1));
+            pk[k >> 1] = pack_bf16x2(p0, p1);
+          }
+          tmem_st16_nowait(t_s + c * 16, pk);
+        }
+        tmem_wait_st();
+        l_run += (acc2[0].x + acc2[0].y) + (acc2[1].x + acc2[1].y);
+        // Rescale O_t (rare): S_t(j) was issued after P V_t(j-1), so that has completed
+        if (any_need && j > 0) {
+#pragma unroll 1
+          for (int c = 0; c < AD / 32; ++c) {
+            float o[32];
+            tmem_ld32(t_o + c * 32, o);
+#pragma unroll
+            for (int k = 0; k < 32; ++k) o[k] *= alpha;
+            tmem_st32(t_o + c * 32, o);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full + 8 * t);
+      }
+      if (!ok) break;
+      if (!mbar_wait_warp(o_done + 8 * t, i & 1, abort_flag, err, kErrTimeoutAttnSoftmax)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int qrow = q0 + t * ABM + r;
+      if (args.part_nslots > 1) {
+        // partial result of this key range: unnormalised O, running max (log2 units), row sum
+        const int64_t prow =
+            (int64_t)(args.part_slot0 + split) * args.part_rows + ((int64_t)b * args.heads + h) * args.Lq + qrow;
+        float4* dst = reinterpret_cast<float4*>(args.o_part + prow * AD);
+#pragma unroll
+        for (int c = 0; c < AD / 32; ++c) {
+          float o[32];
+          tmem_ld32(t_o + c * 32, o);
+          if (qrow < args.Lq) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) dst[c * 8 + q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+          }
+        }
+        if (qrow < args.Lq) *reinterpret_cast<float2*>(args.ml_part + prow * 2) = make_float2(m_used, l_run);
+      } else {
+        const float inv_l = 1.f / l_run;
+        uint4* dst = reinterpret_cast<uint4*>(args.o + (int64_t)b * args.o_batch_stride +
+                                              (int64_t)qrow * args.o_tok_stride + (int64_t)h * AD);
+#pragma unroll
+        for (int c = 0; c < AD / 32; ++c) {
+          float o[32];
+          tmem_ld32(t_o + c * 32, o);
+          if (qrow < args.Lq) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 w;
+              w.x = pack_bf16x2(o[q * 8 + 0] * inv_l, o[q * 8 + 1] * inv_l);
+              w.y = pack_bf16x2(o[q * 8 + 2] * inv_l, o[q * 8 + 3] * inv_l);
+              w.z = pack_bf16x2(o[q * 8 + 4] * inv_l, o[q * 8 + 5] * inv_l);
+              w.w = pack_bf16x2(o[q * 8 + 6] * inv_l, o[q * 8 + 7] * inv_l);
+              dst[c * 4 + q] = w;
+            }
+          }
+        }
+      }
+      // O_t has been read into registers: the next unit's first P V may overwrite it
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(o_free + 8 * t);
+      jg += nkv;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 9) tmem_dealloc(tmem_base, A_TMEM_COLS);
+}
+
 // Merge of the split-KV partials: one warp per (batch, head, query row), lane l owns head
 // dimensions 4l..4l+3.  O = sum_s 2^(m_s - m) O_s / sum_s 2^(m_s - m) l_s with m = max_s m_s.
 __global__ void __launch_bounds__(256) attn_combine_kernel(const AttnArgs a) {
@@ -584,18 +921,24 @@ int attn_launch(const wanb200_attn_params* p, int* err, cudaStream_t st, const A
   if (!attr_set[dev][f8 ? 1 : 0].load(std::memory_order_acquire)) {
     cudaError_t e = f8 ? cudaFuncSetAttribute(attn_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               A_SMEM_BYTES8)
-                       : cudaFuncSetAttribute(attn_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       : cudaFuncSetAttribute(attn_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               A_SMEM_BYTES);
     if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(attn)", e);
     attr_set[dev][f8 ? 1 : 0].store(true, std::memory_order_release);
   }
-  const int64_t gx = ((p->q_len + 2 * ABM - 1) / (2 * ABM)) * p->kv_splits;
-  if (gx > INT32_MAX) return set_error(WANB200_EINVAL, "attn: grid too large");
-  dim3 grid((unsigned)gx, (unsigned)p->heads, (unsigned)p->batch);
-  if (f8)
+  const int64_t nqp = (p->q_len + 2 * ABM - 1) / (2 * ABM);
+  const int64_t gx = nqp * p->kv_splits;
+  const int64_t units = gx * p->heads * p->batch;
+  if (gx > INT32_MAX || units > INT32_MAX) return set_error(WANB200_EINVAL, "attn: grid too large");
+  aa.units = (int)units;
+  aa.nqp = (int)nqp;
+  if (f8) {
+    dim3 grid((unsigned)gx, (unsigned)p->heads, (unsigned)p->batch);
     attn_fwd_kernel<true><<<grid, A_THREADS, A_SMEM_BYTES8, st>>>(tq, tk, tv, aa);
-  else
-    attn_fwd_kernel<false><<<grid, A_THREADS, A_SMEM_BYTES, st>>>(tq, tk, tv, aa);
+  } else {  // bf16: persistent, at most one CTA per SM walking the units
+    const unsigned grid = (unsigned)std::min<int64_t>(units, num_sms());
+    attn_persistent_kernel<<<grid, A_THREADS, A_SMEM_BYTES, st>>>(tq, tk, tv, aa);
+  }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error("attn_fwd_kernel launch", e);
   if (aa.part_nslots > 1 && !p->defer_combine) {

@@ -29,41 +29,47 @@ struct LnArgs {
   int e0_one_row;
 };
 
-// RW warps per row (RW = 2 when dim % 512 == 0, else 1): thread t < 32*RW of the row holds the
+// RW warps per row (4 when dim % 1024 == 0, 2 when dim % 512 == 0, else 1): thread t < 32*RW of the row holds the
 // 16-byte vectors at columns (i*32*RW + t)*8, i < NVEC = dim / (256*RW); the row statistics are
-// reduced over the row's warps through shared memory.  Two warps per row halve the registers a
-// thread holds, so twice as many rows are in flight per SM (the kernel is latency-bound).
+// reduced over the row's warps through shared memory.  The grid is a few blocks per SM and every
+// warp group walks rows with a grid stride, loading its NEXT row into a second register buffer
+// before it reduces and writes the current one, so each SM keeps two rows per warp group in
+// flight to HBM instead of stalling on every row's loads; the warps of a row synchronise with
+// their own named barrier, never with the rest of the block.
 //   MODE 0 (modulate): WanLayerNorm without affine (wan/modules/model.py:89-99), then
 //     `_modulate` (models/fast_dit.py:172-176): y * (1 + scale[f]) + shift[f] with
 //     shift/scale[f, c] = modulation[idx, c] + e0[f, idx, c] (fast_dit.py:276-277).
 //   MODE 1 (affine): norm3 = WanLayerNorm(elementwise_affine=True) (model.py:207-209).
 //   XF32: x is fp32 (the residual stream kept in fp32 across the step); the output stays bf16.
+constexpr int LN_BLOCKS_PER_SM = 2;
+
 template <int MODE, int NVEC, bool PUSH, int RW, bool XF32>
-__global__ void __launch_bounds__(256, RW == 2 ? 3 : 2) layernorm_kernel(const LnArgs a) {
+__global__ void __launch_bounds__(256, LN_BLOCKS_PER_SM) layernorm_kernel(const LnArgs a) {
   __shared__ float red[8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < a.zero_count;
        i += (int64_t)gridDim.x * blockDim.x)
     a.zero_buf[i] = 0.f;
-  const int64_t row = (int64_t)blockIdx.x * (8 / RW) + warp / RW;
+  constexpr int RPB = 8 / RW;  // rows per block per pass
+  constexpr int W = XF32 ? 2 : 1;  // 16-byte words per 8 values: bf16 1, fp32 2
   const int t = (warp % RW) * 32 + lane;
-  const bool live = row < a.rows;  // dead rows still join the block's barriers
-  // the row stays in registers as loaded: 8 values per 16 bytes of bf16, per 32 bytes of fp32
-  constexpr int W = XF32 ? 2 : 1;
-  const uint4* xr = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.x) +
-                                                   (live ? row : 0) * a.dim * (XF32 ? 4 : 2));
-  uint4 xv[NVEC * W];
+  const int64_t stride = (int64_t)gridDim.x * RPB;
+  int64_t row = (int64_t)blockIdx.x * RPB + warp / RW;
+  auto load = [&](int64_t r, uint4 (&v)[NVEC * W]) {
+    const uint4* xr =
+        reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.x) + r * a.dim * (XF32 ? 4 : 2));
 #pragma unroll
-  for (int i = 0; i < NVEC; ++i)
+    for (int i = 0; i < NVEC; ++i)
 #pragma unroll
-    for (int w = 0; w < W; ++w) xv[i * W + w] = live ? __ldg(xr + (i * 32 * RW + t) * W + w) : make_uint4(0, 0, 0, 0);
-  auto values = [&](int i, float* x) {  // the 8 values of vector i as fp32
+      for (int w = 0; w < W; ++w) v[i * W + w] = __ldg(xr + (i * 32 * RW + t) * W + w);
+  };
+  auto values = [](const uint4 (&v)[NVEC * W], int i, float* x) {  // the 8 values of vector i as fp32
     if constexpr (XF32) {
-      const uint4 lo = xv[2 * i], hi = xv[2 * i + 1];
+      const uint4 lo = v[2 * i], hi = v[2 * i + 1];
       x[0] = __uint_as_float(lo.x); x[1] = __uint_as_float(lo.y); x[2] = __uint_as_float(lo.z); x[3] = __uint_as_float(lo.w);
       x[4] = __uint_as_float(hi.x); x[5] = __uint_as_float(hi.y); x[6] = __uint_as_float(hi.z); x[7] = __uint_as_float(hi.w);
     } else {
-      unpack_bf16x8(xv[i], x);
+      unpack_bf16x8(v[i], x);
     }
   };
   auto row_sum = [&](float v) {
@@ -71,94 +77,116 @@ __global__ void __launch_bounds__(256, RW == 2 ? 3 : 2) layernorm_kernel(const L
     for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     if constexpr (RW == 1) return v;
     if (lane == 0) red[warp] = v;
-    __syncthreads();
-    const float tot = red[warp & ~1] + red[warp | 1];
-    __syncthreads();  // red is reused by the next reduction
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + warp / RW), "r"(32 * RW) : "memory");  // this row's warps
+    const int g0 = warp - warp % RW;
+    float tot = red[g0];
+#pragma unroll
+    for (int k = 1; k < RW; ++k) tot += red[g0 + k];
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + warp / RW), "r"(32 * RW) : "memory");  // red is reused next
     return tot;
   };
-  float sum = 0.f;
+  if (row >= a.rows) return;  // uniform over a row's warps: they walk the same rows
+  uint4 xv[NVEC * W], xn[NVEC * W];
+  load(row, xv);
+  for (;; row += stride) {
+    const bool more = row + stride < a.rows;
+    if (more) load(row + stride, xn);  // the next row's loads fly while this one is reduced
+    float sum = 0.f;
 #pragma unroll
-  for (int i = 0; i < NVEC; ++i) {
-    float x[8];
-    values(i, x);
+    for (int i = 0; i < NVEC; ++i) {
+      float x[8];
+      values(xv, i, x);
 #pragma unroll
-    for (int k = 0; k < 8; ++k) sum += x[k];
-  }
-  const float mean = row_sum(sum) / a.dim;
-  float var = 0.f;
-#pragma unroll
-  for (int i = 0; i < NVEC; ++i) {
-    float x[8];
-    values(i, x);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const float d = x[k] - mean;
-      var = fmaf(d, d, var);
+      for (int k = 0; k < 8; ++k) sum += x[k];
     }
-  }
-  const float rstd = rsqrtf(row_sum(var) / a.dim + a.eps);
-  if (!live) return;
+    const float mean = row_sum(sum) / a.dim;
+    float var = 0.f;
+#pragma unroll
+    for (int i = 0; i < NVEC; ++i) {
+      float x[8];
+      values(xv, i, x);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float d = x[k] - mean;
+        var = fmaf(d, d, var);
+      }
+    }
+    const float rstd = rsqrtf(row_sum(var) / a.dim + a.eps);
 
-  const float* shp = nullptr;
-  const float* scp = nullptr;
-  if constexpr (MODE == 0) {
-    const int64_t f = frame_of_row(row, a.rows_per_seq, a.row_offset, a.seq_len, a.tokens_per_frame);
-    shp = a.e0 + f * a.e0_frame_stride + (a.e0_one_row ? 0 : (int64_t)a.shift_idx * a.dim);
-    scp = a.e0 + f * a.e0_frame_stride + (a.e0_one_row ? 0 : (int64_t)a.scale_idx * a.dim);
-  }
-  uint4* outr = a.out ? reinterpret_cast<uint4*>(a.out + row * a.dim) : nullptr;
-#pragma unroll
-  for (int i = 0; i < NVEC; ++i) {
-    const int v = i * 32 * RW + t;
-    const int col = v * 8;
-    float x[8], y[8];
-    values(i, x);
+    const float* shp = nullptr;
+    const float* scp = nullptr;
     if constexpr (MODE == 0) {
-      float ms[8], mc[8];
-      unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.modulation + (int64_t)a.shift_idx * a.dim + col)), ms);
-      unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.modulation + (int64_t)a.scale_idx * a.dim + col)), mc);
-      const float4 s0 = __ldg(reinterpret_cast<const float4*>(shp + col));
-      const float4 s1 = __ldg(reinterpret_cast<const float4*>(shp + col + 4));
-      const float4 c0 = __ldg(reinterpret_cast<const float4*>(scp + col));
-      const float4 c1 = __ldg(reinterpret_cast<const float4*>(scp + col + 4));
-      const float sh[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-      const float sc[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-#pragma unroll
-      for (int k = 0; k < 8; ++k) y[k] = fmaf((x[k] - mean) * rstd, 1.f + (mc[k] + sc[k]), ms[k] + sh[k]);
-    } else {
-      float w[8], bb[8];
-      unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.weight + col)), w);
-      unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.bias + col)), bb);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) y[k] = fmaf((x[k] - mean) * rstd, w[k], bb[k]);
+      const int64_t f = frame_of_row(row, a.rows_per_seq, a.row_offset, a.seq_len, a.tokens_per_frame);
+      shp = a.e0 + f * a.e0_frame_stride + (a.e0_one_row ? 0 : (int64_t)a.shift_idx * a.dim);
+      scp = a.e0 + f * a.e0_frame_stride + (a.e0_one_row ? 0 : (int64_t)a.scale_idx * a.dim);
     }
-    uint4 u;
-    u.x = pack_bf16x2(y[0], y[1]);
-    u.y = pack_bf16x2(y[2], y[3]);
-    u.z = pack_bf16x2(y[4], y[5]);
-    u.w = pack_bf16x2(y[6], y[7]);
-    if (!PUSH || outr) outr[v] = u;
+    uint4* outr = a.out ? reinterpret_cast<uint4*>(a.out + row * a.dim) : nullptr;
 #pragma unroll
-    for (int p = 0; p < (PUSH ? WANB200_MAX_PEERS : 0); ++p)  // all-gather fused into the norm: push the row to every rank
-      if (p < a.npush) reinterpret_cast<uint4*>(a.push_out[p] + (a.push_row0 + row) * a.dim)[v] = u;
+    for (int i = 0; i < NVEC; ++i) {
+      const int v = i * 32 * RW + t;
+      const int col = v * 8;
+      float x[8], y[8];
+      values(xv, i, x);
+      if constexpr (MODE == 0) {
+        float ms[8], mc[8];
+        unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.modulation + (int64_t)a.shift_idx * a.dim + col)), ms);
+        unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.modulation + (int64_t)a.scale_idx * a.dim + col)), mc);
+        const float4 s0 = __ldg(reinterpret_cast<const float4*>(shp + col));
+        const float4 s1 = __ldg(reinterpret_cast<const float4*>(shp + col + 4));
+        const float4 c0 = __ldg(reinterpret_cast<const float4*>(scp + col));
+        const float4 c1 = __ldg(reinterpret_cast<const float4*>(scp + col + 4));
+        const float sh[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+        const float sc[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) y[k] = fmaf((x[k] - mean) * rstd, 1.f + (mc[k] + sc[k]), ms[k] + sh[k]);
+      } else {
+        float w[8], bb[8];
+        unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.weight + col)), w);
+        unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.bias + col)), bb);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) y[k] = fmaf((x[k] - mean) * rstd, w[k], bb[k]);
+      }
+      uint4 u;
+      u.x = pack_bf16x2(y[0], y[1]);
+      u.y = pack_bf16x2(y[2], y[3]);
+      u.z = pack_bf16x2(y[4], y[5]);
+      u.w = pack_bf16x2(y[6], y[7]);
+      if (!PUSH || outr) outr[v] = u;
+#pragma unroll
+      for (int p = 0; p < (PUSH ? WANB200_MAX_PEERS : 0); ++p)  // all-gather fused into the norm: push the row to every rank
+        if (p < a.npush) reinterpret_cast<uint4*>(a.push_out[p] + (a.push_row0 + row) * a.dim)[v] = u;
+    }
+    if (!more) break;
+#pragma unroll
+    for (int i = 0; i < NVEC * W; ++i) xv[i] = xn[i];
   }
 }
 
 template <int MODE, bool PUSH, bool XF32>
 static void launch_ln(int dim, const LnArgs& a, int64_t rows, cudaStream_t st) {
-  if (dim % 512 == 0) {  // two warps per row, 4 rows per block
-    const unsigned blocks = (unsigned)((rows + 3) / 4);
+  const int64_t resident = (int64_t)num_sms() * LN_BLOCKS_PER_SM;
+  if (dim % 1024 == 0) {  // four warps per row, 2 rows per block pass
+    const unsigned blocks = (unsigned)std::min<int64_t>((rows + 1) / 2, resident);
+    switch (dim / 1024) {
+      case 1: layernorm_kernel<MODE, 1, PUSH, 4, XF32><<<blocks, 256, 0, st>>>(a); break;
+      case 2: layernorm_kernel<MODE, 2, PUSH, 4, XF32><<<blocks, 256, 0, st>>>(a); break;
+      case 3: layernorm_kernel<MODE, 3, PUSH, 4, XF32><<<blocks, 256, 0, st>>>(a); break;
+      default: layernorm_kernel<MODE, 4, PUSH, 4, XF32><<<blocks, 256, 0, st>>>(a); break;
+    }
+    return;
+  }
+  if (dim % 512 == 0) {  // two warps per row, 4 rows per block pass
+    const unsigned blocks = (unsigned)std::min<int64_t>((rows + 3) / 4, resident);
     switch (dim / 512) {
 #define WANB200_LN_CASE2(n) \
   case n: layernorm_kernel<MODE, n, PUSH, 2, XF32><<<blocks, 256, 0, st>>>(a); break;
-      WANB200_LN_CASE2(1) WANB200_LN_CASE2(2) WANB200_LN_CASE2(3) WANB200_LN_CASE2(4) WANB200_LN_CASE2(5)
-      WANB200_LN_CASE2(6) WANB200_LN_CASE2(7)
-      default: layernorm_kernel<MODE, 8, PUSH, 2, XF32><<<blocks, 256, 0, st>>>(a); break;
+      WANB200_LN_CASE2(1) WANB200_LN_CASE2(3) WANB200_LN_CASE2(5)
+      default: layernorm_kernel<MODE, 7, PUSH, 2, XF32><<<blocks, 256, 0, st>>>(a); break;
 #undef WANB200_LN_CASE2
     }
     return;
   }
-  const unsigned blocks = (unsigned)((rows + 7) / 8);
+  const unsigned blocks = (unsigned)std::min<int64_t>((rows + 7) / 8, resident);
   switch (dim / 256) {
 #define WANB200_LN_CASE(n) \
   case n: layernorm_kernel<MODE, n, PUSH, 1, XF32><<<blocks, 256, 0, st>>>(a); break;
