@@ -330,7 +330,7 @@ def run_ours(args):
 
     peaks = measured_peaks()
     hbm_kinds = {"layernorm", "qk_norm_rope", "bias_gate_residual", "kv_gather", "peer_barrier",
-                 "tp_allreduce_exposed", "patchify", "unpatchify"}
+                 "tp_allreduce_exposed", "patchify", "unpatchify", "sumsq_reduce"}
     total_ms = sum(x[1] for x in kern.values())
     per_kernel = {k: {"launches": v[0], "ms": v[1], "share": v[1] / total_ms,
                       ("tflops" if k not in hbm_kinds else "gbs"):

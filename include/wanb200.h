@@ -41,8 +41,13 @@ extern "C" {
  *                             SiLU in front of time_projection, wan/modules/model.py:381-386)
  *   WANB200_EPI_BIAS_GATE_RES d = residual + (acc + bias) * gate[frame(row)]  (_gate + residual, 294/311)
  *   WANB200_EPI_BIAS_RES      d = residual + acc + bias                       (cross-attn residual, 305)
- *   WANB200_EPI_BIAS_SUMSQ    d = acc + bias; rowss[s*M + row] += sum over section s of d^2
- *                             (the sum of squares of `_tp_rms_qk` 138-140 / `_tp_rms` 158)
+ *   WANB200_EPI_BIAS_SUMSQ    d = acc + bias; for every 32-column chunk k < P = ss_cols / 32,
+ *                             rowss[row*P + k] = sum over the chunk of d^2 (fp32, before rounding)
+ *                             -- the partial sums of squares of `_tp_rms_qk` 138-140 / `_tp_rms`
+ *                             158.  Each entry is written once by a plain store (no atomics, no
+ *                             pre-zeroing), and wanb200_qk_norm_rope or wanb200_sumsq_reduce
+ *                             add a row's partials in a fixed order, so the norms are
+ *                             bit-reproducible run to run
  *   WANB200_EPI_NONE          d = acc (row-parallel partial sum before the TP all-reduce, 127)
  *   WANB200_EPI_SCATTER       the reduce-scatter half of that all-reduce, fused: row r of acc is
  *                             stored (bf16, over NVLink) into the inbox of its owner o = r / shard_rows,
@@ -78,7 +83,7 @@ typedef struct wanb200_gemm_params {
   const void* gate_mod;                            /* [N] bf16 for GATE_RES */
   const float* gate_e0; int64_t gate_frame_stride; /* e0 row of frame 0, stride between frames */
   int64_t seq_len, tokens_per_frame, row_offset, rows_per_seq; /* frame(row) for GATE_RES */
-  float* rowss; int64_t ss_section; int ss_nsections; /* SUMSQ: [ss_nsections, M] fp32, pre-zeroed */
+  float* rowss; int64_t ss_cols;   /* SUMSQ: [M, ss_cols / 32] fp32 partials; ss_cols % 32 == 0, <= N */
   void* peer_out[WANB200_MAX_PEERS]; int npeers; int src_rank; int64_t shard_rows; /* SCATTER */
   int tile_n;  /* tile width along N: 0 = the library's choice (fills the SMs' last wave), else a
                 * multiple of 32 in 64..256 (for tuning; results do not depend on it) */
@@ -163,8 +168,7 @@ int wanb200_attn_kv_splits(int64_t batch, int64_t heads, int64_t q_len, int64_t 
  *   (`blk.norm1/norm2` = WanLayerNorm, wan/modules/model.py:89-99, then `_modulate`,
  *   fast_dit.py:172-176), shift/scale[f, c] = modulation[idx, c] + e0[f, idx, c].
  * mode WANB200_LN_AFFINE: out = LN(x) * weight + bias   (`blk.norm3`, model.py:207-209)
- * LN has no affine in MODULATE mode, eps as given (1e-6).  Optionally zeroes zero_buf[0..n)
- * (the GEMM sum-of-squares accumulators of the next projection).
+ * LN has no affine in MODULATE mode, eps as given (1e-6).
  * Limits: dim % 256 == 0, dim <= 4096. */
 #define WANB200_LN_MODULATE 0
 #define WANB200_LN_AFFINE 1
@@ -177,7 +181,6 @@ typedef struct wanb200_ln_params {
   int shift_idx, scale_idx;
   int64_t seq_len, tokens_per_frame, row_offset, rows_per_seq; /* frame(row) as for the GEMM */
   const void* weight; const void* bias;   /* [dim] bf16 for AFFINE */
-  float* zero_buf; int64_t zero_count;
   /* all-gather fused into the norm: when npush > 0 every output row is also stored at
    * push_out[p] + (push_row0 + row) * dim for p < npush (peer-mapped buffers; out may be NULL) */
   void* push_out[WANB200_MAX_PEERS]; int npush; int64_t push_row0;
@@ -191,21 +194,41 @@ typedef struct wanb200_ln_params {
 int wanb200_layernorm(const wanb200_ln_params* p, void* stream);
 
 /* ---------------------------------------------------------------- QK RMSNorm + 3-D RoPE
- * In place on column sections of x: y = x * rsqrt(ss[row] * inv_dim + eps) * gamma[c], then
+ * In place on column sections of x: y = x * rsqrt(S(row) * inv_dim + eps) * gamma[c], then
  * (if rope) the interleaved-pair rotation with cos/sin[pos, pair], pos = row % seq_len,
  * pair = (c % 128) / 2.  `_tp_rms_qk` + `_rope` (fast_dit.py:134-147, 163-169) for self-attn
  * q and k (nsections 2); `_tp_rms` (fast_dit.py:156-160) for cross-attn q (nsections 1,
- * rope 0).  ss are the (TP all-reduced) sums of squares over the global 3072 channels.
- * Limits: width % 128 == 0, ld % 8 == 0. */
+ * rope 0).  S(row) is the sum of squares over the global 3072 channels, given as ss_parts
+ * partial sums per row and section: S = sum over k < ss_parts of ss[s][row * ss_row_stride + k]
+ * (the SUMSQ GEMM's chunk partials on one GPU: ss_parts = width / 32, ss[s] pointing at the
+ * section's first chunk), added in a fixed order (a warp butterfly per 32 partials, then the
+ * warps in order); or ss_parts = 1 for finished sums (after wanb200_sumsq_reduce and the TP
+ * all-reduce), ss_row_stride 1 for a packed [rows] array.
+ * Limits: width % 128 == 0, ld % 8 == 0, 1 <= ss_parts <= width / 8, ss_row_stride >= ss_parts. */
 typedef struct wanb200_qknorm_params {
   void* x; int64_t ld, rows;
   int nsections; int64_t col0[2]; int64_t width;
   const float* ss[2]; const void* gamma[2];
+  int ss_parts; int64_t ss_row_stride;  /* 0, 0 are read as 1, 1: one finished sum per row */
   float inv_dim, eps;
   int rope; const float* cos; const float* sin; int64_t seq_len; /* tables [seq_len, 64] fp32 */
 } wanb200_qknorm_params;
 
 int wanb200_qk_norm_rope(const wanb200_qknorm_params* p, void* stream);
+
+/* ---------------------------------------------------------------- partial-sum reduction
+ * out[s * out_stride + row] = sum over k < parts of part[row * row_stride + part0[s] + k], for
+ * s < nsections and row < rows, added in the order k = 0, 1, ... -- the per-rank sums of
+ * squares of `_tp_rms_qk` / `_tp_rms` (fast_dit.py:138-140, 158) from the SUMSQ GEMM's chunk
+ * partials, before the TP all-reduce of those sums (fast_dit.py:141, 159).
+ * Limits: 1 <= nsections <= 2, parts >= 1, part0[s] + parts <= row_stride, out_stride >= rows. */
+typedef struct wanb200_sumsq_reduce_params {
+  const float* part; int64_t rows, row_stride;
+  int nsections; int64_t part0[2]; int parts;
+  float* out; int64_t out_stride;
+} wanb200_sumsq_reduce_params;
+
+int wanb200_sumsq_reduce(const wanb200_sumsq_reduce_params* p, void* stream);
 
 /* ---------------------------------------------------------------- bias + gate + residual
  * out = residual + (y + bias) * gate[frame(row)]   (gate_mod != NULL)
@@ -355,10 +378,10 @@ int wanb200_device_error(int reset);
  * be page-locked for the copy to be asynchronous.  Lets a step driver check every step at no
  * cost to the pipeline (the word is sticky, so a later read also reports an earlier expiry). */
 int wanb200_device_error_async(int* host_out, void* stream);
-/* Library version, e.g. 200 for 0.2.0. */
+/* Library version, e.g. 201 for 0.2.1. */
 int wanb200_version(void);
 /* sizeof of the parameter structs (gemm, attn, ln, qknorm, residual, shard_gather, attn_fp8, block,
- * patchify, unpatchify)
+ * patchify, unpatchify, sumsq_reduce)
  * written to out[0..n); returns the number of structs.  Lets a binding detect a library built
  * from a different header. */
 int wanb200_struct_sizes(int64_t* out, int n);

@@ -26,7 +26,7 @@ def test_library_exports_every_declared_function():
     for n in names:
         assert hasattr(lib, n), n
     assert set(names) == set(L.EXPORTS)
-    assert lib.wanb200_version() == 200
+    assert lib.wanb200_version() == 201
 
 
 STRUCTS = {
@@ -41,6 +41,7 @@ STRUCTS = {
     "wanb200_block_weights": L.BlockWeightsC,
     "wanb200_patchify_params": L.PatchifyParams,
     "wanb200_unpatchify_params": L.UnpatchifyParams,
+    "wanb200_sumsq_reduce_params": L.SumsqReduceParams,
 }
 
 
@@ -141,6 +142,25 @@ def test_layernorm_and_qknorm_reject_bad_args_on_host():
     q.x, q.ld, q.rows, q.width, q.nsections = 64, 384, 4, 100, 1
     rc, msg = _rc_msg(lib.wanb200_qk_norm_rope, q)
     assert rc == -1 and "width" in msg
+    # more partial sums per row than the row has threads to add them
+    q.width, q.ld = 256, 256
+    q.ss[0], q.gamma[0] = 64, 64
+    q.ss_parts, q.ss_row_stride = 64, 64
+    rc, msg = _rc_msg(lib.wanb200_qk_norm_rope, q)
+    assert rc == -1 and "ss_parts" in msg
+    q.ss_parts, q.ss_row_stride = 8, 4  # a row's partials would overlap the next row's
+    rc, msg = _rc_msg(lib.wanb200_qk_norm_rope, q)
+    assert rc == -1 and "ss_row_stride" in msg
+    s = L.SumsqReduceParams()
+    s.part, s.out, s.rows, s.row_stride, s.nsections, s.parts, s.out_stride = 64, 64, 4, 4, 3, 2, 4
+    rc, msg = _rc_msg(lib.wanb200_sumsq_reduce, s)
+    assert rc == -1 and "nsections" in msg
+    s.nsections, s.out_stride = 2, 3
+    rc, msg = _rc_msg(lib.wanb200_sumsq_reduce, s)
+    assert rc == -1 and "out_stride" in msg
+    s.out_stride, s.part0[1] = 4, 3  # 3 + 2 partials > row stride 4
+    rc, msg = _rc_msg(lib.wanb200_sumsq_reduce, s)
+    assert rc == -1 and "row_stride" in msg
     r = L.ResidualParams()
     r.out = r.residual = r.y = r.bias = 64
     r.rows, r.dim = 4, 12

@@ -162,6 +162,10 @@ int wanb200_qk_norm_rope(const wanb200_qknorm_params* p, void* stream) {
   return qk_norm_rope(p, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int wanb200_sumsq_reduce(const wanb200_sumsq_reduce_params* p, void* stream) {
+  return sumsq_reduce(p, reinterpret_cast<cudaStream_t>(stream));
+}
+
 int wanb200_bias_gate_residual(const wanb200_residual_params* p, void* stream) {
   return bias_gate_residual(p, reinterpret_cast<cudaStream_t>(stream));
 }
@@ -217,16 +221,17 @@ int wanb200_device_error_async(int* host_out, void* stream) {
   return WANB200_OK;
 }
 
-int wanb200_version(void) { return 200; }
+int wanb200_version(void) { return 201; }
 
 int wanb200_struct_sizes(int64_t* out, int n) {
-  const int64_t sizes[10] = {(int64_t)sizeof(wanb200_gemm_params), (int64_t)sizeof(wanb200_attn_params),
+  const int64_t sizes[11] = {(int64_t)sizeof(wanb200_gemm_params), (int64_t)sizeof(wanb200_attn_params),
                              (int64_t)sizeof(wanb200_ln_params), (int64_t)sizeof(wanb200_qknorm_params),
                              (int64_t)sizeof(wanb200_residual_params), (int64_t)sizeof(wanb200_shard_gather_params),
                              (int64_t)sizeof(wanb200_attn_fp8_params), (int64_t)sizeof(wanb200_block_params),
-                             (int64_t)sizeof(wanb200_patchify_params), (int64_t)sizeof(wanb200_unpatchify_params)};
-  for (int i = 0; i < n && i < 10; ++i) out[i] = sizes[i];
-  return 10;
+                             (int64_t)sizeof(wanb200_patchify_params), (int64_t)sizeof(wanb200_unpatchify_params),
+                             (int64_t)sizeof(wanb200_sumsq_reduce_params)};
+  for (int i = 0; i < n && i < 11; ++i) out[i] = sizes[i];
+  return 11;
 }
 
 }  // extern "C"

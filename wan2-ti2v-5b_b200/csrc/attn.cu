@@ -6,12 +6,16 @@
 // (kernels/cross_attention.py:17-123).  Exact softmax (running max / running sum), no mask
 // other than the key tail, non-causal.
 //
-// One CTA = one (batch, head) and TWO 128-query tiles (t = 0, 1).  Per 128-key tile j:
+// One work unit = one (batch, head), one key range and TWO 128-query tiles (t = 0, 1).  Per
+// 128-key tile j:
 //   S_t = Q_t K_j^T          UMMA 128x128x128 into TMEM (S_0 cols 0..127, S_1 cols 128..255)
-//   P_t = exp2(S_t*c - m_t)  softmax warpgroup t, bf16 pairs written back into TMEM over the
-//                            first 64 columns of S_t (e4m3 variant: swizzled shared memory)
-//   O_t += P_t V_j           UMMA with A = P_t read from TMEM, into TMEM (O_0 cols 256..383,
+//   P_t = exp2(S_t*c - m_t)  softmax warpgroup t; bf16 kernel: bf16 pairs written back into
+//                            TMEM over the first 64 columns of S_t; e4m3 kernel: e4m3 in
+//                            swizzled shared memory
+//   O_t += P_t V_j           UMMA (bf16: A = P_t read from TMEM) into TMEM (O_0 cols 256..383,
 //                            O_1 cols 384..511)
+// Two kernels: attn_persistent_kernel (bf16, the product path; one CTA per SM walking the units)
+// and attn_fp8_kernel (e4m3 operands, one CTA per unit).
 // The tensor core alternates between the tiles, so the MMAs of one tile run while the other
 // tile's warpgroup exponentiates.  O stays in TMEM for the whole key loop; the running max used
 // for the exponent is only raised when a tile's max exceeds it by more than 8 (a factor 256 in
@@ -78,14 +82,13 @@ struct AttnArgs {
 // FP8: Q, K e4m3 [B, L, H, 128] and V transposed e4m3 [B, H, 128, L] (keys contiguous, so both
 // MMAs take K-major operands), P packed to e4m3; S is dequantised by the q and k block scales
 // inside the exponent's multiplier, O by the v scale at the end.
-template <bool FP8>
 __global__ void __launch_bounds__(A_THREADS, 1)
-    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+    attn_fp8_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const AttnArgs args) {
-  constexpr int TILE = FP8 ? A_BLK : A_TILE;
-  constexpr int RING = FP8 ? A_RING : A_RING16;
-  // bf16: [Q_0 Q_1 | ring]; e4m3: [Q_0 Q_1 | P_0 P_1 | ring] (the bf16 P goes to tensor memory)
-  constexpr int OFF_Q = 0, OFF_P = 2 * TILE, OFF_R = (FP8 ? 4 : 2) * TILE, TILES_END = OFF_R + RING * TILE;
+  constexpr int TILE = A_BLK;
+  constexpr int RING = A_RING;
+  // [Q_0 Q_1 | P_0 P_1 | ring]
+  constexpr int OFF_Q = 0, OFF_P = 2 * TILE, OFF_R = 4 * TILE, TILES_END = OFF_R + RING * TILE;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
@@ -146,7 +149,6 @@ __global__ void __launch_bounds__(A_THREADS, 1)
       mbar_expect_tx(q_full, 2 * TILE);
       for (int t = 0; t < 2; ++t) {
         tma_load_4d(sbase + OFF_Q + t * TILE, &tmQ, q_full, 0, h, q0 + t * ABM, b);
-        if constexpr (!FP8) tma_load_4d(sbase + OFF_Q + t * TILE + A_BLK, &tmQ, q_full, 64, h, q0 + t * ABM, b);
       }
       for (int i = 0; i < 2 * nkv; ++i) {
         const int slot = i % RING;
@@ -159,15 +161,10 @@ __global__ void __launch_bounds__(A_THREADS, 1)
         const uint32_t dst = sbase + OFF_R + slot * TILE;
         const int key0 = (kv0 + (i >> 1)) * ABN;
         mbar_expect_tx(kv_full + 8 * slot, TILE);
-        if constexpr (FP8) {
-          if (i & 1)
-            tma_load_4d(dst, map, kv_full + 8 * slot, key0, 0, h, b);  // V^T: (key, d, head, batch)
-          else
-            tma_load_4d(dst, map, kv_full + 8 * slot, 0, h, key0, b);
-        } else {
+        if (i & 1)
+          tma_load_4d(dst, map, kv_full + 8 * slot, key0, 0, h, b);  // V^T: (key, d, head, batch)
+        else
           tma_load_4d(dst, map, kv_full + 8 * slot, 0, h, key0, b);
-          tma_load_4d(dst + A_BLK, map, kv_full + 8 * slot, 64, h, key0, b);
-        }
         issued |= 1u << slot;
         last_ph = (last_ph & ~(1u << slot)) | (ph << slot);
       }
@@ -180,9 +177,9 @@ __global__ void __launch_bounds__(A_THREADS, 1)
   } else if (warp == 9) {
     // ------------------------------------------------------------ UMMA issuer
     if (lane == 0) {
-      // bf16: Q, K both K(=d)-major; P K-major, V MN(=d)-major.  e4m3: every operand K-major.
-      constexpr uint32_t idesc_s = FP8 ? idesc_e4m3_f32(ABM, ABN, false, false) : idesc_bf16_f32(ABM, ABN, false, false);
-      constexpr uint32_t idesc_o = FP8 ? idesc_e4m3_f32(ABM, AD, false, false) : idesc_bf16_f32(ABM, AD, false, true);
+      // every e4m3 operand is K-major (V is stored transposed)
+      constexpr uint32_t idesc_s = idesc_e4m3_f32(ABM, ABN, false, false);
+      constexpr uint32_t idesc_o = idesc_e4m3_f32(ABM, AD, false, false);
       auto kv_wait = [&](int i) -> bool {
         return mbar_wait(kv_full + 8 * (i % RING), (i / RING) & 1, abort_flag, err, kErrTimeoutAttnMma);
       };
@@ -192,17 +189,9 @@ __global__ void __launch_bounds__(A_THREADS, 1)
         const uint32_t d = tmem_base + t * ABN;
         const uint32_t qb = sbase + OFF_Q + t * TILE;
         const uint32_t kb = sbase + OFF_R + slot * TILE;
-        if constexpr (FP8) {
-#pragma unroll
-          for (int kk = 0; kk < AD / 32; ++kk)  // 32 one-byte elements = 32 B per instruction
-            umma_e4m3(d, sw128_desc(qb + kk * 32, 16, 1024), sw128_desc(kb + kk * 32, 16, 1024), idesc_s, kk != 0);
-        } else {
-#pragma unroll
-          for (int kk = 0; kk < AD / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * A_BLK + (kk & 3) * 32;
-            umma_bf16(d, sw128_desc(qb + off, 16, 1024), sw128_desc(kb + off, 16, 1024), idesc_s, kk != 0);
-          }
-        }
+        #pragma unroll
+        for (int kk = 0; kk < AD / 32; ++kk)  // 32 one-byte elements = 32 B per instruction
+          umma_e4m3(d, sw128_desc(qb + kk * 32, 16, 1024), sw128_desc(kb + kk * 32, 16, 1024), idesc_s, kk != 0);
         umma_commit(s_full + 8 * t);
         if (t == 1) umma_commit(kv_empty + 8 * slot);
       };
@@ -212,21 +201,11 @@ __global__ void __launch_bounds__(A_THREADS, 1)
         tc_fence_after();
         const uint32_t d = tmem_base + 2 * ABN + t * AD;
         const uint32_t vb = sbase + OFF_R + slot * TILE;
-        if constexpr (FP8) {
-          const uint32_t pb = sbase + OFF_P + t * TILE;
+        const uint32_t pb = sbase + OFF_P + t * TILE;
 #pragma unroll
-          for (int kk = 0; kk < ABN / 32; ++kk)  // P (query x key) and V^T (d x key), both key-major
-            umma_e4m3(d, sw128_desc(pb + kk * 32, 16, 1024), sw128_desc(vb + kk * 32, 16, 1024), idesc_o,
-                      (j | kk) != 0);
-        } else {
-          // P_t in tensor memory, in the columns of S_t (64 columns of bf16 pairs); the next
-          // S_t = Q_t K^T is issued after this MMA and UMMAs of one thread execute in order.
-          const uint32_t pa = tmem_base + t * ABN;
-#pragma unroll
-          for (int kk = 0; kk < ABN / 16; ++kk)
-            // V tile: key row k at k*128 B inside each 64-wide d block; d blocks 16 KB apart.
-            umma_bf16_tmem_a(d, pa + kk * 8, sw128_desc(vb + kk * 2048, A_BLK, 1024), idesc_o, (j | kk) != 0);
-        }
+        for (int kk = 0; kk < ABN / 32; ++kk)  // P (query x key) and V^T (d x key), both key-major
+          umma_e4m3(d, sw128_desc(pb + kk * 32, 16, 1024), sw128_desc(vb + kk * 32, 16, 1024), idesc_o,
+                    (j | kk) != 0);
         if (t == 1) umma_commit(kv_empty + 8 * slot);
         if (j == nkv - 1) umma_commit(o_done + 8 * t);
         return true;
@@ -257,13 +236,9 @@ __global__ void __launch_bounds__(A_THREADS, 1)
     const uint32_t t_o = tmem_base + lane_off + 2 * ABN + t * AD;
     uint8_t* pbuf = smem + OFF_P + t * TILE;
     const float sl2_base = args.scale_log2;
-    const float* ksc = nullptr;
-    float qsc = 1.f;
-    if constexpr (FP8) {
-      // the second tile of the last pair may lie past q_len (its rows are never stored)
-      qsc = __ldg(args.q_scale + ((int64_t)b * args.heads + h) * args.nqb + min(q0 / ABM + t, args.nqb - 1));
-      ksc = args.k_scale + ((int64_t)b * args.heads + h) * args.nkb + kv0;
-    }
+    // the second tile of the last pair may lie past q_len (its rows are never stored)
+    const float qsc = __ldg(args.q_scale + ((int64_t)b * args.heads + h) * args.nqb + min(q0 / ABM + t, args.nqb - 1));
+    const float* ksc = args.k_scale + ((int64_t)b * args.heads + h) * args.nkb + kv0;
     float m_used = -INFINITY, l_run = 0.f;
     bool ok = true;
 
@@ -278,8 +253,7 @@ __global__ void __launch_bounds__(A_THREADS, 1)
       for (int c = 0; c < ABN / 32; ++c) tmem_ld32_nowait(t_s + c * 32, sr + c * 32);
       tmem_wait_ld();
       float* s = reinterpret_cast<float*>(sr);
-      float sl2 = sl2_base;  // e4m3: scores carry the q and k block scales
-      if constexpr (FP8) sl2 = sl2_base * qsc * __ldg(ksc + j);
+      const float sl2 = sl2_base * qsc * __ldg(ksc + j);  // scores carry the q and k block scales
       const int kbase = (kv0 + j) * ABN;
       if (kbase + ABN > args.Lk) {  // CTA-uniform: mask the key tail
 #pragma unroll
@@ -308,50 +282,26 @@ __global__ void __launch_bounds__(A_THREADS, 1)
       }
       const float neg = -m_used;
       float r8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // 8 partial row sums (short dependency chains)
-      if constexpr (FP8) {
-        // P in e4m3 (at most 2^8 under the lazy max, inside the 448 range): 32 keys = 32 bytes
-        uint8_t* rowp = pbuf + (r >> 3) * 1024 + (r & 7) * 128;
+      // P in e4m3 (at most 2^8 under the lazy max, inside the 448 range): 32 keys = 32 bytes
+      uint8_t* rowp = pbuf + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
-        for (int c = 0; c < ABN / 32; ++c) {
-          uint32_t pk[8];
+      for (int c = 0; c < ABN / 32; ++c) {
+        uint32_t pk[8];
 #pragma unroll
-          for (int k = 0; k < 32; k += 4) {
-            const float p0 = ex2_approx(fmaf(s[c * 32 + k], sl2, neg));
-            const float p1 = ex2_approx(fmaf(s[c * 32 + k + 1], sl2, neg));
-            const float p2 = ex2_approx(fmaf(s[c * 32 + k + 2], sl2, neg));
-            const float p3 = ex2_approx(fmaf(s[c * 32 + k + 3], sl2, neg));
-            r8[(k >> 2) & 7] += (p0 + p1) + (p2 + p3);
-            pk[k >> 2] = pack_e4m3x2(p0, p1) | (pack_e4m3x2(p2, p3) << 16);
-          }
-#pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            const int ch = c * 2 + q;
-            *reinterpret_cast<uint4*>(rowp + ((ch ^ (r & 7)) << 4)) =
-                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-          }
+        for (int k = 0; k < 32; k += 4) {
+          const float p0 = ex2_approx(fmaf(s[c * 32 + k], sl2, neg));
+          const float p1 = ex2_approx(fmaf(s[c * 32 + k + 1], sl2, neg));
+          const float p2 = ex2_approx(fmaf(s[c * 32 + k + 2], sl2, neg));
+          const float p3 = ex2_approx(fmaf(s[c * 32 + k + 3], sl2, neg));
+          r8[(k >> 2) & 7] += (p0 + p1) + (p2 + p3);
+          pk[k >> 2] = pack_e4m3x2(p0, p1) | (pack_e4m3x2(p2, p3) << 16);
         }
-      } else {
-        // P in bf16 pairs straight into tensor memory over S_t's first 64 columns (S is already
-        // in registers); packed fp32x2 FMA / add halve the instructions of the scale and the sums
-        const float2 sl2v = make_float2(sl2, sl2), negv = make_float2(neg, neg);
-        float2 acc2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};  // 4 partial sums (4 pairs spill)
 #pragma unroll
-        for (int c = 0; c < ABN / 32; ++c) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int k = 0; k < 32; k += 2) {
-            const float2 x = __ffma2_rn(make_float2(s[c * 32 + k], s[c * 32 + k + 1]), sl2v, negv);
-            const float p0 = ex2_approx(x.x), p1 = ex2_approx(x.y);
-            acc2[(k >> 1) & 1] = __fadd2_rn(acc2[(k >> 1) & 1], make_float2(p0, p1));
-            pk[k >> 1] = pack_bf16x2(p0, p1);
-          }
-          tmem_st16_nowait(t_s + c * 16, pk);
+        for (int q = 0; q < 2; ++q) {
+          const int ch = c * 2 + q;
+          *reinterpret_cast<uint4*>(rowp + ((ch ^ (r & 7)) << 4)) =
+              make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
         }
-        tmem_wait_st();
-        r8[0] = acc2[0].x;
-        r8[1] = acc2[0].y;
-        r8[2] = acc2[1].x;
-        r8[3] = acc2[1].y;
       }
       l_run += ((r8[0] + r8[1]) + (r8[2] + r8[3])) + ((r8[4] + r8[5]) + (r8[6] + r8[7]));
       // Rescale O_t (rare).  PV_t(j-1) has completed (see the ordering note above) and PV_t(j)
@@ -367,13 +317,13 @@ __global__ void __launch_bounds__(A_THREADS, 1)
         }
       }
       tc_fence_before();
-      if constexpr (FP8) fence_proxy_async_smem();  // e4m3 P in shared memory, read by the async proxy
+      fence_proxy_async_smem();  // e4m3 P in shared memory, read by the async proxy
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full + 8 * t);
     }
     if (ok) ok = mbar_wait_warp(o_done + 8 * t, 0, abort_flag, err, kErrTimeoutAttnSoftmax);
-    float vsc = 1.f;  // e4m3: O carries the v scale
-    if constexpr (FP8) vsc = __ldg(args.v_scale + (int64_t)b * args.heads + h);
+    const float vsc = __ldg(  // O carries the v scale
+        args.v_scale + (int64_t)b * args.heads + h);
     if (ok && args.part_nslots > 1) {
       // partial result of this key range: unnormalised O, running max (log2 units), row sum
       tc_fence_after();
@@ -425,10 +375,11 @@ __global__ void __launch_bounds__(A_THREADS, 1)
 
 // Persistent bf16 attention.  The grid is at most one CTA per SM; CTA c walks the units
 // u = c, c + grid, ... of (query-tile pair, key split, head, batch), consecutive units sharing a
-// head's K / V in L2.  The roles and the per-tile protocol are those of attn_fwd_kernel<false>; what
-// is new is the hand-over between units, so that a unit's prologue and epilogue overlap the
-// neighbouring units' work instead of costing a CTA launch each (a cross-attention unit has only
-// four key tiles; a 1080-token self-attention unit nine):
+// head's K / V in L2.  Within a unit the roles and the per-tile protocol are the ones described at
+// the top of this file (those of attn_fp8_kernel, with P in TMEM).  Across units comes the
+// hand-over, so that a unit's prologue and epilogue overlap the neighbouring units' work instead
+// of costing a CTA launch each (a cross-attention unit has only four key tiles; a 1080-token
+// self-attention unit nine):
 //   * Q has one buffer: the producer loads unit i+1's Q as soon as unit i's last QK has completed
 //     (q_empty), while the softmax warps finish unit i's last tile and epilogue;
 //   * the first QKs of unit i+1 write S while the softmax warps still read unit i's O from TMEM;
@@ -919,7 +870,7 @@ int attn_launch(const wanb200_attn_params* p, int* err, cudaStream_t st, const A
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= kMaxDevices) return set_error(WANB200_EINVAL, "device index out of range");
   if (!attr_set[dev][f8 ? 1 : 0].load(std::memory_order_acquire)) {
-    cudaError_t e = f8 ? cudaFuncSetAttribute(attn_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = f8 ? cudaFuncSetAttribute(attn_fp8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               A_SMEM_BYTES8)
                        : cudaFuncSetAttribute(attn_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               A_SMEM_BYTES);
@@ -934,13 +885,13 @@ int attn_launch(const wanb200_attn_params* p, int* err, cudaStream_t st, const A
   aa.nqp = (int)nqp;
   if (f8) {
     dim3 grid((unsigned)gx, (unsigned)p->heads, (unsigned)p->batch);
-    attn_fwd_kernel<true><<<grid, A_THREADS, A_SMEM_BYTES8, st>>>(tq, tk, tv, aa);
+    attn_fp8_kernel<<<grid, A_THREADS, A_SMEM_BYTES8, st>>>(tq, tk, tv, aa);
   } else {  // bf16: persistent, at most one CTA per SM walking the units
     const unsigned grid = (unsigned)std::min<int64_t>(units, num_sms());
     attn_persistent_kernel<<<grid, A_THREADS, A_SMEM_BYTES, st>>>(tq, tk, tv, aa);
   }
   cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return set_cuda_error("attn_fwd_kernel launch", e);
+  if (e != cudaSuccess) return set_cuda_error("attention kernel launch", e);
   if (aa.part_nslots > 1 && !p->defer_combine) {
     attn_combine_kernel<<<(unsigned)((aa.part_rows + 7) / 8), 256, 0, st>>>(aa);
     e = cudaGetLastError();

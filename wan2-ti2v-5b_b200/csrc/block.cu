@@ -2,13 +2,13 @@
 // of models/fast_dit.py:260-311 (batched CFG, per-frame modulation, TP by heads).  It queues the
 // block's launches on one stream with the library's own launchers, in the order of the Python
 // block op (wanb200/block.py):
-//    1  h   = LN1(x) * (1 + scale) + shift                   (also zeroes the three Σx² rows)
-//    2  qkv = h W_qkv^T + b, Σq², Σk² per row                [TP: all-reduce Σq², Σk²]
+//    1  h   = LN1(x) * (1 + scale) + shift
+//    2  qkv = h W_qkv^T + b, Σq², Σk² per row and 32 columns [TP: reduce, all-reduce Σq², Σk²]
 //    3  q, k = RoPE(x * rsqrt(Σ/C + eps) * γ)                 in place
 //    4  y   = softmax(q k^T / sqrt(d)) v
 //    5  x1  = x + (y W_o^T + b_o) * gate2                     [TP: partial -> all-reduce -> residual pass]
 //    6  h   = LN3_affine(x1)
-//    7  qc  = h W_cq^T + b, Σqc²                             [TP: all-reduce Σ]
+//    7  qc  = h W_cq^T + b, Σqc²                             [TP: reduce, all-reduce Σ]
 //    8  qc  = qc * rsqrt(Σ/C + eps) * γ
 //    9  y   = attention(qc, ck, cv)
 //   10  x1 += y W_co^T + b_co                                 [TP: AR path]
@@ -26,7 +26,7 @@ namespace wanb200 {
 namespace {
 
 struct BlockLayout {
-  int64_t h, qkv, y, cq, f, ss, x1, part, attn, total;
+  int64_t h, qkv, y, cq, f, ss, ssr, x1, part, attn, total;
   int splits_self, splits_cross;
 };
 
@@ -47,8 +47,10 @@ BlockLayout block_layout(int64_t batch, int64_t seq_len, int64_t dim, int64_t lo
   off += up256(N * Cl * 2);
   l.f = off;
   off += up256(N * ffn_local * 2);
-  l.ss = off;
-  off += up256(3 * N * 4);
+  l.ss = off;  // Σx² chunk partials of q and k, [N, 2 Cl / 32] (the cross-q GEMM: [N, Cl / 32])
+  off += up256(2 * (Cl / 32) * N * 4);
+  l.ssr = off;  // TP: the partials reduced per section, all-reduced in place
+  if (tp_size > 1) off += up256(3 * N * 4);
   l.x1 = off;
   off += up256(N * dim * 4);
   l.part = off;
@@ -111,6 +113,7 @@ int block_forward(const wanb200_block_params* p, cudaStream_t st) {
   void* cq = ws + l.cq;
   void* f = ws + l.f;
   float* ss = reinterpret_cast<float*>(ws + l.ss);
+  float* ssr = reinterpret_cast<float*>(ws + l.ssr);
   float* x1 = reinterpret_cast<float*>(ws + l.x1);
   void* part = ws + l.part;
   void* attn_ws = ws + l.attn;
@@ -122,7 +125,7 @@ int block_forward(const wanb200_block_params* p, cudaStream_t st) {
     return r ? set_error(WANB200_ECUDA, "block: the all_reduce callback failed") : WANB200_OK;
   };
 
-  auto ln_mod = [&](const void* x, int xf32, int shift, int scale, float* zero, int64_t zcount) {
+  auto ln_mod = [&](const void* x, int xf32, int shift, int scale) {
     wanb200_ln_params q = {};
     q.x = x;
     q.x_f32 = xf32;
@@ -138,8 +141,6 @@ int block_forward(const wanb200_block_params* p, cudaStream_t st) {
     q.scale_idx = scale;
     q.seq_len = Lx;
     q.tokens_per_frame = tpf;
-    q.zero_buf = zero;
-    q.zero_count = zcount;
     return layernorm(&q, st);
   };
   auto gemm = [&](const void* a, int64_t K, const void* wt, const void* bias, int64_t Nout, void* d, int epi) {
@@ -231,16 +232,39 @@ int block_forward(const wanb200_block_params* p, cudaStream_t st) {
     return gemm_bf16(&g, st);
   };
 
+  // Σx² of `nsec` sections of Cl columns from the GEMM's chunk partials ([N, nsec * Cl / 32]): on
+  // one GPU the norm kernel adds them itself; under TP they are reduced per section into
+  // ssr + sec0 * N first and those sums all-reduced
+  auto sumsq_tp = [&](int nsec, int64_t sec0) -> int {
+    if (!tp) return WANB200_OK;
+    wanb200_sumsq_reduce_params r = {};
+    r.part = ss;
+    r.rows = N;
+    r.row_stride = nsec * (Cl / 32);
+    r.nsections = nsec;
+    r.part0[0] = 0;
+    r.part0[1] = Cl / 32;
+    r.parts = (int)(Cl / 32);
+    r.out = ssr + sec0 * N;
+    r.out_stride = N;
+    int rc2 = sumsq_reduce(&r, st);
+    return rc2 ? rc2 : all_reduce(ssr + sec0 * N, nsec * N, 0);
+  };
+  auto set_ss = [&](wanb200_qknorm_params& q, int nsec, int64_t sec0) {
+    for (int s = 0; s < nsec; ++s) q.ss[s] = tp ? ssr + (sec0 + s) * N : ss + s * (Cl / 32);
+    q.ss_parts = tp ? 1 : (int)(Cl / 32);
+    q.ss_row_stride = tp ? 1 : nsec * (Cl / 32);
+  };
+
   // -- self-attention
-  if ((rc = ln_mod(p->x, p->x_f32, 0, 1, ss, 3 * N))) return rc;
+  if ((rc = ln_mod(p->x, p->x_f32, 0, 1))) return rc;
   {
     wanb200_gemm_params g = gemm(h, C, w.w_qkv, w.b_qkv, 3 * Cl, qkv, WANB200_EPI_BIAS_SUMSQ);
     g.rowss = ss;
-    g.ss_section = Cl;
-    g.ss_nsections = 2;
+    g.ss_cols = 2 * Cl;
     if ((rc = gemm_bf16(&g, st))) return rc;
   }
-  if ((rc = all_reduce(ss, 2 * N, 0))) return rc;
+  if ((rc = sumsq_tp(2, 0))) return rc;
   {
     wanb200_qknorm_params q = {};
     q.x = qkv;
@@ -250,8 +274,7 @@ int block_forward(const wanb200_block_params* p, cudaStream_t st) {
     q.col0[0] = 0;
     q.col0[1] = Cl;
     q.width = Cl;
-    q.ss[0] = ss;
-    q.ss[1] = ss + N;
+    set_ss(q, 2, 0);
     q.gamma[0] = w.g_q;
     q.gamma[1] = w.g_k;
     q.inv_dim = 1.f / (float)C;
@@ -283,12 +306,11 @@ int block_forward(const wanb200_block_params* p, cudaStream_t st) {
   }
   {
     wanb200_gemm_params g = gemm(h, C, w.w_cq, w.b_cq, Cl, cq, WANB200_EPI_BIAS_SUMSQ);
-    g.rowss = ss + 2 * N;
-    g.ss_section = Cl;
-    g.ss_nsections = 1;
+    g.rowss = ss;
+    g.ss_cols = Cl;
     if ((rc = gemm_bf16(&g, st))) return rc;
   }
-  if ((rc = all_reduce(ss + 2 * N, N, 0))) return rc;
+  if ((rc = sumsq_tp(1, 2))) return rc;
   {
     wanb200_qknorm_params q = {};
     q.x = cq;
@@ -296,7 +318,7 @@ int block_forward(const wanb200_block_params* p, cudaStream_t st) {
     q.rows = N;
     q.nsections = 1;
     q.width = Cl;
-    q.ss[0] = ss + 2 * N;
+    set_ss(q, 1, 2);
     q.gamma[0] = w.g_cq;
     q.inv_dim = 1.f / (float)C;
     q.eps = p->eps;
@@ -307,7 +329,7 @@ int block_forward(const wanb200_block_params* p, cudaStream_t st) {
   if ((rc = projection(y, Cl, w.w_co, w.b_co, x1, 1, -1, x1, 1))) return rc;
 
   // -- FFN
-  if ((rc = ln_mod(x1, 1, 3, 4, nullptr, 0))) return rc;
+  if ((rc = ln_mod(x1, 1, 3, 4))) return rc;
   {
     wanb200_gemm_params g = gemm(h, C, w.w1, w.b1, Fl, f, WANB200_EPI_BIAS_GELU);
     if ((rc = gemm_bf16(&g, st))) return rc;

@@ -21,8 +21,6 @@ struct LnArgs {
   int64_t seq_len, tokens_per_frame, row_offset, rows_per_seq;
   const __nv_bfloat16* weight;
   const __nv_bfloat16* bias;
-  float* zero_buf;
-  int64_t zero_count;
   __nv_bfloat16* push_out[WANB200_MAX_PEERS];
   int npush;
   int64_t push_row0;
@@ -47,9 +45,6 @@ template <int MODE, int NVEC, bool PUSH, int RW, bool XF32>
 __global__ void __launch_bounds__(256, LN_BLOCKS_PER_SM) layernorm_kernel(const LnArgs a) {
   __shared__ float red[8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < a.zero_count;
-       i += (int64_t)gridDim.x * blockDim.x)
-    a.zero_buf[i] = 0.f;
   constexpr int RPB = 8 / RW;  // rows per block per pass
   constexpr int W = XF32 ? 2 : 1;  // 16-byte words per 8 values: bf16 1, fp32 2
   const int t = (warp % RW) * 32 + lane;
@@ -228,8 +223,6 @@ int layernorm(const wanb200_ln_params* p, cudaStream_t st) {
   } else {
     return set_error(WANB200_EINVAL, "layernorm: bad mode");
   }
-  if (p->zero_count < 0 || (p->zero_count > 0 && !p->zero_buf))
-    return set_error(WANB200_EINVAL, "layernorm: zero_count > 0 needs zero_buf");
   LnArgs a;
   a.x = p->x;
   a.out = reinterpret_cast<__nv_bfloat16*>(p->out);
@@ -247,8 +240,6 @@ int layernorm(const wanb200_ln_params* p, cudaStream_t st) {
   a.rows_per_seq = p->rows_per_seq;
   a.weight = reinterpret_cast<const __nv_bfloat16*>(p->weight);
   a.bias = reinterpret_cast<const __nv_bfloat16*>(p->bias);
-  a.zero_buf = p->zero_buf;
-  a.zero_count = p->zero_count;
   for (int i = 0; i < WANB200_MAX_PEERS; ++i)
     a.push_out[i] = reinterpret_cast<__nv_bfloat16*>(i < p->npush ? p->push_out[i] : nullptr);
   a.npush = p->npush;
@@ -272,6 +263,8 @@ struct QkArgs {
   int64_t col0[2];
   int width;
   const float* ss[2];
+  int ss_parts;
+  int64_t ss_row_stride;
   const __nv_bfloat16* gamma[2];
   float inv_dim, eps;
   int rope;
@@ -280,44 +273,84 @@ struct QkArgs {
   int seq_len;
 };
 
-// Thread (x, y) = 8 consecutive channels (4 rotation pairs) x of row blockIdx.x * blockDim.y + y,
-// section blockIdx.y: 2-D blocks so that a thread finds its row without integer division (the
-// kernel streams 16 bytes per thread; a 64-bit divide per thread would cost more than the load).
+// Thread (x, y) = 8 consecutive channels (4 rotation pairs) x of row blockIdx.x * blockDim.y + y
+// in each of the NSEC sections (q and k of self-attention, cross q alone): 2-D blocks so that a
+// thread finds its row without integer division, and both sections' 16-byte loads of a row in
+// flight together, sharing the row's rotation angles.
 // `_tp_rms_qk` (models/fast_dit.py:134-147): x * rsqrt(ss/3072 + eps) * gamma, then `_rope`
 // (fast_dit.py:163-169): (x0, x1) -> (x0 c - x1 s, x0 s + x1 c) with the pair's angle.
+// The row's sum of squares arrives as ss_parts partial sums per section (the SUMSQ GEMM's
+// 32-column chunks, contiguous per row): thread x < ss_parts of the row loads partial x of each
+// section, each warp adds its 32 by a butterfly and the row's warps are added in order through
+// shared memory -- the same order on every run.
+template <int NSEC>
 __global__ void __launch_bounds__(1024) qknorm_rope_kernel(const QkArgs a) {
-  const int sec = blockIdx.y;
+  __shared__ float red[8][NSEC][8];  // [row of the block][section][warp of the row]
   const int vpr = a.width >> 3;
   const int row = blockIdx.x * blockDim.y + threadIdx.y;
-  if (threadIdx.x >= vpr || row >= a.rows) return;
+  const bool live_row = row < a.rows, active = live_row && (int)threadIdx.x < vpr;
   const int cv = threadIdx.x * 8;
-  const int64_t col0 = sec ? a.col0[1] : a.col0[0];
-  const float* ss = sec ? a.ss[1] : a.ss[0];
-  const __nv_bfloat16* gamma = sec ? a.gamma[1] : a.gamma[0];
-  uint4* p = reinterpret_cast<uint4*>(a.x + (int64_t)row * a.ld + col0 + cv);
-  float v[8], g[8];
-  unpack_bf16x8(*p, v);
-  unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(gamma + cv)), g);
-  const float rs = rsqrtf(__ldg(ss + row) * a.inv_dim + a.eps);
+  uint4* p[NSEC];
+  uint4 raw[NSEC];
 #pragma unroll
-  for (int k = 0; k < 8; ++k) v[k] *= rs * g[k];
+  for (int s = 0; s < NSEC; ++s) {
+    p[s] = reinterpret_cast<uint4*>(a.x + (int64_t)row * a.ld + a.col0[s] + cv);
+    raw[s] = active ? *p[s] : make_uint4(0u, 0u, 0u, 0u);
+  }
+  float sum[NSEC];
+  if (a.ss_parts == 1) {  // grid-uniform
+#pragma unroll
+    for (int s = 0; s < NSEC; ++s) sum[s] = live_row ? __ldg(a.ss[s] + (int64_t)row * a.ss_row_stride) : 0.f;
+  } else {
+    const bool ld = live_row && (int)threadIdx.x < a.ss_parts;
+    float part[NSEC];
+#pragma unroll
+    for (int s = 0; s < NSEC; ++s) part[s] = ld ? __ldg(a.ss[s] + (int64_t)row * a.ss_row_stride + threadIdx.x) : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int s = 0; s < NSEC; ++s) part[s] += __shfl_xor_sync(0xffffffffu, part[s], o);
+    const int nw = (a.ss_parts + 31) >> 5;
+    if ((threadIdx.x & 31) == 0 && (int)(threadIdx.x >> 5) < nw)
+#pragma unroll
+      for (int s = 0; s < NSEC; ++s) red[threadIdx.y][s][threadIdx.x >> 5] = part[s];
+    __syncthreads();
+#pragma unroll
+    for (int s = 0; s < NSEC; ++s) {
+      sum[s] = red[threadIdx.y][s][0];
+      for (int w = 1; w < nw; ++w) sum[s] += red[threadIdx.y][s][w];
+    }
+  }
+  if (!active) return;
+  float4 c4 = make_float4(1.f, 1.f, 1.f, 1.f), s4 = make_float4(0.f, 0.f, 0.f, 0.f);
   if (a.rope) {
     const int pos = row % a.seq_len;
     const int pair0 = (cv & 127) >> 1;
-    const float4 c4 = __ldg(reinterpret_cast<const float4*>(a.cos + (int64_t)pos * 64 + pair0));
-    const float4 s4 = __ldg(reinterpret_cast<const float4*>(a.sin + (int64_t)pos * 64 + pair0));
-    float x0, x1;
-    x0 = v[0]; x1 = v[1]; v[0] = x0 * c4.x - x1 * s4.x; v[1] = x0 * s4.x + x1 * c4.x;
-    x0 = v[2]; x1 = v[3]; v[2] = x0 * c4.y - x1 * s4.y; v[3] = x0 * s4.y + x1 * c4.y;
-    x0 = v[4]; x1 = v[5]; v[4] = x0 * c4.z - x1 * s4.z; v[5] = x0 * s4.z + x1 * c4.z;
-    x0 = v[6]; x1 = v[7]; v[6] = x0 * c4.w - x1 * s4.w; v[7] = x0 * s4.w + x1 * c4.w;
+    c4 = __ldg(reinterpret_cast<const float4*>(a.cos + (int64_t)pos * 64 + pair0));
+    s4 = __ldg(reinterpret_cast<const float4*>(a.sin + (int64_t)pos * 64 + pair0));
   }
-  uint4 u;
-  u.x = pack_bf16x2(v[0], v[1]);
-  u.y = pack_bf16x2(v[2], v[3]);
-  u.z = pack_bf16x2(v[4], v[5]);
-  u.w = pack_bf16x2(v[6], v[7]);
-  *p = u;
+#pragma unroll
+  for (int s = 0; s < NSEC; ++s) {
+    float v[8], g[8];
+    unpack_bf16x8(raw[s], v);
+    unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.gamma[s] + cv)), g);
+    const float rs = rsqrtf(sum[s] * a.inv_dim + a.eps);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] *= rs * g[k];
+    if (a.rope) {
+      float x0, x1;
+      x0 = v[0]; x1 = v[1]; v[0] = x0 * c4.x - x1 * s4.x; v[1] = x0 * s4.x + x1 * c4.x;
+      x0 = v[2]; x1 = v[3]; v[2] = x0 * c4.y - x1 * s4.y; v[3] = x0 * s4.y + x1 * c4.y;
+      x0 = v[4]; x1 = v[5]; v[4] = x0 * c4.z - x1 * s4.z; v[5] = x0 * s4.z + x1 * c4.z;
+      x0 = v[6]; x1 = v[7]; v[6] = x0 * c4.w - x1 * s4.w; v[7] = x0 * s4.w + x1 * c4.w;
+    }
+    uint4 u;
+    u.x = pack_bf16x2(v[0], v[1]);
+    u.y = pack_bf16x2(v[2], v[3]);
+    u.z = pack_bf16x2(v[4], v[5]);
+    u.w = pack_bf16x2(v[6], v[7]);
+    *p[s] = u;
+  }
 }
 
 // Block shape of the row-streaming kernels: x = the row's 16-byte vectors (rounded up to a warp,
@@ -349,6 +382,10 @@ int qk_norm_rope(const wanb200_qknorm_params* p, cudaStream_t st) {
   a.width = (int)p->width;
   a.ss[0] = p->ss[0];
   a.ss[1] = p->ss[1];
+  a.ss_parts = p->ss_parts > 0 ? p->ss_parts : 1;
+  a.ss_row_stride = p->ss_row_stride > 0 ? p->ss_row_stride : 1;
+  if (a.ss_parts > p->width / 8 || a.ss_parts > 256 || a.ss_row_stride < a.ss_parts)
+    return set_error(WANB200_EINVAL, "qk_norm_rope: ss_parts must be <= width / 8 (<= 256) and <= ss_row_stride");
   a.gamma[0] = reinterpret_cast<const __nv_bfloat16*>(p->gamma[0]);
   a.gamma[1] = reinterpret_cast<const __nv_bfloat16*>(p->gamma[1]);
   a.inv_dim = p->inv_dim;
@@ -362,9 +399,58 @@ int qk_norm_rope(const wanb200_qknorm_params* p, cudaStream_t st) {
     return set_error(WANB200_EINVAL, "qk_norm_rope: rows < 2^30, width <= 8192");
   const dim3 blk = row_block(p->width / 8);
   const int64_t blocks = (p->rows + blk.y - 1) / blk.y;
-  qknorm_rope_kernel<<<dim3((unsigned)blocks, (unsigned)p->nsections), blk, 0, st>>>(a);
+  if (p->nsections == 2)
+    qknorm_rope_kernel<2><<<(unsigned)blocks, blk, 0, st>>>(a);
+  else
+    qknorm_rope_kernel<1><<<(unsigned)blocks, blk, 0, st>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error("qknorm_rope_kernel launch", e);
+  return WANB200_OK;
+}
+
+// ------------------------------------------------------------------ partial-sum reduction
+// Thread = (row, section): the section's partials of the row added in order.
+// The per-rank sums of squares of `_tp_rms_qk` / `_tp_rms` (fast_dit.py:138-140, 158) that the
+// TP all-reduce (fast_dit.py:141, 159) then adds over ranks.
+struct SumsqArgs {
+  const float* part;
+  int64_t rows, row_stride, part0[2], out_stride;
+  int parts;
+  float* out;
+};
+
+__global__ void __launch_bounds__(256) sumsq_reduce_kernel(const SumsqArgs a) {
+  const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int sec = blockIdx.y;
+  if (row >= a.rows) return;
+  const float* src = a.part + row * a.row_stride + (sec ? a.part0[1] : a.part0[0]);
+  float s = 0.f;
+  for (int k = 0; k < a.parts; ++k) s += __ldg(src + k);
+  a.out[sec * a.out_stride + row] = s;
+}
+
+int sumsq_reduce(const wanb200_sumsq_reduce_params* p, cudaStream_t st) {
+  if (!p) return set_error(WANB200_EINVAL, "sumsq_reduce: null params");
+  if (!p->part || !p->out || p->rows <= 0 || p->nsections < 1 || p->nsections > 2 || p->parts < 1 ||
+      p->out_stride < p->rows)
+    return set_error(WANB200_EINVAL, "sumsq_reduce: need part, out, rows > 0, 1 <= nsections <= 2, parts >= 1, "
+                                     "out_stride >= rows");
+  for (int s = 0; s < p->nsections; ++s)
+    if (p->part0[s] < 0 || p->part0[s] + p->parts > p->row_stride)
+      return set_error(WANB200_EINVAL, "sumsq_reduce: part0[s] + parts must lie in 0..row_stride");
+  if ((p->rows + 255) / 256 > INT32_MAX) return set_error(WANB200_EINVAL, "sumsq_reduce: too many rows");
+  SumsqArgs a;
+  a.part = p->part;
+  a.rows = p->rows;
+  a.row_stride = p->row_stride;
+  a.part0[0] = p->part0[0];
+  a.part0[1] = p->nsections > 1 ? p->part0[1] : 0;
+  a.out_stride = p->out_stride;
+  a.parts = p->parts;
+  a.out = p->out;
+  sumsq_reduce_kernel<<<dim3((unsigned)((p->rows + 255) / 256), (unsigned)p->nsections), 256, 0, st>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error("sumsq_reduce_kernel launch", e);
   return WANB200_OK;
 }
 

@@ -59,8 +59,8 @@ struct GemmArgs {
   int64_t gate_frame_stride;
   int seq_len, tokens_per_frame;
   int64_t row_offset, rows_per_seq;
-  float* rowss;
-  int ss_section, ss_nsections;
+  float* rowss;  // SUMSQ: [M, ss_cols / 32] chunk partials
+  int ss_cols;
   __nv_bfloat16* peer_out[WANB200_MAX_PEERS];
   int npeers, src_rank;
   int64_t shard_rows;
@@ -138,8 +138,8 @@ __device__ __forceinline__ void residual_values(const GemmArgs& a, const uint4 (
 }
 
 template <int EPI>
-__device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v, int row, int col0, float& ss_acc,
-                                                    int& ss_sec, const uint4 (&res)[8], const float* gate_row) {
+__device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v, int row, int col0,
+                                                    const uint4 (&res)[8], const float* gate_row) {
   if constexpr (EPI != WANB200_EPI_NONE && EPI != WANB200_EPI_SCATTER) {
     const uint4* bp = reinterpret_cast<const uint4*>(a.bias + col0);
 #pragma unroll
@@ -182,14 +182,17 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v,
     }
   }
   if constexpr (EPI == WANB200_EPI_BIAS_SUMSQ) {
-    const int sec = col0 / a.ss_section;
-    if (sec != ss_sec) {
-      if (ss_sec >= 0 && ss_sec < a.ss_nsections && row < a.M) atomicAdd(a.rowss + (int64_t)ss_sec * a.M + row, ss_acc);
-      ss_acc = 0.f;
-      ss_sec = sec;
-    }
+    // this chunk's sum of squares, stored once (no atomics); the consumer adds a row's partials
+    // in a fixed order
+    if (col0 < a.ss_cols && row < a.M) {
+      float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) ss_acc = fmaf(v[i], v[i], ss_acc);
+      for (int i = 0; i < 32; i += 2) {
+        s0 = fmaf(v[i], v[i], s0);
+        s1 = fmaf(v[i + 1], v[i + 1], s1);
+      }
+      a.rowss[(int64_t)row * (a.ss_cols >> 5) + (col0 >> 5)] = s0 + s1;
+    }
   }
   if (EPI != WANB200_EPI_SCATTER && EPI != WANB200_EPI_BIAS_SUMSQ && a.out_f32) {
     if (row < a.M) {
@@ -350,8 +353,6 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       tile_origin(tile, num_m, num_n, bn, m0, n0);
       const int row = m0 + r;
       const uint32_t t_row = tmem_base + (uint32_t(quad * 32) << 16) + acc * GBN;
-      float ss_acc = 0.f;
-      int ss_sec = -1;
       if constexpr (EPI == WANB200_EPI_SCATTER) {
         // stage this warp's 32 rows (lane = row), then write each row as one 512-byte segment
         // (the first warp of each lane quarter does the whole tile; the second only arrives)
@@ -399,12 +400,8 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           }
           float v[32];
           tmem_ld32(t_row + c * 32, v);
-          gemm_epilogue_chunk<EPI>(args, v, row, col0, ss_acc, ss_sec, res_cur, gate_row);
+          gemm_epilogue_chunk<EPI>(args, v, row, col0, res_cur, gate_row);
         }
-      }
-      if constexpr (EPI == WANB200_EPI_BIAS_SUMSQ) {
-        if (ss_sec >= 0 && ss_sec < args.ss_nsections && row < args.M)
-          atomicAdd(args.rowss + (int64_t)ss_sec * args.M + row, ss_acc);
       }
       tc_fence_before();
       mbar_arrive(tempty0 + 8 * acc);
@@ -502,8 +499,8 @@ int gemm_bf16(const wanb200_gemm_params* p, cudaStream_t st) {
   if (p->tile_n != 0 && (p->tile_n < 64 || p->tile_n > GBN || p->tile_n % 32))
     return set_error(WANB200_EINVAL, "gemm: tile_n must be 0 (library's choice) or a multiple of 32 in 64..256");
   if (epi == WANB200_EPI_BIAS_SUMSQ) {
-    if (!p->rowss || p->ss_section <= 0 || (p->ss_section % 32) || p->ss_nsections <= 0 || p->ss_section > INT32_MAX)
-      return set_error(WANB200_EINVAL, "gemm: sumsq epilogue needs rowss and a section width that is a multiple of 32");
+    if (!p->rowss || p->ss_cols <= 0 || (p->ss_cols % 32) || p->ss_cols > p->N)
+      return set_error(WANB200_EINVAL, "gemm: sumsq epilogue needs rowss and ss_cols, a multiple of 32 in 32..N");
   }
 
   int* err = device_error_word();
@@ -535,8 +532,7 @@ int gemm_bf16(const wanb200_gemm_params* p, cudaStream_t st) {
   ga.row_offset = p->row_offset;
   ga.rows_per_seq = p->rows_per_seq;
   ga.rowss = p->rowss;
-  ga.ss_section = (int)(p->ss_section > 0 ? p->ss_section : 1);
-  ga.ss_nsections = p->ss_nsections;
+  ga.ss_cols = epi == WANB200_EPI_BIAS_SUMSQ ? (int)p->ss_cols : 0;
   for (int i = 0; i < WANB200_MAX_PEERS; ++i)
     ga.peer_out[i] = reinterpret_cast<__nv_bfloat16*>(i < p->npeers ? p->peer_out[i] : p->peer_out[0]);
   ga.npeers = p->npeers;

@@ -58,6 +58,7 @@ int64_t attn_workspace_bytes(int64_t batch, int64_t heads, int64_t q_len, int kv
 int attn_kv_splits(int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len);
 int layernorm(const wanb200_ln_params* p, cudaStream_t st);
 int qk_norm_rope(const wanb200_qknorm_params* p, cudaStream_t st);
+int sumsq_reduce(const wanb200_sumsq_reduce_params* p, cudaStream_t st);
 int bias_gate_residual(const wanb200_residual_params* p, cudaStream_t st);
 int peer_barrier(int* const* flags, int rank, int world, int epoch, cudaStream_t st);
 int shard_gather(const wanb200_shard_gather_params* p, cudaStream_t st);

@@ -26,8 +26,7 @@ class GemmParams(ctypes.Structure):
                 ("bias", c_void_p), ("residual", c_void_p), ("ldr", c_int64), ("gate_mod", c_void_p),
                 ("gate_e0", c_void_p), ("gate_frame_stride", c_int64), ("seq_len", c_int64),
                 ("tokens_per_frame", c_int64), ("row_offset", c_int64), ("rows_per_seq", c_int64), ("rowss", c_void_p),
-                ("ss_section", c_int64),
-                ("ss_nsections", c_int), ("peer_out", c_void_p * 8), ("npeers", c_int), ("src_rank", c_int),
+                ("ss_cols", c_int64), ("peer_out", c_void_p * 8), ("npeers", c_int), ("src_rank", c_int),
                 ("shard_rows", c_int64), ("tile_n", c_int), ("residual_f32", c_int), ("out_f32", c_int)]
 
 
@@ -46,7 +45,7 @@ class LnParams(ctypes.Structure):
                 ("mode", c_int), ("modulation", c_void_p), ("e0", c_void_p), ("e0_frame_stride", c_int64),
                 ("shift_idx", c_int), ("scale_idx", c_int), ("seq_len", c_int64), ("tokens_per_frame", c_int64),
                 ("row_offset", c_int64), ("rows_per_seq", c_int64),
-                ("weight", c_void_p), ("bias", c_void_p), ("zero_buf", c_void_p), ("zero_count", c_int64),
+                ("weight", c_void_p), ("bias", c_void_p),
                 ("push_out", c_void_p * 8), ("npush", c_int), ("push_row0", c_int64), ("x_f32", c_int),
                 ("e0_one_row", c_int)]
 
@@ -54,8 +53,13 @@ class LnParams(ctypes.Structure):
 class QkNormParams(ctypes.Structure):
     _fields_ = [("x", c_void_p), ("ld", c_int64), ("rows", c_int64), ("nsections", c_int),
                 ("col0", c_int64 * 2), ("width", c_int64), ("ss", c_void_p * 2), ("gamma", c_void_p * 2),
-                ("inv_dim", c_float), ("eps", c_float), ("rope", c_int), ("cos", c_void_p), ("sin", c_void_p),
+                ("ss_parts", c_int), ("ss_row_stride", c_int64), ("inv_dim", c_float), ("eps", c_float), ("rope", c_int), ("cos", c_void_p), ("sin", c_void_p),
                 ("seq_len", c_int64)]
+
+
+class SumsqReduceParams(ctypes.Structure):
+    _fields_ = [("part", c_void_p), ("rows", c_int64), ("row_stride", c_int64), ("nsections", c_int),
+                ("part0", c_int64 * 2), ("parts", c_int), ("out", c_void_p), ("out_stride", c_int64)]
 
 
 class ResidualParams(ctypes.Structure):
@@ -114,7 +118,7 @@ EXPORTS = ("wanb200_gemm_bf16", "wanb200_attn_fwd", "wanb200_layernorm", "wanb20
            "wanb200_struct_sizes", "wanb200_peer_barrier", "wanb200_attn_workspace_bytes",
            "wanb200_attn_kv_splits", "wanb200_attn_fwd_noalloc", "wanb200_shard_gather", "wanb200_attn_fwd_fp8",
            "wanb200_attn_fp8_workspace_bytes", "wanb200_device_error_async", "wanb200_block_forward",
-           "wanb200_block_workspace_bytes", "wanb200_patchify", "wanb200_unpatchify_cfg")
+           "wanb200_block_workspace_bytes", "wanb200_patchify", "wanb200_unpatchify_cfg", "wanb200_sumsq_reduce")
 
 _lock = threading.Lock()
 _lib = None
@@ -173,8 +177,10 @@ def load():
             lib.wanb200_patchify.restype = c_int
             lib.wanb200_unpatchify_cfg.argtypes = [ctypes.POINTER(UnpatchifyParams), c_void_p]
             lib.wanb200_unpatchify_cfg.restype = c_int
+            lib.wanb200_sumsq_reduce.argtypes = [ctypes.POINTER(SumsqReduceParams), c_void_p]
+            lib.wanb200_sumsq_reduce.restype = c_int
             structs = (GemmParams, AttnParams, LnParams, QkNormParams, ResidualParams, ShardGatherParams,
-                       AttnFp8Params, BlockParams, PatchifyParams, UnpatchifyParams)
+                       AttnFp8Params, BlockParams, PatchifyParams, UnpatchifyParams, SumsqReduceParams)
             sizes = (c_int64 * len(structs))()
             n = lib.wanb200_struct_sizes(sizes, len(structs))
             want = [ctypes.sizeof(c) for c in structs]

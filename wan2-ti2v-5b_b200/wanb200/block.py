@@ -6,15 +6,15 @@ heads with in-graph all-reduces).  `FastCrossKV.forward(context) -> (ck, cv)` is
 `_FastCrossKV` (fast_dit.py:464-477), run once per generation.
 
 Op sequence of one block (N = B*L tokens, C = 3072, C_l = C / TP, F_l = 14336 / TP):
-   1  h   = LN1(x) * (1 + scale) + shift                    layernorm (also zeroes the Σx² slots)
-   2  qkv = h W_qkv^T + b, Σq², Σk² per row                 tcgen05 GEMM, SUMSQ epilogue
-      [TP: all-reduce Σq², Σk²]
+   1  h   = LN1(x) * (1 + scale) + shift                    layernorm
+   2  qkv = h W_qkv^T + b, Σq², Σk² per row and 32 columns  tcgen05 GEMM, SUMSQ epilogue
+      [TP: sumsq_reduce, all-reduce Σq², Σk²]
    3  q,k = RoPE(x * rsqrt(Σ/C + eps) * γ)                   qk_norm_rope (in place)
    4  y   = softmax(q k^T / sqrt(d)) v                       flash attention
    5  x1  = x + (y W_o^T + b_o) * gate2                      GEMM, GATE_RES epilogue (x1 fp32)
       [TP: GEMM partial -> all-reduce -> bias_gate_residual]
    6  h   = LN3_affine(x1)
-   7  qc  = h W_cq^T + b, Σqc²                              GEMM, SUMSQ  [TP: all-reduce Σ]
+   7  qc  = h W_cq^T + b, Σqc²                              GEMM, SUMSQ  [TP: reduce, all-reduce Σ]
    8  qc  = qc * rsqrt(Σ/C + eps) * γ                        qk_norm_rope (no rotation)
    9  y   = attention(qc, ck, cv)                            flash attention over 512 keys
   10  x1 += y W_co^T + b_co                                  GEMM, RES epilogue [TP: AR path]
@@ -55,7 +55,11 @@ class Workspace:
         self.y = torch.empty(n_tok, local_dim, **kw)
         self.cq = torch.empty(n_tok, local_dim, **kw)
         self.f = torch.empty(n_tok, ffn_local, **kw)
-        self.ss = torch.empty(3, n_tok, device=device, dtype=torch.float32)
+        # Σx² of q and k per row and 32 output columns (the SUMSQ GEMM's chunk partials, [rows, 2P];
+        # the cross-q GEMM writes [rows, P] into the same storage), and under TP the per-section
+        # sums all-reduced
+        self.ssp = torch.empty(n_tok * 2 * local_dim // 32, device=device, dtype=torch.float32)
+        self.ss = torch.empty(3, n_tok, device=device, dtype=torch.float32) if tp else None
         self.part = torch.empty(n_tok, dim, **kw) if tp else None
 
 
@@ -103,6 +107,25 @@ class FastBlock:
     def _all_reduce(self, t):
         if self.tp:
             dist.all_reduce(t, group=self.tp_group)
+
+    def _sumsq(self, ws, nsec, sec0):
+        """The Σx² operands of qk_norm_rope for nsec sections of local_dim columns: on one GPU the
+        GEMM's chunk partials themselves (the norm kernel adds them in a fixed order); under TP the
+        partials reduced per section into ws.ss[sec0:] and all-reduced over the group
+        (`_tp_rms_qk` / `_tp_rms`, models/fast_dit.py:138-141, 158-159)."""
+        P = self.w.local_dim // 32
+        part = self._partials(ws, nsec)
+        if not self.tp:
+            return [part[:, s * P:(s + 1) * P] for s in range(nsec)]
+        out = ws.ss[sec0:sec0 + nsec]
+        ops.sumsq_reduce(part, [s * P for s in range(nsec)], P, out)
+        self._all_reduce(out)
+        return [out[s] for s in range(nsec)]
+
+    def _partials(self, ws, nsec):
+        """ws.ssp as the [rows, nsec * P] output of a SUMSQ GEMM over nsec sections."""
+        n = nsec * self.w.local_dim // 32
+        return ws.ssp[:ws.h.shape[0] * n].view(ws.h.shape[0], n)
 
     def _row_parallel(self, a, wmat, part, kind):
         """part = all_reduce(a @ wmat^T) over the TP group: the partial sums of a row-parallel
@@ -158,11 +181,11 @@ class FastBlock:
         mod = w.modulation
 
         # -- self-attention
-        ops.layernorm_modulate(xf, mod, e0, 0, 1, frames, out=ws.h, eps=self.eps, zero=ws.ss)
-        ops.linear(ws.h, w.w_qkv, w.b_qkv, epilogue=L.EPI_BIAS_SUMSQ, out=ws.qkv, rowss=ws.ss,
-                   ss_section=Cl, ss_nsections=2, kind="gemm_qkv")
-        self._all_reduce(ws.ss[0:2])
-        ops.qk_norm_rope(ws.qkv, [(0, ws.ss[0], w.g_q), (Cl, ws.ss[1], w.g_k)], Cl, C, eps=self.eps,
+        ops.layernorm_modulate(xf, mod, e0, 0, 1, frames, out=ws.h, eps=self.eps)
+        ops.linear(ws.h, w.w_qkv, w.b_qkv, epilogue=L.EPI_BIAS_SUMSQ, out=ws.qkv, rowss=self._partials(ws, 2),
+                   ss_cols=2 * Cl, kind="gemm_qkv")
+        ssq, ssk = self._sumsq(ws, 2, 0)
+        ops.qk_norm_rope(ws.qkv, [(0, ssq, w.g_q), (Cl, ssk, w.g_k)], Cl, C, eps=self.eps,
                          cos=cos2, sin=sin2, seq_len=Lx)
         q = ws.qkv[:, :Cl].view(B, Lx, nl, 128)
         y = ws.y.view(B, Lx, nl, 128)
@@ -208,10 +231,10 @@ class FastBlock:
 
         # -- cross-attention (ck/cv cached per generation)
         ops.layernorm_affine(x1, w.ln3_w, w.ln3_b, out=ws.h, eps=self.eps)
-        ops.linear(ws.h, w.w_cq, w.b_cq, epilogue=L.EPI_BIAS_SUMSQ, out=ws.cq, rowss=ws.ss[2],
-                   ss_section=Cl, ss_nsections=1, kind="gemm_cross_q")
-        self._all_reduce(ws.ss[2])
-        ops.qk_norm_rope(ws.cq, [(0, ws.ss[2], w.g_cq)], Cl, C, eps=self.eps)
+        ops.linear(ws.h, w.w_cq, w.b_cq, epilogue=L.EPI_BIAS_SUMSQ, out=ws.cq, rowss=self._partials(ws, 1),
+                   ss_cols=Cl, kind="gemm_cross_q")
+        (ssc,) = self._sumsq(ws, 1, 2)
+        ops.qk_norm_rope(ws.cq, [(0, ssc, w.g_cq)], Cl, C, eps=self.eps)
         ops.attention(ws.cq.view(B, Lx, nl, 128), ck, cv, out=ws.y.view(B, Lx, nl, 128), kind="attn_cross")
         if self.tp:
             self._row_parallel(ws.y, w.w_co, ws.part, "gemm_cross_o")
@@ -237,7 +260,7 @@ class FastBlock:
     # launches it makes)
     @property
     def launches(self) -> int:
-        n = 13 if not self.tp else 16 + 3 * (self.tp_chunks - 1)
+        n = 13 if not self.tp else 18 + 3 * (self.tp_chunks - 1)
         if self.sp is not None and self.sp.overlapped:
             n += 3  # shard gather + peer barrier + the second attention piece
         return n
@@ -257,11 +280,13 @@ class FastCrossKV:
         B, Lc, C = context.shape
         N, Cl, nh = B * Lc, w.cross_dim, w.cross_heads
         ctx = context.reshape(N, C).to(BF16).contiguous()
-        ss = torch.zeros(N, device=context.device, dtype=torch.float32)
-        kv = ops.linear(ctx, w.w_ckv, w.b_ckv, epilogue=L.EPI_BIAS_SUMSQ, rowss=ss, ss_section=Cl, ss_nsections=1,
-                        kind="gemm_cross_kv")
+        ss = torch.empty(N, Cl // 32, device=context.device, dtype=torch.float32)  # Σk² chunk partials
+        kv = ops.linear(ctx, w.w_ckv, w.b_ckv, epilogue=L.EPI_BIAS_SUMSQ, rowss=ss, ss_cols=Cl, kind="gemm_cross_kv")
         if w.tp_size > 1 and not w.local_cross:
-            dist.all_reduce(ss, group=self.tp_group)
+            ss_sum = torch.empty(N, device=context.device, dtype=torch.float32)
+            ops.sumsq_reduce(ss, [0], Cl // 32, ss_sum)
+            dist.all_reduce(ss_sum, group=self.tp_group)
+            ss = ss_sum
         ops.qk_norm_rope(kv, [(0, ss, w.g_ck)], Cl, C, eps=self.eps)
         ck = kv[:, :Cl].view(B, Lc, nh, 128)
         cv = kv[:, Cl:].view(B, Lc, nh, 128)
@@ -285,8 +310,9 @@ class SPWorkspace:
         self.cq = torch.empty(S, dim, **kw)
         self.yc = torch.empty(S, dim, **kw)
         self.f = torch.empty(Np, ffn_local, **kw)
-        self.ss = torch.empty(2, Np, device=device, dtype=torch.float32)
-        self.ssc = torch.empty(S, device=device, dtype=torch.float32)
+        self.ssp = torch.empty(Np, 2 * local_dim // 32, device=device, dtype=torch.float32)  # Σq², Σk² partials
+        self.ss = torch.empty(2, Np, device=device, dtype=torch.float32)  # their sums, all-reduced
+        self.sscp = torch.empty(S, dim // 32, device=device, dtype=torch.float32)  # Σ(cross q)² partials
 
 
 _SPWS = {}
@@ -316,14 +342,13 @@ class FastBlockSP:
         self.T, self.rank = weights.tp_size, weights.tp_rank
         self.comm = comm
 
-    def _ln_gather(self, xs, mod, e0, shift, scale, frames, ws, zero=None):
+    def _ln_gather(self, xs, mod, e0, shift, scale, frames, ws):
         """LN + modulation of the shard, all-gathered to [T*S, C]; returns the gathered buffer."""
         if self.comm is not None:
-            ops.layernorm_modulate(xs, mod, e0, shift, scale, frames, out=None, eps=self.eps, zero=zero,
-                                   push=self.comm.push)
+            ops.layernorm_modulate(xs, mod, e0, shift, scale, frames, out=None, eps=self.eps, push=self.comm.push)
             self.comm.barrier()
             return self.comm.hf
-        ops.layernorm_modulate(xs, mod, e0, shift, scale, frames, out=ws.h_s, eps=self.eps, zero=zero)
+        ops.layernorm_modulate(xs, mod, e0, shift, scale, frames, out=ws.h_s, eps=self.eps)
         dist.all_gather_into_tensor(ws.hf, ws.h_s, group=self.tp_group)
         return ws.hf
 
@@ -364,9 +389,11 @@ class FastBlockSP:
         mod = w.modulation
 
         # -- self-attention: LN on the shard, all-gather, column-parallel QKV on all tokens
-        hf = self._ln_gather(xs, mod, e0, 0, 1, frames_s, ws, zero=ws.ss)
-        ops.linear(hf, w.w_qkv, w.b_qkv, epilogue=L.EPI_BIAS_SUMSQ, out=ws.qkv, rowss=ws.ss,
-                   ss_section=Cl, ss_nsections=2, kind="gemm_qkv")
+        hf = self._ln_gather(xs, mod, e0, 0, 1, frames_s, ws)
+        ops.linear(hf, w.w_qkv, w.b_qkv, epilogue=L.EPI_BIAS_SUMSQ, out=ws.qkv, rowss=ws.ssp, ss_cols=2 * Cl,
+                   kind="gemm_qkv")
+        P = Cl // 32
+        ops.sumsq_reduce(ws.ssp, [0, P], P, ws.ss)
         dist.all_reduce(ws.ss, group=g)
         ops.qk_norm_rope(ws.qkv, [(0, ws.ss[0], w.g_q), (Cl, ws.ss[1], w.g_k)], Cl, C, eps=self.eps,
                          cos=cos2, sin=sin2, seq_len=Lx)
@@ -381,10 +408,10 @@ class FastBlockSP:
         self._rowpar_residual(ws.y, w.w_o, w.b_o, xs, (mod[2], e0[:, 2, :]), frames_s, x1, ws, "gemm_o")
 
         # -- cross-attention on the shard, all heads, no collective
-        ops.layernorm_affine(x1, w.ln3_w, w.ln3_b, out=ws.h_s, eps=self.eps, zero=ws.ssc)
-        ops.linear(ws.h_s, w.w_cq, w.b_cq, epilogue=L.EPI_BIAS_SUMSQ, out=ws.cq, rowss=ws.ssc, ss_section=C,
-                   ss_nsections=1, kind="gemm_cross_q")
-        ops.qk_norm_rope(ws.cq, [(0, ws.ssc, w.g_cq)], C, C, eps=self.eps)
+        ops.layernorm_affine(x1, w.ln3_w, w.ln3_b, out=ws.h_s, eps=self.eps)
+        ops.linear(ws.h_s, w.w_cq, w.b_cq, epilogue=L.EPI_BIAS_SUMSQ, out=ws.cq, rowss=ws.sscp, ss_cols=C,
+                   kind="gemm_cross_q")
+        ops.qk_norm_rope(ws.cq, [(0, ws.sscp, w.g_cq)], C, C, eps=self.eps)
         H = w.cross_heads
         ops.attention(ws.cq.view(1, S, H, 128), ck, cv, out=ws.yc.view(1, S, H, 128), kind="attn_cross")
         ops.linear(ws.yc, w.w_co, w.b_co, epilogue=L.EPI_BIAS_RES, out=x1, residual=x1, kind="gemm_cross_o")
@@ -399,7 +426,7 @@ class FastBlockSP:
 
     @property
     def launches(self) -> int:
-        return 15
+        return 16
 
 
 

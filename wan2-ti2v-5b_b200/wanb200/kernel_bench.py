@@ -3,6 +3,7 @@
     python -m wanb200.kernel_bench gemm --M 15708 --N 14336 --K 3072 --epi gelu [--iters 20]
     python -m wanb200.kernel_bench attn --B 2 --H 24 --Lq 7854 --Lk 7854 [--iters 20]
     python -m wanb200.kernel_bench ln --M 15708 --C 3072 [--f32]
+    python -m wanb200.kernel_bench qknorm --M 15708 --C 3072
     python -m wanb200.kernel_bench gemm --M 15708 --N 3072 --K 3072 --epi gate_res --f32
 
 (run from wan2-ti2v-5b_b200/ or with it on sys.path).  Prints one JSON line with the mean
@@ -53,8 +54,8 @@ def bench_gemm(a):
         kw["gate"] = (torch.zeros(a.N, device=dev, dtype=torch.bfloat16), torch.ones(21, 6 * a.N, device=dev)[:, :a.N])
         kw["frames"] = (a.M, max(1, a.M // 21))
     if epi == L.EPI_BIAS_SUMSQ:
-        kw["rowss"] = torch.zeros(2, a.M, device=dev)
-        kw["ss_section"], kw["ss_nsections"] = a.N // 3, 2
+        kw["rowss"] = torch.empty(a.M, 2 * (a.N // 3) // 32, device=dev)  # q and k chunk partials
+        kw["ss_cols"] = 2 * (a.N // 3)
     ms = _time(lambda: ops.linear(x, w, b if epi else None, epilogue=epi, out=out, tile_n=a.tile_n, **kw), a.iters)
     return {"kernel": "gemm", "M": a.M, "N": a.N, "K": a.K, "epi": a.epi, "f32_residual": a.f32,
             "tile_n": a.tile_n, "ms": ms,
@@ -86,9 +87,27 @@ def bench_ln(a):
             "gbs": (x.element_size() + 2) * a.M * a.C / ms / 1e6}
 
 
+def bench_qknorm(a):
+    """q and k sections of a [M, 3C] QKV buffer normed and rotated in place, the sums of squares
+    given as the QKV GEMM's 32-column chunk partials (one GPU), B = 2 sequences of M / 2 tokens."""
+    dev = "cuda"
+    C, M = a.C, a.M
+    qkv = torch.randn(M, 3 * C, device=dev).to(torch.bfloat16)
+    part = torch.rand(M, 2 * C // 32, device=dev) * 32
+    g = torch.ones(C, device=dev, dtype=torch.bfloat16)
+    Lx = max(1, M // 2)
+    ang = torch.rand(Lx, 64, device=dev)
+    cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
+    P = C // 32
+    fn = lambda: ops.qk_norm_rope(qkv, [(0, part[:, :P], g), (C, part[:, P:], g)], C, C, cos=cos, sin=sin, seq_len=Lx)
+    ms = _time(fn, a.iters)
+    nbytes = 2 * (4 * M * C + 4 * M * P)
+    return {"kernel": "qk_norm_rope", "M": M, "C": C, "ms": ms, "gbs": nbytes / ms / 1e6}
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("kind", choices=["gemm", "attn", "ln"])
+    ap.add_argument("kind", choices=["gemm", "attn", "ln", "qknorm"])
     ap.add_argument("--M", type=int, default=15708)
     ap.add_argument("--N", type=int, default=14336)
     ap.add_argument("--K", type=int, default=3072)
@@ -104,7 +123,7 @@ def main():
     ap.add_argument("--f32", action="store_true", help="gemm residual epilogues / ln: the fp32 residual stream")
     a = ap.parse_args()
     torch.cuda.set_device(0)
-    r = {"gemm": bench_gemm, "attn": bench_attn, "ln": bench_ln}[a.kind](a)
+    r = {"gemm": bench_gemm, "attn": bench_attn, "ln": bench_ln, "qknorm": bench_qknorm}[a.kind](a)
     r["device_error"] = L.device_error(reset=True)
     print(json.dumps(r), flush=True)
 

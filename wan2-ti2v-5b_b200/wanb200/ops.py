@@ -112,14 +112,15 @@ def _rows(t: torch.Tensor, name: str):
 
 # ---------------------------------------------------------------------------- GEMM
 def linear(a, w, bias=None, *, epilogue=L.EPI_BIAS, out=None, residual=None, gate=None, frames=None,
-           rowss=None, ss_section=0, ss_nsections=0, kind="gemm", scatter=None, tile_n=0):
+           rowss=None, ss_cols=0, kind="gemm", scatter=None, tile_n=0):
     """out[M, N] = epilogue(a[M, K] @ w[N, K]^T) on tcgen05 (see include/wanb200.h).
 
     tile_n: width of the output tile along N (0 = the library's choice; 64..256, multiple of 32).
 
     gate: (gate_mod [N] bf16, gate_e0 [F, N] fp32 view with unit column stride) for EPI_BIAS_GATE_RES.
     frames: (seq_len, tokens_per_frame) mapping a row to its latent frame.
-    rowss: fp32 [ss_nsections, M] accumulators for EPI_BIAS_SUMSQ (must be zeroed first).
+    rowss: fp32 [M, ss_cols / 32] for EPI_BIAS_SUMSQ: rowss[r, k] receives row r's sum of squares
+    over output columns 32k .. 32k+31 (written, not accumulated; see qk_norm_rope / sumsq_reduce).
     residual / out may be fp32 for the residual epilogues (the fp32 residual stream).
     """
     _cuda(a, w, bias, out, residual, rowss)
@@ -149,8 +150,9 @@ def linear(a, w, bias=None, *, epilogue=L.EPI_BIAS, out=None, residual=None, gat
     if frames is not None:
         _set_frames(p, frames)
     if rowss is not None:
-        _need(rowss.dtype == torch.float32, "linear: rowss must be fp32")
-        p.rowss, p.ss_section, p.ss_nsections = _p(rowss), ss_section, ss_nsections
+        _need(rowss.dtype == torch.float32 and rowss.is_contiguous() and rowss.numel() >= (ss_cols // 32) * M,
+              "linear: rowss must be contiguous fp32 [M, ss_cols / 32]")
+        p.rowss, p.ss_cols = _p(rowss), ss_cols
     if scatter is not None:  # (peer inbox pointers, this rank, rows per shard)
         ptrs, src, shard_rows = scatter
         _need(epilogue == L.EPI_SCATTER and 1 <= len(ptrs) <= L.MAX_PEERS, "linear: bad scatter")
@@ -253,12 +255,12 @@ def _ln_input(x):
           "layernorm: x must be contiguous bf16 or fp32 [M, C]")
 
 
-def layernorm_modulate(x, modulation, e0, shift_idx, scale_idx, frames, out=None, eps=1e-6, zero=None, push=None,
+def layernorm_modulate(x, modulation, e0, shift_idx, scale_idx, frames, out=None, eps=1e-6, push=None,
                        one_row=False):
     """LN(x) * (1 + scale[f]) + shift[f] -> bf16; x [M, C] bf16 or fp32 (the fp32 residual
     stream), modulation [6, C] bf16, e0 [F, 6, C] fp32.  one_row: the head's modulation
     (modulation [2, C], e0 [F, C]: shift and scale both add the frame's time-embedding row)."""
-    _cuda(x, modulation, e0, out, zero)
+    _cuda(x, modulation, e0, out)
     _ln_input(x)
     _need(e0.dtype == torch.float32 and e0.is_contiguous() and modulation.dtype == BF16, "layernorm: bad mod tensors")
     M, C = x.shape
@@ -272,17 +274,15 @@ def layernorm_modulate(x, modulation, e0, shift_idx, scale_idx, frames, out=None
     p.modulation, p.e0, p.e0_frame_stride = _p(modulation), _p(e0), (C if one_row else 6 * C)
     p.shift_idx, p.scale_idx = shift_idx, scale_idx
     _set_frames(p, frames)
-    if zero is not None:
-        p.zero_buf, p.zero_count = _p(zero), zero.numel()
     lib = L.load()
     L.check(_launch(x, "layernorm", (x.element_size() + 2.0) * M * C,
                     lambda: lib.wanb200_layernorm(ctypes.byref(p), _stream(x))), "wanb200_layernorm")
     return out
 
 
-def layernorm_affine(x, weight, bias, out=None, eps=1e-6, zero=None):
+def layernorm_affine(x, weight, bias, out=None, eps=1e-6):
     """LN(x) * weight + bias -> bf16; x [M, C] bf16 or fp32."""
-    _cuda(x, weight, bias, out, zero)
+    _cuda(x, weight, bias, out)
     _ln_input(x)
     M, C = x.shape
     if out is None:
@@ -291,8 +291,6 @@ def layernorm_affine(x, weight, bias, out=None, eps=1e-6, zero=None):
     p.x_f32 = int(x.dtype == torch.float32)
     p.x, p.out, p.rows, p.dim, p.eps, p.mode = _p(x), _p(out), M, C, eps, L.LN_AFFINE
     p.weight, p.bias = _p(weight), _p(bias)
-    if zero is not None:
-        p.zero_buf, p.zero_count = _p(zero), zero.numel()
     lib = L.load()
     L.check(_launch(x, "layernorm", (x.element_size() + 2.0) * M * C,
                     lambda: lib.wanb200_layernorm(ctypes.byref(p), _stream(x))), "wanb200_layernorm")
@@ -300,25 +298,62 @@ def layernorm_affine(x, weight, bias, out=None, eps=1e-6, zero=None):
 
 
 def qk_norm_rope(x, sections, width, global_dim, eps=1e-6, cos=None, sin=None, seq_len=0):
-    """In place on x [M, ld]: for each (col0, ss [M] fp32, gamma [width] bf16) section,
-    x[:, col0:col0+width] = RoPE(x * rsqrt(ss/global_dim + eps) * gamma) (RoPE if cos given)."""
+    """In place on x [M, ld]: for each (col0, ss, gamma [width] bf16) section,
+    x[:, col0:col0+width] = RoPE(x * rsqrt(S/global_dim + eps) * gamma) (RoPE if cos given).
+
+    ss is either [M] fp32 (finished sums S, e.g. after the TP all-reduce) or an [M, P] fp32 view
+    with unit column stride: P partial sums per row (the SUMSQ GEMM's 32-column chunks, e.g. a
+    column slice of its [M, 2P] output) that the kernel adds in a fixed order.  Every section
+    takes the same form."""
     _cuda(x, cos, sin)
     ld = _rows(x, "x")
     p = L.QkNormParams()
     p.x, p.ld, p.rows, p.nsections, p.width = _p(x), ld, x.shape[0], len(sections), width
+    M = x.shape[0]
+    forms = set()
     for i, (c0, ss, g) in enumerate(sections):
         _cuda(ss, g)
         _need(ss.dtype == torch.float32 and g.dtype == BF16, "qk_norm_rope: ss fp32, gamma bf16")
+        if ss.dim() == 1:
+            _need(ss.numel() >= M and ss.stride(0) == 1, "qk_norm_rope: ss must hold a sum per row")
+            forms.add((1, 1))
+        else:
+            _need(ss.dim() == 2 and ss.shape[0] >= M and ss.stride(1) == 1, "qk_norm_rope: ss partials must be [M, P]")
+            forms.add((ss.shape[1], ss.stride(0)))
         p.col0[i], p.ss[i], p.gamma[i] = c0, _p(ss), _p(g)
+    _need(len(forms) == 1, "qk_norm_rope: every section's ss must have the same partial count and row stride")
+    p.ss_parts, p.ss_row_stride = forms.pop()
     p.inv_dim, p.eps = 1.0 / global_dim, eps
     if cos is not None:
         _need(cos.dtype == torch.float32 and cos.is_contiguous() and sin.is_contiguous(), "qk_norm_rope: bad tables")
         p.rope, p.cos, p.sin, p.seq_len = 1, _p(cos), _p(sin), seq_len
     lib = L.load()
-    nbytes = 4.0 * x.shape[0] * width * len(sections) + 4.0 * x.shape[0] * len(sections)
+    nbytes = 4.0 * M * width * len(sections) + 4.0 * M * p.ss_parts * len(sections)
     L.check(_launch(x, "qk_norm_rope", nbytes, lambda: lib.wanb200_qk_norm_rope(ctypes.byref(p), _stream(x))),
             "wanb200_qk_norm_rope")
     return x
+
+
+def sumsq_reduce(part, part0, parts, out):
+    """out[s, r] = part[r, part0[s]] + ... + part[r, part0[s] + parts - 1] (added in that order) for
+    the one or two sections s, part [M, P] fp32 (the SUMSQ GEMM's chunk partials): the per-rank
+    sums of squares ahead of the TP all-reduce.  out: [sections, M] or [M] for one section."""
+    _cuda(part, out)
+    _need(part.dtype == torch.float32 and part.dim() == 2 and part.stride(1) == 1, "sumsq_reduce: part [M, P] fp32")
+    _need(out.dtype == torch.float32 and out.stride(-1) == 1 and 1 <= len(part0) <= 2, "sumsq_reduce: bad out")
+    M = part.shape[0]
+    out2 = out if out.dim() == 2 else out.view(1, -1)
+    _need(out2.shape[0] == len(part0) and out2.shape[1] >= M, "sumsq_reduce: out must be [sections, M]")
+    _need(all(0 <= q and q + parts <= part.shape[1] for q in part0), "sumsq_reduce: partials out of range")
+    p = L.SumsqReduceParams()
+    p.part, p.rows, p.row_stride, p.nsections, p.parts, p.out = _p(part), M, part.stride(0), len(part0), parts, _p(out2)
+    p.out_stride = out2.stride(0) if out2.shape[0] > 1 else M
+    for i, q in enumerate(part0):
+        p.part0[i] = q
+    lib = L.load()
+    L.check(_launch(part, "sumsq_reduce", 4.0 * M * (parts + 1) * len(part0),
+                    lambda: lib.wanb200_sumsq_reduce(ctypes.byref(p), _stream(part))), "wanb200_sumsq_reduce")
+    return out
 
 
 def bias_gate_residual(residual, y, bias, gate=None, frames=None, out=None, nsum=1):
