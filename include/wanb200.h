@@ -94,20 +94,9 @@ typedef struct wanb200_gemm_params {
    * step; the patch embedding writes the stream's first value and the time embedding its
    * fp32 modulation rows the same way. */
   int residual_f32, out_f32;
-  /* split-K, for short-M shards whose few tiles leave SMs idle: k_splits 0 = the library's
-   * choice (no split unless splitk_ws is given and large enough for it), 1 = none, >= 2 = that
-   * many consecutive K ranges per output tile (at most K / 64; not with SCATTER).  The CTA of the
-   * last range adds the other ranges' fp32 partials in range order before the epilogue, so the
-   * result is bit-reproducible for a given tiling.  splitk_ws: 256-byte aligned, of
-   * wanb200_gemm_splitk_workspace_bytes() bytes, zero-filled before its first use (its arrival
-   * flags are back at zero when a launch ends); launches sharing it must be stream-ordered. */
-  int k_splits; void* splitk_ws; int64_t splitk_ws_bytes;
 } wanb200_gemm_params;
 
 int wanb200_gemm_bf16(const wanb200_gemm_params* p, void* stream);
-/* Bytes of splitk_ws for this shape, tile width (0 = the library's) and k_splits (0 = the
- * library's choice, which may be no split: 0 bytes). */
-int64_t wanb200_gemm_splitk_workspace_bytes(int64_t M, int64_t N, int64_t K, int tile_n, int k_splits);
 
 /* ---------------------------------------------------------------- attention
  * o[b, i, h, :] = softmax_j(q[b,i,h,:] . k[b,j,h,:] * softmax_scale) v[b, j, h, :]
@@ -389,7 +378,7 @@ int wanb200_device_error(int reset);
  * be page-locked for the copy to be asynchronous.  Lets a step driver check every step at no
  * cost to the pipeline (the word is sticky, so a later read also reports an earlier expiry). */
 int wanb200_device_error_async(int* host_out, void* stream);
-/* Library version, e.g. 202 for 0.2.2. */
+/* Library version, e.g. 201 for 0.2.1. */
 int wanb200_version(void);
 /* sizeof of the parameter structs (gemm, attn, ln, qknorm, residual, shard_gather, attn_fp8, block,
  * patchify, unpatchify, sumsq_reduce)

@@ -26,7 +26,7 @@ def test_library_exports_every_declared_function():
     for n in names:
         assert hasattr(lib, n), n
     assert set(names) == set(L.EXPORTS)
-    assert lib.wanb200_version() == 202
+    assert lib.wanb200_version() == 201
 
 
 STRUCTS = {
@@ -102,18 +102,6 @@ def test_gemm_rejects_bad_shapes_on_host():
     p.epilogue, p.residual_f32, p.out_f32 = L.EPI_BIAS_SUMSQ, 0, 1
     rc, msg = _rc_msg(lib.wanb200_gemm_bf16, p)
     assert rc == -1 and "out_f32" in msg
-    p.epilogue, p.out_f32 = L.EPI_BIAS, 0
-    p.k_splits = 3  # more K ranges than the 2 K blocks
-    rc, msg = _rc_msg(lib.wanb200_gemm_bf16, p)
-    assert rc == -1 and "k_splits" in msg
-    p.k_splits = 2  # no workspace
-    rc, msg = _rc_msg(lib.wanb200_gemm_bf16, p)
-    assert rc == -1 and "splitk_ws" in msg
-    p.splitk_ws, p.splitk_ws_bytes = 256, 1024  # too small
-    rc, msg = _rc_msg(lib.wanb200_gemm_bf16, p)
-    assert rc == -1 and "splitk_ws" in msg
-    assert lib.wanb200_gemm_splitk_workspace_bytes(8, 64, 128, 64, 2) > 1024
-    assert lib.wanb200_gemm_splitk_workspace_bytes(8, 64, 128, 0, 1) == 0
 
 
 def test_attn_rejects_bad_args_on_host():

@@ -93,60 +93,6 @@ def test_gemm_tile_widths(tile_n):
     assert rel(ss, ref_parts) < 1e-3
 
 
-@pytest.mark.parametrize("epi,S", [("bias", 2), ("gelu", 3), ("gate_res_f32", 3), ("res", 4), ("sumsq", 2),
-                                   ("none", 3)])
-def test_gemm_split_k(epi, S):
-    """K cut into S ranges per tile: the last range's CTA adds the other ranges' fp32 partials
-    before the epilogue.  Ragged M and N; the same launch twice gives the same bits; the
-    workspace's arrival flags are back at zero after every launch (a second shape reuses it)."""
-    M, N, K = 300, 416, 640
-    Lx, nf = 150, 5
-    a, w, b = randn(M, K, seed=61), randn(N, K, scale=0.05, seed=62), randn(N, scale=0.1, seed=63)
-    kw, ref = {}, a.float() @ w.float().t() + b.float()
-    E = {"bias": L.EPI_BIAS, "gelu": L.EPI_BIAS_GELU, "gate_res_f32": L.EPI_BIAS_GATE_RES, "res": L.EPI_BIAS_RES,
-         "sumsq": L.EPI_BIAS_SUMSQ, "none": L.EPI_NONE}[epi]
-    if epi == "none":
-        b, ref = None, a.float() @ w.float().t()
-    if epi == "gelu":
-        ref = torch.nn.functional.gelu(ref, approximate="tanh")
-    if epi == "gate_res_f32":
-        res = torch.randn(M, N, device=DEV)
-        mod, e0 = randn(6, N, scale=0.1, seed=64), torch.randn(nf, 6, N, device=DEV) * 0.1
-        kw = dict(residual=res, gate=(mod[2], e0[:, 2, :]), frames=(Lx, Lx // nf), out=torch.empty(M, N, device=DEV))
-        g = (mod[2].float() + e0[:, 2, :]).repeat_interleave(Lx // nf, 0).repeat(M // Lx, 1)
-        ref = res + ref * g
-    if epi == "res":
-        res = randn(M, N, seed=65)
-        kw = dict(residual=res)
-        ref = res.float() + ref
-    if epi == "sumsq":
-        kw = dict(rowss=torch.empty(M, N // 32, device=DEV), ss_cols=N)
-    outs = [ops.linear(a, w, b, epilogue=E, k_splits=S, tile_n=128, **kw).clone() for _ in range(2)]
-    assert rel(outs[0], ref) < 4e-3
-    assert torch.equal(outs[0], outs[1])
-    if epi == "sumsq":
-        assert rel(kw["rowss"], ref.reshape(M, N // 32, 32).pow(2).sum(2)) < 1e-3
-    # the unsplit launch agrees to rounding (the split only reorders the fp32 sums)
-    one = ops.linear(a, w, b, epilogue=E, k_splits=1, tile_n=128, **kw)
-    assert rel(one, outs[0]) < 4e-3
-    # another shape through the same workspace
-    a2, w2 = randn(200, 256, seed=66), randn(192, 256, scale=0.05, seed=67)
-    o2 = ops.linear(a2, w2, None, epilogue=L.EPI_NONE, k_splits=4)
-    assert rel(o2, a2.float() @ w2.float().t()) < 4e-3
-
-
-def test_gemm_split_k_library_choice_on_shard_shapes():
-    """The library's split choice for the short-M shard GEMMs of 8-GPU sequence parallelism (and
-    none for the full-size shapes): results agree with the unsplit launch."""
-    lib = L.load()
-    assert lib.wanb200_gemm_splitk_workspace_bytes(15708, 3072, 3072, 0, 0) == 0
-    M, N, K = 1964, 3072, 14336
-    a, w, b = randn(M, K, seed=68), randn(N, K, scale=0.01, seed=69), randn(N, scale=0.1, seed=70)
-    auto = ops.linear(a, w, b, epilogue=L.EPI_BIAS, k_splits=0)
-    one = ops.linear(a, w, b, epilogue=L.EPI_BIAS, k_splits=1)
-    assert rel(auto, one) < 4e-3
-
-
 def test_gemm_gate_residual_on_a_sequence_shard():
     """rows_per_seq / row_offset: a [2, S] buffer holding tokens 40 .. 40+S-1 of each sequence."""
     Lx, nf, S, off = 180, 6, 70, 40

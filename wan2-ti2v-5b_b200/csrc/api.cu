@@ -162,10 +162,6 @@ int wanb200_qk_norm_rope(const wanb200_qknorm_params* p, void* stream) {
   return qk_norm_rope(p, reinterpret_cast<cudaStream_t>(stream));
 }
 
-int64_t wanb200_gemm_splitk_workspace_bytes(int64_t M, int64_t N, int64_t K, int tile_n, int k_splits) {
-  return gemm_splitk_workspace_bytes(M, N, K, tile_n, k_splits);
-}
-
 int wanb200_sumsq_reduce(const wanb200_sumsq_reduce_params* p, void* stream) {
   return sumsq_reduce(p, reinterpret_cast<cudaStream_t>(stream));
 }
@@ -225,7 +221,7 @@ int wanb200_device_error_async(int* host_out, void* stream) {
   return WANB200_OK;
 }
 
-int wanb200_version(void) { return 202; }
+int wanb200_version(void) { return 201; }
 
 int wanb200_struct_sizes(int64_t* out, int n) {
   const int64_t sizes[11] = {(int64_t)sizeof(wanb200_gemm_params), (int64_t)sizeof(wanb200_attn_params),

@@ -21,7 +21,6 @@ enum DevError : int {
   kErrTimeoutGemmProducer = 101,
   kErrTimeoutGemmMma = 102,
   kErrTimeoutGemmEpilogue = 103,
-  kErrTimeoutGemmSplitK = 104,
   kErrTimeoutAttnProducer = 201,
   kErrTimeoutAttnMma = 202,
   kErrTimeoutAttnSoftmax = 203,
@@ -105,32 +104,6 @@ __device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity, int* e
     if (globaltimer() - t0 > 100000000ull) {  // 100 ms
       atomicCAS(err, 0, kErrTimeoutDrain);
       return;
-    }
-  }
-}
-
-// Bounded spin of one thread until the int at p (written by other CTAs) reaches `target`, with
-// acquire semantics at GPU scope, so the data the writers published before their release is
-// visible to this warp after a __syncwarp.  false on expiry (error `code`, abort raised) or
-// when another role of the CTA already aborted.
-__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ bool flag_wait_geq(const int* p, int target, volatile int* abort, int* err, int code) {
-  if (ld_acquire_gpu(p) >= target) return true;
-  const unsigned long long t0 = globaltimer();
-  while (true) {
-#pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-      if (ld_acquire_gpu(p) >= target) return true;
-    if (*abort) return false;
-    if (globaltimer() - t0 > kWaitTimeoutNs) {
-      atomicCAS(err, 0, code);
-      *abort = 1;
-      return false;
     }
   }
 }

@@ -65,11 +65,6 @@ struct GemmArgs {
   int npeers, src_rank;
   int64_t shard_rows;
   int bn;  // tile width along N: multiple of 32, <= GBN
-  // split-K: every output tile's K range is cut into k_splits consecutive work units; the last
-  // one (the reducer) adds the others' fp32 partials in split order before its epilogue
-  int k_splits;
-  float* sk_part;  // [tiles, k_splits - 1, GBN / 32 chunks, GBM rows, 32] fp32
-  int* sk_flags;   // [tiles, G_EPI_WARPS] arrivals of the partial writers (zero between launches)
   int stages;             // TMA ring depth
   uint32_t stage_bytes;   // A tile + BN-wide W tile
   uint32_t tiles_bytes;   // stages * stage_bytes
@@ -276,20 +271,16 @@ __global__ void __launch_bounds__(G_THREADS, 1)
   const int num_m = (args.M + GBM - 1) / GBM;
   const int num_tiles = num_m * num_n;
   const int kblocks = args.K / GBK;
-  const int S = args.k_splits;  // 1 <= S <= kblocks (host)
-  const int num_units = num_tiles * S;
 
   if (warp == 0) {
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0, issued = 0, last_phase = 0;
       bool ok = true;
-      for (int unit = blockIdx.x; ok && unit < num_units; unit += gridDim.x) {
-        const int tile = unit / S, split = unit - tile * S;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
         int m0, n0;
         tile_origin(tile, num_m, num_n, bn, m0, n0);
-        const int kb1 = (split + 1) * kblocks / S;
-        for (int kb = split * kblocks / S; kb < kb1; ++kb) {
+        for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, abort_flag, err, kErrTimeoutGemmProducer)) {
             ok = false;
             break;
@@ -317,12 +308,11 @@ __global__ void __launch_bounds__(G_THREADS, 1)
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
-      for (int unit = blockIdx.x; ok && unit < num_units; unit += gridDim.x) {
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
         if (!mbar_wait(tempty0 + 8 * acc, acc_phase ^ 1, abort_flag, err, kErrTimeoutGemmMma)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * GBN;
-        const int split = unit % S, kb0 = split * kblocks / S, kb1 = (split + 1) * kblocks / S;
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(full0 + 8 * stage, phase, abort_flag, err, kErrTimeoutGemmMma)) {
             ok = false;
             break;
@@ -333,7 +323,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
 #pragma unroll
           for (int kk = 0; kk < GBK / 16; ++kk) {
             umma_bf16(d_tmem, sw128_desc(a_addr + kk * 32, 16, 1024), sw128_desc(b_addr + kk * 32, 16, 1024), idesc,
-                      (kb != kb0 || kk != 0));
+                      (kb | kk) != 0);
           }
           umma_commit(empty0 + 8 * stage);
           if (++stage == GSTAGES) {
@@ -356,36 +346,14 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     const int r = quad * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
-    bool ok = true;
-    for (int unit = blockIdx.x; ok && unit < num_units; unit += gridDim.x) {
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       if (!mbar_wait_warp(tfull0 + 8 * acc, acc_phase, abort_flag, err, kErrTimeoutGemmEpilogue)) break;
       tc_fence_after();
-      const int tile = unit / S, split = unit - tile * S;
       int m0, n0;
       tile_origin(tile, num_m, num_n, bn, m0, n0);
       const int row = m0 + r;
       const uint32_t t_row = tmem_base + (uint32_t(quad * 32) << 16) + acc * GBN;
-      // split-K partials of this tile: [split][chunk][tile row][32], each thread's 32 values of a
-      // chunk are 128 contiguous bytes and a warp's 32 rows one 4 KB block
-      float* const part_tile = args.sk_part + (int64_t)tile * (S - 1) * (GBN / 32) * (GBM * 32);
-      int* const flag = args.sk_flags + tile * G_EPI_WARPS + (warp - 2);
-      if (split < S - 1) {
-        // a partial: store the fp32 accumulator chunks of this warp, then count this warp in
-#pragma unroll 1
-        for (int c = half; c < bn / 32; c += 2) {
-          if (n0 + c * 32 >= args.N) break;  // warp-uniform
-          float v[32];
-          tmem_ld32(t_row + c * 32, v);
-          float4* dst = reinterpret_cast<float4*>(part_tile + (((int64_t)split * (GBN / 32) + c) * GBM + r) * 32);
-#pragma unroll
-          for (int q = 0; q < 8; ++q) __stcg(dst + q, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
-        }
-        __syncwarp();
-        if (lane == 0) {
-          __threadfence();  // release: the warp's partial is visible before the count
-          atomicAdd(flag, 1);
-        }
-      } else if constexpr (EPI == WANB200_EPI_SCATTER) {
+      if constexpr (EPI == WANB200_EPI_SCATTER) {
         // stage this warp's 32 rows (lane = row), then write each row as one 512-byte segment
         // (the first warp of each lane quarter does the whole tile; the second only arrives)
         constexpr int SR = GemmCfg<EPI>::STAGING_ROW;
@@ -411,18 +379,6 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         }
         __syncwarp();
       } else {
-        if (S > 1) {  // the reducer: wait until the other splits' warps on these rows and chunks wrote
-          bool got = true;
-          if (lane == 0) {
-            got = flag_wait_geq(flag, S - 1, abort_flag, err, kErrTimeoutGemmSplitK);
-            *flag = 0;  // re-armed for the next launch (stream order)
-          }
-          __syncwarp();  // orders the lanes' partial loads after lane 0's acquire
-          if (!__shfl_sync(0xffffffffu, got, 0)) {
-            ok = false;
-            break;
-          }
-        }
         uint4 res_next[8] = {}, res_cur[8];
         if constexpr (epi_has_residual(EPI)) load_residual_chunk(args, row, n0 + half * 32, res_next);
         // the gate row of this tile row's latent frame (once per tile, not per chunk)
@@ -444,19 +400,6 @@ __global__ void __launch_bounds__(G_THREADS, 1)
           }
           float v[32];
           tmem_ld32(t_row + c * 32, v);
-#pragma unroll 1
-          for (int sp = 0; sp < S - 1; ++sp) {  // this split's accumulator + the partials in split order
-            const float4* src =
-                reinterpret_cast<const float4*>(part_tile + (((int64_t)sp * (GBN / 32) + c) * GBM + r) * 32);
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              const float4 x = __ldcg(src + q);
-              v[4 * q] += x.x;
-              v[4 * q + 1] += x.y;
-              v[4 * q + 2] += x.z;
-              v[4 * q + 3] += x.w;
-            }
-          }
           gemm_epilogue_chunk<EPI>(args, v, row, col0, res_cur, gate_row);
         }
       }
@@ -494,70 +437,23 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmA
   return WANB200_OK;
 }
 
-// Tile width along N and split-K count for a launch: the candidate with the smallest makespan
-// rounds * (K blocks per unit + c0) * (BN + 64), rounds = ceil(tiles * splits / SMs) over the
-// persistent grid.  BN + 64 is a unit's cost per K block (the MMA work plus the A tile load
-// that does not shrink with BN), c0 the per-unit cost in K blocks (accumulator hand-off,
-// pipeline refill).  BN stays 256 unless a narrower tile removes a mostly empty last round;
-// K is split (the fp32 partials cost a write and a read in L2 per extra split) only when that
-// beats the best unsplit tiling by more than kSplitGain -- in practice for the short-M shard
-// GEMMs of the sequence-parallel layouts, whose 1.3-1.7 rounds of long-K tiles leave SMs idle.
-constexpr double kSplitC0 = 4.0, kSplitGain = 1.10;
-constexpr int kMaxSplits = 4;
-
-static void choose_tiling(int64_t M, int64_t N, int64_t K, int sms, int tile_n, int max_splits, int& bn_out,
-                          int& splits_out) {
-  const int64_t num_m = (M + GBM - 1) / GBM, kb = K / GBK;
-  double best1 = 1e300, best = 1e300;
-  int bn1 = GBN, bn_best = GBN, s_best = 1;
-  for (int bn = tile_n ? tile_n : GBN; bn >= (tile_n ? tile_n : 128); bn -= 32) {
+// Tile width along N for a launch: the candidate (multiples of 32 from 256 down to 128) with the
+// smallest makespan waves * (BN + c), waves = ceil(tiles / SMs) over the persistent grid.  c
+// stands for the per-tile cost that does not shrink with BN (the A tile loads, the accumulator
+// hand-off); it keeps BN at 256 unless a narrower tile removes a mostly empty last wave.
+static int choose_tile_n(int64_t M, int64_t N, int sms) {
+  const int64_t num_m = (M + GBM - 1) / GBM;
+  int best = GBN;
+  double best_t = 1e300;
+  for (int bn = GBN; bn >= 128; bn -= 32) {
     const int64_t tiles = num_m * ((N + bn - 1) / bn);
-    for (int sp = 1; sp <= std::min<int64_t>(max_splits, kb); ++sp) {
-      const int64_t rounds = (tiles * sp + sms - 1) / sms;
-      const double t = (double)rounds * ((double)((kb + sp - 1) / sp) + kSplitC0) * (bn + 64.0);
-      if (sp == 1 && t < best1 - 1e-9) {
-        best1 = t;
-        bn1 = bn;
-      }
-      if (t < best - 1e-9) {
-        best = t;
-        bn_best = bn;
-        s_best = sp;
-      }
+    const double t = (double)((tiles + sms - 1) / sms) * (bn + 64.0);
+    if (t < best_t - 1e-9) {
+      best_t = t;
+      best = bn;
     }
   }
-  if (s_best > 1 && best * kSplitGain < best1) {
-    bn_out = bn_best;
-    splits_out = s_best;
-  } else {
-    bn_out = bn1;
-    splits_out = 1;
-  }
-}
-
-// Split-K workspace: the arrival flags of every tile (one int per epilogue warp), then the
-// partials of the k_splits - 1 non-reducing units of every tile.
-static int64_t splitk_flag_bytes(int64_t tiles) { return (tiles * G_EPI_WARPS * 4 + 255) / 256 * 256; }
-static int64_t splitk_bytes(int64_t M, int64_t N, int bn, int splits) {
-  if (splits <= 1) return 0;
-  const int64_t tiles = ((M + GBM - 1) / GBM) * ((N + bn - 1) / bn);
-  return splitk_flag_bytes(tiles) + tiles * (splits - 1) * (int64_t)GBM * GBN * 4;
-}
-
-int64_t gemm_splitk_workspace_bytes(int64_t M, int64_t N, int64_t K, int tile_n, int k_splits) {
-  if (M <= 0 || N <= 0 || K <= 0 || K % GBK || tile_n < 0 || k_splits < 0) return 0;
-  int bn = 0, splits = 1;
-  if (k_splits == 0) {
-    choose_tiling(M, N, K, num_sms(), tile_n, kMaxSplits, bn, splits);
-  } else {
-    splits = (int)std::min<int64_t>(k_splits, K / GBK);
-    int unused = 1;
-    if (tile_n)
-      bn = tile_n;
-    else
-      choose_tiling(M, N, K, num_sms(), 0, 1, bn, unused);
-  }
-  return splitk_bytes(M, N, bn, splits);
+  return best;
 }
 
 int gemm_bf16(const wanb200_gemm_params* p, cudaStream_t st) {
@@ -606,26 +502,11 @@ int gemm_bf16(const wanb200_gemm_params* p, cudaStream_t st) {
     if (!p->rowss || p->ss_cols <= 0 || (p->ss_cols % 32) || p->ss_cols > p->N)
       return set_error(WANB200_EINVAL, "gemm: sumsq epilogue needs rowss and ss_cols, a multiple of 32 in 32..N");
   }
-  if (p->k_splits < 0 || p->k_splits > p->K / GBK || (scatter && p->k_splits > 1))
-    return set_error(WANB200_EINVAL, "gemm: k_splits must be in 0..K/64 (1 or 0 for the scatter epilogue)");
-  if (p->k_splits > 1 && (!p->splitk_ws || (reinterpret_cast<uintptr_t>(p->splitk_ws) & 255)))
-    return set_error(WANB200_EINVAL, "gemm: k_splits > 1 needs a 256-byte aligned splitk_ws");
 
-  const int sms = num_sms();
-  int bn = p->tile_n, splits = 1;
-  if (p->k_splits == 0 && p->splitk_ws && !scatter) {  // the library's choice, within the workspace given
-    choose_tiling(p->M, p->N, p->K, sms, p->tile_n, kMaxSplits, bn, splits);
-    if (splitk_bytes(p->M, p->N, bn, splits) > p->splitk_ws_bytes)
-      choose_tiling(p->M, p->N, p->K, sms, p->tile_n, 1, bn, splits);
-  } else {
-    int unused = 1;
-    if (!bn) choose_tiling(p->M, p->N, p->K, sms, 0, 1, bn, unused);
-    splits = p->k_splits > 1 ? p->k_splits : 1;
-    if (splitk_bytes(p->M, p->N, bn, splits) > p->splitk_ws_bytes)
-      return set_error(WANB200_EINVAL, "gemm: splitk_ws is smaller than wanb200_gemm_splitk_workspace_bytes()");
-  }
   int* err = device_error_word();
   if (!err) return WANB200_ECUDA;
+  const int sms = num_sms();
+  const int bn = p->tile_n ? p->tile_n : choose_tile_n(p->M, p->N, sms);
   CUtensorMap ta, tb;
   int rc = make_tmap_2d(&ta, p->a, p->K, p->M, p->lda, GBK, GBM);
   if (rc) return rc;
@@ -658,13 +539,6 @@ int gemm_bf16(const wanb200_gemm_params* p, cudaStream_t st) {
   ga.src_rank = p->src_rank;
   ga.shard_rows = p->shard_rows > 0 ? p->shard_rows : 1;
   ga.bn = bn;
-  ga.k_splits = splits;
-  {
-    const int64_t tiles = ((p->M + GBM - 1) / GBM) * ((p->N + bn - 1) / bn);
-    uint8_t* ws = static_cast<uint8_t*>(p->splitk_ws);
-    ga.sk_flags = splits > 1 ? reinterpret_cast<int*>(ws) : nullptr;
-    ga.sk_part = splits > 1 ? reinterpret_cast<float*>(ws + splitk_flag_bytes(tiles)) : nullptr;
-  }
   ga.stage_bytes = (uint32_t)(G_A_BYTES + bn * GBK * 2);
   {
     const int fixed = scatter ? GemmCfg<WANB200_EPI_SCATTER>::FIXED : GemmCfg<WANB200_EPI_NONE>::FIXED;
@@ -673,9 +547,8 @@ int gemm_bf16(const wanb200_gemm_params* p, cudaStream_t st) {
   ga.tiles_bytes = (uint32_t)ga.stages * ga.stage_bytes;
   ga.err = err;
 
-  const int64_t units = ((p->M + GBM - 1) / GBM) * ((p->N + bn - 1) / bn) * splits;
-  if (units > INT32_MAX) return set_error(WANB200_EINVAL, "gemm: too many tiles");
-  const int grid = (int)std::min<int64_t>(units, sms);
+  const int64_t tiles = ((p->M + GBM - 1) / GBM) * ((p->N + bn - 1) / bn);
+  const int grid = (int)std::min<int64_t>(tiles, sms);
   switch (epi) {
     case WANB200_EPI_NONE: return launch_gemm<WANB200_EPI_NONE>(ta, tb, ga, grid, st);
     case WANB200_EPI_BIAS: return launch_gemm<WANB200_EPI_BIAS>(ta, tb, ga, grid, st);

@@ -38,7 +38,6 @@ int make_tmap_4d_u8(CUtensorMap* m, const void* base, const int64_t dims[4], con
 
 // Launchers (one per public entry point).
 int gemm_bf16(const wanb200_gemm_params* p, cudaStream_t st);
-int64_t gemm_splitk_workspace_bytes(int64_t M, int64_t N, int64_t K, int tile_n, int k_splits);
 int attn_fwd(const wanb200_attn_params* p, cudaStream_t st);
 // e4m3 operands of the attention (quantised by attn_fwd_fp8)
 struct AttnFp8Operands {

@@ -27,8 +27,7 @@ class GemmParams(ctypes.Structure):
                 ("gate_e0", c_void_p), ("gate_frame_stride", c_int64), ("seq_len", c_int64),
                 ("tokens_per_frame", c_int64), ("row_offset", c_int64), ("rows_per_seq", c_int64), ("rowss", c_void_p),
                 ("ss_cols", c_int64), ("peer_out", c_void_p * 8), ("npeers", c_int), ("src_rank", c_int),
-                ("shard_rows", c_int64), ("tile_n", c_int), ("residual_f32", c_int), ("out_f32", c_int),
-                ("k_splits", c_int), ("splitk_ws", c_void_p), ("splitk_ws_bytes", c_int64)]
+                ("shard_rows", c_int64), ("tile_n", c_int), ("residual_f32", c_int), ("out_f32", c_int)]
 
 
 class AttnParams(ctypes.Structure):
@@ -119,8 +118,7 @@ EXPORTS = ("wanb200_gemm_bf16", "wanb200_attn_fwd", "wanb200_layernorm", "wanb20
            "wanb200_struct_sizes", "wanb200_peer_barrier", "wanb200_attn_workspace_bytes",
            "wanb200_attn_kv_splits", "wanb200_attn_fwd_noalloc", "wanb200_shard_gather", "wanb200_attn_fwd_fp8",
            "wanb200_attn_fp8_workspace_bytes", "wanb200_device_error_async", "wanb200_block_forward",
-           "wanb200_block_workspace_bytes", "wanb200_patchify", "wanb200_unpatchify_cfg", "wanb200_sumsq_reduce",
-           "wanb200_gemm_splitk_workspace_bytes")
+           "wanb200_block_workspace_bytes", "wanb200_patchify", "wanb200_unpatchify_cfg", "wanb200_sumsq_reduce")
 
 _lock = threading.Lock()
 _lib = None
@@ -179,8 +177,6 @@ def load():
             lib.wanb200_patchify.restype = c_int
             lib.wanb200_unpatchify_cfg.argtypes = [ctypes.POINTER(UnpatchifyParams), c_void_p]
             lib.wanb200_unpatchify_cfg.restype = c_int
-            lib.wanb200_gemm_splitk_workspace_bytes.argtypes = [c_int64, c_int64, c_int64, c_int, c_int]
-            lib.wanb200_gemm_splitk_workspace_bytes.restype = c_int64
             lib.wanb200_sumsq_reduce.argtypes = [ctypes.POINTER(SumsqReduceParams), c_void_p]
             lib.wanb200_sumsq_reduce.restype = c_int
             structs = (GemmParams, AttnParams, LnParams, QkNormParams, ResidualParams, ShardGatherParams,

@@ -56,10 +56,9 @@ def bench_gemm(a):
     if epi == L.EPI_BIAS_SUMSQ:
         kw["rowss"] = torch.empty(a.M, 2 * (a.N // 3) // 32, device=dev)  # q and k chunk partials
         kw["ss_cols"] = 2 * (a.N // 3)
-    ms = _time(lambda: ops.linear(x, w, b if epi else None, epilogue=epi, out=out, tile_n=a.tile_n,
-                                  k_splits=a.k_splits, **kw), a.iters)
+    ms = _time(lambda: ops.linear(x, w, b if epi else None, epilogue=epi, out=out, tile_n=a.tile_n, **kw), a.iters)
     return {"kernel": "gemm", "M": a.M, "N": a.N, "K": a.K, "epi": a.epi, "f32_residual": a.f32,
-            "tile_n": a.tile_n, "k_splits": a.k_splits, "ms": ms,
+            "tile_n": a.tile_n, "ms": ms,
             "tflops": 2 * a.M * a.N * a.K / ms / 1e9}
 
 
@@ -120,7 +119,6 @@ def main():
     ap.add_argument("--Lk", type=int, default=7854)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--tile-n", type=int, default=0, help="gemm tile width along N (0 = the library's choice)")
-    ap.add_argument("--k-splits", type=int, default=0, help="gemm split-K ranges per tile (0 = the library's choice)")
     ap.add_argument("--fp8", action="store_true", help="attn: the e4m3 variant (quantisation included in the time)")
     ap.add_argument("--f32", action="store_true", help="gemm residual epilogues / ln: the fp32 residual stream")
     a = ap.parse_args()

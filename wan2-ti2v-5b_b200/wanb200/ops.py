@@ -111,26 +111,11 @@ def _rows(t: torch.Tensor, name: str):
 
 
 # ---------------------------------------------------------------------------- GEMM
-_SPLITK_WS = {}
-
-
-def _splitk_workspace(device, nbytes):
-    """The device's split-K workspace: zero-filled once (the kernels leave its arrival flags at
-    zero), grown when a launch needs more; shared by the stream-ordered GEMMs of the device."""
-    key = str(device)
-    ws = _SPLITK_WS.get(key)
-    if ws is None or ws.numel() < nbytes:
-        ws = _SPLITK_WS[key] = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
-    return ws
-
-
 def linear(a, w, bias=None, *, epilogue=L.EPI_BIAS, out=None, residual=None, gate=None, frames=None,
-           rowss=None, ss_cols=0, kind="gemm", scatter=None, tile_n=0, k_splits=0):
+           rowss=None, ss_cols=0, kind="gemm", scatter=None, tile_n=0):
     """out[M, N] = epilogue(a[M, K] @ w[N, K]^T) on tcgen05 (see include/wanb200.h).
 
     tile_n: width of the output tile along N (0 = the library's choice; 64..256, multiple of 32).
-    k_splits: K ranges per output tile (0 = the library's choice, 1 = none); a split launch gets
-    the device's split-K workspace.
 
     gate: (gate_mod [N] bf16, gate_e0 [F, N] fp32 view with unit column stride) for EPI_BIAS_GATE_RES.
     frames: (seq_len, tokens_per_frame) mapping a row to its latent frame.
@@ -155,12 +140,6 @@ def linear(a, w, bias=None, *, epilogue=L.EPI_BIAS, out=None, residual=None, gat
     p.a, p.lda, p.w, p.ldw, p.d, p.ldd = _p(a), lda, _p(w), ldw, _p(out), ldd
     p.M, p.N, p.K, p.epilogue = M, N, K, epilogue
     p.tile_n = tile_n
-    p.k_splits = k_splits
-    if scatter is None and k_splits != 1:
-        need = L.load().wanb200_gemm_splitk_workspace_bytes(M, N, K, tile_n, k_splits)
-        if need > 0:
-            ws = _splitk_workspace(a.device, need)
-            p.splitk_ws, p.splitk_ws_bytes = ws.data_ptr(), ws.numel()
     p.bias = _p(bias)
     if residual is not None:
         p.residual, p.ldr = _p(residual), _rows(residual, "residual")
