@@ -198,12 +198,16 @@ int wanb200_layernorm(const wanb200_ln_params* p, void* stream);
  * (if rope) the interleaved-pair rotation with cos/sin[pos, pair], pos = row % seq_len,
  * pair = (c % 128) / 2.  `_tp_rms_qk` + `_rope` (fast_dit.py:134-147, 163-169) for self-attn
  * q and k (nsections 2); `_tp_rms` (fast_dit.py:156-160) for cross-attn q (nsections 1,
- * rope 0).  S(row) is the sum of squares over the global 3072 channels, given as ss_parts
- * partial sums per row and section: S = sum over k < ss_parts of ss[s][row * ss_row_stride + k]
- * (the SUMSQ GEMM's chunk partials on one GPU: ss_parts = width / 32, ss[s] pointing at the
- * section's first chunk), added in a fixed order (a warp butterfly per 32 partials, then the
- * warps in order); or ss_parts = 1 for finished sums (after wanb200_sumsq_reduce and the TP
- * all-reduce), ss_row_stride 1 for a packed [rows] array.
+ * rope 0).  S(row) is the sum of squares over the global 3072 channels:
+ *   ss[s] == NULL (every section): formed here from the section's own bf16 values, which then
+ *     hold the whole global dim (one GPU) -- the squares of the rounded values, as the
+ *     reference's `q.float().pow(2).sum(-1)`;
+ *   else ss_parts partial sums per row and section, S = sum over k < ss_parts of
+ *     ss[s][row * ss_row_stride + k] (a SUMSQ GEMM's chunk partials), or ss_parts = 1 for
+ *     finished sums (after wanb200_sumsq_reduce and the TP all-reduce), ss_row_stride 1 for a
+ *     packed [rows] array.
+ * Every sum is added in a fixed order (a warp butterfly, then the row's warps in order), so the
+ * results are bit-reproducible run to run.
  * Limits: width % 128 == 0, ld % 8 == 0, 1 <= ss_parts <= width / 8, ss_row_stride >= ss_parts. */
 typedef struct wanb200_qknorm_params {
   void* x; int64_t ld, rows;

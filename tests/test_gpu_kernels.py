@@ -276,10 +276,10 @@ def test_layernorm_small_dim():
     assert rel(h, torch.nn.functional.layer_norm(x.float(), (256,), wgt.float(), bia.float(), eps=1e-6)) < 4e-3
 
 
-@pytest.mark.parametrize("form", ["sums", "partials"])
+@pytest.mark.parametrize("form", ["sums", "partials", "self"])
 def test_qk_norm_rope_vs_oracle(form):
-    """The sums of squares as finished per-row sums (the TP path) or as the GEMM's 32-column
-    chunk partials that the kernel adds itself (one GPU)."""
+    """The sums of squares as finished per-row sums (the TP path), as a GEMM's 32-column chunk
+    partials, or formed by the kernel from the section's own bf16 values (one GPU)."""
     from oracle import dit_ref as R
     grid = (3, 5, 7)
     Lx = 105
@@ -289,18 +289,22 @@ def test_qk_norm_rope_vs_oracle(form):
     qkv = randn(M, 3 * Cl, seed=33)
     ref_in = qkv.float().clone()
     ss = torch.stack([ref_in[:, :Cl].pow(2).sum(1), ref_in[:, Cl:2 * Cl].pow(2).sum(1)]) * 8.0  # "global" dim 8x
+    gd = 8 * Cl
     if form == "sums":
         ssq, ssk = ss[0], ss[1]
+    elif form == "self":  # the section is the whole global dim
+        ssq = ssk = None
+        ss, gd = ss / 8.0, Cl
     else:
         parts = ref_in[:, :2 * Cl].reshape(M, 2 * Cl // 32, 32).pow(2).sum(2) * 8.0  # [M, 2P]
         ssq, ssk = parts[:, :Cl // 32], parts[:, Cl // 32:]
     gq, gk = randn(Cl, scale=0.1, seed=34).float().add(1).to(torch.bfloat16), randn(Cl, seed=35)
     cos, sin = R.rope_tables(R.model_freqs(128), grid, 128)
-    ops.qk_norm_rope(qkv, [(0, ssq, gq), (Cl, ssk, gk)], Cl, 8 * Cl, cos=cos.reshape(Lx, 64).to(DEV),
+    ops.qk_norm_rope(qkv, [(0, ssq, gq), (Cl, ssk, gk)], Cl, gd, cos=cos.reshape(Lx, 64).to(DEV),
                      sin=sin.reshape(Lx, 64).to(DEV), seq_len=Lx)
     for sec, g in ((0, gq), (1, gk)):
         x = ref_in[:, sec * Cl:(sec + 1) * Cl]
-        y = x * torch.rsqrt(ss[sec][:, None] / (8 * Cl) + 1e-6) * g.float()
+        y = x * torch.rsqrt(ss[sec][:, None] / gd + 1e-6) * g.float()
         y = R.rope(y.view(B, Lx, H, 128).cpu(), cos, sin).reshape(B * Lx, Cl)
         assert rel(qkv[:, sec * Cl:(sec + 1) * Cl].cpu(), y) < 4e-3
     assert torch.equal(qkv[:, 2 * Cl:], ref_in[:, 2 * Cl:].to(torch.bfloat16))

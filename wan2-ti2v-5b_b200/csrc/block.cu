@@ -3,12 +3,13 @@
 // block's launches on one stream with the library's own launchers, in the order of the Python
 // block op (wanb200/block.py):
 //    1  h   = LN1(x) * (1 + scale) + shift
-//    2  qkv = h W_qkv^T + b, Σq², Σk² per row and 32 columns [TP: reduce, all-reduce Σq², Σk²]
-//    3  q, k = RoPE(x * rsqrt(Σ/C + eps) * γ)                 in place
+//    2  qkv = h W_qkv^T + b                                 [TP: Σq², Σk² per row and 32 columns,
+//                                                              reduced, all-reduced]
+//    3  q, k = RoPE(x * rsqrt(Σ/C + eps) * γ)                 in place (one GPU: Σ formed here)
 //    4  y   = softmax(q k^T / sqrt(d)) v
 //    5  x1  = x + (y W_o^T + b_o) * gate2                     [TP: partial -> all-reduce -> residual pass]
 //    6  h   = LN3_affine(x1)
-//    7  qc  = h W_cq^T + b, Σqc²                             [TP: reduce, all-reduce Σ]
+//    7  qc  = h W_cq^T + b                                  [TP: Σqc² partials, reduce, all-reduce]
 //    8  qc  = qc * rsqrt(Σ/C + eps) * γ
 //    9  y   = attention(qc, ck, cv)
 //   10  x1 += y W_co^T + b_co                                 [TP: AR path]
@@ -47,8 +48,8 @@ BlockLayout block_layout(int64_t batch, int64_t seq_len, int64_t dim, int64_t lo
   off += up256(N * Cl * 2);
   l.f = off;
   off += up256(N * ffn_local * 2);
-  l.ss = off;  // Σx² chunk partials of q and k, [N, 2 Cl / 32] (the cross-q GEMM: [N, Cl / 32])
-  off += up256(2 * (Cl / 32) * N * 4);
+  l.ss = off;  // TP: Σx² chunk partials of q and k, [N, 2 Cl / 32] (the cross-q GEMM: [N, Cl / 32])
+  if (tp_size > 1) off += up256(2 * (Cl / 32) * N * 4);
   l.ssr = off;  // TP: the partials reduced per section, all-reduced in place
   if (tp_size > 1) off += up256(3 * N * 4);
   l.x1 = off;
@@ -232,9 +233,9 @@ int block_forward(const wanb200_block_params* p, cudaStream_t st) {
     return gemm_bf16(&g, st);
   };
 
-  // Σx² of `nsec` sections of Cl columns from the GEMM's chunk partials ([N, nsec * Cl / 32]): on
-  // one GPU the norm kernel adds them itself; under TP they are reduced per section into
-  // ssr + sec0 * N first and those sums all-reduced
+  // Σx² of `nsec` sections of Cl columns: on one GPU the norm kernel forms it from the bf16 values
+  // (ss NULL); under TP the SUMSQ GEMM's chunk partials ([N, nsec * Cl / 32]) are reduced per
+  // section into ssr + sec0 * N and those sums all-reduced
   auto sumsq_tp = [&](int nsec, int64_t sec0) -> int {
     if (!tp) return WANB200_OK;
     wanb200_sumsq_reduce_params r = {};
@@ -251,17 +252,17 @@ int block_forward(const wanb200_block_params* p, cudaStream_t st) {
     return rc2 ? rc2 : all_reduce(ssr + sec0 * N, nsec * N, 0);
   };
   auto set_ss = [&](wanb200_qknorm_params& q, int nsec, int64_t sec0) {
-    for (int s = 0; s < nsec; ++s) q.ss[s] = tp ? ssr + (sec0 + s) * N : ss + s * (Cl / 32);
-    q.ss_parts = tp ? 1 : (int)(Cl / 32);
-    q.ss_row_stride = tp ? 1 : nsec * (Cl / 32);
+    for (int s = 0; s < nsec; ++s) q.ss[s] = tp ? ssr + (sec0 + s) * N : nullptr;
+    q.ss_parts = 1;
+    q.ss_row_stride = 1;
   };
 
   // -- self-attention
   if ((rc = ln_mod(p->x, p->x_f32, 0, 1))) return rc;
   {
-    wanb200_gemm_params g = gemm(h, C, w.w_qkv, w.b_qkv, 3 * Cl, qkv, WANB200_EPI_BIAS_SUMSQ);
-    g.rowss = ss;
-    g.ss_cols = 2 * Cl;
+    wanb200_gemm_params g = gemm(h, C, w.w_qkv, w.b_qkv, 3 * Cl, qkv, tp ? WANB200_EPI_BIAS_SUMSQ : WANB200_EPI_BIAS);
+    g.rowss = tp ? ss : nullptr;
+    g.ss_cols = tp ? 2 * Cl : 0;
     if ((rc = gemm_bf16(&g, st))) return rc;
   }
   if ((rc = sumsq_tp(2, 0))) return rc;
@@ -305,9 +306,9 @@ int block_forward(const wanb200_block_params* p, cudaStream_t st) {
     if ((rc = layernorm(&q, st))) return rc;
   }
   {
-    wanb200_gemm_params g = gemm(h, C, w.w_cq, w.b_cq, Cl, cq, WANB200_EPI_BIAS_SUMSQ);
-    g.rowss = ss;
-    g.ss_cols = Cl;
+    wanb200_gemm_params g = gemm(h, C, w.w_cq, w.b_cq, Cl, cq, tp ? WANB200_EPI_BIAS_SUMSQ : WANB200_EPI_BIAS);
+    g.rowss = tp ? ss : nullptr;
+    g.ss_cols = tp ? Cl : 0;
     if ((rc = gemm_bf16(&g, st))) return rc;
   }
   if ((rc = sumsq_tp(1, 2))) return rc;

@@ -55,10 +55,10 @@ class Workspace:
         self.y = torch.empty(n_tok, local_dim, **kw)
         self.cq = torch.empty(n_tok, local_dim, **kw)
         self.f = torch.empty(n_tok, ffn_local, **kw)
-        # Σx² of q and k per row and 32 output columns (the SUMSQ GEMM's chunk partials, [rows, 2P];
-        # the cross-q GEMM writes [rows, P] into the same storage), and under TP the per-section
-        # sums all-reduced
-        self.ssp = torch.empty(n_tok * 2 * local_dim // 32, device=device, dtype=torch.float32)
+        # TP: Σx² of q and k per row and 32 output columns (the SUMSQ GEMM's chunk partials,
+        # [rows, 2P]; the cross-q GEMM writes [rows, P] into the same storage) and their
+        # per-section sums, all-reduced (one GPU: the norm kernel forms Σx² itself)
+        self.ssp = torch.empty(n_tok * 2 * local_dim // 32, device=device, dtype=torch.float32) if tp else None
         self.ss = torch.empty(3, n_tok, device=device, dtype=torch.float32) if tp else None
         self.part = torch.empty(n_tok, dim, **kw) if tp else None
 
@@ -108,15 +108,22 @@ class FastBlock:
         if self.tp:
             dist.all_reduce(t, group=self.tp_group)
 
+    def _qk_proj(self, a, wmat, bias, out, ws, nsec, kind):
+        """The projection ahead of a QK-norm (QKV: nsec 2, cross q: 1) and the Σx² operands of
+        qk_norm_rope for its nsec sections of local_dim columns: on one GPU None (the norm kernel
+        forms Σx² from the bf16 values, as `_tp_rms_qk` does, models/fast_dit.py:138-140); under TP
+        the GEMM's chunk partials reduced per section and all-reduced over the group (141, 159)."""
+        if not self.tp:
+            ops.linear(a, wmat, bias, epilogue=L.EPI_BIAS, out=out, kind=kind)
+            return [None] * nsec
+        ops.linear(a, wmat, bias, epilogue=L.EPI_BIAS_SUMSQ, out=out, rowss=self._partials(ws, nsec),
+                   ss_cols=nsec * self.w.local_dim, kind=kind)
+        return self._sumsq(ws, nsec, 0 if nsec == 2 else 2)
+
     def _sumsq(self, ws, nsec, sec0):
-        """The Σx² operands of qk_norm_rope for nsec sections of local_dim columns: on one GPU the
-        GEMM's chunk partials themselves (the norm kernel adds them in a fixed order); under TP the
-        partials reduced per section into ws.ss[sec0:] and all-reduced over the group
-        (`_tp_rms_qk` / `_tp_rms`, models/fast_dit.py:138-141, 158-159)."""
+        """TP: the partials of nsec sections reduced per section into ws.ss[sec0:] and all-reduced."""
         P = self.w.local_dim // 32
         part = self._partials(ws, nsec)
-        if not self.tp:
-            return [part[:, s * P:(s + 1) * P] for s in range(nsec)]
         out = ws.ss[sec0:sec0 + nsec]
         ops.sumsq_reduce(part, [s * P for s in range(nsec)], P, out)
         self._all_reduce(out)
@@ -182,9 +189,7 @@ class FastBlock:
 
         # -- self-attention
         ops.layernorm_modulate(xf, mod, e0, 0, 1, frames, out=ws.h, eps=self.eps)
-        ops.linear(ws.h, w.w_qkv, w.b_qkv, epilogue=L.EPI_BIAS_SUMSQ, out=ws.qkv, rowss=self._partials(ws, 2),
-                   ss_cols=2 * Cl, kind="gemm_qkv")
-        ssq, ssk = self._sumsq(ws, 2, 0)
+        ssq, ssk = self._qk_proj(ws.h, w.w_qkv, w.b_qkv, ws.qkv, ws, 2, "gemm_qkv")
         ops.qk_norm_rope(ws.qkv, [(0, ssq, w.g_q), (Cl, ssk, w.g_k)], Cl, C, eps=self.eps,
                          cos=cos2, sin=sin2, seq_len=Lx)
         q = ws.qkv[:, :Cl].view(B, Lx, nl, 128)
@@ -231,9 +236,7 @@ class FastBlock:
 
         # -- cross-attention (ck/cv cached per generation)
         ops.layernorm_affine(x1, w.ln3_w, w.ln3_b, out=ws.h, eps=self.eps)
-        ops.linear(ws.h, w.w_cq, w.b_cq, epilogue=L.EPI_BIAS_SUMSQ, out=ws.cq, rowss=self._partials(ws, 1),
-                   ss_cols=Cl, kind="gemm_cross_q")
-        (ssc,) = self._sumsq(ws, 1, 2)
+        (ssc,) = self._qk_proj(ws.h, w.w_cq, w.b_cq, ws.cq, ws, 1, "gemm_cross_q")
         ops.qk_norm_rope(ws.cq, [(0, ssc, w.g_cq)], Cl, C, eps=self.eps)
         ops.attention(ws.cq.view(B, Lx, nl, 128), ck, cv, out=ws.y.view(B, Lx, nl, 128), kind="attn_cross")
         if self.tp:
@@ -280,13 +283,16 @@ class FastCrossKV:
         B, Lc, C = context.shape
         N, Cl, nh = B * Lc, w.cross_dim, w.cross_heads
         ctx = context.reshape(N, C).to(BF16).contiguous()
-        ss = torch.empty(N, Cl // 32, device=context.device, dtype=torch.float32)  # Σk² chunk partials
-        kv = ops.linear(ctx, w.w_ckv, w.b_ckv, epilogue=L.EPI_BIAS_SUMSQ, rowss=ss, ss_cols=Cl, kind="gemm_cross_kv")
-        if w.tp_size > 1 and not w.local_cross:
-            ss_sum = torch.empty(N, device=context.device, dtype=torch.float32)
-            ops.sumsq_reduce(ss, [0], Cl // 32, ss_sum)
-            dist.all_reduce(ss_sum, group=self.tp_group)
-            ss = ss_sum
+        if w.tp_size > 1 and not w.local_cross:  # k's Σx² over the group: partials, reduce, all-reduce
+            part = torch.empty(N, Cl // 32, device=context.device, dtype=torch.float32)
+            kv = ops.linear(ctx, w.w_ckv, w.b_ckv, epilogue=L.EPI_BIAS_SUMSQ, rowss=part, ss_cols=Cl,
+                            kind="gemm_cross_kv")
+            ss = torch.empty(N, device=context.device, dtype=torch.float32)
+            ops.sumsq_reduce(part, [0], Cl // 32, ss)
+            dist.all_reduce(ss, group=self.tp_group)
+        else:  # the whole k row is here: the norm kernel forms its Σx²
+            kv = ops.linear(ctx, w.w_ckv, w.b_ckv, epilogue=L.EPI_BIAS, kind="gemm_cross_kv")
+            ss = None
         ops.qk_norm_rope(kv, [(0, ss, w.g_ck)], Cl, C, eps=self.eps)
         ck = kv[:, :Cl].view(B, Lc, nh, 128)
         cv = kv[:, Cl:].view(B, Lc, nh, 128)
@@ -312,7 +318,7 @@ class SPWorkspace:
         self.f = torch.empty(Np, ffn_local, **kw)
         self.ssp = torch.empty(Np, 2 * local_dim // 32, device=device, dtype=torch.float32)  # Σq², Σk² partials
         self.ss = torch.empty(2, Np, device=device, dtype=torch.float32)  # their sums, all-reduced
-        self.sscp = torch.empty(S, dim // 32, device=device, dtype=torch.float32)  # Σ(cross q)² partials
+
 
 
 _SPWS = {}
@@ -409,9 +415,8 @@ class FastBlockSP:
 
         # -- cross-attention on the shard, all heads, no collective
         ops.layernorm_affine(x1, w.ln3_w, w.ln3_b, out=ws.h_s, eps=self.eps)
-        ops.linear(ws.h_s, w.w_cq, w.b_cq, epilogue=L.EPI_BIAS_SUMSQ, out=ws.cq, rowss=ws.sscp, ss_cols=C,
-                   kind="gemm_cross_q")
-        ops.qk_norm_rope(ws.cq, [(0, ws.sscp, w.g_cq)], C, C, eps=self.eps)
+        ops.linear(ws.h_s, w.w_cq, w.b_cq, epilogue=L.EPI_BIAS, out=ws.cq, kind="gemm_cross_q")
+        ops.qk_norm_rope(ws.cq, [(0, None, w.g_cq)], C, C, eps=self.eps)  # all heads here: Σx² formed in the norm
         H = w.cross_heads
         ops.attention(ws.cq.view(1, S, H, 128), ck, cv, out=ws.yc.view(1, S, H, 128), kind="attn_cross")
         ops.linear(ws.yc, w.w_co, w.b_co, epilogue=L.EPI_BIAS_RES, out=x1, residual=x1, kind="gemm_cross_o")

@@ -88,8 +88,9 @@ def bench_ln(a):
 
 
 def bench_qknorm(a):
-    """q and k sections of a [M, 3C] QKV buffer normed and rotated in place, the sums of squares
-    given as the QKV GEMM's 32-column chunk partials (one GPU), B = 2 sequences of M / 2 tokens."""
+    """q and k sections of a [M, 3C] QKV buffer normed and rotated in place, B = 2 sequences of M / 2
+    tokens; the sums of squares formed by the kernel (--ss self, one GPU), or given as a GEMM's
+    32-column chunk partials or as finished sums (the TP path)."""
     dev = "cuda"
     C, M = a.C, a.M
     qkv = torch.randn(M, 3 * C, device=dev).to(torch.bfloat16)
@@ -99,10 +100,19 @@ def bench_qknorm(a):
     ang = torch.rand(Lx, 64, device=dev)
     cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
     P = C // 32
-    fn = lambda: ops.qk_norm_rope(qkv, [(0, part[:, :P], g), (C, part[:, P:], g)], C, C, cos=cos, sin=sin, seq_len=Lx)
+    if a.ss == "sums":  # finished per-row sums (the TP path, after the all-reduce)
+        ss = part[:, :2].t().contiguous()
+        fn = lambda: ops.qk_norm_rope(qkv, [(0, ss[0], g), (C, ss[1], g)], C, C, cos=cos, sin=sin, seq_len=Lx)
+        P = 1
+    elif a.ss == "self":
+        fn = lambda: ops.qk_norm_rope(qkv, [(0, None, g), (C, None, g)], C, C, cos=cos, sin=sin, seq_len=Lx)
+        P = 0
+    else:
+        fn = lambda: ops.qk_norm_rope(qkv, [(0, part[:, :P], g), (C, part[:, P:], g)], C, C, cos=cos, sin=sin,
+                                      seq_len=Lx)
     ms = _time(fn, a.iters)
     nbytes = 2 * (4 * M * C + 4 * M * P)
-    return {"kernel": "qk_norm_rope", "M": M, "C": C, "ms": ms, "gbs": nbytes / ms / 1e6}
+    return {"kernel": "qk_norm_rope", "M": M, "C": C, "ss": a.ss, "ms": ms, "gbs": nbytes / ms / 1e6}
 
 
 def main():
@@ -121,6 +131,7 @@ def main():
     ap.add_argument("--tile-n", type=int, default=0, help="gemm tile width along N (0 = the library's choice)")
     ap.add_argument("--fp8", action="store_true", help="attn: the e4m3 variant (quantisation included in the time)")
     ap.add_argument("--f32", action="store_true", help="gemm residual epilogues / ln: the fp32 residual stream")
+    ap.add_argument("--ss", default="self", choices=["self", "partials", "sums"], help="qknorm: where the sums of squares come from")
     a = ap.parse_args()
     torch.cuda.set_device(0)
     r = {"gemm": bench_gemm, "attn": bench_attn, "ln": bench_ln, "qknorm": bench_qknorm}[a.kind](a)

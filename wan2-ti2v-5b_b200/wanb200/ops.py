@@ -301,9 +301,10 @@ def qk_norm_rope(x, sections, width, global_dim, eps=1e-6, cos=None, sin=None, s
     """In place on x [M, ld]: for each (col0, ss, gamma [width] bf16) section,
     x[:, col0:col0+width] = RoPE(x * rsqrt(S/global_dim + eps) * gamma) (RoPE if cos given).
 
-    ss is either [M] fp32 (finished sums S, e.g. after the TP all-reduce) or an [M, P] fp32 view
-    with unit column stride: P partial sums per row (the SUMSQ GEMM's 32-column chunks, e.g. a
-    column slice of its [M, 2P] output) that the kernel adds in a fixed order.  Every section
+    ss is None (the kernel forms S from the section's own bf16 values: one GPU, the section is the
+    whole global dim), [M] fp32 (finished sums S, e.g. after the TP all-reduce) or an [M, P] fp32
+    view with unit column stride: P partial sums per row (the SUMSQ GEMM's 32-column chunks, e.g.
+    a column slice of its [M, 2P] output) that the kernel adds in a fixed order.  Every section
     takes the same form."""
     _cuda(x, cos, sin)
     ld = _rows(x, "x")
@@ -313,8 +314,10 @@ def qk_norm_rope(x, sections, width, global_dim, eps=1e-6, cos=None, sin=None, s
     forms = set()
     for i, (c0, ss, g) in enumerate(sections):
         _cuda(ss, g)
-        _need(ss.dtype == torch.float32 and g.dtype == BF16, "qk_norm_rope: ss fp32, gamma bf16")
-        if ss.dim() == 1:
+        _need(g.dtype == BF16 and (ss is None or ss.dtype == torch.float32), "qk_norm_rope: ss fp32, gamma bf16")
+        if ss is None:
+            forms.add((0, 0))
+        elif ss.dim() == 1:
             _need(ss.numel() >= M and ss.stride(0) == 1, "qk_norm_rope: ss must hold a sum per row")
             forms.add((1, 1))
         else:
@@ -323,12 +326,14 @@ def qk_norm_rope(x, sections, width, global_dim, eps=1e-6, cos=None, sin=None, s
         p.col0[i], p.ss[i], p.gamma[i] = c0, _p(ss), _p(g)
     _need(len(forms) == 1, "qk_norm_rope: every section's ss must have the same partial count and row stride")
     p.ss_parts, p.ss_row_stride = forms.pop()
+    if p.ss_parts == 0:
+        p.ss_parts = 1
     p.inv_dim, p.eps = 1.0 / global_dim, eps
     if cos is not None:
         _need(cos.dtype == torch.float32 and cos.is_contiguous() and sin.is_contiguous(), "qk_norm_rope: bad tables")
         p.rope, p.cos, p.sin, p.seq_len = 1, _p(cos), _p(sin), seq_len
     lib = L.load()
-    nbytes = 4.0 * M * width * len(sections) + 4.0 * M * p.ss_parts * len(sections)
+    nbytes = 4.0 * M * width * len(sections) + (0.0 if sections[0][1] is None else 4.0 * M * p.ss_parts * len(sections))
     L.check(_launch(x, "qk_norm_rope", nbytes, lambda: lib.wanb200_qk_norm_rope(ctypes.byref(p), _stream(x))),
             "wanb200_qk_norm_rope")
     return x
