@@ -208,7 +208,7 @@ int wanb200_layernorm(const wanb200_ln_params* p, void* stream);
  *     packed [rows] array.
  * Every sum is added in a fixed order (a warp butterfly, then the row's warps in order), so the
  * results are bit-reproducible run to run.
- * Limits: width % 128 == 0, ld % 8 == 0, 1 <= ss_parts <= width / 8, ss_row_stride >= ss_parts. */
+ * Limits: width % 128 == 0 (<= 4096), ld % 8 == 0, 1 <= ss_parts <= width / 8, ss_row_stride >= ss_parts. */
 typedef struct wanb200_qknorm_params {
   void* x; int64_t ld, rows;
   int nsections; int64_t col0[2]; int64_t width;

@@ -630,15 +630,7 @@ __global__ void __launch_bounds__(A_THREADS, 1)
 #pragma unroll
           for (int k = 0; k < 32; k += 2) {
             const float2 x = __ffma2_rn(make_float2(s[c * 32 + k], s[c * 32 + k + 1]), sl2v, negv);
-            float p0, p1;
-            if (k >= 24) {  // a quarter of the exponentials on the FMA pipe: the two tiles' softmax
-              const float2 e = exp2_fma2(x);  // phases overlap and would otherwise queue on MUFU
-              p0 = e.x;
-              p1 = e.y;
-            } else {
-              p0 = ex2_approx(x.x);
-              p1 = ex2_approx(x.y);
-            }
+            const float p0 = ex2_approx(x.x), p1 = ex2_approx(x.y);
             acc2[(k >> 1) & 1] = __fadd2_rn(acc2[(k >> 1) & 1], make_float2(p0, p1));
             pk[k >> 1] = pack_bf16x2(p0, p1);
           }

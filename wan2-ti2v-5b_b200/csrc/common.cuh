@@ -303,25 +303,6 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_byte
 }
 
 // ------------------------------------------------------------------ misc math
-// 2^x for a pair on the FMA pipe, to take part of the exponentials off MUFU: Cody-Waite range
-// reduction (x = i + f with i = round(x) by the 1.5 * 2^23 shifter, f in [-0.5, 0.5]), 2^f by a
-// degree-3 polynomial whose coefficients were fitted here to minimise the relative error on that
-// interval (at most 7.7e-5, far below the bf16 rounding of the probabilities it feeds), and 2^i
-// added to the exponent field.  x is clamped to [-125, 126], so -inf gives 2^-125 (~2e-38).
-__device__ __forceinline__ float2 exp2_fma2(float2 x) {
-  x.x = fminf(fmaxf(x.x, -125.f), 126.f);
-  x.y = fminf(fmaxf(x.y, -125.f), 126.f);
-  const float2 sh = make_float2(12582912.f, 12582912.f), nsh = make_float2(-12582912.f, -12582912.f);
-  const float2 t = __fadd2_rn(x, sh);
-  const float2 f = __ffma2_rn(__fadd2_rn(t, nsh), make_float2(-1.f, -1.f), x);  // x - round(x)
-  float2 p = __ffma2_rn(make_float2(0.05518098175525665f, 0.05518098175525665f), f,
-                        make_float2(0.2426345944404602f, 0.2426345944404602f));
-  p = __ffma2_rn(p, f, make_float2(0.6932613253593445f, 0.6932613253593445f));
-  p = __ffma2_rn(p, f, make_float2(0.9999262094497681f, 0.9999262094497681f));
-  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
-                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
-}
-
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

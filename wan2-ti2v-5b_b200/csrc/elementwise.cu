@@ -276,104 +276,101 @@ struct QkArgs {
   int seq_len;
 };
 
-// Thread (x, y) = 8 consecutive channels (4 rotation pairs) x of row blockIdx.x * blockDim.y + y
-// in each of the NSEC sections (q and k of self-attention, cross q alone): 2-D blocks so that a
-// thread finds its row without integer division, and both sections' 16-byte loads of a row in
-// flight together, sharing the row's rotation angles.
-// `_tp_rms_qk` (models/fast_dit.py:134-147): x * rsqrt(ss/3072 + eps) * gamma, then `_rope`
-// (fast_dit.py:163-169): (x0, x1) -> (x0 c - x1 s, x0 s + x1 c) with the pair's angle.
-// The row's sum of squares is either formed here from the section's own bf16 values (ss[s] ==
-// NULL: the whole global dim is in the section, one GPU; the squares of the rounded values, as
-// `q.float().pow(2).sum(-1)` does) or arrives as ss_parts partial sums per section (the SUMSQ
-// GEMM's 32-column chunks, contiguous per row: thread x < ss_parts loads partial x), or as one
-// finished sum.  A warp adds its values by a butterfly and the row's warps are added in order
-// through shared memory -- the same order on every run.
-template <int NSEC>
-__global__ void __launch_bounds__(1024) qknorm_rope_kernel(const QkArgs a) {
-  // [section][row of the block * warps per row + warp]: row_block() gives at most 32 warps per block
-  __shared__ float red[NSEC][32];
-  const int wpr = (int)(blockDim.x >> 5), slot0 = threadIdx.y * wpr;
+// One warp per row: lane l holds the 16-byte vectors l, l + 32, ... (NV of them, 8 channels = 4
+// rotation pairs each) of each of the NSEC sections (q and k of self-attention, cross q alone),
+// so a row's loads are all in flight at once and its sum of squares is a warp butterfly -- no
+// block barrier.  `_tp_rms_qk` (models/fast_dit.py:134-147): x * rsqrt(ss/3072 + eps) * gamma,
+// then `_rope` (fast_dit.py:163-169): (x0, x1) -> (x0 c - x1 s, x0 s + x1 c) with the pair's
+// angle.  The sum of squares is either formed from the section's own bf16 values (ss[s] == NULL:
+// the section is the whole global dim, one GPU; the squares of the rounded values, as
+// `q.float().pow(2).sum(-1)`), or added from ss_parts partials per row (a SUMSQ GEMM's 32-column
+// chunks), or read as one finished sum; each lane adds its share in order, then the butterfly --
+// the same order on every run.
+template <int NSEC, int NV>
+__global__ void __launch_bounds__(256) qknorm_rope_kernel(const QkArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= a.rows) return;  // warp-uniform
   const int vpr = a.width >> 3;
-  const int row = blockIdx.x * blockDim.y + threadIdx.y;
-  const bool live_row = row < a.rows, active = live_row && (int)threadIdx.x < vpr;
-  const int cv = threadIdx.x * 8;
-  uint4* p[NSEC];
-  uint4 raw[NSEC];
+  uint4 raw[NSEC][NV];
 #pragma unroll
   for (int s = 0; s < NSEC; ++s) {
-    p[s] = reinterpret_cast<uint4*>(a.x + (int64_t)row * a.ld + a.col0[s] + cv);
-    raw[s] = active ? *p[s] : make_uint4(0u, 0u, 0u, 0u);
+    const uint4* xr = reinterpret_cast<const uint4*>(a.x + (int64_t)row * a.ld + a.col0[s]);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int v = i * 32 + lane;
+      raw[s][i] = v < vpr ? xr[v] : make_uint4(0u, 0u, 0u, 0u);
+    }
   }
   float sum[NSEC];
-  if (a.self_ss) {  // grid-uniform
-#pragma unroll
-    for (int s = 0; s < NSEC; ++s) {
-      float v[8], q = 0.f;
-      unpack_bf16x8(raw[s], v);  // zeros for the threads past the row's width
-#pragma unroll
-      for (int k = 0; k < 8; ++k) q = fmaf(v[k], v[k], q);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
-      if ((threadIdx.x & 31) == 0) red[s][slot0 + (threadIdx.x >> 5)] = q;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int s = 0; s < NSEC; ++s) {
-      sum[s] = red[s][slot0];
-      for (int w = 1; w < wpr; ++w) sum[s] += red[s][slot0 + w];
-    }
-  } else if (a.ss_parts == 1) {  // grid-uniform
-#pragma unroll
-    for (int s = 0; s < NSEC; ++s) sum[s] = live_row ? __ldg(a.ss[s] + (int64_t)row * a.ss_row_stride) : 0.f;
-  } else {
-    const bool ld = live_row && (int)threadIdx.x < a.ss_parts;
-    float part[NSEC];
-#pragma unroll
-    for (int s = 0; s < NSEC; ++s) part[s] = ld ? __ldg(a.ss[s] + (int64_t)row * a.ss_row_stride + threadIdx.x) : 0.f;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-      for (int s = 0; s < NSEC; ++s) part[s] += __shfl_xor_sync(0xffffffffu, part[s], o);
-    const int nw = (a.ss_parts + 31) >> 5;
-    if ((threadIdx.x & 31) == 0 && (int)(threadIdx.x >> 5) < nw)
-#pragma unroll
-      for (int s = 0; s < NSEC; ++s) red[s][slot0 + (threadIdx.x >> 5)] = part[s];
-    __syncthreads();
-#pragma unroll
-    for (int s = 0; s < NSEC; ++s) {
-      sum[s] = red[s][slot0];
-      for (int w = 1; w < nw; ++w) sum[s] += red[s][slot0 + w];
-    }
-  }
-  if (!active) return;
-  float4 c4 = make_float4(1.f, 1.f, 1.f, 1.f), s4 = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (a.rope) {
-    const int pos = row % a.seq_len;
-    const int pair0 = (cv & 127) >> 1;
-    c4 = __ldg(reinterpret_cast<const float4*>(a.cos + (int64_t)pos * 64 + pair0));
-    s4 = __ldg(reinterpret_cast<const float4*>(a.sin + (int64_t)pos * 64 + pair0));
-  }
 #pragma unroll
   for (int s = 0; s < NSEC; ++s) {
-    float v[8], g[8];
-    unpack_bf16x8(raw[s], v);
-    unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.gamma[s] + cv)), g);
-    const float rs = rsqrtf(sum[s] * a.inv_dim + a.eps);
+    float q = 0.f;
+    if (a.self_ss) {  // grid-uniform branches
 #pragma unroll
-    for (int k = 0; k < 8; ++k) v[k] *= rs * g[k];
-    if (a.rope) {
-      float x0, x1;
-      x0 = v[0]; x1 = v[1]; v[0] = x0 * c4.x - x1 * s4.x; v[1] = x0 * s4.x + x1 * c4.x;
-      x0 = v[2]; x1 = v[3]; v[2] = x0 * c4.y - x1 * s4.y; v[3] = x0 * s4.y + x1 * c4.y;
-      x0 = v[4]; x1 = v[5]; v[4] = x0 * c4.z - x1 * s4.z; v[5] = x0 * s4.z + x1 * c4.z;
-      x0 = v[6]; x1 = v[7]; v[6] = x0 * c4.w - x1 * s4.w; v[7] = x0 * s4.w + x1 * c4.w;
+      for (int i = 0; i < NV; ++i) {
+        float v[8];
+        unpack_bf16x8(raw[s][i], v);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) q = fmaf(v[k], v[k], q);
+      }
+    } else if (a.ss_parts > 1) {
+      for (int k = lane; k < a.ss_parts; k += 32) q += __ldg(a.ss[s] + (int64_t)row * a.ss_row_stride + k);
+    } else if (lane == 0) {
+      q = __ldg(a.ss[s] + (int64_t)row * a.ss_row_stride);
     }
-    uint4 u;
-    u.x = pack_bf16x2(v[0], v[1]);
-    u.y = pack_bf16x2(v[2], v[3]);
-    u.z = pack_bf16x2(v[4], v[5]);
-    u.w = pack_bf16x2(v[6], v[7]);
-    *p[s] = u;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+    sum[s] = q;
+  }
+  const int pos = a.rope ? row % a.seq_len : 0;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int v = i * 32 + lane;
+    if (v >= vpr) break;
+    const int cv = v * 8;
+    float4 c4 = make_float4(1.f, 1.f, 1.f, 1.f), s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (a.rope) {
+      const int pair0 = (cv & 127) >> 1;
+      c4 = __ldg(reinterpret_cast<const float4*>(a.cos + (int64_t)pos * 64 + pair0));
+      s4 = __ldg(reinterpret_cast<const float4*>(a.sin + (int64_t)pos * 64 + pair0));
+    }
+#pragma unroll
+    for (int s = 0; s < NSEC; ++s) {
+      float x[8], g[8];
+      unpack_bf16x8(raw[s][i], x);
+      unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.gamma[s] + cv)), g);
+      const float rs = rsqrtf(sum[s] * a.inv_dim + a.eps);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) x[k] *= rs * g[k];
+      if (a.rope) {
+        float x0, x1;
+        x0 = x[0]; x1 = x[1]; x[0] = x0 * c4.x - x1 * s4.x; x[1] = x0 * s4.x + x1 * c4.x;
+        x0 = x[2]; x1 = x[3]; x[2] = x0 * c4.y - x1 * s4.y; x[3] = x0 * s4.y + x1 * c4.y;
+        x0 = x[4]; x1 = x[5]; x[4] = x0 * c4.z - x1 * s4.z; x[5] = x0 * s4.z + x1 * c4.z;
+        x0 = x[6]; x1 = x[7]; x[6] = x0 * c4.w - x1 * s4.w; x[7] = x0 * s4.w + x1 * c4.w;
+      }
+      uint4 u;
+      u.x = pack_bf16x2(x[0], x[1]);
+      u.y = pack_bf16x2(x[2], x[3]);
+      u.z = pack_bf16x2(x[4], x[5]);
+      u.w = pack_bf16x2(x[6], x[7]);
+      reinterpret_cast<uint4*>(a.x + (int64_t)row * a.ld + a.col0[s])[v] = u;
+    }
+  }
+}
+
+template <int NSEC>
+static void launch_qknorm(const QkArgs& a, int nv, unsigned blocks, cudaStream_t st) {
+  switch (nv) {
+    case 1: qknorm_rope_kernel<NSEC, 1><<<blocks, 256, 0, st>>>(a); break;
+    case 2: qknorm_rope_kernel<NSEC, 2><<<blocks, 256, 0, st>>>(a); break;
+    case 3: qknorm_rope_kernel<NSEC, 3><<<blocks, 256, 0, st>>>(a); break;
+    case 4: qknorm_rope_kernel<NSEC, 4><<<blocks, 256, 0, st>>>(a); break;
+    case 6: qknorm_rope_kernel<NSEC, 6><<<blocks, 256, 0, st>>>(a); break;
+    case 8: qknorm_rope_kernel<NSEC, 8><<<blocks, 256, 0, st>>>(a); break;
+    case 12: qknorm_rope_kernel<NSEC, 12><<<blocks, 256, 0, st>>>(a); break;
+    default: qknorm_rope_kernel<NSEC, 16><<<blocks, 256, 0, st>>>(a); break;
   }
 }
 
@@ -409,8 +406,8 @@ int qk_norm_rope(const wanb200_qknorm_params* p, cudaStream_t st) {
   a.self_ss = p->ss[0] == nullptr;
   a.ss_parts = p->ss_parts > 0 ? p->ss_parts : 1;
   a.ss_row_stride = p->ss_row_stride > 0 ? p->ss_row_stride : 1;
-  if (a.ss_parts > p->width / 8 || a.ss_parts > 256 || a.ss_row_stride < a.ss_parts)
-    return set_error(WANB200_EINVAL, "qk_norm_rope: ss_parts must be <= width / 8 (<= 256) and <= ss_row_stride");
+  if (a.ss_parts > p->width / 8 || a.ss_row_stride < a.ss_parts)
+    return set_error(WANB200_EINVAL, "qk_norm_rope: ss_parts must be <= width / 8 and <= ss_row_stride");
   a.gamma[0] = reinterpret_cast<const __nv_bfloat16*>(p->gamma[0]);
   a.gamma[1] = reinterpret_cast<const __nv_bfloat16*>(p->gamma[1]);
   a.inv_dim = p->inv_dim;
@@ -420,14 +417,16 @@ int qk_norm_rope(const wanb200_qknorm_params* p, cudaStream_t st) {
   a.sin = p->sin;
   if (p->seq_len > INT32_MAX) return set_error(WANB200_EINVAL, "qk_norm_rope: seq_len too large");
   a.seq_len = p->seq_len > 0 ? (int)p->seq_len : 1;
-  if (p->rows > INT32_MAX / 2 || p->width / 8 > 1024)
-    return set_error(WANB200_EINVAL, "qk_norm_rope: rows < 2^30, width <= 8192");
-  const dim3 blk = row_block(p->width / 8);
-  const int64_t blocks = (p->rows + blk.y - 1) / blk.y;
+  if (p->rows > INT32_MAX / 2 || p->width > 4096)
+    return set_error(WANB200_EINVAL, "qk_norm_rope: rows < 2^30, width <= 4096");
+  // vectors per lane, rounded up to an instantiated count
+  int nv = (int)((p->width / 8 + 31) / 32);
+  nv = nv <= 4 ? nv : nv <= 6 ? 6 : nv <= 8 ? 8 : nv <= 12 ? 12 : 16;
+  const unsigned blocks = (unsigned)((p->rows + 7) / 8);  // 8 rows (warps) per block
   if (p->nsections == 2)
-    qknorm_rope_kernel<2><<<(unsigned)blocks, blk, 0, st>>>(a);
+    launch_qknorm<2>(a, nv, blocks, st);
   else
-    qknorm_rope_kernel<1><<<(unsigned)blocks, blk, 0, st>>>(a);
+    launch_qknorm<1>(a, nv, blocks, st);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error("qknorm_rope_kernel launch", e);
   return WANB200_OK;
