@@ -85,8 +85,12 @@ struct GatherArgs {
 
 // One warp per (row, destination): blockIdx.y picks the destination, the warp's row is one of
 // the batch * valid_rows rows of the shard.  Lanes move consecutive 16-byte vectors, so every
-// store instruction of the warp writes 512 contiguous bytes of the peer's row.
-__global__ void __launch_bounds__(256) shard_gather_kernel(const GatherArgs a) {
+// store instruction of the warp writes 512 contiguous bytes of the peer's row.  At most 40
+// registers a thread (launch bounds of 6 CTAs of 256 threads per SM): the push runs on a side
+// stream while the local attention holds every SM with one CTA of 320 threads x 168 registers,
+// and at 48 registers a 256-thread push CTA did not fit in the 11776 registers left beside it,
+// so the push only started when the attention's CTAs exited.
+__global__ void __launch_bounds__(256, 6) shard_gather_kernel(const GatherArgs a) {
   const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   if (r >= a.rows) return;
   const int lane = threadIdx.x & 31;

@@ -69,9 +69,21 @@ def bench_attn(a):
     k = torch.randn(a.B, a.Lk, a.H, 128, generator=g, device=dev).to(torch.bfloat16)
     v = torch.randn(a.B, a.Lk, a.H, 128, generator=g, device=dev).to(torch.bfloat16)
     o = torch.empty_like(q)
-    ms = _time(lambda: ops.attention(q, k, v, out=o, fp8=a.fp8), a.iters)
-    return {"kernel": "attn_fp8" if a.fp8 else "attn", "B": a.B, "H": a.H, "Lq": a.Lq, "Lk": a.Lk, "ms": ms,
-            "tflops": 4 * a.B * a.H * a.Lq * a.Lk * 128 / ms / 1e9}
+    if a.local:  # the Q-local SP pattern: the shard's own a.local keys, then the rest, merged
+        n_rem = a.Lk - a.local
+        s_loc = a.kv_splits or ops.kv_splits(a.B, a.H, a.Lq, a.local)
+        s_rem = a.kv_splits_rem or ops.kv_splits(a.B, a.H, a.Lq, n_rem)
+        n = s_loc + s_rem
+
+        def fn():
+            ops.attention(q, k[:, :a.local], v[:, :a.local], out=o, kv_splits=s_loc, parts=(0, n, True))
+            ops.attention(q, k[:, a.local:], v[:, a.local:], out=o, kv_splits=s_rem, parts=(s_loc, n, False))
+        ms = _time(fn, a.iters)
+        return {"kernel": "attn_sp", "B": a.B, "H": a.H, "Lq": a.Lq, "Lk": a.Lk, "local": a.local, "s_loc": s_loc,
+                "s_rem": s_rem, "ms": ms, "tflops": 4 * a.B * a.H * a.Lq * a.Lk * 128 / ms / 1e9}
+    ms = _time(lambda: ops.attention(q, k, v, out=o, fp8=a.fp8, kv_splits=a.kv_splits or None), a.iters)
+    return {"kernel": "attn_fp8" if a.fp8 else "attn", "B": a.B, "H": a.H, "Lq": a.Lq, "Lk": a.Lk,
+            "kv_splits": a.kv_splits, "ms": ms, "tflops": 4 * a.B * a.H * a.Lq * a.Lk * 128 / ms / 1e9}
 
 
 def bench_ln(a):
@@ -129,6 +141,9 @@ def main():
     ap.add_argument("--Lk", type=int, default=7854)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--tile-n", type=int, default=0, help="gemm tile width along N (0 = the library's choice)")
+    ap.add_argument("--kv-splits", type=int, default=0, help="attn: key splits (0 = the library's choice)")
+    ap.add_argument("--local", type=int, default=0, help="attn: the Q-local SP pattern with this many local keys")
+    ap.add_argument("--kv-splits-rem", type=int, default=0, help="attn --local: splits of the remote keys")
     ap.add_argument("--fp8", action="store_true", help="attn: the e4m3 variant (quantisation included in the time)")
     ap.add_argument("--f32", action="store_true", help="gemm residual epilogues / ln: the fp32 residual stream")
     ap.add_argument("--ss", default="self", choices=["self", "partials", "sums"], help="qknorm: where the sums of squares come from")
