@@ -185,12 +185,15 @@ def test_double_buffered_variant_needs_a_p_barrier_per_buffer():
 def run_persistent(units_nkv, ring, seed):
     """The shipped bf16 kernel's persistent form (attn_persistent_kernel): one CTA walks several
     units (query-tile pairs) of nkv key tiles each.  Q has one buffer (reloaded once the unit's last
-    QK is done: q_empty); the ring, s_full and p_full run on across units; the first P V of a unit
-    waits for the softmax warps to have read the previous unit's O (o_free)."""
+    QK is done: q_empty); the ring, s_full and the P barriers run on across units; the first P V of a
+    unit waits for the softmax warps to have read the previous unit's O (o_free).  P is handed over
+    in two parts: the first 96 key columns (p_part), on which the issuer starts the P V MMA, then the
+    last 32 (p_full)."""
     rnd = random.Random(seed)
     kv_full = [Bar(1) for _ in range(ring)]
     kv_empty = [Bar(1) for _ in range(ring)]
     s_full, p_full = [Bar(1) for _ in range(2)], [Bar(1) for _ in range(2)]
+    p_part = [Bar(1) for _ in range(2)]
     o_done, o_free = [Bar(1) for _ in range(2)], [Bar(1) for _ in range(2)]
     q_full, q_empty = Bar(1), Bar(1)
     pipe = []
@@ -222,8 +225,8 @@ def run_persistent(units_nkv, ring, seed):
                     if j == nkv - 1:
                         pipe.append(["commit", q_empty])
 
-            def pv(t, j):
-                pipe.append(["mma", rnd.randint(2, 4)])
+            def pv_rest(t, j):
+                pipe.append(["mma", rnd.randint(1, 2)])
                 if t == 1:
                     pipe.append(["commit", kv_empty[(g + 2 * j + 1) % ring]])
                 if j == nkv - 1:
@@ -235,10 +238,12 @@ def run_persistent(units_nkv, ring, seed):
             for j in range(nkv):
                 yield kv_wait(g + 2 * j + 1)
                 for t in (0, 1):
-                    yield ("wait", p_full[t], (jg + j) & 1)
+                    yield ("wait", p_part[t], (jg + j) & 1)
                     if j == 0:
                         yield ("wait", o_free[t], (i & 1) ^ 1)
-                    pv(t, j)
+                    pipe.append(["mma", rnd.randint(1, 3)])  # the P V K-steps over the first part
+                    yield ("wait", p_full[t], (jg + j) & 1)
+                    pv_rest(t, j)
                     if j + 1 < nkv:
                         if t == 0:
                             yield kv_wait(g + 2 * j + 2)
@@ -251,7 +256,9 @@ def run_persistent(units_nkv, ring, seed):
         for i, nkv in enumerate(units_nkv):
             for j in range(nkv):
                 yield ("wait", s_full[t], (jg + j) & 1)
-                yield ("work", rnd.randint(1, 12))
+                yield ("work", rnd.randint(1, 9))
+                p_part[t].arrive()
+                yield ("work", rnd.randint(1, 3))
                 p_full[t].arrive()
             yield ("wait", o_done[t], i & 1)
             yield ("work", rnd.randint(1, 6))  # the epilogue reads O_t

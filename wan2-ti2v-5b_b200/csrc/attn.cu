@@ -28,7 +28,10 @@
 // be rescaled before PV_t(j+1) is issued (which waits for this warpgroup's p_full).
 //
 // Warp roles (320 threads): warps 0-3 softmax of tile 0, warps 4-7 softmax of tile 1 (thread
-// row = TMEM lane), warp 8 TMA producer, warp 9 TMEM allocator + UMMA issuer.  K and V tiles
+// row = TMEM lane), warp 8 TMA producer, warp 9 TMEM allocator + UMMA issuer.  The persistent
+// bf16 kernel launches 384: warps 10 and 11 only complete the producer / MMA warpgroup, so that
+// setmaxnreg can move registers from it to the two softmax warpgroups (192 each, no spills), and
+// hands P to the P V MMA in two parts (the first 96 keys, then the last 32).  K and V tiles
 // stream through one ring (K_0, V_0, K_1, V_1, ...): 5 slots of 32 KB in the bf16 kernel, whose
 // P needs no shared memory, 3 slots of 16 KB in the e4m3 one.
 #include <atomic>
@@ -52,7 +55,9 @@ constexpr int A_SMEM_BYTES8 = A_TILES_END8 + 256 + 1024;
 constexpr float A_E4M3_MAX = 448.f;
 constexpr uint32_t A_TMEM_COLS = 512;
 constexpr int A_THREADS = 320;
+constexpr int A_THREADS_P = 384;  // persistent kernel: 10 working warps + 2 idle (setmaxnreg warpgroups)
 constexpr float A_RESCALE_THRESHOLD = 8.0f;  // log2 units
+constexpr int A_P_SPLIT = 96;  // bf16 kernel: keys of P handed to the P V MMA ahead of the rest
 
 struct AttnArgs {
   __nv_bfloat16* o;
@@ -385,7 +390,7 @@ __global__ void __launch_bounds__(A_THREADS, 1)
 //   * the first QKs of unit i+1 write S while the softmax warps still read unit i's O from TMEM;
 //     unit i+1's first P V (which overwrites O) waits for their o_free arrival;
 //   * the K/V ring, s_full and p_full run on across units (their phases count tiles globally).
-__global__ void __launch_bounds__(A_THREADS, 1)
+__global__ void __launch_bounds__(A_THREADS_P, 1)
     attn_persistent_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                            const __grid_constant__ CUtensorMap tmV, const AttnArgs args) {
   constexpr int TILE = A_TILE, RING = A_RING16;
@@ -405,8 +410,9 @@ __global__ void __launch_bounds__(A_THREADS, 1)
   const uint32_t o_done = m0 + 128;     // 2
   const uint32_t o_free = m0 + 144;     // 2
   const uint32_t done_bar = m0 + 160;   // 1
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(meta + 168);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(meta + 172);
+  const uint32_t p_part = m0 + 168;     // 2: the first A_P_SPLIT key columns of P_t are in TMEM
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(meta + 184);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(meta + 188);
   int* err = args.err;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -434,6 +440,7 @@ __global__ void __launch_bounds__(A_THREADS, 1)
     for (int t = 0; t < 2; ++t) {
       mbar_init(s_full + 8 * t, 1);
       mbar_init(p_full + 8 * t, 4);
+      mbar_init(p_part + 8 * t, 4);
       mbar_init(o_done + 8 * t, 1);
       mbar_init(o_free + 8 * t, 4);
     }
@@ -455,6 +462,11 @@ __global__ void __launch_bounds__(A_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  // Registers by warpgroup (setmaxnreg acts on whole warpgroups, hence the two idle warps 10, 11):
+  // the producer / MMA warpgroup gives up what the softmax warpgroups take, 256 x 192 + 128 x 96 =
+  // 61440 <= 384 x 168 at launch; the softmax code then runs without spills.
+  if (warp >= 8) {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 96;\n" ::: "memory");
   if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -529,7 +541,9 @@ __global__ void __launch_bounds__(A_THREADS, 1)
           }
         };
         auto pv = [&](int t, int j) -> bool {
-          if (!mbar_wait(p_full + 8 * t, (jg + j) & 1, abort_flag, err, kErrTimeoutAttnMma)) return false;
+          // P_t arrives in two parts: the K-steps over its first A_P_SPLIT keys start while the
+          // softmax warps still exponentiate the rest
+          if (!mbar_wait(p_part + 8 * t, (jg + j) & 1, abort_flag, err, kErrTimeoutAttnMma)) return false;
           // the unit's first P V overwrites O_t: the softmax warps must have read the last unit's
           if (j == 0 && !mbar_wait(o_free + 8 * t, (i & 1) ^ 1, abort_flag, err, kErrTimeoutAttnMma)) return false;
           const int slot = (g + 2 * j + 1) % RING;
@@ -538,8 +552,13 @@ __global__ void __launch_bounds__(A_THREADS, 1)
           const uint32_t pa = tmem_base + t * ABN;  // P_t over the first 64 columns of S_t
           const uint32_t vb = sbase + OFF_R + slot * TILE;
 #pragma unroll
-          for (int kk = 0; kk < ABN / 16; ++kk)
+          for (int kk = 0; kk < A_P_SPLIT / 16; ++kk)
             umma_bf16_tmem_a(d, pa + kk * 8, sw128_desc(vb + kk * 2048, A_BLK, 1024), idesc_o, (j | kk) != 0);
+          if (!mbar_wait(p_full + 8 * t, (jg + j) & 1, abort_flag, err, kErrTimeoutAttnMma)) return false;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = A_P_SPLIT / 16; kk < ABN / 16; ++kk)
+            umma_bf16_tmem_a(d, pa + kk * 8, sw128_desc(vb + kk * 2048, A_BLK, 1024), idesc_o, true);
           if (t == 1) umma_commit(kv_empty + 8 * slot);
           if (j == nkv - 1) umma_commit(o_done + 8 * t);
           return true;
@@ -572,7 +591,9 @@ __global__ void __launch_bounds__(A_THREADS, 1)
       umma_commit(done_bar);
       mbar_drain(done_bar, 0, err);
     }
+  }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 192;\n" ::: "memory");
     // ------------------------------------------------------------ softmax + output (warps 0..7)
     const int t = warp >> 2;                    // query tile of this warpgroup
     const int r = threadIdx.x & 127;            // query row within the tile == TMEM lane
@@ -621,11 +642,29 @@ __global__ void __launch_bounds__(A_THREADS, 1)
           l_run *= alpha;
           m_used = m_new;
         }
+        // Rescale O_t (rare) before any of this tile's P V: S_t(j) was issued after P V_t(j-1), so
+        // that has completed, and P V_t(j) waits for this warpgroup's p_part arrival below
+        if (any_need && j > 0) {
+#pragma unroll 1
+          for (int c = 0; c < AD / 32; ++c) {
+            float o[32];
+            tmem_ld32(t_o + c * 32, o);
+#pragma unroll
+            for (int k = 0; k < 32; ++k) o[k] *= alpha;
+            tmem_st32(t_o + c * 32, o);
+          }
+        }
         const float neg = -m_used;
         const float2 sl2v = make_float2(sl2, sl2), negv = make_float2(neg, neg);
         float2 acc2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
         for (int c = 0; c < ABN / 32; ++c) {
+          if (c == A_P_SPLIT / 32) {  // the first part of P_t is in TMEM: hand it to the P V MMA
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(p_part + 8 * t);
+          }
           uint32_t pk[16];
 #pragma unroll
           for (int k = 0; k < 32; k += 2) {
@@ -638,17 +677,6 @@ __global__ void __launch_bounds__(A_THREADS, 1)
         }
         tmem_wait_st();
         l_run += (acc2[0].x + acc2[0].y) + (acc2[1].x + acc2[1].y);
-        // Rescale O_t (rare): S_t(j) was issued after P V_t(j-1), so that has completed
-        if (any_need && j > 0) {
-#pragma unroll 1
-          for (int c = 0; c < AD / 32; ++c) {
-            float o[32];
-            tmem_ld32(t_o + c * 32, o);
-#pragma unroll
-            for (int k = 0; k < 32; ++k) o[k] *= alpha;
-            tmem_st32(t_o + c * 32, o);
-          }
-        }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(p_full + 8 * t);
@@ -888,7 +916,7 @@ int attn_launch(const wanb200_attn_params* p, int* err, cudaStream_t st, const A
     attn_fp8_kernel<<<grid, A_THREADS, A_SMEM_BYTES8, st>>>(tq, tk, tv, aa);
   } else {  // bf16: persistent, at most one CTA per SM walking the units
     const unsigned grid = (unsigned)std::min<int64_t>(units, num_sms());
-    attn_persistent_kernel<<<grid, A_THREADS, A_SMEM_BYTES, st>>>(tq, tk, tv, aa);
+    attn_persistent_kernel<<<grid, A_THREADS_P, A_SMEM_BYTES, st>>>(tq, tk, tv, aa);
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error("attention kernel launch", e);
