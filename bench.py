@@ -46,7 +46,7 @@ CTX_LEN, TEXT_DIM = 512, 4096
 # role, from ncu captures summarised in profiles/ (command lines there).
 NCU_TRAFFIC_PER_LAUNCH = {
     "attn_self": (364_468_992, "ncu dram__bytes_read.sum + dram__bytes_write.sum of the self-attention launch "
-                               "inside a 2-layer config-2 step (profiles/attn_fwd_self_b2h24_l7854.txt); "
+                               "inside a 2-layer config-2 step (profiles/attn_persistent_self_b2h24_l7854.txt); "
                                "algorithmic bytes q+k+v+o = 386 MB"),
 }
 

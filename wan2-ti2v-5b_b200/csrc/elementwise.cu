@@ -276,101 +276,91 @@ struct QkArgs {
   int seq_len;
 };
 
-// One warp per row: lane l holds the 16-byte vectors l, l + 32, ... (NV of them, 8 channels = 4
-// rotation pairs each) of each of the NSEC sections (q and k of self-attention, cross q alone),
-// so a row's loads are all in flight at once and its sum of squares is a warp butterfly -- no
-// block barrier.  `_tp_rms_qk` (models/fast_dit.py:134-147): x * rsqrt(ss/3072 + eps) * gamma,
-// then `_rope` (fast_dit.py:163-169): (x0, x1) -> (x0 c - x1 s, x0 s + x1 c) with the pair's
-// angle.  The sum of squares is either formed from the section's own bf16 values (ss[s] == NULL:
-// the section is the whole global dim, one GPU; the squares of the rounded values, as
-// `q.float().pow(2).sum(-1)`), or added from ss_parts partials per row (a SUMSQ GEMM's 32-column
-// chunks), or read as one finished sum; each lane adds its share in order, then the butterfly --
-// the same order on every run.
-template <int NSEC, int NV>
-__global__ void __launch_bounds__(256) qknorm_rope_kernel(const QkArgs a) {
+// One warp per (row, section): lane l holds the 16-byte vectors l, l + 32, ... (NV of them, 8
+// channels = 4 rotation pairs each) of one section of one row (q or k of self-attention, cross q
+// alone), so the section's loads are all in flight at once and its sum of squares is a warp
+// butterfly -- no block barrier; with one section per warp a thread needs few enough registers
+// for several blocks per SM, whose load and store phases then overlap.
+// `_tp_rms_qk` (models/fast_dit.py:134-147): x * rsqrt(ss/3072 + eps) * gamma, then `_rope`
+// (fast_dit.py:163-169): (x0, x1) -> (x0 c - x1 s, x0 s + x1 c) with the pair's angle.  The sum
+// of squares is either formed from the section's own bf16 values (ss[s] == NULL: the section is
+// the whole global dim, one GPU; the squares of the rounded values, as `q.float().pow(2).sum(-1)`),
+// or added from ss_parts partials per row (a SUMSQ GEMM's 32-column chunks), or read as one
+// finished sum; each lane adds its share in order, then the butterfly -- the same order on every
+// run.
+template <int NV>
+__global__ void __launch_bounds__(256, 2) qknorm_rope_kernel(const QkArgs a, int nsec) {
   const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int gw = blockIdx.x * 8 + (threadIdx.x >> 5);  // (row, section) of this warp
+  const int row = nsec == 2 ? gw >> 1 : gw, sec = nsec == 2 ? gw & 1 : 0;
   if (row >= a.rows) return;  // warp-uniform
   const int vpr = a.width >> 3;
-  uint4 raw[NSEC][NV];
+  __nv_bfloat16* xs = a.x + (int64_t)row * a.ld + (sec ? a.col0[1] : a.col0[0]);
+  const float* ss = sec ? a.ss[1] : a.ss[0];
+  const __nv_bfloat16* gamma = sec ? a.gamma[1] : a.gamma[0];
+  uint4 raw[NV];
 #pragma unroll
-  for (int s = 0; s < NSEC; ++s) {
-    const uint4* xr = reinterpret_cast<const uint4*>(a.x + (int64_t)row * a.ld + a.col0[s]);
+  for (int i = 0; i < NV; ++i) {
+    const int v = i * 32 + lane;
+    raw[i] = v < vpr ? reinterpret_cast<const uint4*>(xs)[v] : make_uint4(0u, 0u, 0u, 0u);
+  }
+  float q = 0.f;
+  if (a.self_ss) {  // grid-uniform branches
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      const int v = i * 32 + lane;
-      raw[s][i] = v < vpr ? xr[v] : make_uint4(0u, 0u, 0u, 0u);
+      float v[8];
+      unpack_bf16x8(raw[i], v);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) q = fmaf(v[k], v[k], q);
     }
+  } else if (a.ss_parts > 1) {
+    for (int k = lane; k < a.ss_parts; k += 32) q += __ldg(ss + (int64_t)row * a.ss_row_stride + k);
+  } else if (lane == 0) {
+    q = __ldg(ss + (int64_t)row * a.ss_row_stride);
   }
-  float sum[NSEC];
 #pragma unroll
-  for (int s = 0; s < NSEC; ++s) {
-    float q = 0.f;
-    if (a.self_ss) {  // grid-uniform branches
-#pragma unroll
-      for (int i = 0; i < NV; ++i) {
-        float v[8];
-        unpack_bf16x8(raw[s][i], v);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) q = fmaf(v[k], v[k], q);
-      }
-    } else if (a.ss_parts > 1) {
-      for (int k = lane; k < a.ss_parts; k += 32) q += __ldg(a.ss[s] + (int64_t)row * a.ss_row_stride + k);
-    } else if (lane == 0) {
-      q = __ldg(a.ss[s] + (int64_t)row * a.ss_row_stride);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
-    sum[s] = q;
-  }
+  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+  const float rs = rsqrtf(q * a.inv_dim + a.eps);
   const int pos = a.rope ? row % a.seq_len : 0;
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
     const int v = i * 32 + lane;
     if (v >= vpr) break;
     const int cv = v * 8;
-    float4 c4 = make_float4(1.f, 1.f, 1.f, 1.f), s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    float x[8], g[8];
+    unpack_bf16x8(raw[i], x);
+    unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(gamma + cv)), g);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) x[k] *= rs * g[k];
     if (a.rope) {
       const int pair0 = (cv & 127) >> 1;
-      c4 = __ldg(reinterpret_cast<const float4*>(a.cos + (int64_t)pos * 64 + pair0));
-      s4 = __ldg(reinterpret_cast<const float4*>(a.sin + (int64_t)pos * 64 + pair0));
+      const float4 c4 = __ldg(reinterpret_cast<const float4*>(a.cos + (int64_t)pos * 64 + pair0));
+      const float4 s4 = __ldg(reinterpret_cast<const float4*>(a.sin + (int64_t)pos * 64 + pair0));
+      float x0, x1;
+      x0 = x[0]; x1 = x[1]; x[0] = x0 * c4.x - x1 * s4.x; x[1] = x0 * s4.x + x1 * c4.x;
+      x0 = x[2]; x1 = x[3]; x[2] = x0 * c4.y - x1 * s4.y; x[3] = x0 * s4.y + x1 * c4.y;
+      x0 = x[4]; x1 = x[5]; x[4] = x0 * c4.z - x1 * s4.z; x[5] = x0 * s4.z + x1 * c4.z;
+      x0 = x[6]; x1 = x[7]; x[6] = x0 * c4.w - x1 * s4.w; x[7] = x0 * s4.w + x1 * c4.w;
     }
-#pragma unroll
-    for (int s = 0; s < NSEC; ++s) {
-      float x[8], g[8];
-      unpack_bf16x8(raw[s][i], x);
-      unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(a.gamma[s] + cv)), g);
-      const float rs = rsqrtf(sum[s] * a.inv_dim + a.eps);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) x[k] *= rs * g[k];
-      if (a.rope) {
-        float x0, x1;
-        x0 = x[0]; x1 = x[1]; x[0] = x0 * c4.x - x1 * s4.x; x[1] = x0 * s4.x + x1 * c4.x;
-        x0 = x[2]; x1 = x[3]; x[2] = x0 * c4.y - x1 * s4.y; x[3] = x0 * s4.y + x1 * c4.y;
-        x0 = x[4]; x1 = x[5]; x[4] = x0 * c4.z - x1 * s4.z; x[5] = x0 * s4.z + x1 * c4.z;
-        x0 = x[6]; x1 = x[7]; x[6] = x0 * c4.w - x1 * s4.w; x[7] = x0 * s4.w + x1 * c4.w;
-      }
-      uint4 u;
-      u.x = pack_bf16x2(x[0], x[1]);
-      u.y = pack_bf16x2(x[2], x[3]);
-      u.z = pack_bf16x2(x[4], x[5]);
-      u.w = pack_bf16x2(x[6], x[7]);
-      reinterpret_cast<uint4*>(a.x + (int64_t)row * a.ld + a.col0[s])[v] = u;
-    }
+    uint4 u;
+    u.x = pack_bf16x2(x[0], x[1]);
+    u.y = pack_bf16x2(x[2], x[3]);
+    u.z = pack_bf16x2(x[4], x[5]);
+    u.w = pack_bf16x2(x[6], x[7]);
+    reinterpret_cast<uint4*>(xs)[v] = u;
   }
 }
 
-template <int NSEC>
-static void launch_qknorm(const QkArgs& a, int nv, unsigned blocks, cudaStream_t st) {
+static void launch_qknorm(const QkArgs& a, int nsec, int nv, unsigned blocks, cudaStream_t st) {
   switch (nv) {
-    case 1: qknorm_rope_kernel<NSEC, 1><<<blocks, 256, 0, st>>>(a); break;
-    case 2: qknorm_rope_kernel<NSEC, 2><<<blocks, 256, 0, st>>>(a); break;
-    case 3: qknorm_rope_kernel<NSEC, 3><<<blocks, 256, 0, st>>>(a); break;
-    case 4: qknorm_rope_kernel<NSEC, 4><<<blocks, 256, 0, st>>>(a); break;
-    case 6: qknorm_rope_kernel<NSEC, 6><<<blocks, 256, 0, st>>>(a); break;
-    case 8: qknorm_rope_kernel<NSEC, 8><<<blocks, 256, 0, st>>>(a); break;
-    case 12: qknorm_rope_kernel<NSEC, 12><<<blocks, 256, 0, st>>>(a); break;
-    default: qknorm_rope_kernel<NSEC, 16><<<blocks, 256, 0, st>>>(a); break;
+    case 1: qknorm_rope_kernel<1><<<blocks, 256, 0, st>>>(a, nsec); break;
+    case 2: qknorm_rope_kernel<2><<<blocks, 256, 0, st>>>(a, nsec); break;
+    case 3: qknorm_rope_kernel<3><<<blocks, 256, 0, st>>>(a, nsec); break;
+    case 4: qknorm_rope_kernel<4><<<blocks, 256, 0, st>>>(a, nsec); break;
+    case 6: qknorm_rope_kernel<6><<<blocks, 256, 0, st>>>(a, nsec); break;
+    case 8: qknorm_rope_kernel<8><<<blocks, 256, 0, st>>>(a, nsec); break;
+    case 12: qknorm_rope_kernel<12><<<blocks, 256, 0, st>>>(a, nsec); break;
+    default: qknorm_rope_kernel<16><<<blocks, 256, 0, st>>>(a, nsec); break;
   }
 }
 
@@ -422,11 +412,8 @@ int qk_norm_rope(const wanb200_qknorm_params* p, cudaStream_t st) {
   // vectors per lane, rounded up to an instantiated count
   int nv = (int)((p->width / 8 + 31) / 32);
   nv = nv <= 4 ? nv : nv <= 6 ? 6 : nv <= 8 ? 8 : nv <= 12 ? 12 : 16;
-  const unsigned blocks = (unsigned)((p->rows + 7) / 8);  // 8 rows (warps) per block
-  if (p->nsections == 2)
-    launch_qknorm<2>(a, nv, blocks, st);
-  else
-    launch_qknorm<1>(a, nv, blocks, st);
+  const unsigned blocks = (unsigned)((p->rows * p->nsections + 7) / 8);  // 8 (row, section) warps per block
+  launch_qknorm(a, p->nsections, nv, blocks, st);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error("qknorm_rope_kernel launch", e);
   return WANB200_OK;
