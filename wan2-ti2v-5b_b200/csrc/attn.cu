@@ -390,7 +390,7 @@ __global__ void __launch_bounds__(A_THREADS, 1)
 //   * the first QKs of unit i+1 write S while the softmax warps still read unit i's O from TMEM;
 //     unit i+1's first P V (which overwrites O) waits for their o_free arrival;
 //   * the K/V ring, s_full and p_full run on across units (their phases count tiles globally).
-__global__ void __launch_bounds__(A_THREADS_P, 1)
+__global__ void __maxnreg__(160)
     attn_persistent_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                            const __grid_constant__ CUtensorMap tmV, const AttnArgs args) {
   constexpr int TILE = A_TILE, RING = A_RING16;
@@ -464,7 +464,8 @@ __global__ void __launch_bounds__(A_THREADS_P, 1)
 
   // Registers by warpgroup (setmaxnreg acts on whole warpgroups, hence the two idle warps 10, 11):
   // the producer / MMA warpgroup gives up what the softmax warpgroups take, 256 x 192 + 128 x 96 =
-  // 61440 <= 384 x 168 at launch; the softmax code then runs without spills.
+  // 61440 = 384 x 160 at launch; the softmax code then runs without spills, and the 4096 registers
+  // the launch leaves free fit a K/V push CTA beside it (wanb200_shard_gather on a side stream).
   if (warp >= 8) {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 96;\n" ::: "memory");
   if (warp == 8) {

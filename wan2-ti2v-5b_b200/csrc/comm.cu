@@ -85,35 +85,28 @@ struct GatherArgs {
 
 // One warp per (row, destination): blockIdx.y picks the destination, the warp's row is one of
 // the batch * valid_rows rows of the shard.  Lanes move consecutive 16-byte vectors, so every
-// store instruction of the warp writes 512 contiguous bytes of the peer's row.  At most 40
-// registers a thread (launch bounds of 6 CTAs of 256 threads per SM): the push runs on a side
-// stream while the local attention holds every SM with one CTA of 320 threads x 168 registers,
-// and at 48 registers a 256-thread push CTA did not fit in the 11776 registers left beside it,
-// so the push only started when the attention's CTAs exited.
-__global__ void __launch_bounds__(256, 6) shard_gather_kernel(const GatherArgs a) {
-  const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+// store instruction of the warp writes 512 contiguous bytes of the peer's row.  CTAs of 4 warps
+// at no more than 32 registers a thread (4096 registers): the push runs on a side stream while the
+// local attention holds every SM with one CTA of 384 threads x 160 registers at launch, and a
+// push CTA has to fit in the registers left beside it, or the push only starts once the
+// attention's CTAs have exited.
+__global__ void __launch_bounds__(128, 16) shard_gather_kernel(const GatherArgs a) {
+  const int64_t r = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
   if (r >= a.rows) return;
   const int lane = threadIdx.x & 31;
   const int64_t b = r / a.valid_rows, i = r - b * a.valid_rows;
-  __nv_bfloat16* dst = a.dst[0];
-  int64_t row0 = a.dst_row0[0];
-#pragma unroll
-  for (int k = 1; k < WANB200_MAX_PEERS; ++k)
-    if ((int)blockIdx.y == k) {
-      dst = a.dst[k];
-      row0 = a.dst_row0[k];
-    }
+  __nv_bfloat16* dst = a.dst[blockIdx.y];  // a uniform, constant-bank read (blockIdx.y < ndst)
+  const int64_t row0 = a.dst_row0[blockIdx.y];
   const uint4* s = reinterpret_cast<const uint4*>(a.src + (b * a.shard_rows + i) * a.src_ld);
   uint4* d = reinterpret_cast<uint4*>(dst + b * a.dst_batch_stride + (row0 + i) * a.dst_ld);
+  const int nv = a.vecs;
   int v = lane;
-  for (; v + 96 < a.vecs; v += 128) {
-    const uint4 x0 = s[v], x1 = s[v + 32], x2 = s[v + 64], x3 = s[v + 96];
+  for (; v + 32 < nv; v += 64) {  // two 512-byte segments of the row in flight per warp
+    const uint4 x0 = s[v], x1 = s[v + 32];
     d[v] = x0;
     d[v + 32] = x1;
-    d[v + 64] = x2;
-    d[v + 96] = x3;
   }
-  for (; v < a.vecs; v += 32) d[v] = s[v];
+  if (v < nv) d[v] = s[v];
 }
 
 int shard_gather(const wanb200_shard_gather_params* p, cudaStream_t st) {
@@ -145,9 +138,9 @@ int shard_gather(const wanb200_shard_gather_params* p, cudaStream_t st) {
   a.vecs = (int)(p->width / 8);
   a.dst_ld = p->dst_ld;
   a.dst_batch_stride = p->dst_batch_stride;
-  const int64_t blocks = (a.rows + 7) / 8;
+  const int64_t blocks = (a.rows + 3) / 4;  // 4 rows (warps) per CTA
   if (blocks > INT32_MAX || p->width / 8 > INT32_MAX) return set_error(WANB200_EINVAL, "shard_gather: too large");
-  shard_gather_kernel<<<dim3((unsigned)blocks, (unsigned)p->ndst), 256, 0, st>>>(a);
+  shard_gather_kernel<<<dim3((unsigned)blocks, (unsigned)p->ndst), 128, 0, st>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error("shard_gather_kernel launch", e);
   return WANB200_OK;
