@@ -474,6 +474,7 @@ def run_config4(args):
     e1.record(stream)
     barrier()
     e2e_s = max_over_ranks(e0.elapsed_time(e1) / 1e3, world, device)
+    derr = int(max_over_ranks(float(fast.check_device_errors(raise_error=False)), world, device))
     if rank == 0:
         L4 = GRID4[0] * GRID4[1] * GRID4[2]
         fl = block_flops(CFG_BATCH * L4, L4)
@@ -488,10 +489,13 @@ def run_config4(args):
                        "parallelism": lay.describe(world), "seq_len": L4, "layers": args.layers},
             "e2e": {"value": e2e_s, "unit": "s/loop", "h2d_bytes_per_loop": (latent_host.numel() + image_host.numel()) * 4,
                     "d2h_bytes_per_loop": out_host.numel() * 4},
-            "gpu_launches": launches, "loop_tflops": loop_flops / loop_s / 1e12, "clocks": clk}), flush=True)
+            "gpu_launches": launches, "loop_tflops": loop_flops / loop_s / 1e12, "clocks": clk,
+            "device_error": derr}), flush=True)
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
+    if derr:
+        raise SystemExit(f"invalid run: device error word {derr}")
 
 
 def main():
