@@ -29,11 +29,11 @@ struct LnArgs {
 
 // RW warps per row (4 when dim % 1024 == 0, 2 when dim % 512 == 0, else 1): thread t < 32*RW of the row holds the
 // 16-byte vectors at columns (i*32*RW + t)*8, i < NVEC = dim / (256*RW); the row statistics are
-// reduced over the row's warps through shared memory.  The grid is a few blocks per SM and every
-// warp group walks rows with a grid stride, loading its NEXT row into a second register buffer
-// before it reduces and writes the current one, so each SM keeps two rows per warp group in
-// flight to HBM instead of stalling on every row's loads; the warps of a row synchronise with
-// their own named barrier, never with the rest of the block.  x is loaded and the output stored
+// reduced over the row's warps through shared memory.  The grid is 4 blocks per SM (at most 64
+// registers a thread) and every warp group walks rows with a grid stride; the 32 warps per SM keep
+// 8 rows in flight to HBM (a next-row prefetch into a second register buffer held only 16 warps
+// per SM at 128 registers and was 3-7% slower); the warps of a row synchronise with their own
+// named barrier, never with the rest of the block.  x is loaded and the output stored
 // with the streaming cache hint, so the L1 keeps the frame's modulation rows that every row of the
 // frame re-reads (7% faster than default caching at config 2).
 //   MODE 0 (modulate): WanLayerNorm without affine (wan/modules/model.py:89-99), then
@@ -41,7 +41,7 @@ struct LnArgs {
 //     shift/scale[f, c] = modulation[idx, c] + e0[f, idx, c] (fast_dit.py:276-277).
 //   MODE 1 (affine): norm3 = WanLayerNorm(elementwise_affine=True) (model.py:207-209).
 //   XF32: x is fp32 (the residual stream kept in fp32 across the step); the output stays bf16.
-constexpr int LN_BLOCKS_PER_SM = 2;
+constexpr int LN_BLOCKS_PER_SM = 4;
 
 template <int MODE, int NVEC, bool PUSH, int RW, bool XF32>
 __global__ void __launch_bounds__(256, LN_BLOCKS_PER_SM) layernorm_kernel(const LnArgs a) {
@@ -83,11 +83,10 @@ __global__ void __launch_bounds__(256, LN_BLOCKS_PER_SM) layernorm_kernel(const 
     return tot;
   };
   if (row >= a.rows) return;  // uniform over a row's warps: they walk the same rows
-  uint4 xv[NVEC * W], xn[NVEC * W];
-  load(row, xv);
+  uint4 xv[NVEC * W];
   for (;; row += stride) {
     const bool more = row + stride < a.rows;
-    if (more) load(row + stride, xn);  // the next row's loads fly while this one is reduced
+    load(row, xv);
     float sum = 0.f;
 #pragma unroll
     for (int i = 0; i < NVEC; ++i) {
@@ -154,8 +153,6 @@ __global__ void __launch_bounds__(256, LN_BLOCKS_PER_SM) layernorm_kernel(const 
         if (p < a.npush) reinterpret_cast<uint4*>(a.push_out[p] + (a.push_row0 + row) * a.dim)[v] = u;
     }
     if (!more) break;
-#pragma unroll
-    for (int i = 0; i < NVEC * W; ++i) xv[i] = xn[i];
   }
 }
 
