@@ -58,6 +58,8 @@ constexpr int A_THREADS = 320;
 constexpr int A_THREADS_P = 384;  // persistent kernel: 10 working warps + 2 idle (setmaxnreg warpgroups)
 constexpr float A_RESCALE_THRESHOLD = 8.0f;  // log2 units
 constexpr int A_P_SPLIT = 96;  // bf16 kernel: keys of P handed to the P V MMA ahead of the rest
+static_assert(A_P_SPLIT % 32 == 0 && A_P_SPLIT > 0 && A_P_SPLIT < 128,
+              "the softmax hands P over in 32-key chunks");
 
 struct AttnArgs {
   __nv_bfloat16* o;
