@@ -360,6 +360,34 @@ def test_gemm_residual_fp32_stream():
     assert rel(out, res0 + a.float() @ w.float().t() + b.float()) < 1e-6
 
 
+@pytest.mark.parametrize("epi", [L.EPI_BIAS_GATE_RES, L.EPI_BIAS_RES])
+def test_gemm_fp32_stream_row_segment_epilogue(epi):
+    """The fp32 residual update in place at tile width 256 (the accumulator chunk staged in shared
+    memory, row-segment residual loads and stores) and 224 / 192 / 128 (one row per lane): the same
+    values as each other and as the fp32 reference, with a ragged last row block, a partial last
+    column tile and a sequence-shard frame map."""
+    Lx, nf, S, off = 540, 6, 300, 120
+    M, N, K = 2 * S, 672, 256
+    a, w, b = randn(M, K, seed=71), randn(N, K, scale=0.05, seed=72), randn(N, scale=0.1, seed=73)
+    res0 = torch.randn(M, N, generator=torch.Generator(device=DEV).manual_seed(74), device=DEV) * 3
+    mod = randn(6, N, scale=0.1, seed=75)
+    e0 = torch.randn(nf, 6, N, device=DEV) * 0.1
+    kw = dict(gate=(mod[2], e0[:, 2, :]), frames=(Lx, Lx // nf, off, S)) if epi == L.EPI_BIAS_GATE_RES else {}
+    y = a.float() @ w.float().t() + b.float()
+    if epi == L.EPI_BIAS_GATE_RES:
+        frame = ((torch.arange(M, device=DEV) % S) + off) // (Lx // nf)
+        y = y * (mod[2].float() + e0[frame, 2, :])
+    outs = {}
+    for tn in (256, 224, 192, 128):
+        res = res0.clone()
+        out = ops.linear(a, w, b, epilogue=epi, residual=res, out=res, tile_n=tn, **kw)
+        assert out is res
+        assert rel(res - res0, y) < 1e-5, tn
+        outs[tn] = res
+    for tn in (224, 192, 128):
+        assert rel(outs[tn], outs[256]) < 1e-6, tn
+
+
 def test_layernorm_reads_the_fp32_stream():
     B, Lx, nf, C = 2, 540, 6, 3072
     x = torch.randn(B * Lx, C, device=DEV) * 4 + 1

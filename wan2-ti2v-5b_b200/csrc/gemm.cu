@@ -45,6 +45,12 @@ struct GemmCfg {
   static constexpr int STAGING = EPI == WANB200_EPI_SCATTER ? 4 * 32 * STAGING_ROW : 0;
   static constexpr int FIXED = STAGING + 256 + 1024;  // staging + barriers + alignment slack
 };
+// The fp32 residual epilogues (GATE_RES / RES with an fp32 residual and output) can pass each
+// 32 x 32 accumulator chunk through 4 KB of shared memory per epilogue warp, so that the
+// residual loads and the output stores run along rows (8 lanes per 128-byte row segment, 4 rows
+// per instruction) instead of one row per lane (32 rows touched by every 16-byte access).  The
+// host uses it on 256-wide tiles, where it costs the TMA ring no stage.
+constexpr int G_RES_STAGING = G_EPI_WARPS * 32 * 32 * 4;  // 32 KB
 
 struct GemmArgs {
   void* d;  // bf16, or fp32 when out_f32
@@ -66,6 +72,7 @@ struct GemmArgs {
   int64_t shard_rows;
   int bn;  // tile width along N: multiple of 32, <= GBN
   int stages;             // TMA ring depth
+  int res_staging;        // bytes of the fp32 residual staging (0 or G_RES_STAGING)
   uint32_t stage_bytes;   // A tile + BN-wide W tile
   uint32_t tiles_bytes;   // stages * stage_bytes
   int* err;
@@ -219,6 +226,94 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmArgs& a, float* v,
   }
 }
 
+// The bf16 pair packed in one 32-bit word, as two floats (exact).
+__device__ __forceinline__ float bf16_lo(uint32_t u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
+
+// The fp32 residual epilogue of one tile for the epilogue warp on lane quarter `quad` that takes
+// the 32-column chunks half, half + 2, ...  Each 32 x 32 accumulator chunk (lane = row after the
+// tcgen05.ld) goes to the warp's 4 KB staging buffer and comes back with lane = (sub, cg): rows
+// 4i + sub (i = 0..7) of the chunk at columns 4cg..4cg+3, so every residual load and output store
+// covers 4 whole 128-byte row segments.  The 16-byte column groups of a staging row are XOR-
+// swizzled by the row's low three bits: the row-per-lane writes and the row-segment reads are
+// both free of bank conflicts.  The arithmetic per element is gemm_epilogue_chunk's (bias add,
+// then r + v * g for GATE_RES, v + r for RES), so both paths give the same bits.
+template <int EPI>
+__device__ __forceinline__ void residual_tile_staged(const GemmArgs& a, float* stg, uint32_t t_row, int m0, int n0,
+                                                     int quad, int half, int lane) {
+  const int sub = lane >> 3, cg = lane & 7;
+  const int rbase = m0 + quad * 32 + sub;  // the row of i = 0; a lane's rows step by 4
+  int fr[8];
+  if constexpr (EPI == WANB200_EPI_BIAS_GATE_RES) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int row = rbase + 4 * i;
+      fr[i] = row < a.M ? (int)frame_of_row(row, a.rows_per_seq, a.row_offset, a.seq_len, a.tokens_per_frame) : 0;
+    }
+  }
+  const float* res = static_cast<const float*>(a.residual);
+  float* out = static_cast<float*>(a.d);
+  const int nchunks = a.bn / 32;
+  // r[i]: the residual of row 4i + sub in the current chunk; each is reloaded for the warp's next
+  // chunk right after its use, so the loads run under the rest of this chunk and the next
+  // chunk's TMEM load
+  float4 r[8] = {};
+  if (n0 + half * 32 < a.N) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int row = rbase + 4 * i;
+      if (row < a.M) r[i] = *reinterpret_cast<const float4*>(res + (int64_t)row * a.ldr + n0 + half * 32 + 4 * cg);
+    }
+  }
+#pragma unroll 1
+  for (int c = half; c < nchunks; c += 2) {
+    const int col0 = n0 + c * 32;
+    if (col0 >= a.N) break;  // warp-uniform (N is a multiple of 32)
+    const bool more = c + 2 < nchunks && col0 + 64 < a.N;
+    float v[32];
+    tmem_ld32(t_row + c * 32, v);
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      *reinterpret_cast<float4*>(stg + lane * 32 + ((q ^ (lane & 7)) << 2)) =
+          make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    __syncwarp();
+    const uint2 bu = __ldg(reinterpret_cast<const uint2*>(a.bias + col0 + 4 * cg));
+    const float b[4] = {bf16_lo(bu.x), bf16_hi(bu.x), bf16_lo(bu.y), bf16_hi(bu.y)};
+    float gm[4] = {0.f, 0.f, 0.f, 0.f};
+    if constexpr (EPI == WANB200_EPI_BIAS_GATE_RES) {
+      const uint2 gu = __ldg(reinterpret_cast<const uint2*>(a.gate_mod + col0 + 4 * cg));
+      gm[0] = bf16_lo(gu.x);
+      gm[1] = bf16_hi(gu.x);
+      gm[2] = bf16_lo(gu.y);
+      gm[3] = bf16_hi(gu.y);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int rl = 4 * i + sub;
+      const int row = m0 + quad * 32 + rl;
+      const float4 x = *reinterpret_cast<const float4*>(stg + rl * 32 + ((cg ^ (rl & 7)) << 2));
+      if (row < a.M) {
+        float xv[4] = {x.x + b[0], x.y + b[1], x.z + b[2], x.w + b[3]};
+        const float rv[4] = {r[i].x, r[i].y, r[i].z, r[i].w};
+        if constexpr (EPI == WANB200_EPI_BIAS_GATE_RES) {
+          const float4 e = __ldg(reinterpret_cast<const float4*>(a.gate_e0 + (int64_t)fr[i] * a.gate_frame_stride +
+                                                                 col0 + 4 * cg));
+          const float g[4] = {gm[0] + e.x, gm[1] + e.y, gm[2] + e.z, gm[3] + e.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) xv[j] = rv[j] + xv[j] * g[j];
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) xv[j] += rv[j];
+        }
+        float* orow = out + (int64_t)row * a.ldd + col0 + 4 * cg;
+        *reinterpret_cast<float4*>(orow) = make_float4(xv[0], xv[1], xv[2], xv[3]);
+        if (more) r[i] = *reinterpret_cast<const float4*>(res + (int64_t)row * a.ldr + col0 + 64 + 4 * cg);
+      }
+    }
+    __syncwarp();  // the staging buffer is rewritten by the next chunk
+  }
+}
+
 template <int EPI>
 __global__ void __launch_bounds__(G_THREADS, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -229,7 +324,7 @@ __global__ void __launch_bounds__(G_THREADS, 1)
   const uint32_t tiles = smem_u32(smem);
   const int GSTAGES = args.stages;
   const uint32_t SB = args.stage_bytes;
-  uint8_t* meta = smem + args.tiles_bytes + GemmCfg<EPI>::STAGING;
+  uint8_t* meta = smem + args.tiles_bytes + GemmCfg<EPI>::STAGING + args.res_staging;
   const uint32_t full0 = smem_u32(meta);             // G_MAX_STAGES x 8
   const uint32_t empty0 = full0 + 8 * G_MAX_STAGES;  // G_MAX_STAGES x 8
   const uint32_t tfull0 = empty0 + 8 * G_MAX_STAGES;  // 2 x 8
@@ -378,6 +473,11 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                 *reinterpret_cast<const uint4*>(stg + rr * SR + lane * 16);
         }
         __syncwarp();
+      } else if (epi_has_residual(EPI) && args.res_staging) {
+        if constexpr (epi_has_residual(EPI)) {
+          float* stg = reinterpret_cast<float*>(smem + args.tiles_bytes + GemmCfg<EPI>::STAGING) + (warp - 2) * 1024;
+          residual_tile_staged<EPI>(args, stg, t_row, m0, n0, quad, half, lane);
+        }
       } else {
         uint4 res_next[8] = {}, res_cur[8];
         if constexpr (epi_has_residual(EPI)) load_residual_chunk(args, row, n0 + half * 32, res_next);
@@ -430,7 +530,7 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmA
     if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(gemm)", e);
     attr_set[dev].store(true, std::memory_order_release);
   }
-  const int smem = (int)ga.tiles_bytes + GemmCfg<EPI>::FIXED;
+  const int smem = (int)ga.tiles_bytes + GemmCfg<EPI>::FIXED + ga.res_staging;
   gemm_bf16_kernel<EPI><<<grid, G_THREADS, smem, st>>>(ta, tb, ga);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error("gemm_bf16_kernel launch", e);
@@ -543,6 +643,14 @@ int gemm_bf16(const wanb200_gemm_params* p, cudaStream_t st) {
   {
     const int fixed = scatter ? GemmCfg<WANB200_EPI_SCATTER>::FIXED : GemmCfg<WANB200_EPI_NONE>::FIXED;
     ga.stages = std::min<int>(G_MAX_STAGES, (G_SMEM_LIMIT - fixed) / (int)ga.stage_bytes);
+    // the row-segment fp32 residual epilogue on full-width tiles, where its staging leaves the
+    // ring depth as it is (measured at 15708 x 3072 x 3072: +6% GATE_RES, +10% RES; on 128-wide
+    // tiles it lost 0-5%, so narrower tiles keep one row per lane)
+    ga.res_staging = 0;
+    if ((epi == WANB200_EPI_BIAS_GATE_RES || epi == WANB200_EPI_BIAS_RES) && ga.res_f32 && ga.out_f32 &&
+        bn == GBN &&
+        std::min<int>(G_MAX_STAGES, (G_SMEM_LIMIT - fixed - G_RES_STAGING) / (int)ga.stage_bytes) == ga.stages)
+      ga.res_staging = G_RES_STAGING;
   }
   ga.tiles_bytes = (uint32_t)ga.stages * ga.stage_bytes;
   ga.err = err;
