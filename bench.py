@@ -350,7 +350,7 @@ def run_ours(args):
         achieved = work / n / (ms / n / 1e3) / 1e12
         roof = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s"}
     roof["frac"] = roof["achieved"] / roof["peak"]
-    roof["kernel"] = ("attn_fwd_kernel (" + dom[5:] + ")") if dom.startswith("attn") else (
+    roof["kernel"] = ("attn_persistent_kernel (" + dom[5:] + ")") if dom.startswith("attn") else (
         "gemm_bf16_kernel (" + dom[5:] + ")" if dom.startswith("gemm") else dom)
     roof["peak_kind"] = f"{peaks['source']} {'sustained bf16' if roof['bound'] == 'tensor' else 'HBM copy'}"
     if roof["bound"] == "tensor":
