@@ -16,7 +16,9 @@ Weights are seeded N(0, 0.02) bf16 with the TI2V-5B shapes, the text context is 
 `data` is synthetic.  `device_error` is the kernels' error word after all the timed steps (max
 over ranks); `parity` is the rel-RMS of the step-0 prediction against the fp32 CPU oracle over
 all the layers (N = 1; that oracle run is also the `cpu_baseline`) or against a single-GPU run of
-the same model (N > 1).  A non-zero error word or a parity miss ends the run with a non-zero
+the same model (N > 1).  `graph` (N = 1) is the device time per replay of the same step
+captured as one CUDA graph (`FastWanDiT.capture`) and whether its prediction equals the eager
+step's.  A non-zero error word or a parity miss ends the run with a non-zero
 status after the line is printed.  `--impl reference` times the CPU oracle (the reference's fp32
 block math, ref_fp32.main restated in oracle/dit_ref.py): one whole step on this host's cores.
 """
@@ -295,6 +297,28 @@ def run_ours(args):
     e2e_s = max_over_ranks(e0.elapsed_time(e1) / 1e3 / args.steps, world, device)
     assert torch.isfinite(out_host).all()
 
+    # ---- the same step captured as one CUDA graph (FastWanDiT.capture; single GPU only): device
+    # time per replay and whether its prediction equals the eager step's bit for bit
+    graph = None
+    if world == 1 and not args.no_graph:
+        try:
+            step = fast.capture(latent_dev)
+            for _ in range(args.warmup):
+                step(latent_dev, T_STEP)
+            barrier()
+            g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            g0.record(stream)
+            for _ in range(args.steps):
+                out_g = step(latent_dev, T_STEP)
+            g1.record(stream)
+            barrier()
+            graph = {"value": g0.elapsed_time(g1) / 1e3 / args.steps, "unit": "s/step", "steps": args.steps,
+                     "equal_to_eager": bool(torch.equal(out_g, fast(latent_dev, T_STEP))),
+                     "what": "FastWanDiT.capture: the whole step as one CUDA graph, replayed with the same inputs"}
+            del step, out_g
+        except RuntimeError as exc:  # reported, not fatal: the headline is the eager step above
+            graph = {"error": str(exc).splitlines()[0][:200]}
+
     # ---- device error word: every bounded wait inside the kernels of all the steps above
     derr = int(max_over_ranks(float(fast.check_device_errors(raise_error=False)), world, device))
 
@@ -394,6 +418,7 @@ def run_ours(args):
         "clocks": clk,
         "device_error": derr,
         "parity": parity,
+        "graph": graph,
     }
     if oracle_s is not None:
         line["cpu_baseline"] = {"value": oracle_s, "unit": "s/step", "cores": torch.get_num_threads(),
@@ -514,6 +539,8 @@ def main():
     ap.add_argument("--layers", type=int, default=30, help="blocks per step (30 for the bench line)")
     ap.add_argument("--no-cpu-baseline", action="store_true",
                     help="skip the CPU oracle step (the N = 1 cpu_baseline and parity keys)")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="skip the N = 1 CUDA-graph replay of the step (the graph key)")
     ap.add_argument("--workload", default="config2", choices=["config2", "config4"],
                     help="config2: the bench line (s/step at 7854 tokens); config4: one line for the "
                          "10-step UniPC loop at 27280 tokens (--loops loops timed)")

@@ -111,3 +111,23 @@ def test_denoise_loop_ends_with_the_device_error_check():
     with pytest.raises(WanB200Error, match="202"):
         denoise(Dit(), torch.randn(4, 3, 2, 2), 2, 5.0)
     assert len(calls) == 2
+
+
+def test_captured_step_refuses_the_multi_gpu_layouts():
+    """FastWanDiT.capture is single-GPU only: the CFG-parallel, TP and SP layouts run NCCL
+    collectives and peer barriers with host-side epochs that a graph replay would not advance."""
+    from wanb200 import CapturedStep
+
+    def bare(**kw):
+        fd = FastWanDiT.__new__(FastWanDiT)
+        fd.cfg_group, fd.pair_group, fd.tp_size, fd.sp, fd.kv_gather, fd.context = None, None, 1, False, None, None
+        for k, v in kw.items():
+            setattr(fd, k, v)
+        return fd
+
+    lat = torch.zeros(48, 2, 4, 4)
+    for kw in ({"cfg_group": 0}, {"tp_size": 2}, {"sp": True}, {"kv_gather": object()}, {"pair_group": object()}):
+        with pytest.raises(ValueError, match="single-GPU"):
+            bare(context=[None], **kw).capture(lat)
+    with pytest.raises(RuntimeError, match="set_context"):
+        CapturedStep(bare(), lat)

@@ -367,3 +367,46 @@ def test_embeddings_and_head_on_the_kernels_vs_oracle():
         parts = [fd.head_tokens(xp[:, r * S:(r + 1) * S].contiguous(), es.to(DEV), r * S) for r in range(sp)]
         got = torch.cat(parts, dim=1)[:, :L_]
         assert R.rel_rms(got.cpu(), tok.cpu()) < 1e-6, sp
+
+
+def test_captured_step_replays_the_eager_step():
+    """FastWanDiT.capture: the whole step as one CUDA graph gives the eager step's output bit for
+    bit (the same kernels in the same order), follows new latents and timesteps through its static
+    buffers (device or page-locked host latents), and refuses to run once set_context() replaced
+    the cross K/V baked into the graph."""
+    mg = torch.load(os.path.join(GOLD, "model_small.pt"), weights_only=False)
+    fast = _golden_dit(mg)
+    fast.set_context(mg["ctx"].to(DEV), mg["ctx_null"].to(DEV))
+    lat = mg["latent"].to(DEV)
+    lat2 = lat * 0.5 + 0.1
+    want1 = fast(lat, mg["t"])
+    want2 = fast(lat2, 500.0)
+    assert not torch.equal(want1, want2)
+    step = fast.capture(lat)
+    assert torch.equal(step(lat, mg["t"]), want1)
+    assert torch.equal(step(lat2.cpu().pin_memory(), 500.0), want2)
+    assert torch.equal(step(lat, mg["t"]), want1)
+    assert fast.check_device_errors() == 0
+    fast.set_context(mg["ctx"].to(DEV), mg["ctx_null"].to(DEV))
+    with pytest.raises(RuntimeError, match="capture again"):
+        step(lat, mg["t"])
+
+
+def test_captured_step_full_width():
+    """The captured step of the TI2V-5B architecture (dim 3072, 24 heads, 4 of its 30 layers, seeded
+    weights) at 1080 tokens: the full-size kernel configurations (tile widths, key splits) under
+    capture, bit-identical to the eager step for two timesteps."""
+    from wanb200 import TI2V_5B, random_model_state
+    spec = TI2V_5B
+    sd = random_model_state(spec, seed=21, device=DEV, num_layers=4)
+    g = torch.Generator().manual_seed(22)
+    lat = torch.randn(48, 6, 24, 30, generator=g).to(DEV)
+    ctx, ctx_null = torch.randn(512, 4096, generator=g), torch.randn(512, 4096, generator=g)
+    fast = FastWanDiT((spec, sd), (6, 12, 15), 5.0, DEV, num_layers=4)
+    fast.set_context(ctx.to(DEV), ctx_null.to(DEV))
+    want = [fast(lat, t) for t in (999.0, 321.0)]
+    step = fast.capture(lat)
+    for t, w in zip((999.0, 321.0), want):
+        got = step(lat, t)
+        assert got.dtype == torch.bfloat16 and torch.equal(got, w), t
+    assert fast.check_device_errors() == 0

@@ -11,7 +11,7 @@ sequence-parallel block of `WanSelfAttentionSP`), `FastBlockSP` (= `_FastBlockSP
 from ._lib import LIB_PATH, WanB200Error, device_error, load  # noqa: F401
 from .block import FastBlock, FastBlockSP, FastCrossKV  # noqa: F401
 from .checkpoint import load_wan_checkpoint, save_wan_checkpoint  # noqa: F401
-from .dit import FastWanDiT, block_flops, rope_tables  # noqa: F401
+from .dit import CapturedStep, FastWanDiT, block_flops, rope_tables  # noqa: F401
 from .unipc import FlowUniPC, denoise  # noqa: F401
 from .weights import TI2V_5B, BlockWeights, WanSpec, random_block_state, random_model_state  # noqa: F401
 

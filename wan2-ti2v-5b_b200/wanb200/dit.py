@@ -197,13 +197,17 @@ class FastWanDiT:
         context = ops.linear(h, ew["text2_w"], ew["text2_b"], epilogue=L.EPI_BIAS, kind="gemm_text")
         self.context = [kv(context.view(B, Lc, -1)) for kv in self.cross_kv]
 
-    def _sinusoid(self, t):
-        """The per-frame sinusoid of timestep t (float64 on the host, frame 0 at t = 0, as
-        `_time_embed` computes it, fast_dit.py:677-684) in bf16 on the device, through a two-slot
-        page-locked ring so that the copy is asynchronous."""
+    def _sinusoid_host(self, t):
+        """The per-frame sinusoid of timestep t in bf16 on the host (float64 arithmetic, frame 0
+        at t = 0, as `_time_embed` computes it, fast_dit.py:677-684)."""
         tf = torch.full((self.num_frames,), float(t), dtype=torch.float64)
         tf[0] = 0.0
-        s = sinusoidal_embedding_1d(self.spec.freq_dim, tf).to(BF16)
+        return sinusoidal_embedding_1d(self.spec.freq_dim, tf).to(BF16)
+
+    def _sinusoid(self, t):
+        """The per-frame sinusoid of timestep t in bf16 on the device, through a two-slot
+        page-locked ring so that the copy is asynchronous."""
+        s = self._sinusoid_host(t)
         if self._sin_ring is None:
             self._sin_ring = [[torch.empty_like(s).pin_memory(), torch.empty_like(s, device=self.device), None]
                               for _ in range(2)]
@@ -222,8 +226,11 @@ class FastWanDiT:
         """Per-frame embedding, frame 0 (the image frame) at t=0 (fast_dit.py:677-687):
         time_embedding = Linear, SiLU, Linear; time_projection = SiLU, Linear.  Returns
         e [F, C] fp32 (the head's modulation rows) and e0 [F, 6, C] fp32 (the blocks')."""
+        return self.time_embed_from(self._sinusoid(t))
+
+    def time_embed_from(self, s):
+        """time_embed from the sinusoid s [F, freq_dim] bf16 already on the device."""
         ew, F_, C = self.ew, self.num_frames, self.spec.dim
-        s = self._sinusoid(t)
         a1 = ops.linear(s, ew["time0_w"], ew["time0_b"], epilogue=L.EPI_BIAS_SILU, kind="gemm_time")
         e = torch.empty(F_, C, device=self.device, dtype=torch.float32)
         ops.linear(a1, ew["time2_w"], ew["time2_b"], epilogue=L.EPI_BIAS, out=e, kind="gemm_time")
@@ -357,6 +364,83 @@ class FastWanDiT:
     @property
     def launches_per_step(self) -> int:
         return sum(b.launches for b in self.blocks)
+
+    def capture(self, latent_like) -> "CapturedStep":
+        """The whole noise prediction (time and patch embeddings, every block, head, CFG combine)
+        captured as one CUDA graph for latents shaped like `latent_like`; single GPU only.  Call
+        it after set_context(); it runs the step once to warm up, then captures it."""
+        return CapturedStep(self, latent_like)
+
+
+class CapturedStep:
+    """One CFG noise prediction of a single-GPU FastWanDiT, captured as a CUDA graph.
+
+    The graph holds every launch of `FastWanDiT.__call__`: the time-embedding GEMMs (read from a
+    static sinusoid buffer), patchify and the patch-embedding GEMM (from a static latent buffer),
+    the blocks, the head and the CFG combine (into a static output).  A call computes the sinusoid
+    of t on the host, copies it (through page-locked memory) and the latent into the static
+    buffers on the current stream, replays the graph and returns a copy of the output: one graph
+    launch per step instead of ~400 kernel launches issued from Python.  The kernels and their
+    order are the eager step's, so the output is the same bit for bit.  The reference compiles its
+    whole step for its device for the same reason (`torch.compile(backend="neuron")` of the
+    block stack, fast_dit.py:586, 646-649).
+
+    The cross K/V that set_context() made are baked into the graph by address: after a later
+    set_context() a call raises (capture again).  The multi-GPU layouts are refused: their NCCL
+    collectives and peer barriers take host-side epochs that a replay would not advance.
+    """
+
+    def __init__(self, model: FastWanDiT, latent_like):
+        if (model.cfg_group is not None or model.tp_size > 1 or model.sp or model.kv_gather is not None
+                or model.pair_group is not None):
+            raise ValueError("CapturedStep: single-GPU layout only (no CFG / TP / SP groups)")
+        if model.context is None:
+            raise RuntimeError("call set_context() first")
+        dev = model.device
+        self.model = model
+        self._ctx = model.context
+        self.latent = torch.empty(tuple(latent_like.shape), dtype=latent_like.dtype, device=dev)
+        self.latent.copy_(latent_like)
+        s = model._sinusoid_host(0.0)
+        self._sin_host = torch.empty_like(s).pin_memory()
+        self._sin = s.to(dev)
+        self._sin_copied = None  # event after the last copy out of _sin_host
+        # warm-up outside the capture: every lazy setup (kernel attributes, workspaces) happens here
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            self._body()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = self._body()
+
+    def _body(self):
+        m = self.model
+        e, e0 = m.time_embed_from(self._sin)
+        return m.head(m.forward_blocks(m.patch(self.latent), e0), e)
+
+    def __call__(self, latent, t):
+        """latent [C, F, H, W] (device, or page-locked host memory), timestep t -> [C, F, H, W] bf16."""
+        m = self.model
+        if m.context is not self._ctx:
+            raise RuntimeError("set_context() replaced the cross K/V after the capture: capture again")
+        L.raise_on_device_error(m._err_probe.poll(), "CapturedStep")
+        s = m._sinusoid_host(t)
+        if self._sin_copied is not None:
+            self._sin_copied.synchronize()  # the previous call's copy has read the page-locked buffer
+        self._sin_host.copy_(s)
+        stream = torch.cuda.current_stream(m.device)
+        self._sin.copy_(self._sin_host, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        self._sin_copied = ev
+        self.latent.copy_(latent, non_blocking=True)
+        self.graph.replay()
+        out = self.out.clone()
+        m._err_probe.post()
+        return out
 
 
 def block_flops(n_tok: int, seq_len: int, dim: int = 3072, ffn: int = 14336, heads: int = 24, ctx_len: int = 512,
