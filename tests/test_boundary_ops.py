@@ -131,3 +131,9 @@ def test_captured_step_refuses_the_multi_gpu_layouts():
             bare(context=[None], **kw).capture(lat)
     with pytest.raises(RuntimeError, match="set_context"):
         CapturedStep(bare(), lat)
+    # the denoise loop's closing check reaches the captured model's error word
+    step = CapturedStep.__new__(CapturedStep)
+    step.model = _bare(401)
+    with pytest.raises(WanB200Error, match="device error word 401"):
+        step.check_device_errors()
+    assert step.check_device_errors(raise_error=False) == 401

@@ -386,7 +386,11 @@ def test_captured_step_replays_the_eager_step():
     assert torch.equal(step(lat, mg["t"]), want1)
     assert torch.equal(step(lat2.cpu().pin_memory(), 500.0), want2)
     assert torch.equal(step(lat, mg["t"]), want1)
-    assert fast.check_device_errors() == 0
+    assert fast.check_device_errors() == 0 and step.check_device_errors() == 0
+    # the denoise loop driven by the captured step: the eager loop's latent bit for bit
+    from wanb200.unipc import denoise
+    img = torch.randn(lat.shape[0], 1, lat.shape[2], lat.shape[3], generator=torch.Generator().manual_seed(9))
+    assert torch.equal(denoise(step, lat, 3, 5.0, img.to(DEV)), denoise(fast, lat, 3, 5.0, img.to(DEV)))
     fast.set_context(mg["ctx"].to(DEV), mg["ctx_null"].to(DEV))
     with pytest.raises(RuntimeError, match="capture again"):
         step(lat, mg["t"])

@@ -442,6 +442,10 @@ class CapturedStep:
         m._err_probe.post()
         return out
 
+    def check_device_errors(self, raise_error: bool = True) -> int:
+        """FastWanDiT.check_device_errors of the captured model (the denoise loop ends with it)."""
+        return self.model.check_device_errors(raise_error)
+
 
 def block_flops(n_tok: int, seq_len: int, dim: int = 3072, ffn: int = 14336, heads: int = 24, ctx_len: int = 512,
                 batch: int = 2) -> dict:
