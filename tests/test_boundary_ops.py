@@ -131,8 +131,14 @@ def test_captured_step_refuses_the_multi_gpu_layouts():
             bare(context=[None], **kw).capture(lat)
     with pytest.raises(RuntimeError, match="set_context"):
         CapturedStep(bare(), lat)
-    # the denoise loop's closing check reaches the captured model's error word
+    # a latent of another shape is refused (copy_ would broadcast it into the static buffer)
     step = CapturedStep.__new__(CapturedStep)
+    step.model = _bare(0)
+    step._ctx = step.model.context
+    step.latent = torch.zeros(48, 2, 4, 4)
+    with pytest.raises(ValueError, match="captured"):
+        step(torch.zeros(48, 1, 4, 4), 999.0)
+    # the denoise loop's closing check reaches the captured model's error word
     step.model = _bare(401)
     with pytest.raises(WanB200Error, match="device error word 401"):
         step.check_device_errors()

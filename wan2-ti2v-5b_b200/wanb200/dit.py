@@ -426,6 +426,8 @@ class CapturedStep:
         m = self.model
         if m.context is not self._ctx:
             raise RuntimeError("set_context() replaced the cross K/V after the capture: capture again")
+        if tuple(latent.shape) != tuple(self.latent.shape):
+            raise ValueError(f"latent shape {tuple(latent.shape)} differs from the captured {tuple(self.latent.shape)}")
         L.raise_on_device_error(m._err_probe.poll(), "CapturedStep")
         s = m._sinusoid_host(t)
         if self._sin_copied is not None:
