@@ -28,6 +28,7 @@ import torch.distributed as dist
 
 from . import _lib as L
 from . import ops
+from . import block as _block_mod
 from .block import FastBlock, FastBlockSP, FastCrossKV, register_block
 from .weights import BlockWeights, WanSpec, block_state
 
@@ -386,7 +387,8 @@ class CapturedStep:
     block stack, fast_dit.py:586, 646-649).
 
     The cross K/V that set_context() made are baked into the graph by address: after a later
-    set_context() a call raises (capture again).  The multi-GPU layouts are refused: their NCCL
+    set_context() a call raises (capture again).  So are the blocks' shared scratch buffers and the
+    attention workspaces, which the object keeps alive.  The multi-GPU layouts are refused: their NCCL
     collectives and peer barriers take host-side epochs that a replay would not advance.
     """
 
@@ -415,6 +417,10 @@ class CapturedStep:
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
             self.out = self._body()
+        # the graph reads and writes the shared scratch buffers by address: hold them, so that a
+        # later clear_workspaces() or a grown workspace cannot hand their memory to other tensors
+        self._keep = (list(_block_mod._WS.values()), list(ops._WORKSPACES.values()),
+                      list(ops._FP8_WORKSPACES.values()))
 
     def _body(self):
         m = self.model
