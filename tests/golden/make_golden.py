@@ -235,12 +235,16 @@ def import_reference_scheduler():
 def unipc_golden():
     Sched = import_reference_scheduler()
     cases = []
-    for dtype, shift, steps in ((torch.float32, 5.0, 10), (torch.float32, 1.0, 10), (torch.bfloat16, 5.0, 10),
-                                (torch.float32, 5.0, 3)):
+    small, tiny = (1, 48, 2, 4, 6), (1, 48, 1, 2, 2)
+    for dtype, shift, steps, shape in ((torch.float32, 5.0, 10, small), (torch.float32, 1.0, 10, small),
+                                       (torch.bfloat16, 5.0, 10, small), (torch.float32, 5.0, 3, small),
+                                       # the pipeline's default 50 steps, a 2-step (first-order only)
+                                       # schedule, and a bf16 latent over 25 steps at shift 3
+                                       (torch.float32, 5.0, 50, tiny), (torch.float32, 5.0, 2, tiny),
+                                       (torch.bfloat16, 3.0, 25, tiny)):
         s = Sched(num_train_timesteps=1000, shift=1, use_dynamic_shifting=False)
         s.set_timesteps(steps, device=torch.device("cpu"), shift=shift)
         g = torch.Generator().manual_seed(len(cases))
-        shape = (1, 48, 2, 4, 6)
         x = torch.randn(shape, generator=g).to(dtype)
         x_init, outs, mos = x.clone(), [], []
         for i, t in enumerate(s.timesteps):

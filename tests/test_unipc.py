@@ -3,8 +3,9 @@
 tests/golden/make_golden.py exactly as inference_neuron_ti2v.py:497-532 runs it.
 
 On the CPU the restatement must reproduce the reference bit for bit: the timesteps, the sigma
-schedule and every step's sample, for fp32 and bf16 latents, shift 5 (the pipeline's) and 1
-(the linear schedule of the 27280-token workload), 10 and 3 steps.
+schedule and every step's sample, for fp32 and bf16 latents, shift 5 (the pipeline's), 3 and 1
+(the linear schedule of the 27280-token workload), 50 (the pipeline's default), 25, 10, 3 and 2
+(first-order only) steps.
 """
 import os
 
